@@ -1,0 +1,374 @@
+"""Benchmark: MX-int4 7B-MLP linear pair (up 4096->11008, down 11008->4096),
+the reference's MX qlinear hot path, on B200.
+
+One step = one token batch through quantise(x) -> up GEMV -> requantise ->
+down GEMV (fp32 in, fp32 out).  The headline is batch 1 (decode); batches 8,
+64 and 512 (GEMV -> tensor-core GEMM crossover) are reported under "sweep".
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Under torchrun each rank runs an independent replica on its own GPU (weights
+replicated, its own token stream; no collective on the data path), so
+`value` is the whole-job tokens/s over all ranks and scaling is weak.
+
+Weights: int4 uniform in [-8, 7], E8M0 exponents uniform in [-8, -3];
+activations fp32 N(0, 1) (seeded synthetic data, see cpu_model_b200.synth).
+Eight distinct copies of the weight pair (8 x 47.9 MB = 383 MB, > 3x the
+126 MB L2) are rotated step by step, so every step streams its weights from
+HBM.
+"""
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+UP = (11008, 4096)     # (N, K)
+DOWN = (4096, 11008)
+EMIN, EMAX = -8, -3
+COPIES = 8
+SWEEP = [8, 64, 512]
+
+
+def pair_bytes(b):
+    """Algorithmic bytes of one pair step: packed int4 weights + E8M0 scales
+    + MX activations in (u8 + scale) + fp32 outputs, for both linears."""
+    tot = 0
+    for n, k in (UP, DOWN):
+        tot += n * k // 2 + n * k // 32 + b * (k + k // 32) + b * n * 4
+    return tot
+
+
+def gemv_bytes(n, k, b):
+    return n * k // 2 + n * k // 32 + b * (k + k // 32) + b * n * 4
+
+
+def pair_flops(b):
+    return 2 * b * (UP[0] * UP[1] + DOWN[0] * DOWN[1])
+
+
+def load_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return {"hbm_gbs": d["hbm_gbs"], "bf16_tflops": d["bf16_tflops"], "src": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "src": "fallback"}
+
+
+class Clocks:
+    """nvidia-smi sampling during the timed region."""
+
+    def __init__(self, index):
+        self.index = index
+        self.proc = None
+        self.path = None
+
+    def __enter__(self):
+        fd, self.path = tempfile.mkstemp(suffix=".csv")
+        os.close(fd)
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.index),
+                 "--query-gpu=clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+                 "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+                 "clocks_event_reasons.sw_power_cap",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except (OSError, FileNotFoundError):
+            self.proc = None
+        time.sleep(0.3)
+        return self
+
+    def __exit__(self, *a):
+        if self.proc:
+            self.proc.terminate()
+            self.proc.wait()
+
+    def summary(self):
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        try:
+            for line in open(self.path):
+                f = [v.strip() for v in line.split(",")]
+                if len(f) < 7:
+                    continue
+                try:
+                    sm.append(float(f[0]))
+                    mx.append(float(f[1]))
+                except ValueError:
+                    continue
+                for nm, v in zip(names, f[3:7]):
+                    if v.lower() == "active":
+                        reasons.add(nm)
+            os.remove(self.path)
+        except OSError:
+            pass
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def dist_env():
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return rank, world, local
+
+
+# --------------------------------------------------------------- CPU ---
+def cpu_pair_sample(seconds=10.0, batch=1, threads=0):
+    """The multi-threaded dpbusd restatement of the removed reference VNNI
+    kernel (oracle/mx_cpu_baseline.c), timed on the host over whole pair
+    steps for about `seconds`."""
+    from oracle import oracle
+    from cpu_model_b200 import synth
+    wu, su = synth.weights(4, UP[0], UP[1], EMIN, EMAX, 101)
+    wd, sd = synth.weights(4, DOWN[0], DOWN[1], EMIN, EMAX, 102)
+    swu = oracle.weight_sums(4, wu, *UP)
+    swd = oracle.weight_sums(4, wd, *DOWN)
+    x = synth.normal((batch, UP[1]), 103)
+    steps = 0
+    used = False
+    t0 = time.perf_counter()
+    while True:
+        xq, xs = oracle.quantize_x(x)
+        y1, used = oracle.baseline_gemv(4, xq, xs, wu, su, swu, UP[0], UP[1], threads)
+        hq, hs = oracle.quantize_x(y1)
+        oracle.baseline_gemv(4, hq, hs, wd, sd, swd, DOWN[0], DOWN[1], threads)
+        steps += 1
+        el = time.perf_counter() - t0
+        if el >= seconds:
+            break
+    cores = threads if threads > 0 else oracle.max_threads()
+    return {"value": batch * steps / el, "unit": "tokens/s", "cores": cores, "kind": "port",
+            "sample": "%d pair steps at batch %d (%.1f s), %s" % (
+                steps, batch, el, "AVX-512 VNNI dpbusd" if used else "portable int loop")}
+
+
+def run_reference(args):
+    rank, world, _ = dist_env()
+    if rank != 0:
+        return
+    os.environ.setdefault("OMP_NUM_THREADS", str(os.cpu_count()))
+    from oracle import oracle
+    oracle.build()
+    per_step = []
+    for i in range(args.warmup + args.steps):
+        s = cpu_pair_sample(seconds=1.0, batch=1)
+        if i >= args.warmup:
+            per_step.append(s)
+    value = statistics.mean(p["value"] for p in per_step)
+    line = {
+        "impl": "reference", "metric": "MX-int4 qlinear tokens/s (7B MLP up+down pair)",
+        "value": value, "unit": "tokens/s", "n_gpus": args.gpus, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": 1000.0 / value, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "mx-int4 (int4 w, int8 a, int32 dot, fp32 sum)",
+        "data": "synthetic", "config": workload_config(1),
+        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": per_step[0]["cores"], "kind": "port",
+                         "sample": "each step ~1 s of whole pair steps at batch 1 (CPU restatement of the "
+                                   "reference's removed AVX-512 VNNI MX kernel; the reference's own MX code is "
+                                   "absent from its snapshot)"},
+        "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def workload_config(batch):
+    return {"workload": "mx_int4_mlp_pair_7b", "up": "4096->11008", "down": "11008->4096",
+            "batch": batch, "weights": "int4 [-8,7], E8M0 exp [-8,-3]", "activations": "fp32 N(0,1) -> MX-int8",
+            "l2": "rotating %d weight copies (%.0f MB) > 126 MB L2" % (COPIES, COPIES * pair_bytes(0) / 1e6),
+            "parallelism": "replicas"}
+
+
+# --------------------------------------------------------------- GPU ---
+def run_ours(args):
+    import torch
+    rank, world, local = dist_env()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
+    from cpu_model_b200 import mx, synth
+
+    ctx = mx.MXContext(local)
+    peaks = load_peaks()
+    stream = torch.cuda.current_stream(dev)
+
+    # weights: COPIES distinct pairs (seeded per copy), uploaded once
+    pairs = []
+    for c in range(COPIES):
+        wu, su = synth.weights(4, UP[0], UP[1], EMIN, EMAX, 1000 + 2 * c)
+        wd, sd = synth.weights(4, DOWN[0], DOWN[1], EMIN, EMAX, 1001 + 2 * c)
+        pairs.append((mx.MXWeight(torch.from_numpy(wu), torch.from_numpy(su), 4, UP[0], UP[1], ctx),
+                      mx.MXWeight(torch.from_numpy(wd), torch.from_numpy(sd), 4, DOWN[0], DOWN[1], ctx)))
+    ctx.reserve(max(SWEEP + [args.batch]), DOWN[1])
+
+    def barrier():
+        if world > 1:
+            import torch.distributed as dist
+            dist.barrier()
+
+    def max_over_ranks(v):
+        if world == 1:
+            return v
+        import torch.distributed as dist
+        t = torch.tensor([v], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def time_pairs(batch, steps, warmup):
+        x = torch.from_numpy(synth.normal((batch, UP[1]), 7 + rank)).to(dev)
+        y = torch.empty((batch, DOWN[0]), dtype=torch.float32, device=dev)
+        ctx._bind()
+        lib = ctx.lib
+        for i in range(warmup):
+            wu, wd = pairs[i % COPIES]
+            mx.check(lib.mxq_linear_pair(ctx.h, wu.h, wd.h, mx._ptr(x), batch, mx._ptr(y)), ctx.h)
+        ctx.synchronize()
+        barrier()
+        torch.cuda.synchronize()
+        l0 = ctx.launch_count()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for i in range(steps):
+            wu, wd = pairs[(warmup + i) % COPIES]
+            mx.check(lib.mxq_linear_pair(ctx.h, wu.h, wd.h, mx._ptr(x), batch, mx._ptr(y)), ctx.h)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        barrier()
+        ms = max_over_ranks(e0.elapsed_time(e1))
+        ctx.synchronize()
+        return ms / steps, ctx.launch_count() - l0
+
+    def time_gemv(batch, steps):
+        """The dominant kernel alone: the up-projection linear kernel (GEMV or
+        tensor-core GEMM by batch) on pre-quantised activations, rotating
+        weight copies; CUDA events on the launching stream."""
+        x = torch.from_numpy(synth.normal((batch, UP[1]), 9)).to(dev)
+        a = mx.mx_quantize_x(x, ctx)
+        y = torch.empty((batch, UP[0]), dtype=torch.float32, device=dev)
+        lib = ctx.lib
+        ctx._bind()
+        for i in range(3):
+            mx.check(lib.mxq_gemv(ctx.h, pairs[i % COPIES][0].h, mx._ptr(a.q), mx._ptr(a.s), batch, mx._ptr(y)), ctx.h)
+        torch.cuda.synchronize()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for i in range(steps):
+            mx.check(lib.mxq_gemv(ctx.h, pairs[i % COPIES][0].h, mx._ptr(a.q), mx._ptr(a.s), batch, mx._ptr(y)), ctx.h)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        ctx.synchronize()
+        return e0.elapsed_time(e1) / steps
+
+    def time_e2e(batch, steps):
+        """Through the public host-buffer entry (mxq_linear_pair_host):
+        pinned x in, y out, copies inside the timed region."""
+        xh = torch.from_numpy(synth.normal((batch, UP[1]), 11)).pin_memory()
+        yh = torch.empty((batch, DOWN[0]), dtype=torch.float32).pin_memory()
+        lib = ctx.lib
+        ctx._bind()
+        for i in range(3):
+            wu, wd = pairs[i % COPIES]
+            mx.check(lib.mxq_linear_pair_host(ctx.h, wu.h, wd.h, mx._ptr(xh), batch, mx._ptr(yh)), ctx.h)
+        barrier()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for i in range(steps):
+            wu, wd = pairs[i % COPIES]
+            mx.check(lib.mxq_linear_pair_host(ctx.h, wu.h, wd.h, mx._ptr(xh), batch, mx._ptr(yh)), ctx.h)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        barrier()
+        ms = max_over_ranks(e0.elapsed_time(e1)) / steps
+        return ms, batch * UP[1] * 4, batch * DOWN[0] * 4
+
+    b = args.batch
+    with Clocks(local) as clk:
+        ms, launches = time_pairs(b, args.steps, args.warmup)
+    clocks = clk.summary()
+    value = world * b / (ms / 1e3)
+    gemv_ms = time_gemv(b, max(args.steps, 20))
+    gbytes = gemv_bytes(UP[0], UP[1], b)
+    achieved = gbytes / (gemv_ms / 1e3) / 1e9
+    e2e_ms, h2d, d2h = time_e2e(b, max(10, args.steps // 4))
+
+    sweep = {}
+    for sb in ([] if args.no_sweep else SWEEP):
+        sms, _ = time_pairs(sb, max(10, args.steps // 4), 3)
+        kms = time_gemv(sb, 20)
+        fl = 2 * sb * UP[0] * UP[1]
+        entry = {"tokens_per_s": world * sb / (sms / 1e3), "ms_per_step": sms,
+                 "up_kernel_ms": kms,
+                 "up_kernel_hbm_gbs": gemv_bytes(UP[0], UP[1], sb) / (kms / 1e3) / 1e9,
+                 "up_kernel_tflops": fl / (kms / 1e3) / 1e12}
+        entry["path"] = "gemv-dp4a" if sb <= 8 else "tcgen05-bf16"
+        sweep[str(sb)] = entry
+
+    if rank == 0:
+        line = {
+            "metric": "MX-int4 qlinear tokens/s (7B MLP up+down pair)",
+            "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "mx-int4 (int4 w, int8 a, int32 dot, fp32 sum)",
+            "data": "synthetic", "config": workload_config(b),
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                         "frac": achieved / peaks["hbm_gbs"], "traffic": None,
+                         "kernel": "gemv_kernel<int4> (up 4096->11008)",
+                         "algorithmic_bytes_per_launch": gbytes, "launch_ms": gemv_ms,
+                         "peak_src": peaks["src"] + " hbm_gbs (burst copy)"},
+            "pair_hbm_gbs": pair_bytes(b) / (ms / 1e3) / 1e9,
+            "e2e": {"value": world * b / (e2e_ms / 1e3), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": d2h, "api": "mxq_linear_pair_host"},
+            "gpu_launches": launches,
+            "clocks": clocks,
+            "sweep": sweep,
+        }
+        if world == 1 and not args.no_cpu:
+            line["cpu_baseline"] = cpu_pair_sample(seconds=args.cpu_seconds, batch=b)
+        print(json.dumps(line), flush=True)
+
+    for p in pairs:
+        p[0].close()
+        p[1].close()
+    ctx.close()
+    if world > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--batch", type=int, default=1)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-sweep", action="store_true")
+    ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

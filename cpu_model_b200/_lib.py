@@ -1,0 +1,96 @@
+"""ctypes binding of libmxq.so (include/mxq.h).
+
+The shared library is the product: there is no CPU or PyTorch fallback.  If
+the library is missing the import fails loudly; if no sm_100a device is
+present, creating a context fails with MXQ_ERR_UNSUPPORTED / CUDA errors.
+"""
+import ctypes
+import os
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "libmxq.so")
+
+MXQ_OK = 0
+MXQ_ERR_INVALID_ARGUMENT = -1
+MXQ_ERR_CUDA = -2
+MXQ_ERR_TIMEOUT = -3
+MXQ_ERR_OUT_OF_MEMORY = -4
+MXQ_ERR_UNSUPPORTED = -5
+
+FMT_INT4 = 4
+FMT_INT8 = 8
+ACT_NONE = 0
+ACT_SILU = 1
+PATH_AUTO = 0
+PATH_GEMV = 1
+PATH_GEMM = 2
+
+_vp = ctypes.c_void_p
+_sz = ctypes.c_size_t
+_i = ctypes.c_int
+_f = ctypes.c_float
+
+# name -> argtypes (restype is int for all but mxq_last_error)
+SIGNATURES = {
+    "mxq_abi_version": [],
+    "mxq_create": [_i, ctypes.POINTER(_vp)],
+    "mxq_destroy": [_vp],
+    "mxq_set_stream": [_vp, _vp],
+    "mxq_set_path": [_vp, _i],
+    "mxq_reserve": [_vp, _sz, _sz],
+    "mxq_synchronize": [_vp],
+    "mxq_last_error": [_vp],
+    "mxq_launch_count": [_vp, ctypes.POINTER(ctypes.c_uint64)],
+    "mxq_weight_create": [_vp, _i, _sz, _sz, _vp, _vp, _i, ctypes.POINTER(_vp)],
+    "mxq_weight_destroy": [_vp],
+    "mxq_weight_shape": [_vp, ctypes.POINTER(_i), ctypes.POINTER(_sz), ctypes.POINTER(_sz)],
+    "mxq_quantize_x": [_vp, _vp, _sz, _sz, _i, _vp, _vp],
+    "mxq_swiglu_quantize": [_vp, _vp, _vp, _sz, _sz, _vp, _vp],
+    "mxq_gemv": [_vp, _vp, _vp, _vp, _sz, _vp],
+    "mxq_gather_dot": [_vp, _vp, _vp, _vp, _sz, _vp, _sz, _vp],
+    "mxq_block_dots": [_vp, _vp, _vp, _sz, _vp],
+    "mxq_linear": [_vp, _vp, _vp, _sz, _vp],
+    "mxq_linear_host": [_vp, _vp, _vp, _sz, _vp],
+    "mxq_linear_pair": [_vp, _vp, _vp, _vp, _sz, _vp],
+    "mxq_linear_pair_host": [_vp, _vp, _vp, _vp, _sz, _vp],
+    "mxq_mlp_swiglu": [_vp, _vp, _vp, _vp, _vp, _sz, _vp],
+    "mxq_route_topk": [_vp, _vp, _sz, _sz, _sz, _vp, _vp],
+    "mxq_gae": [_vp, _vp, _vp, _vp, _vp, _sz, _sz, _f, _f, _vp, _vp],
+}
+
+_lib = None
+
+
+def load():
+    """Load libmxq.so once; raise ImportError if it is not built."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not os.path.exists(LIB_PATH):
+        raise ImportError(
+            "libmxq.so is not built (expected at %s); run `python -m cpu_model_b200.build`" % LIB_PATH)
+    lib = ctypes.CDLL(LIB_PATH)
+    for name, args in SIGNATURES.items():
+        fn = getattr(lib, name)
+        fn.argtypes = args
+        fn.restype = ctypes.c_char_p if name == "mxq_last_error" else ctypes.c_int
+    _lib = lib
+    return lib
+
+
+class MXError(RuntimeError):
+    def __init__(self, code, msg):
+        super().__init__("%s (status %d)" % (msg, code))
+        self.code = code
+
+
+def check(rc, ctx_handle=None):
+    """Raise on a negative status: ValueError for invalid arguments (the
+    reference operators throw std::invalid_argument), MXError otherwise."""
+    if rc == MXQ_OK:
+        return
+    msg = load().mxq_last_error(ctx_handle)
+    msg = msg.decode() if msg else "error"
+    if rc == MXQ_ERR_INVALID_ARGUMENT:
+        raise ValueError(msg)
+    raise MXError(rc, msg)

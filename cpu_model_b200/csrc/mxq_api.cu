@@ -1,0 +1,704 @@
+// mxq_api.cu -- the C-ABI (include/mxq.h): contexts, weight handles,
+// workspace, regime selection and the small kernels (weight repack, top-k
+// routing, GAE).  No exception crosses the boundary; every entry returns an
+// MXQ_* status.
+#include <cstdio>
+#include <cstring>
+#include <cstdarg>
+#include <new>
+#include <string>
+
+#include "../../include/mxq.h"
+#include "mxq_internal.h"
+
+using namespace mxq;
+
+struct mxq_context {
+  int device = 0;
+  cudaStream_t stream = nullptr;
+  int path = MXQ_PATH_AUTO;
+  uint32_t* status = nullptr;  // device status word
+  uint64_t launches = 0;
+  std::string err;
+  // workspace (device)
+  uint8_t* ws_q = nullptr;   size_t ws_q_bytes = 0;    // MX activation
+  uint8_t* ws_s = nullptr;   size_t ws_s_bytes = 0;    // MX scales
+  uint8_t* ws_op = nullptr;  size_t ws_op_bytes = 0;   // GEMM operand
+  float* ws_f0 = nullptr;    size_t ws_f0_bytes = 0;   // fp32 intermediates
+  float* ws_f1 = nullptr;    size_t ws_f1_bytes = 0;
+  float* ws_in = nullptr;    size_t ws_in_bytes = 0;   // host-call staging
+  float* ws_out = nullptr;   size_t ws_out_bytes = 0;
+};
+
+struct mxq_weight_s {
+  mxq_context* ctx = nullptr;
+  WeightView v{};
+  uint8_t* data = nullptr;
+  uint8_t* scales = nullptr;
+};
+
+namespace {
+
+thread_local std::string g_err;
+
+int fail(mxq_context* c, int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  if (c) c->err = buf;
+  g_err = buf;
+  return code;
+}
+
+int cuda_fail(mxq_context* c, cudaError_t e, const char* what) {
+  return fail(c, e == cudaErrorMemoryAllocation ? MXQ_ERR_OUT_OF_MEMORY : MXQ_ERR_CUDA,
+              "%s: %s", what, cudaGetErrorString(e));
+}
+
+struct DeviceGuard {
+  int prev = -1;
+  explicit DeviceGuard(int dev) {
+    if (cudaGetDevice(&prev) == cudaSuccess && prev != dev) cudaSetDevice(dev);
+    else prev = -1;
+  }
+  ~DeviceGuard() {
+    if (prev >= 0) cudaSetDevice(prev);
+  }
+};
+
+template <typename T>
+int ensure(mxq_context* c, T*& p, size_t& cap, size_t bytes, const char* what) {
+  if (bytes <= cap) return MXQ_OK;
+  if (p) cudaFree(p);
+  p = nullptr;
+  cap = 0;
+  void* q = nullptr;
+  cudaError_t e = cudaMalloc(&q, bytes);
+  if (e != cudaSuccess) return cuda_fail(c, e, what);
+  p = static_cast<T*>(q);
+  cap = bytes;
+  return MXQ_OK;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// ------------------------------------------------------------ repack ---
+__global__ void repack_kernel(const uint8_t* __restrict__ data,
+                              const uint8_t* __restrict__ scales, int fmt, int N,
+                              int K, int Npad, int Kpad, uint8_t* __restrict__ od,
+                              uint8_t* __restrict__ os) {
+  const int TB = fmt == 4 ? 32 : 64;
+  const int KT = Kpad / kTileK;
+  const long total = (long)Npad * KT;
+  const int row_bytes = fmt == 4 ? K / 2 : K;
+  for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+       i += (long)gridDim.x * blockDim.x) {
+    const int n = (int)(i / KT), kt = (int)(i % KT);
+    const long dst = (((long)(n / 128) * KT + kt) * 128 + (n % 128));
+    for (int j = 0; j < TB; ++j) {
+      const int byte = kt * TB + j;
+      od[dst * TB + j] = (n < N && byte < row_bytes) ? data[(long)n * row_bytes + byte] : 0;
+    }
+    for (int h = 0; h < 2; ++h) {
+      const int b = kt * 2 + h;
+      os[dst * 2 + h] = (n < N && b < K / kBlock) ? scales[(long)n * (K / kBlock) + b] : 127;
+    }
+  }
+}
+
+// ------------------------------------------------------------ routing ---
+__global__ void route_topk_kernel(const float* __restrict__ logits, int T, int E,
+                                  int k, int32_t* __restrict__ idx,
+                                  float* __restrict__ gate) {
+  const int t = blockIdx.x * blockDim.x + threadIdx.x;
+  if (t >= T) return;
+  const float* l = logits + (long)t * E;
+  int32_t id[64];
+  float ex[64];
+  for (int j = 0; j < k; ++j) {
+    int best = -1;
+    for (int e = 0; e < E; ++e) {
+      bool used = false;
+      for (int p = 0; p < j; ++p) used |= id[p] == e;
+      if (used) continue;
+      if (best < 0 || l[e] > l[best]) best = e;
+    }
+    id[j] = best;
+  }
+  const float mx = l[id[0]];
+  float den = 0.0f;
+  for (int j = 0; j < k; ++j) {
+    ex[j] = det_expf(__fsub_rn(l[id[j]], mx));
+    den = __fadd_rn(den, ex[j]);
+  }
+  for (int j = 0; j < k; ++j) {
+    idx[(long)t * k + j] = id[j];
+    gate[(long)t * k + j] = __fdiv_rn(ex[j], den);
+  }
+}
+
+// ---------------------------------------------------------------- GAE ---
+// agentic_env/replay_memory.cpp:230-251: backward over t, one thread per env,
+// the reference's float operations in the reference's order.
+__global__ void gae_kernel(const float* __restrict__ r, const float* __restrict__ v,
+                           const uint8_t* __restrict__ d, const float* __restrict__ nv,
+                           int T, int E, float gamma, float gl,
+                           float* __restrict__ adv, float* __restrict__ ret) {
+  const int k = blockIdx.x * blockDim.x + threadIdx.x;
+  if (k >= E) return;
+  float acc = 0.0f, vn = nv[k];
+  for (int t = T - 1; t >= 0; --t) {
+    const long i = (long)t * E + k;
+    const float df = d[i] ? 0.0f : 1.0f;
+    const float vt = v[i];
+    const float delta = __fsub_rn(__fadd_rn(r[i], __fmul_rn(__fmul_rn(gamma, vn), df)), vt);
+    acc = __fadd_rn(delta, __fmul_rn(__fmul_rn(gl, acc), df));
+    adv[i] = acc;
+    ret[i] = __fadd_rn(acc, vt);
+    vn = vt;
+  }
+}
+
+int check_ctx(mxq_context* c) {
+  return c ? MXQ_OK : fail(nullptr, MXQ_ERR_INVALID_ARGUMENT, "null context");
+}
+
+int check_weight(mxq_context* c, mxq_weight w) {
+  if (!w || !w->data) return fail(c, MXQ_ERR_INVALID_ARGUMENT, "null weight handle");
+  return MXQ_OK;
+}
+
+int use_gemv(mxq_context* c, size_t b) {
+  if (c->path == MXQ_PATH_GEMV) return 1;
+  if (c->path == MXQ_PATH_GEMM) return 0;
+  return b <= (size_t)gemv_max_batch();
+}
+
+int after_launch(mxq_context* c, cudaError_t e, const char* what) {
+  if (e != cudaSuccess) return cuda_fail(c, e, what);
+  c->launches++;
+  return MXQ_OK;
+}
+
+// fp32 x [B][K] (device) -> y [B][N] through quantise + GEMV or GEMM.
+int linear_dev(mxq_context* c, mxq_weight w, const float* x, size_t b, float* y,
+               int act) {
+  const int K = w->v.K;
+  int rc;
+  if (use_gemv(c, b)) {
+    if (b > (size_t)gemv_max_batch())
+      return fail(c, MXQ_ERR_INVALID_ARGUMENT, "GEMV path supports batch <= %d", gemv_max_batch());
+    if ((rc = ensure(c, c->ws_q, c->ws_q_bytes, b * K, "workspace q"))) return rc;
+    if ((rc = ensure(c, c->ws_s, c->ws_s_bytes, b * K / kBlock, "workspace s"))) return rc;
+    QuantArgs qa{};
+    qa.x = x;
+    qa.B = (int)b;
+    qa.K = K;
+    qa.out_q = c->ws_q;
+    qa.out_s = c->ws_s;
+    if ((rc = after_launch(c, launch_quantize(qa, act, c->stream, true), "quantize"))) return rc;
+    GemvArgs ga{};
+    ga.w = w->v;
+    ga.xq = c->ws_q;
+    ga.xs = c->ws_s;
+    ga.y = y;
+    ga.B = (int)b;
+    return after_launch(c, launch_gemv(ga, c->stream, true), "gemv");
+  }
+  const int BN = gemm_pick_bn((int)b);
+  const int Bpad = (int)((b + BN - 1) / BN * BN);
+  if ((rc = ensure(c, c->ws_op, c->ws_op_bytes, (size_t)Bpad * w->v.Kpad * 2, "workspace operand")))
+    return rc;
+  QuantArgs qa{};
+  qa.x = x;
+  qa.B = (int)b;
+  qa.K = K;
+  qa.opnd = reinterpret_cast<__nv_bfloat16*>(c->ws_op);
+  qa.Bpad = Bpad;
+  qa.Kpad = w->v.Kpad;
+  qa.BN = BN;
+  qa.int4_order = w->v.fmt == 4;
+  if ((rc = after_launch(c, launch_quantize(qa, act, c->stream, true), "quantize"))) return rc;
+  GemmArgs ga{};
+  ga.w = w->v;
+  ga.opnd = qa.opnd;
+  ga.y = y;
+  ga.B = (int)b;
+  ga.Bpad = Bpad;
+  ga.BN = BN;
+  ga.status = c->status;
+  return after_launch(c, launch_gemm(ga, c->stream, true), "gemm");
+}
+
+// MX activation (device) -> y
+int gemv_dev(mxq_context* c, mxq_weight w, const uint8_t* xq, const uint8_t* xs,
+             size_t b, float* y) {
+  int rc;
+  if (use_gemv(c, b)) {
+    if (b > (size_t)gemv_max_batch())
+      return fail(c, MXQ_ERR_INVALID_ARGUMENT, "GEMV path supports batch <= %d", gemv_max_batch());
+    GemvArgs ga{};
+    ga.w = w->v;
+    ga.xq = xq;
+    ga.xs = xs;
+    ga.y = y;
+    ga.B = (int)b;
+    return after_launch(c, launch_gemv(ga, c->stream, true), "gemv");
+  }
+  const int BN = gemm_pick_bn((int)b);
+  const int Bpad = (int)((b + BN - 1) / BN * BN);
+  if ((rc = ensure(c, c->ws_op, c->ws_op_bytes, (size_t)Bpad * w->v.Kpad * 2, "workspace operand")))
+    return rc;
+  QuantArgs qa{};
+  qa.in_q = xq;
+  qa.in_s = xs;
+  qa.B = (int)b;
+  qa.K = w->v.K;
+  qa.opnd = reinterpret_cast<__nv_bfloat16*>(c->ws_op);
+  qa.Bpad = Bpad;
+  qa.Kpad = w->v.Kpad;
+  qa.BN = BN;
+  qa.int4_order = w->v.fmt == 4;
+  if ((rc = after_launch(c, launch_quantize(qa, 3, c->stream, true), "operand"))) return rc;
+  GemmArgs ga{};
+  ga.w = w->v;
+  ga.opnd = qa.opnd;
+  ga.y = y;
+  ga.B = (int)b;
+  ga.Bpad = Bpad;
+  ga.BN = BN;
+  ga.status = c->status;
+  return after_launch(c, launch_gemm(ga, c->stream, true), "gemm");
+}
+
+}  // namespace
+
+#define MXQ_TRY(...)                                                     \
+  try {                                                                  \
+    __VA_ARGS__                                                          \
+  } catch (const std::bad_alloc&) {                                      \
+    return fail(nullptr, MXQ_ERR_OUT_OF_MEMORY, "host allocation failed"); \
+  } catch (...) {                                                        \
+    return fail(nullptr, MXQ_ERR_CUDA, "unexpected exception");          \
+  }
+
+extern "C" {
+
+int mxq_abi_version(void) { return 1; }
+
+const char* mxq_last_error(mxq_ctx ctx) {
+  return ctx ? ctx->err.c_str() : g_err.c_str();
+}
+
+int mxq_create(int device, mxq_ctx* out) {
+  MXQ_TRY({
+    if (!out) return fail(nullptr, MXQ_ERR_INVALID_ARGUMENT, "null output pointer");
+    *out = nullptr;
+    int n = 0;
+    cudaError_t e = cudaGetDeviceCount(&n);
+    if (e != cudaSuccess) return cuda_fail(nullptr, e, "cudaGetDeviceCount");
+    if (device < 0 || device >= n)
+      return fail(nullptr, MXQ_ERR_INVALID_ARGUMENT, "device %d out of range (%d devices)", device, n);
+    DeviceGuard g(device);
+    cudaDeviceProp prop;
+    e = cudaGetDeviceProperties(&prop, device);
+    if (e != cudaSuccess) return cuda_fail(nullptr, e, "cudaGetDeviceProperties");
+    if (prop.major != 10)
+      return fail(nullptr, MXQ_ERR_UNSUPPORTED, "device %d is sm_%d%d; this library is built for sm_100a",
+                  device, prop.major, prop.minor);
+    auto* c = new mxq_context();
+    c->device = device;
+    e = cudaMalloc(&c->status, sizeof(uint32_t));
+    if (e == cudaSuccess) e = cudaMemset(c->status, 0, sizeof(uint32_t));
+    if (e != cudaSuccess) {
+      delete c;
+      return cuda_fail(nullptr, e, "status word");
+    }
+    *out = c;
+    return MXQ_OK;
+  })
+}
+
+int mxq_destroy(mxq_ctx c) {
+  MXQ_TRY({
+    if (int rc = check_ctx(c)) return rc;
+    DeviceGuard g(c->device);
+    cudaStreamSynchronize(c->stream);
+    cudaFree(c->status);
+    cudaFree(c->ws_q);
+    cudaFree(c->ws_s);
+    cudaFree(c->ws_op);
+    cudaFree(c->ws_f0);
+    cudaFree(c->ws_f1);
+    cudaFree(c->ws_in);
+    cudaFree(c->ws_out);
+    delete c;
+    return MXQ_OK;
+  })
+}
+
+int mxq_set_stream(mxq_ctx c, void* s) {
+  if (int rc = check_ctx(c)) return rc;
+  c->stream = static_cast<cudaStream_t>(s);
+  return MXQ_OK;
+}
+
+int mxq_set_path(mxq_ctx c, int path) {
+  if (int rc = check_ctx(c)) return rc;
+  if (path < MXQ_PATH_AUTO || path > MXQ_PATH_GEMM)
+    return fail(c, MXQ_ERR_INVALID_ARGUMENT, "unknown path %d", path);
+  c->path = path;
+  return MXQ_OK;
+}
+
+int mxq_launch_count(mxq_ctx c, uint64_t* out) {
+  if (int rc = check_ctx(c)) return rc;
+  if (!out) return fail(c, MXQ_ERR_INVALID_ARGUMENT, "null output pointer");
+  *out = c->launches;
+  return MXQ_OK;
+}
+
+int mxq_reserve(mxq_ctx c, size_t max_batch, size_t max_k) {
+  MXQ_TRY({
+    if (int rc = check_ctx(c)) return rc;
+    if (max_batch == 0 || max_k == 0 || max_k % kBlock)
+      return fail(c, MXQ_ERR_INVALID_ARGUMENT, "reserve: batch and k must be > 0, k a multiple of 32");
+    DeviceGuard g(c->device);
+    const size_t kpad = (max_k + kTileK - 1) / kTileK * kTileK;
+    const size_t bpad = (max_batch + 255) / 256 * 256;
+    int rc;
+    if ((rc = ensure(c, c->ws_q, c->ws_q_bytes, max_batch * max_k, "workspace q"))) return rc;
+    if ((rc = ensure(c, c->ws_s, c->ws_s_bytes, max_batch * max_k / kBlock, "workspace s"))) return rc;
+    if ((rc = ensure(c, c->ws_op, c->ws_op_bytes, bpad * kpad * 2, "workspace operand"))) return rc;
+    if ((rc = ensure(c, c->ws_f0, c->ws_f0_bytes, max_batch * max_k * 4, "workspace f0"))) return rc;
+    if ((rc = ensure(c, c->ws_f1, c->ws_f1_bytes, max_batch * max_k * 4, "workspace f1"))) return rc;
+    if ((rc = ensure(c, c->ws_in, c->ws_in_bytes, max_batch * max_k * 4, "workspace in"))) return rc;
+    if ((rc = ensure(c, c->ws_out, c->ws_out_bytes, max_batch * max_k * 4, "workspace out"))) return rc;
+    return MXQ_OK;
+  })
+}
+
+int mxq_synchronize(mxq_ctx c) {
+  if (int rc = check_ctx(c)) return rc;
+  DeviceGuard g(c->device);
+  cudaError_t e = cudaStreamSynchronize(c->stream);
+  if (e != cudaSuccess) return cuda_fail(c, e, "synchronize");
+  uint32_t st = 0;
+  e = cudaMemcpy(&st, c->status, sizeof(st), cudaMemcpyDeviceToHost);
+  if (e != cudaSuccess) return cuda_fail(c, e, "status read");
+  if (st) {
+    cudaMemset(c->status, 0, sizeof(uint32_t));
+    return fail(c, MXQ_ERR_TIMEOUT, "a device-side bounded wait gave up (status 0x%x)", st);
+  }
+  return MXQ_OK;
+}
+
+int mxq_weight_create(mxq_ctx c, int fmt, size_t n, size_t k, const void* data,
+                      const uint8_t* scales, int on_device, mxq_weight* out) {
+  MXQ_TRY({
+    if (int rc = check_ctx(c)) return rc;
+    if (!out || !data || !scales) return fail(c, MXQ_ERR_INVALID_ARGUMENT, "null pointer");
+    *out = nullptr;
+    if (fmt != MXQ_FMT_INT4 && fmt != MXQ_FMT_INT8)
+      return fail(c, MXQ_ERR_INVALID_ARGUMENT, "unknown weight format %d", fmt);
+    if (n == 0 || k == 0 || k % kBlock)
+      return fail(c, MXQ_ERR_INVALID_ARGUMENT, "weight shape %zux%zu: K must be a positive multiple of 32", n, k);
+    if (n > (1u << 24) || k > (1u << 24))
+      return fail(c, MXQ_ERR_INVALID_ARGUMENT, "weight shape %zux%zu too large", n, k);
+    DeviceGuard g(c->device);
+    const int N = (int)n, K = (int)k;
+    const int Npad = (N + 255) / 256 * 256;
+    const int Kpad = (K + kTileK - 1) / kTileK * kTileK;
+    const size_t src_bytes = fmt == 4 ? n * k / 2 : n * k;
+    const size_t sc_bytes = n * k / kBlock;
+    const size_t dst_bytes = (size_t)Npad * Kpad / (fmt == 4 ? 2 : 1);
+    const size_t dsc_bytes = (size_t)Npad * Kpad / kBlock;
+    auto* w = new mxq_weight_s();
+    w->ctx = c;
+    cudaError_t e = cudaMalloc(&w->data, dst_bytes);
+    if (e == cudaSuccess) e = cudaMalloc(&w->scales, dsc_bytes);
+    const uint8_t* src_d = static_cast<const uint8_t*>(data);
+    const uint8_t* src_s = scales;
+    uint8_t* tmp = nullptr;
+    if (e == cudaSuccess && !on_device) {
+      e = cudaMalloc(&tmp, src_bytes + sc_bytes);
+      if (e == cudaSuccess) e = cudaMemcpy(tmp, data, src_bytes, cudaMemcpyHostToDevice);
+      if (e == cudaSuccess) e = cudaMemcpy(tmp + src_bytes, scales, sc_bytes, cudaMemcpyHostToDevice);
+      src_d = tmp;
+      src_s = tmp + src_bytes;
+    }
+    if (e == cudaSuccess) e = launch_repack(src_d, src_s, fmt, N, K, Npad, Kpad, w->data, w->scales, c->stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(c->stream);
+    if (tmp) cudaFree(tmp);
+    if (e != cudaSuccess) {
+      cudaFree(w->data);
+      cudaFree(w->scales);
+      delete w;
+      return cuda_fail(c, e, "weight upload");
+    }
+    w->v.fmt = fmt;
+    w->v.N = N;
+    w->v.K = K;
+    w->v.Npad = Npad;
+    w->v.Kpad = Kpad;
+    w->v.data = w->data;
+    w->v.scales = w->scales;
+    *out = w;
+    return MXQ_OK;
+  })
+}
+
+int mxq_weight_destroy(mxq_weight w) {
+  if (!w) return fail(nullptr, MXQ_ERR_INVALID_ARGUMENT, "null weight handle");
+  DeviceGuard g(w->ctx->device);
+  cudaFree(w->data);
+  cudaFree(w->scales);
+  delete w;
+  return MXQ_OK;
+}
+
+int mxq_weight_shape(mxq_weight w, int* fmt, size_t* n, size_t* k) {
+  if (!w) return fail(nullptr, MXQ_ERR_INVALID_ARGUMENT, "null weight handle");
+  if (fmt) *fmt = w->v.fmt;
+  if (n) *n = (size_t)w->v.N;
+  if (k) *k = (size_t)w->v.K;
+  return MXQ_OK;
+}
+
+int mxq_quantize_x(mxq_ctx c, const float* x, size_t b, size_t k, int act,
+                   uint8_t* q, uint8_t* s) {
+  if (int rc = check_ctx(c)) return rc;
+  if (!x || !q || !s) return fail(c, MXQ_ERR_INVALID_ARGUMENT, "null pointer");
+  if (b == 0 || k == 0 || k % kBlock)
+    return fail(c, MXQ_ERR_INVALID_ARGUMENT, "quantize: K must be a positive multiple of 32");
+  if (act != MXQ_ACT_NONE && act != MXQ_ACT_SILU)
+    return fail(c, MXQ_ERR_INVALID_ARGUMENT, "unknown activation %d", act);
+  DeviceGuard g(c->device);
+  QuantArgs qa{};
+  qa.x = x;
+  qa.B = (int)b;
+  qa.K = (int)k;
+  qa.out_q = q;
+  qa.out_s = s;
+  return after_launch(c, launch_quantize(qa, act, c->stream, false), "quantize");
+}
+
+int mxq_swiglu_quantize(mxq_ctx c, const float* gate, const float* up, size_t b,
+                        size_t k, uint8_t* q, uint8_t* s) {
+  if (int rc = check_ctx(c)) return rc;
+  if (!gate || !up || !q || !s) return fail(c, MXQ_ERR_INVALID_ARGUMENT, "null pointer");
+  if (b == 0 || k == 0 || k % kBlock)
+    return fail(c, MXQ_ERR_INVALID_ARGUMENT, "quantize: K must be a positive multiple of 32");
+  DeviceGuard g(c->device);
+  QuantArgs qa{};
+  qa.x = gate;
+  qa.up = up;
+  qa.B = (int)b;
+  qa.K = (int)k;
+  qa.out_q = q;
+  qa.out_s = s;
+  return after_launch(c, launch_quantize(qa, 2, c->stream, false), "swiglu quantize");
+}
+
+int mxq_gemv(mxq_ctx c, mxq_weight w, const uint8_t* xq, const uint8_t* xs,
+             size_t b, float* y) {
+  MXQ_TRY({
+    if (int rc = check_ctx(c)) return rc;
+    if (int rc = check_weight(c, w)) return rc;
+    if (!xq || !xs || !y || b == 0) return fail(c, MXQ_ERR_INVALID_ARGUMENT, "null pointer or empty batch");
+    if (!aligned16(xq)) return fail(c, MXQ_ERR_INVALID_ARGUMENT, "activation must be 16-byte aligned");
+    DeviceGuard g(c->device);
+    return gemv_dev(c, w, xq, xs, b, y);
+  })
+}
+
+int mxq_gather_dot(mxq_ctx c, mxq_weight w, const uint8_t* xq, const uint8_t* xs,
+                   size_t b, const int32_t* rows, size_t nrows, float* y) {
+  if (int rc = check_ctx(c)) return rc;
+  if (int rc = check_weight(c, w)) return rc;
+  if (!xq || !xs || !rows || !y || b == 0 || nrows == 0)
+    return fail(c, MXQ_ERR_INVALID_ARGUMENT, "null pointer or empty input");
+  if (b > (size_t)gemv_max_batch())
+    return fail(c, MXQ_ERR_INVALID_ARGUMENT, "gather_dot supports batch <= %d", gemv_max_batch());
+  if (!aligned16(xq)) return fail(c, MXQ_ERR_INVALID_ARGUMENT, "activation must be 16-byte aligned");
+  DeviceGuard g(c->device);
+  GemvArgs ga{};
+  ga.w = w->v;
+  ga.xq = xq;
+  ga.xs = xs;
+  ga.y = y;
+  ga.B = (int)b;
+  ga.rows = rows;
+  ga.nrows = (int)nrows;
+  return after_launch(c, launch_gemv(ga, c->stream, false), "gather_dot");
+}
+
+int mxq_block_dots(mxq_ctx c, mxq_weight w, const uint8_t* xq, size_t b, int32_t* dots) {
+  if (int rc = check_ctx(c)) return rc;
+  if (int rc = check_weight(c, w)) return rc;
+  if (!xq || !dots || b == 0) return fail(c, MXQ_ERR_INVALID_ARGUMENT, "null pointer or empty batch");
+  if (!aligned16(xq)) return fail(c, MXQ_ERR_INVALID_ARGUMENT, "activation must be 16-byte aligned");
+  DeviceGuard g(c->device);
+  GemvArgs ga{};
+  ga.w = w->v;
+  ga.xq = xq;
+  ga.B = (int)b;
+  ga.block_dots = dots;
+  return after_launch(c, launch_gemv(ga, c->stream, false), "block_dots");
+}
+
+int mxq_linear(mxq_ctx c, mxq_weight w, const float* x, size_t b, float* y) {
+  MXQ_TRY({
+    if (int rc = check_ctx(c)) return rc;
+    if (int rc = check_weight(c, w)) return rc;
+    if (!x || !y || b == 0) return fail(c, MXQ_ERR_INVALID_ARGUMENT, "null pointer or empty batch");
+    DeviceGuard g(c->device);
+    return linear_dev(c, w, x, b, y, MXQ_ACT_NONE);
+  })
+}
+
+int mxq_linear_pair(mxq_ctx c, mxq_weight w1, mxq_weight w2, const float* x,
+                    size_t b, float* y) {
+  MXQ_TRY({
+    if (int rc = check_ctx(c)) return rc;
+    if (int rc = check_weight(c, w1)) return rc;
+    if (int rc = check_weight(c, w2)) return rc;
+    if (!x || !y || b == 0) return fail(c, MXQ_ERR_INVALID_ARGUMENT, "null pointer or empty batch");
+    if (w2->v.K != w1->v.N)
+      return fail(c, MXQ_ERR_INVALID_ARGUMENT, "pair shape mismatch: w1 N=%d, w2 K=%d", w1->v.N, w2->v.K);
+    DeviceGuard g(c->device);
+    int rc;
+    if ((rc = ensure(c, c->ws_f0, c->ws_f0_bytes, b * w1->v.N * 4, "workspace mid"))) return rc;
+    if ((rc = linear_dev(c, w1, x, b, c->ws_f0, MXQ_ACT_NONE))) return rc;
+    return linear_dev(c, w2, c->ws_f0, b, y, MXQ_ACT_NONE);
+  })
+}
+
+static int host_call(mxq_context* c, size_t in_elems, size_t out_elems,
+                     const float* x_host, float* y_host,
+                     int (*fn)(mxq_context*, void*, const float*, float*), void* arg) {
+  int rc;
+  if ((rc = ensure(c, c->ws_in, c->ws_in_bytes, in_elems * 4, "workspace in"))) return rc;
+  if ((rc = ensure(c, c->ws_out, c->ws_out_bytes, out_elems * 4, "workspace out"))) return rc;
+  cudaError_t e = cudaMemcpyAsync(c->ws_in, x_host, in_elems * 4, cudaMemcpyHostToDevice, c->stream);
+  if (e != cudaSuccess) return cuda_fail(c, e, "copy in");
+  if ((rc = fn(c, arg, c->ws_in, c->ws_out))) return rc;
+  e = cudaMemcpyAsync(y_host, c->ws_out, out_elems * 4, cudaMemcpyDeviceToHost, c->stream);
+  if (e != cudaSuccess) return cuda_fail(c, e, "copy out");
+  return mxq_synchronize(c);
+}
+
+struct LinArg { mxq_weight w; size_t b; };
+struct PairArg { mxq_weight w1, w2; size_t b; };
+
+int mxq_linear_host(mxq_ctx c, mxq_weight w, const float* x_host, size_t b, float* y_host) {
+  MXQ_TRY({
+    if (int rc = check_ctx(c)) return rc;
+    if (int rc = check_weight(c, w)) return rc;
+    if (!x_host || !y_host || b == 0) return fail(c, MXQ_ERR_INVALID_ARGUMENT, "null pointer or empty batch");
+    DeviceGuard g(c->device);
+    LinArg la{w, b};
+    return host_call(c, b * w->v.K, b * w->v.N, x_host, y_host,
+                     [](mxq_context* cc, void* p, const float* xi, float* yo) {
+                       auto* a = static_cast<LinArg*>(p);
+                       return linear_dev(cc, a->w, xi, a->b, yo, MXQ_ACT_NONE);
+                     }, &la);
+  })
+}
+
+int mxq_linear_pair_host(mxq_ctx c, mxq_weight w1, mxq_weight w2, const float* x_host,
+                         size_t b, float* y_host) {
+  MXQ_TRY({
+    if (int rc = check_ctx(c)) return rc;
+    if (int rc = check_weight(c, w1)) return rc;
+    if (int rc = check_weight(c, w2)) return rc;
+    if (!x_host || !y_host || b == 0) return fail(c, MXQ_ERR_INVALID_ARGUMENT, "null pointer or empty batch");
+    if (w2->v.K != w1->v.N)
+      return fail(c, MXQ_ERR_INVALID_ARGUMENT, "pair shape mismatch: w1 N=%d, w2 K=%d", w1->v.N, w2->v.K);
+    DeviceGuard g(c->device);
+    PairArg pa{w1, w2, b};
+    return host_call(c, b * w1->v.K, b * w2->v.N, x_host, y_host,
+                     [](mxq_context* cc, void* p, const float* xi, float* yo) {
+                       auto* a = static_cast<PairArg*>(p);
+                       return mxq_linear_pair(cc, a->w1, a->w2, xi, a->b, yo);
+                     }, &pa);
+  })
+}
+
+int mxq_mlp_swiglu(mxq_ctx c, mxq_weight wg, mxq_weight wu, mxq_weight wd,
+                   const float* x, size_t b, float* y) {
+  MXQ_TRY({
+    if (int rc = check_ctx(c)) return rc;
+    if (int rc = check_weight(c, wg)) return rc;
+    if (int rc = check_weight(c, wu)) return rc;
+    if (int rc = check_weight(c, wd)) return rc;
+    if (!x || !y || b == 0) return fail(c, MXQ_ERR_INVALID_ARGUMENT, "null pointer or empty batch");
+    if (wg->v.N != wu->v.N || wg->v.K != wu->v.K || wd->v.K != wg->v.N || wd->v.N != wg->v.K)
+      return fail(c, MXQ_ERR_INVALID_ARGUMENT, "gated MLP shape mismatch");
+    DeviceGuard g(c->device);
+    const size_t F = wg->v.N;
+    int rc;
+    if ((rc = ensure(c, c->ws_f0, c->ws_f0_bytes, b * F * 4, "workspace gate"))) return rc;
+    if ((rc = ensure(c, c->ws_f1, c->ws_f1_bytes, b * F * 4, "workspace up"))) return rc;
+    if ((rc = linear_dev(c, wg, x, b, c->ws_f0, MXQ_ACT_NONE))) return rc;
+    if ((rc = linear_dev(c, wu, x, b, c->ws_f1, MXQ_ACT_NONE))) return rc;
+    // silu(gate) * up -> MX into ws_q (the gate/up GEMVs queued before have
+    // consumed their quantised input; stream order makes the reuse safe)
+    const size_t off_s = (b * F + 15) / 16 * 16;
+    if ((rc = ensure(c, c->ws_q, c->ws_q_bytes, off_s + b * F / kBlock, "workspace mid"))) return rc;
+    uint8_t* hq = c->ws_q;
+    uint8_t* hs = c->ws_q + off_s;
+    QuantArgs qa{};
+    qa.x = c->ws_f0;
+    qa.up = c->ws_f1;
+    qa.B = (int)b;
+    qa.K = (int)F;
+    qa.out_q = hq;
+    qa.out_s = hs;
+    if ((rc = after_launch(c, launch_quantize(qa, 2, c->stream, true), "swiglu quantize"))) return rc;
+    return gemv_dev(c, wd, hq, hs, b, y);
+  })
+}
+
+int mxq_route_topk(mxq_ctx c, const float* logits, size_t t, size_t n_experts,
+                   size_t k, int32_t* idx, float* gate) {
+  if (int rc = check_ctx(c)) return rc;
+  if (!logits || !idx || !gate) return fail(c, MXQ_ERR_INVALID_ARGUMENT, "null pointer");
+  if (k == 0 || k > n_experts)
+    return fail(c, MXQ_ERR_INVALID_ARGUMENT, "top-k: k=%zu must be in [1, n_experts=%zu]", k, n_experts);
+  if (k > 64 || n_experts > 4096) return fail(c, MXQ_ERR_UNSUPPORTED, "top-k: k <= 64 and n_experts <= 4096");
+  if (t == 0) return MXQ_OK;
+  DeviceGuard g(c->device);
+  route_topk_kernel<<<(unsigned)((t + 127) / 128), 128, 0, c->stream>>>(logits, (int)t, (int)n_experts,
+                                                                     (int)k, idx, gate);
+  return after_launch(c, cudaGetLastError(), "route_topk");
+}
+
+int mxq_gae(mxq_ctx c, const float* rewards, const float* values, const uint8_t* dones,
+            const float* next_values, size_t t, size_t e, float gamma, float lambda,
+            float* adv, float* ret) {
+  if (int rc = check_ctx(c)) return rc;
+  if (!rewards || !values || !dones || !next_values || !adv || !ret)
+    return fail(c, MXQ_ERR_INVALID_ARGUMENT, "null pointer");
+  if (t == 0 || e == 0) return MXQ_OK;  // the reference returns early on an empty sweep
+  DeviceGuard g(c->device);
+  const float gl = gamma * lambda;
+  gae_kernel<<<(unsigned)((e + 127) / 128), 128, 0, c->stream>>>(rewards, values, dones, next_values,
+                                                                (int)t, (int)e, gamma, gl, adv, ret);
+  return after_launch(c, cudaGetLastError(), "gae");
+}
+
+}  // extern "C"
+
+namespace mxq {
+cudaError_t launch_repack(const uint8_t* data, const uint8_t* scales, int fmt, int N, int K,
+                          int Npad, int Kpad, uint8_t* od, uint8_t* os, cudaStream_t st) {
+  const long total = (long)Npad * (Kpad / kTileK);
+  long ctas = (total + 255) / 256;
+  if (ctas > 148L * 64) ctas = 148L * 64;
+  repack_kernel<<<(unsigned)ctas, 256, 0, st>>>(data, scales, fmt, N, K, Npad, Kpad, od, os);
+  return cudaGetLastError();
+}
+}  // namespace mxq

@@ -1,0 +1,67 @@
+// mxq_internal.h -- launch interfaces shared between the C-ABI layer
+// (mxq_api.cu) and the kernel translation units.
+#pragma once
+#include <cstdint>
+#include <cuda_runtime.h>
+#include "mxq_common.cuh"
+
+namespace mxq {
+
+// Weight tiles in HBM (both GEMV and GEMM read this layout):
+//   data  : [Npad/128][Kpad/64][128 rows][TB bytes]   TB = 32 (int4) / 64 (int8)
+//   scales: [Npad/128][Kpad/64][128 rows][2]          E8M0 per 32-K block
+// Rows >= N and K >= K are zero weights with scale byte 127 (1.0).
+struct WeightView {
+  int fmt;        // 4 or 8
+  int N, K;       // logical shape (rows, reduction length)
+  int Npad, Kpad; // Npad multiple of 256, Kpad multiple of 64
+  const uint8_t* data;
+  const uint8_t* scales;
+};
+
+struct QuantArgs {
+  const float* x;        // fp32 input [B][K] (modes 0-2; gate for mode 2)
+  const float* up;       // up projection (mode 2)
+  const uint8_t* in_q;   // MX input (mode 3)
+  const uint8_t* in_s;
+  int B, K;
+  uint8_t* out_q;        // optional MX output [B][K] (u8 = q + 128)
+  uint8_t* out_s;        // optional scales [B][K/32]
+  __nv_bfloat16* opnd;   // optional GEMM operand (tiled, swizzled)
+  int Bpad, Kpad, BN;
+  int int4_order;        // operand K order for int4 weights
+};
+
+// mode: 0 = plain, 1 = SiLU, 2 = SwiGLU(x, up), 3 = MX input -> operand
+cudaError_t launch_quantize(const QuantArgs& a, int mode, cudaStream_t st, bool pdl);
+
+struct GemvArgs {
+  WeightView w;
+  const uint8_t* xq;     // MX activations [B][K]
+  const uint8_t* xs;     // [B][K/32]
+  float* y;              // [B][N]   (or [B][nrows] when gathering)
+  int B;
+  const int32_t* rows;   // optional gathered row ids (mx_rank16_dot_ptrs)
+  int nrows;
+  int32_t* block_dots;   // optional debug output [B][N][K/32]
+};
+
+cudaError_t launch_gemv(const GemvArgs& a, cudaStream_t st, bool pdl);
+int gemv_max_batch();
+
+struct GemmArgs {
+  WeightView w;
+  const __nv_bfloat16* opnd; // tiled operand (from launch_quantize)
+  float* y;                  // [B][N]
+  int B, Bpad, BN;
+  uint32_t* status;          // device status word (bounded waits)
+};
+
+cudaError_t launch_gemm(const GemmArgs& a, cudaStream_t st, bool pdl);
+int gemm_pick_bn(int B);
+
+cudaError_t launch_repack(const uint8_t* data, const uint8_t* scales, int fmt,
+                          int N, int K, int Npad, int Kpad, uint8_t* out_data,
+                          uint8_t* out_scales, cudaStream_t st);
+
+}  // namespace mxq

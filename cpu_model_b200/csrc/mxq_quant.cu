@@ -1,0 +1,111 @@
+// mxq_quant.cu -- activation quantisers (mx_quantize_x,
+// mx_fused_silu_quantize_x, fused_gated_silu_quantize; reference residue
+// nn/core/layers/ssm.cpp:164-177 and :234-260) and the conversion of an MX
+// activation into the tensor-core operand of the GEMM path.
+//
+// One warp owns one 32-element block at a time (lane = element): a coalesced
+// 128-byte load, a 5-step shuffle max, the E8M0 exponent from the max's
+// bits, and round-half-to-even quantisation -- the same float operations as
+// the CPU oracle, so bytes agree exactly.
+//
+// The GEMM operand is bf16 q * 2^e (exact: |q| <= 127 needs 7 significand
+// bits), laid out as [token tile][k tile][BN rows x 128 B] with the 128-byte
+// swizzle already applied, so the GEMM moves each tile with one 1-D bulk
+// copy.  For int4 weights the eight K slots of each 16-byte chunk hold
+// elements {0,2,4,6,1,3,5,7}: the order in which the GEMM's int4 unpack
+// produces weights (the dot product is invariant to a shared permutation).
+#include "mxq_internal.h"
+
+namespace mxq {
+
+// in-group position -> slot, for the int4 operand order
+__device__ __forceinline__ int int4_slot(int j) { return (j >> 1) + ((j & 1) << 2); }
+
+template <int MODE>
+__global__ void __launch_bounds__(256) quantize_kernel(QuantArgs a) {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  const int lane = threadIdx.x & 31;
+  const long warp = ((long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const long nwarps = ((long)gridDim.x * blockDim.x) >> 5;
+  const int kb = a.K / kBlock;
+  const int rows = a.opnd ? a.Bpad : a.B;
+  const int kbp = a.opnd ? a.Kpad / kBlock : kb;
+  const long total = (long)rows * kbp;
+  for (long blk = warp; blk < total; blk += nwarps) {
+    const int t = (int)(blk / kbp);
+    const int b = (int)(blk % kbp);
+    const bool valid = t < a.B && b < kb;  // warp-uniform
+    int q = 0;
+    uint32_t sb = 0;
+    if (valid) {
+      const long idx = (long)t * a.K + (long)b * kBlock + lane;
+      if (MODE == 3) {
+        q = (int)a.in_q[idx] - 128;
+        sb = a.in_s[(long)t * kb + b];
+      } else {
+        float v;
+        if (MODE == 0) v = a.x[idx];
+        else if (MODE == 1) v = det_silu(a.x[idx]);
+        else v = det_swiglu(a.x[idx], a.up[idx]);
+        const float av = fabsf(v);
+        const bool nonfinite = !(av <= 3.402823466e38f);
+        const bool any_nf = __any_sync(0xffffffffu, nonfinite);
+        const float m = warp_max(nonfinite ? 0.0f : av, 32);
+        if (any_nf) {
+          sb = 255;
+          q = 0;
+        } else if (m == 0.0f) {
+          sb = 0;
+          q = 0;
+        } else {
+          const int e = e8m0_exponent<127>(m);
+          sb = (uint32_t)(e + 127);
+          q = quant_value(v, e);
+        }
+      }
+      if (a.out_q) a.out_q[idx] = (uint8_t)(q + 128);
+      if (a.out_s && lane == 0) a.out_s[(long)t * kb + b] = (uint8_t)sb;
+    }
+    if (a.opnd) {
+      const float f = valid ? __fmul_rn((float)q, e8m0_to_float(sb)) : 0.0f;
+      const int k = b * kBlock + lane;
+      const int kt = k / kTileK;
+      const int kin = k % kTileK;
+      const int chunk = kin >> 3;
+      const int slot = a.int4_order ? int4_slot(kin & 7) : (kin & 7);
+      const long tile = (long)(t / a.BN) * (a.Kpad / kTileK) + kt;
+      const long off = tile * (long)a.BN * 128 + sw128_offset(t % a.BN, chunk) + slot * 2;
+      *reinterpret_cast<__nv_bfloat16*>(reinterpret_cast<uint8_t*>(a.opnd) + off) =
+          __float2bfloat16_rn(f);
+    }
+  }
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+cudaError_t launch_quantize(const QuantArgs& a, int mode, cudaStream_t st,
+                            bool pdl) {
+  const int rows = a.opnd ? a.Bpad : a.B;
+  const int kbp = a.opnd ? a.Kpad / kBlock : a.K / kBlock;
+  const long blocks = (long)rows * kbp;
+  long ctas = (blocks + 7) / 8;
+  if (ctas > 148L * 16) ctas = 148L * 16;
+  if (ctas < 1) ctas = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)ctas);
+  cfg.blockDim = dim3(256);
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  switch (mode) {
+    case 0: return cudaLaunchKernelEx(&cfg, quantize_kernel<0>, a);
+    case 1: return cudaLaunchKernelEx(&cfg, quantize_kernel<1>, a);
+    case 2: return cudaLaunchKernelEx(&cfg, quantize_kernel<2>, a);
+    case 3: return cudaLaunchKernelEx(&cfg, quantize_kernel<3>, a);
+  }
+  return cudaErrorInvalidValue;
+}
+
+}  // namespace mxq

@@ -1,0 +1,340 @@
+"""Host-side mirror of the reference's nca::linalg MX operator interface.
+
+The reference's removed core/linalg/mx_linear.hpp exposed free functions over
+MXUINT8Tensor (activations) and MXINT8Tensor (weights) containers
+(nn/tests/autotest.hpp:93-136; names in nn/tests/test_auto_generated.cpp:
+41-56).  The same names are provided here over torch CUDA tensors, each one a
+thin call into libmxq.so (include/mxq.h).  Shape errors raise ValueError, the
+Python counterpart of the reference's std::invalid_argument.
+
+torch is used only as the device-memory and stream carrier; all arithmetic
+runs in the library's sm_100a kernels.
+"""
+import ctypes
+from dataclasses import dataclass
+
+import torch
+
+from . import _lib
+from ._lib import ACT_NONE, ACT_SILU, FMT_INT4, FMT_INT8, PATH_AUTO, PATH_GEMM, PATH_GEMV, check
+
+__all__ = [
+    "MXContext", "MXWeight", "MXActivation", "context",
+    "mx_quantize_x", "mx_fused_silu_quantize_x", "fused_gated_silu_quantize",
+    "mx_gemv", "mx_dot", "mx_dual_dot", "mx_quad_dot", "mx_rank16_dot",
+    "mx_rank16_dot_ptrs", "mx_block_dots", "mx_linear", "mx_linear_pair",
+    "gated_mlp_step", "route_topk", "HashedRouter", "fused_compute_gae",
+    "FMT_INT4", "FMT_INT8", "PATH_AUTO", "PATH_GEMV", "PATH_GEMM",
+]
+
+
+def _ptr(t):
+    return ctypes.c_void_p(t.data_ptr()) if t is not None else ctypes.c_void_p(0)
+
+
+def _need_cuda(t, dtype, name):
+    if not isinstance(t, torch.Tensor) or not t.is_cuda:
+        raise ValueError("%s must be a CUDA tensor" % name)
+    if t.dtype != dtype:
+        raise ValueError("%s must be %s, got %s" % (name, dtype, t.dtype))
+    if not t.is_contiguous():
+        raise ValueError("%s must be contiguous" % name)
+
+
+class MXContext:
+    """One library context per device; work goes to torch's current stream."""
+
+    def __init__(self, device=0):
+        self.lib = _lib.load()
+        self.device = device
+        h = ctypes.c_void_p()
+        check(self.lib.mxq_create(device, ctypes.byref(h)))
+        self.h = h
+
+    def _bind(self):
+        s = torch.cuda.current_stream(self.device).cuda_stream
+        check(self.lib.mxq_set_stream(self.h, ctypes.c_void_p(s)), self.h)
+
+    def set_path(self, path):
+        check(self.lib.mxq_set_path(self.h, path), self.h)
+
+    def reserve(self, max_batch, max_k):
+        check(self.lib.mxq_reserve(self.h, max_batch, max_k), self.h)
+
+    def synchronize(self):
+        self._bind()
+        check(self.lib.mxq_synchronize(self.h), self.h)
+
+    def launch_count(self):
+        v = ctypes.c_uint64()
+        check(self.lib.mxq_launch_count(self.h, ctypes.byref(v)), self.h)
+        return v.value
+
+    def close(self):
+        if getattr(self, "h", None):
+            self.lib.mxq_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+_contexts = {}
+
+
+def context(device=None):
+    """The default per-device context (created on first use)."""
+    if device is None:
+        device = torch.cuda.current_device()
+    if device not in _contexts:
+        _contexts[device] = MXContext(device)
+    return _contexts[device]
+
+
+@dataclass
+class MXActivation:
+    """MXUINT8Tensor: q = u8 (value + 128) [B][K], s = E8M0 [B][K/32]."""
+    q: torch.Tensor
+    s: torch.Tensor
+
+    @property
+    def batch(self):
+        return self.q.shape[0]
+
+    @property
+    def k(self):
+        return self.q.shape[1]
+
+
+class MXWeight:
+    """MXINT8Tensor (int8 [N][K] or int4 packed [N][K/2]) + E8M0 scales
+    [N][K/32], uploaded once into the library's tiled device layout."""
+
+    def __init__(self, data, scales, fmt, n, k, ctx=None):
+        self.ctx = ctx or context()
+        self.fmt, self.n, self.k = fmt, n, k
+        data = torch.as_tensor(data)
+        scales = torch.as_tensor(scales)
+        exp_bytes = n * k // (2 if fmt == FMT_INT4 else 1)
+        if data.numel() * data.element_size() != exp_bytes:
+            raise ValueError("weight data has %d bytes, expected %d" % (data.numel() * data.element_size(), exp_bytes))
+        if scales.numel() != n * k // 32:
+            raise ValueError("weight scales have %d entries, expected %d" % (scales.numel(), n * k // 32))
+        data = data.contiguous()
+        scales = scales.contiguous()
+        on_dev = 1 if data.is_cuda else 0
+        if data.is_cuda != scales.is_cuda:
+            raise ValueError("data and scales must both be host or both be device tensors")
+        h = ctypes.c_void_p()
+        self.ctx._bind()
+        check(self.ctx.lib.mxq_weight_create(self.ctx.h, fmt, n, k, _ptr(data), _ptr(scales), on_dev,
+                                             ctypes.byref(h)), self.ctx.h)
+        self.h = h
+
+    def close(self):
+        if getattr(self, "h", None):
+            self.ctx.lib.mxq_weight_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+def _quant(x, act, ctx):
+    ctx = ctx or context()
+    _need_cuda(x, torch.float32, "x")
+    if x.dim() == 1:
+        x = x.unsqueeze(0)
+    b, k = x.shape
+    q = torch.empty((b, k), dtype=torch.uint8, device=x.device)
+    s = torch.empty((b, k // 32), dtype=torch.uint8, device=x.device)
+    ctx._bind()
+    check(ctx.lib.mxq_quantize_x(ctx.h, _ptr(x), b, k, act, _ptr(q), _ptr(s)), ctx.h)
+    return MXActivation(q, s)
+
+
+def mx_quantize_x(x, ctx=None):
+    """nca::linalg::mx_quantize_x: fp32 [B][K] -> MXActivation."""
+    return _quant(x, ACT_NONE, ctx)
+
+
+def mx_fused_silu_quantize_x(x, ctx=None):
+    """nca::linalg::mx_fused_silu_quantize_x: silu(x) -> MXActivation."""
+    return _quant(x, ACT_SILU, ctx)
+
+
+def fused_gated_silu_quantize(gate, up, ctx=None):
+    """nca::layers::fused_gated_silu_quantize: silu(gate) * up -> MX."""
+    ctx = ctx or context()
+    _need_cuda(gate, torch.float32, "gate")
+    _need_cuda(up, torch.float32, "up")
+    if gate.shape != up.shape:
+        raise ValueError("gate and up shapes differ")
+    if gate.dim() == 1:
+        gate, up = gate.unsqueeze(0), up.unsqueeze(0)
+    b, k = gate.shape
+    q = torch.empty((b, k), dtype=torch.uint8, device=gate.device)
+    s = torch.empty((b, k // 32), dtype=torch.uint8, device=gate.device)
+    ctx._bind()
+    check(ctx.lib.mxq_swiglu_quantize(ctx.h, _ptr(gate), _ptr(up), b, k, _ptr(q), _ptr(s)), ctx.h)
+    return MXActivation(q, s)
+
+
+def _check_act(x, w):
+    _need_cuda(x.q, torch.uint8, "activation q")
+    _need_cuda(x.s, torch.uint8, "activation scales")
+    if x.k != w.k:
+        raise ValueError("activation K=%d does not match weight K=%d" % (x.k, w.k))
+
+
+def mx_gemv(x, w, ctx=None):
+    """nca::linalg::mx_gemv: y[b][n] = sum_blocks 2^(e_x+e_w) * dot, fp32."""
+    ctx = ctx or w.ctx
+    _check_act(x, w)
+    y = torch.empty((x.batch, w.n), dtype=torch.float32, device=x.q.device)
+    ctx._bind()
+    check(ctx.lib.mxq_gemv(ctx.h, w.h, _ptr(x.q), _ptr(x.s), x.batch, _ptr(y)), ctx.h)
+    return y
+
+
+def _rows(w, n, name):
+    if w.n != n:
+        raise ValueError("%s needs a %d-row weight, got %d rows" % (name, n, w.n))
+
+
+def mx_dot(x, w, ctx=None):
+    """nca::linalg::mx_dot: one weight row."""
+    _rows(w, 1, "mx_dot")
+    return mx_gemv(x, w, ctx)
+
+
+def mx_dual_dot(x, w, ctx=None):
+    _rows(w, 2, "mx_dual_dot")
+    return mx_gemv(x, w, ctx)
+
+
+def mx_quad_dot(x, w, ctx=None):
+    _rows(w, 4, "mx_quad_dot")
+    return mx_gemv(x, w, ctx)
+
+
+def mx_rank16_dot(x, w, ctx=None):
+    _rows(w, 16, "mx_rank16_dot")
+    return mx_gemv(x, w, ctx)
+
+
+def mx_rank16_dot_ptrs(x, w, rows, ctx=None):
+    """nca::linalg::mx_rank16_dot_ptrs: rows gathered by id (the reference
+    passed 16 MXINT8Tensor pointers; here an int32 row-id tensor into one
+    expert-pool weight)."""
+    ctx = ctx or w.ctx
+    _check_act(x, w)
+    _need_cuda(rows, torch.int32, "rows")
+    y = torch.empty((x.batch, rows.numel()), dtype=torch.float32, device=x.q.device)
+    ctx._bind()
+    check(ctx.lib.mxq_gather_dot(ctx.h, w.h, _ptr(x.q), _ptr(x.s), x.batch, _ptr(rows), rows.numel(),
+                                 _ptr(y)), ctx.h)
+    return y
+
+
+def mx_block_dots(x, w, ctx=None):
+    """Per-block int32 dots [B][N][K/32] (the dpbusd - 128*w_sum values)."""
+    ctx = ctx or w.ctx
+    _check_act(x, w)
+    d = torch.empty((x.batch, w.n, w.k // 32), dtype=torch.int32, device=x.q.device)
+    ctx._bind()
+    check(ctx.lib.mxq_block_dots(ctx.h, w.h, _ptr(x.q), x.batch, _ptr(d)), ctx.h)
+    return d
+
+
+def mx_linear(x, w, ctx=None):
+    """fp32 [B][K] -> quantise -> MX linear -> fp32 [B][N]."""
+    ctx = ctx or w.ctx
+    _need_cuda(x, torch.float32, "x")
+    if x.dim() == 1:
+        x = x.unsqueeze(0)
+    if x.shape[1] != w.k:
+        raise ValueError("x K=%d does not match weight K=%d" % (x.shape[1], w.k))
+    y = torch.empty((x.shape[0], w.n), dtype=torch.float32, device=x.device)
+    ctx._bind()
+    check(ctx.lib.mxq_linear(ctx.h, w.h, _ptr(x), x.shape[0], _ptr(y)), ctx.h)
+    return y
+
+
+def mx_linear_pair(x, w1, w2, ctx=None):
+    ctx = ctx or w1.ctx
+    _need_cuda(x, torch.float32, "x")
+    if x.dim() == 1:
+        x = x.unsqueeze(0)
+    y = torch.empty((x.shape[0], w2.n), dtype=torch.float32, device=x.device)
+    ctx._bind()
+    check(ctx.lib.mxq_linear_pair(ctx.h, w1.h, w2.h, _ptr(x), x.shape[0], _ptr(y)), ctx.h)
+    return y
+
+
+def gated_mlp_step(x, w_gate, w_up, w_down, ctx=None):
+    """nca::layers::gated_mlp_step: down(quant(silu(gate x) * up x))."""
+    ctx = ctx or w_gate.ctx
+    _need_cuda(x, torch.float32, "x")
+    if x.dim() == 1:
+        x = x.unsqueeze(0)
+    y = torch.empty((x.shape[0], w_down.n), dtype=torch.float32, device=x.device)
+    ctx._bind()
+    check(ctx.lib.mxq_mlp_swiglu(ctx.h, w_gate.h, w_up.h, w_down.h, _ptr(x), x.shape[0], _ptr(y)), ctx.h)
+    return y
+
+
+def route_topk(logits, k, ctx=None):
+    """Top-k experts per token: (idx int32 [T][k], gate fp32 [T][k])."""
+    ctx = ctx or context()
+    _need_cuda(logits, torch.float32, "logits")
+    t, e = logits.shape
+    if k == 0 or k > e:
+        raise ValueError("Top-K (%d) must be in [1, n_experts=%d]" % (k, e))
+    idx = torch.empty((t, k), dtype=torch.int32, device=logits.device)
+    gate = torch.empty((t, k), dtype=torch.float32, device=logits.device)
+    ctx._bind()
+    check(ctx.lib.mxq_route_topk(ctx.h, _ptr(logits), t, e, k, _ptr(idx), _ptr(gate)), ctx.h)
+    return idx, gate
+
+
+class HashedRouter:
+    """Router with the reference's HashedRouter::Config{d, n_experts, top_k,
+    ...} construction contract (nn/tests/test_robustness.cpp:13-35): top_k >
+    n_experts raises ValueError at construction.  Routing scores are the
+    caller's logits (softmax top-k)."""
+
+    def __init__(self, d, n_experts, top_k, n_hashes=8):
+        if top_k > n_experts or top_k == 0:
+            raise ValueError("HashedRouter: top_k (%d) exceeds n_experts (%d)" % (top_k, n_experts))
+        self.d, self.n_experts, self.top_k, self.n_hashes = d, n_experts, top_k, n_hashes
+
+    def route(self, logits, ctx=None):
+        if logits.shape[-1] != self.n_experts:
+            raise ValueError("logits last dim %d != n_experts %d" % (logits.shape[-1], self.n_experts))
+        return route_topk(logits.reshape(-1, self.n_experts), self.top_k, ctx)
+
+
+def fused_compute_gae(rewards, values, dones, next_values, gamma=0.99, lam=0.95, ctx=None):
+    """nca::env::ReplayMemory::fused_compute_gae on [T][E] interleaved data.
+    Returns (advantages, returns)."""
+    ctx = ctx or context()
+    _need_cuda(rewards, torch.float32, "rewards")
+    _need_cuda(values, torch.float32, "values")
+    _need_cuda(dones, torch.uint8, "dones")
+    _need_cuda(next_values, torch.float32, "next_values")
+    t, e = rewards.shape
+    if values.shape != (t, e) or dones.shape != (t, e) or next_values.numel() != e:
+        raise ValueError("GAE input shapes disagree")
+    adv = torch.empty_like(rewards)
+    ret = torch.empty_like(rewards)
+    ctx._bind()
+    check(ctx.lib.mxq_gae(ctx.h, _ptr(rewards), _ptr(values), _ptr(dones), _ptr(next_values), t, e,
+                          float(gamma), float(lam), _ptr(adv), _ptr(ret)), ctx.h)
+    return adv, ret

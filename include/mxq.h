@@ -1,0 +1,170 @@
+/*
+ * mxq.h -- C-ABI of the B200 MX (E8M0 block-scaled) int8/int4 linear-layer
+ * library, libmxq.so.
+ *
+ * Drop-in boundary for the nca::linalg MX operators of saoxdxd2/cpu_model
+ * (core/linalg/mx_linear.hpp and core/simd/avx512_vnni.hpp, removed from the
+ * snapshot; their names are registered in nn/tests/test_auto_generated.cpp:
+ * 46-56 and their containers shown in nn/tests/autotest.hpp:93-136).  The
+ * opaque-handle / plain-pointer style follows the reference's own C-ABI,
+ * deployment/nca_deploy.h:25-46.
+ *
+ * Conventions
+ *   - Every function returns an int status: MXQ_OK (0) or a negative
+ *     MXQ_ERR_* code; nothing throws across this boundary.  Unlike
+ *     deployment/nca_deploy.cpp:28-61, which silently returns on a null
+ *     handle, a null handle or pointer is MXQ_ERR_INVALID_ARGUMENT.
+ *     mxq_last_error() describes the last failure on a context.
+ *   - Data pointers are DEVICE pointers owned by the caller (16-byte
+ *     aligned), except in the *_host entry points, which take host memory.
+ *     Weight handles own their device copy of the weights.
+ *   - Work is enqueued on the context's stream (mxq_set_stream; default the
+ *     legacy stream) and is asynchronous; mxq_synchronize() waits and
+ *     reports a device-side timeout (MXQ_ERR_TIMEOUT) if any bounded wait in a
+ *     kernel gave up.
+ *   - One context per host thread/stream.  The context grows its device
+ *     workspace on demand (cudaMalloc) the first time a larger batch or K is
+ *     seen; mxq_reserve() sizes it ahead of time so the hot path allocates
+ *     nothing.
+ *
+ * Layouts (the reference's containers, nn/tests/autotest.hpp:93-136)
+ *   MX activation (MXUINT8Tensor): q u8 [B][K] holding q+128, scales E8M0
+ *     [B][K/32].
+ *   MX weight (MXINT8Tensor): int8 [N][K] row-major (or int4 packed
+ *     [N][K/2], element 2i in the low nibble of byte i, two's complement),
+ *     scales E8M0 [N][K/32].  K must be a multiple of 32.  The reference's
+ *     w_sums are a CPU dpbusd artefact and are not needed.
+ *   E8M0 byte s = 2^(s-127), 0xFF = NaN.
+ */
+#ifndef MXQ_H
+#define MXQ_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#if defined(_WIN32)
+#define MXQ_API __declspec(dllexport)
+#else
+#define MXQ_API __attribute__((visibility("default")))
+#endif
+
+#define MXQ_OK 0
+#define MXQ_ERR_INVALID_ARGUMENT (-1)
+#define MXQ_ERR_CUDA (-2)
+#define MXQ_ERR_TIMEOUT (-3)
+#define MXQ_ERR_OUT_OF_MEMORY (-4)
+#define MXQ_ERR_UNSUPPORTED (-5)
+
+#define MXQ_FMT_INT4 4
+#define MXQ_FMT_INT8 8
+
+#define MXQ_ACT_NONE 0
+#define MXQ_ACT_SILU 1
+
+#define MXQ_PATH_AUTO 0 /* GEMV for batch <= 8, tensor-core GEMM above */
+#define MXQ_PATH_GEMV 1
+#define MXQ_PATH_GEMM 2
+
+typedef struct mxq_context* mxq_ctx;
+typedef struct mxq_weight_s* mxq_weight;
+
+/* ---------------------------------------------------------- lifecycle --- */
+/* deployment/nca_deploy.h:28-30 (create/destroy) pattern. */
+MXQ_API int mxq_abi_version(void);
+MXQ_API int mxq_create(int device, mxq_ctx* out);
+MXQ_API int mxq_destroy(mxq_ctx ctx);
+MXQ_API int mxq_set_stream(mxq_ctx ctx, void* cuda_stream);
+/* Regime override, the counterpart of nca::simd::set_override_backend
+ * (nn/core/simd/dispatch.cpp:83-87): MXQ_PATH_*. */
+MXQ_API int mxq_set_path(mxq_ctx ctx, int path);
+MXQ_API int mxq_reserve(mxq_ctx ctx, size_t max_batch, size_t max_k);
+MXQ_API int mxq_synchronize(mxq_ctx ctx);
+MXQ_API const char* mxq_last_error(mxq_ctx ctx);
+/* Number of kernels this context has launched (for launch accounting). */
+MXQ_API int mxq_launch_count(mxq_ctx ctx, uint64_t* out);
+
+/* ------------------------------------------------------------ weights --- */
+/* Uploads an MX weight (MXINT8Tensor layout; int8 or packed int4) from host
+ * (on_device = 0) or device (on_device = 1) memory; replaces the
+ * mx_quantize_w output container (training/fidelity_test.cpp:60-61). */
+MXQ_API int mxq_weight_create(mxq_ctx ctx, int fmt, size_t n, size_t k,
+                              const void* data, const uint8_t* scales,
+                              int on_device, mxq_weight* out);
+MXQ_API int mxq_weight_destroy(mxq_weight w);
+MXQ_API int mxq_weight_shape(mxq_weight w, int* fmt, size_t* n, size_t* k);
+
+/* --------------------------------------------------------- quantisers --- */
+/* nca::linalg::mx_quantize_x / mx_fused_silu_quantize_x
+ * (nn/tests/test_auto_generated.cpp:47-48; semantics
+ * nn/core/layers/ssm.cpp:164-177): x fp32 [B][K] -> q [B][K], s [B][K/32].
+ * act = MXQ_ACT_NONE or MXQ_ACT_SILU. */
+MXQ_API int mxq_quantize_x(mxq_ctx ctx, const float* x, size_t b, size_t k,
+                           int act, uint8_t* q, uint8_t* s);
+/* nca::layers::fused_gated_silu_quantize
+ * (nn/tests/test_auto_generated.cpp:41): silu(gate) * up -> MX. */
+MXQ_API int mxq_swiglu_quantize(mxq_ctx ctx, const float* gate,
+                                const float* up, size_t b, size_t k,
+                                uint8_t* q, uint8_t* s);
+
+/* ------------------------------------------------------------- linear --- */
+/* nca::linalg::mx_gemv (nn/tests/test_auto_generated.cpp:56), batched;
+ * mx_dot / mx_dual_dot / mx_quad_dot / mx_rank16_dot (:51-54) are this call
+ * on a 1/2/4/16-row weight.  MX activations in, y fp32 [B][N]. */
+MXQ_API int mxq_gemv(mxq_ctx ctx, mxq_weight w, const uint8_t* xq,
+                     const uint8_t* xs, size_t b, float* y);
+/* nca::linalg::mx_rank16_dot_ptrs (nn/tests/test_auto_generated.cpp:55;
+ * pointer-array form nn/tests/autotest.hpp:126-136): rows gathered through
+ * a device int32 row-id list; y [B][nrows]. */
+MXQ_API int mxq_gather_dot(mxq_ctx ctx, mxq_weight w, const uint8_t* xq,
+                           const uint8_t* xs, size_t b, const int32_t* rows,
+                           size_t nrows, float* y);
+/* Per-block int32 dots sum_{i<32} q_x * q_w, out [B][N][K/32]; the
+ * dpbusd - 128 * w_sum quantity of the reference's VNNI kernel. */
+MXQ_API int mxq_block_dots(mxq_ctx ctx, mxq_weight w, const uint8_t* xq,
+                           size_t b, int32_t* dots);
+/* fp32 in -> quantise -> MX linear -> fp32 out (the drop-in for the
+ * training/ppo_trainer.cpp:57-61 projections). */
+MXQ_API int mxq_linear(mxq_ctx ctx, mxq_weight w, const float* x, size_t b,
+                       float* y);
+/* Same with HOST buffers; copies in and out on the context stream and
+ * returns when y_host is written. */
+MXQ_API int mxq_linear_host(mxq_ctx ctx, mxq_weight w, const float* x_host,
+                            size_t b, float* y_host);
+/* Two chained linears (w1: K -> M, w2: M -> N) with MX requantisation of the
+ * intermediate, as in a 7B MLP's up/down pair. */
+MXQ_API int mxq_linear_pair(mxq_ctx ctx, mxq_weight w1, mxq_weight w2,
+                            const float* x, size_t b, float* y);
+MXQ_API int mxq_linear_pair_host(mxq_ctx ctx, mxq_weight w1, mxq_weight w2,
+                                 const float* x_host, size_t b, float* y_host);
+/* nca::layers::gated_mlp_step (nn/tests/test_auto_generated.cpp:42):
+ * y = down(quant(silu(gate(x)) * up(x))). */
+MXQ_API int mxq_mlp_swiglu(mxq_ctx ctx, mxq_weight gate, mxq_weight up,
+                           mxq_weight down, const float* x, size_t b,
+                           float* y);
+
+/* ------------------------------------------------------------ routing --- */
+/* Top-k expert selection with the HashedRouter contract
+ * (nn/tests/test_robustness.cpp:13-35: k > n_experts is an invalid
+ * argument): descending logit, ties to the lower id, gate = softmax over
+ * the chosen logits.  idx int32 [T][k], gate fp32 [T][k]. */
+MXQ_API int mxq_route_topk(mxq_ctx ctx, const float* logits, size_t t,
+                           size_t n_experts, size_t k, int32_t* idx,
+                           float* gate);
+
+/* ---------------------------------------------------------------- GAE --- */
+/* nca::env::ReplayMemory::fused_compute_gae
+ * (agentic_env/replay_memory.cpp:204-253) over an interleaved [T][E]
+ * trajectory (dones as bytes); writes advantages and returns. */
+MXQ_API int mxq_gae(mxq_ctx ctx, const float* rewards, const float* values,
+                    const uint8_t* dones, const float* next_values, size_t t,
+                    size_t e, float gamma, float lambda, float* adv,
+                    float* ret);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* MXQ_H */

@@ -1,0 +1,171 @@
+// nca_mx_linear.hpp -- C++ restoration of the reference's nca::linalg MX
+// operator interface (the removed core/linalg/mx_linear.hpp; names in
+// nn/tests/test_auto_generated.cpp:46-56, containers in
+// nn/tests/autotest.hpp:93-136) on top of the C-ABI in mxq.h.
+//
+// Header-only.  Containers hold DEVICE memory; weights are owned by an
+// MXINT8Tensor (upload once, reuse).  Like the reference operators, shape
+// errors throw std::invalid_argument; CUDA or device-timeout failures throw
+// std::runtime_error.  The C-ABI below never throws.
+#pragma once
+#include <cstddef>
+#include <cstdint>
+#include <stdexcept>
+#include <string>
+#include <utility>
+
+#include "mxq.h"
+
+namespace nca::linalg {
+
+inline void mxq_check(int rc, mxq_ctx ctx) {
+  if (rc == MXQ_OK) return;
+  std::string msg = mxq_last_error(ctx);
+  if (rc == MXQ_ERR_INVALID_ARGUMENT) throw std::invalid_argument(msg);
+  throw std::runtime_error(msg + " (status " + std::to_string(rc) + ")");
+}
+
+// One library context per thread/stream (the reference's Dispatcher bound a
+// kernel per process; here the binding is the device + stream).
+class Context {
+ public:
+  explicit Context(int device = 0, void* stream = nullptr) {
+    mxq_check(mxq_create(device, &ctx_), nullptr);
+    if (stream) mxq_check(mxq_set_stream(ctx_, stream), ctx_);
+  }
+  ~Context() {
+    if (ctx_) mxq_destroy(ctx_);
+  }
+  Context(const Context&) = delete;
+  Context& operator=(const Context&) = delete;
+  mxq_ctx get() const { return ctx_; }
+  void synchronize() const { mxq_check(mxq_synchronize(ctx_), ctx_); }
+  // counterpart of nca::simd::set_override_backend: force GEMV or GEMM
+  void set_override_path(int path) const { mxq_check(mxq_set_path(ctx_, path), ctx_); }
+
+ private:
+  mxq_ctx ctx_ = nullptr;
+};
+
+// MXUINT8Tensor: activation view, data = q + 128 (u8), scales = E8M0, one per
+// 32 elements.  `batch` rows of `num_blocks` blocks each; device pointers.
+struct MXUINT8Tensor {
+  uint8_t* data = nullptr;
+  uint8_t* scales = nullptr;
+  size_t num_blocks = 0;  // per row
+  size_t batch = 1;
+  size_t k() const { return num_blocks * 32; }
+};
+
+// MXINT8Tensor: an uploaded MX weight (int8 or packed int4) [rows][K].
+class MXINT8Tensor {
+ public:
+  MXINT8Tensor() = default;
+  MXINT8Tensor(const Context& ctx, int fmt, size_t rows, size_t k, const void* data,
+               const uint8_t* scales, bool on_device) {
+    mxq_check(mxq_weight_create(ctx.get(), fmt, rows, k, data, scales, on_device ? 1 : 0, &w_),
+              ctx.get());
+    rows_ = rows;
+    k_ = k;
+  }
+  ~MXINT8Tensor() {
+    if (w_) mxq_weight_destroy(w_);
+  }
+  MXINT8Tensor(MXINT8Tensor&& o) noexcept
+      : w_(std::exchange(o.w_, nullptr)), rows_(o.rows_), k_(o.k_) {}
+  MXINT8Tensor& operator=(MXINT8Tensor&& o) noexcept {
+    if (this != &o) {
+      if (w_) mxq_weight_destroy(w_);
+      w_ = std::exchange(o.w_, nullptr);
+      rows_ = o.rows_;
+      k_ = o.k_;
+    }
+    return *this;
+  }
+  MXINT8Tensor(const MXINT8Tensor&) = delete;
+  MXINT8Tensor& operator=(const MXINT8Tensor&) = delete;
+  mxq_weight handle() const { return w_; }
+  size_t rows() const { return rows_; }
+  size_t k() const { return k_; }
+  size_t num_blocks() const { return rows_ * k_ / 32; }
+
+ private:
+  mxq_weight w_ = nullptr;
+  size_t rows_ = 0, k_ = 0;
+};
+
+inline void require(bool ok, const char* what) {
+  if (!ok) throw std::invalid_argument(what);
+}
+
+// mx_quantize_x: fp32 [batch][k] (device) -> MXUINT8Tensor
+inline void mx_quantize_x(const Context& c, const float* x, MXUINT8Tensor& out) {
+  mxq_check(mxq_quantize_x(c.get(), x, out.batch, out.k(), MXQ_ACT_NONE, out.data, out.scales),
+            c.get());
+}
+
+// mx_fused_silu_quantize_x: silu(x) -> MXUINT8Tensor
+inline void mx_fused_silu_quantize_x(const Context& c, const float* x, MXUINT8Tensor& out) {
+  mxq_check(mxq_quantize_x(c.get(), x, out.batch, out.k(), MXQ_ACT_SILU, out.data, out.scales),
+            c.get());
+}
+
+// fused_gated_silu_quantize: silu(gate) * up -> MXUINT8Tensor
+inline void fused_gated_silu_quantize(const Context& c, const float* gate, const float* up,
+                                      MXUINT8Tensor& out) {
+  mxq_check(mxq_swiglu_quantize(c.get(), gate, up, out.batch, out.k(), out.data, out.scales),
+            c.get());
+}
+
+// mx_gemv: y[batch][rows] = W x (fp32, device)
+inline void mx_gemv(const Context& c, const MXUINT8Tensor& x, const MXINT8Tensor& w, float* y) {
+  require(x.k() == w.k(), "mx_gemv: activation and weight K differ");
+  mxq_check(mxq_gemv(c.get(), w.handle(), x.data, x.scales, x.batch, y), c.get());
+}
+
+// mx_dot / mx_dual_dot / mx_quad_dot / mx_rank16_dot: 1/2/4/16-row weights
+inline void mx_dot(const Context& c, const MXUINT8Tensor& x, const MXINT8Tensor& w, float* y) {
+  require(w.rows() == 1, "mx_dot: weight must have 1 row");
+  mx_gemv(c, x, w, y);
+}
+inline void mx_dual_dot(const Context& c, const MXUINT8Tensor& x, const MXINT8Tensor& w, float* y) {
+  require(w.rows() == 2, "mx_dual_dot: weight must have 2 rows");
+  mx_gemv(c, x, w, y);
+}
+inline void mx_quad_dot(const Context& c, const MXUINT8Tensor& x, const MXINT8Tensor& w, float* y) {
+  require(w.rows() == 4, "mx_quad_dot: weight must have 4 rows");
+  mx_gemv(c, x, w, y);
+}
+inline void mx_rank16_dot(const Context& c, const MXUINT8Tensor& x, const MXINT8Tensor& w, float* y) {
+  require(w.rows() == 16, "mx_rank16_dot: weight must have 16 rows");
+  mx_gemv(c, x, w, y);
+}
+
+// mx_rank16_dot_ptrs: rows gathered by id from an expert-pool weight
+// (device int32 ids; the reference passed 16 MXINT8Tensor pointers).
+inline void mx_rank16_dot_ptrs(const Context& c, const MXUINT8Tensor& x, const MXINT8Tensor& pool,
+                               const int32_t* row_ids, size_t nrows, float* y) {
+  require(x.k() == pool.k(), "mx_rank16_dot_ptrs: activation and weight K differ");
+  mxq_check(mxq_gather_dot(c.get(), pool.handle(), x.data, x.scales, x.batch, row_ids, nrows, y),
+            c.get());
+}
+
+// fp32 in -> fp32 out (drop-in for a dense projection)
+inline void mx_linear(const Context& c, const float* x, size_t batch, const MXINT8Tensor& w, float* y) {
+  mxq_check(mxq_linear(c.get(), w.handle(), x, batch, y), c.get());
+}
+
+}  // namespace nca::linalg
+
+namespace nca::layers {
+
+// gated_mlp_step: down(quant(silu(gate x) * up x))
+inline void gated_mlp_step(const nca::linalg::Context& c, const float* x, size_t batch,
+                           const nca::linalg::MXINT8Tensor& gate,
+                           const nca::linalg::MXINT8Tensor& up,
+                           const nca::linalg::MXINT8Tensor& down, float* y) {
+  nca::linalg::mxq_check(mxq_mlp_swiglu(c.get(), gate.handle(), up.handle(), down.handle(), x, batch, y),
+                         c.get());
+}
+
+}  // namespace nca::layers

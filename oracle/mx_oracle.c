@@ -1,0 +1,392 @@
+/*
+ * mx_oracle.c -- CPU restatement of the reference's MX linear path.
+ *
+ * TEST INFRASTRUCTURE ONLY (the checker).  Built with -ffp-contract=off so
+ * that every float operation below is evaluated exactly as written; the GPU
+ * kernels evaluate the quantiser's float steps with the same IEEE operations
+ * (explicit round-to-nearest intrinsics), so quantised bytes agree bit for
+ * bit.  See mx_oracle.h for the numeric conventions and reference citations.
+ */
+#include "mx_oracle.h"
+
+#include <math.h>
+#include <stdlib.h>
+#include <string.h>
+
+/* ---------------------------------------------------------------- E8M0 --- */
+
+/* nn/core/layers/ssm.cpp:170 calls extract_e8m0(max_abs); its body is not in
+ * the snapshot.  Here: the smallest integer e with max_abs <= qmax * 2^e, found
+ * with exact double comparisons (qmax * 2^e is exact in double). */
+uint8_t mxo_e8m0_from_absmax(float max_abs, int qmax)
+{
+    if (!(max_abs == max_abs) || isinf(max_abs)) return 0xFF;
+    if (max_abs == 0.0f) return 0;
+    double m = (double)max_abs;
+    int e = (int)floor(log2(m / (double)qmax)) - 2;
+    while (m > ldexp((double)qmax, e)) ++e;
+    if (e < -127) e = -127;
+    if (e > 127) e = 127;
+    return (uint8_t)(e + 127);
+}
+
+/* nn/core/layers/ssm.cpp:171 decode_e8m0_scale: byte -> 2^(byte-127). */
+double mxo_e8m0_decode(uint8_t s)
+{
+    if (s == 0xFF) return NAN;
+    return ldexp(1.0, (int)s - 127);
+}
+
+/* ------------------------------------------------------ exp and SiLU --- */
+
+/* exp(x) by Cody-Waite argument reduction (ln2 split into an exactly
+ * representable high part and a correction, as in the fdlibm expf design)
+ * followed by the degree-7 Taylor polynomial of e^r on |r| <= ln2/2,
+ * evaluated by Horner's rule with fused multiply-adds.  2^n is applied by
+ * building the IEEE exponent directly.  Every step is a single IEEE
+ * operation so the GPU evaluates the same sequence to the same bits. */
+static float pow2i(int n) /* 2^n for n in [-126, 127] */
+{
+    union { uint32_t u; float f; } v;
+    v.u = (uint32_t)(n + 127) << 23;
+    return v.f;
+}
+
+float mxo_expf(float x)
+{
+    const float LOG2E = 1.44269504088896341f;
+    const float LN2_HI = 6.93145751953125e-1f;
+    const float LN2_LO = 1.42860682030941723212e-6f;
+    if (x != x) return x;
+    if (x > 88.72283935546875f) return INFINITY;
+    if (x < -103.972084045410f) return 0.0f;
+    float t = x * LOG2E;
+    float nf = rintf(t);
+    int n = (int)nf;
+    float r = fmaf(-nf, LN2_HI, x);
+    r = fmaf(-nf, LN2_LO, r);
+    float p = 1.0f / 5040.0f;
+    p = fmaf(p, r, 1.0f / 720.0f);
+    p = fmaf(p, r, 1.0f / 120.0f);
+    p = fmaf(p, r, 1.0f / 24.0f);
+    p = fmaf(p, r, 1.0f / 6.0f);
+    p = fmaf(p, r, 0.5f);
+    p = fmaf(p, r, 1.0f);
+    p = fmaf(p, r, 1.0f);
+    if (n > 127) {
+        p = p * pow2i(n - 1);
+        p = p * 2.0f;
+    } else if (n < -126) {
+        p = p * pow2i(n + 64);
+        p = p * pow2i(-64);
+    } else {
+        p = p * pow2i(n);
+    }
+    return p;
+}
+
+/* SiLU as in nn/core/layers/ssm.cpp:159 (y / (1 + exp(-y))). */
+float mxo_silu(float x)
+{
+    float e = mxo_expf(-x);
+    float d = 1.0f + e;
+    return x / d;
+}
+
+/* ----------------------------------------------------------- quantise --- */
+
+/* One 32-element block: v[32] -> 32 bytes (q+128) + scale byte.
+ * Follows nn/core/layers/ssm.cpp:164-177 with round-half-to-even
+ * (the _mm512_cvtps_epi32 behaviour of nn/core/layers/ssm.cpp:249). */
+static void quantize_block(const float* v, uint8_t* q, uint8_t* s)
+{
+    float max_abs = 0.0f;
+    int finite = 1;
+    for (int i = 0; i < MXO_BLOCK; ++i) {
+        float a = fabsf(v[i]);
+        if (!(a == a) || isinf(a)) finite = 0;
+        else if (a > max_abs) max_abs = a;
+    }
+    if (!finite) {
+        *s = 0xFF;
+        memset(q, 128, MXO_BLOCK);
+        return;
+    }
+    uint8_t sb = mxo_e8m0_from_absmax(max_abs, 127);
+    *s = sb;
+    int e = (int)sb - 127;
+    float inv = pow2i(-e); /* e in [-127, 122] for finite float input */
+    for (int i = 0; i < MXO_BLOCK; ++i) {
+        float val = rintf(v[i] * inv);
+        float c = val + 128.0f;
+        if (c < 0.0f) c = 0.0f;
+        if (c > 255.0f) c = 255.0f;
+        q[i] = (uint8_t)c;
+    }
+}
+
+void mxo_quantize_x(const float* x, size_t B, size_t K, int act,
+                    uint8_t* q, uint8_t* s)
+{
+    float buf[MXO_BLOCK];
+    size_t nb = K / MXO_BLOCK;
+    for (size_t r = 0; r < B; ++r)
+        for (size_t b = 0; b < nb; ++b) {
+            const float* src = x + r * K + b * MXO_BLOCK;
+            for (int i = 0; i < MXO_BLOCK; ++i)
+                buf[i] = act == 1 ? mxo_silu(src[i]) : src[i];
+            quantize_block(buf, q + r * K + b * MXO_BLOCK, s + r * nb + b);
+        }
+}
+
+void mxo_swiglu_quantize(const float* gate, const float* up, size_t B, size_t K,
+                         uint8_t* q, uint8_t* s)
+{
+    float buf[MXO_BLOCK];
+    size_t nb = K / MXO_BLOCK;
+    for (size_t r = 0; r < B; ++r)
+        for (size_t b = 0; b < nb; ++b) {
+            size_t o = r * K + b * MXO_BLOCK;
+            for (int i = 0; i < MXO_BLOCK; ++i)
+                buf[i] = mxo_silu(gate[o + i]) * up[o + i];
+            quantize_block(buf, q + o, s + r * nb + b);
+        }
+}
+
+/* ------------------------------------------------------------ weights --- */
+
+int mxo_weight_at(int fmt, const void* data, size_t K, size_t n, size_t k)
+{
+    if (fmt == MXO_FMT_INT8) return ((const int8_t*)data)[n * K + k];
+    uint8_t byte = ((const uint8_t*)data)[n * (K / 2) + k / 2];
+    int nib = (k & 1) ? (byte >> 4) : (byte & 0xF);
+    return nib >= 8 ? nib - 16 : nib;
+}
+
+void mxo_quantize_w(int fmt, const float* w, size_t N, size_t K,
+                    void* data, uint8_t* scales, int32_t* w_sums)
+{
+    int qmax = fmt == MXO_FMT_INT8 ? 127 : 7;
+    size_t nb = K / MXO_BLOCK;
+    if (fmt == MXO_FMT_INT4) memset(data, 0, N * K / 2);
+    for (size_t n = 0; n < N; ++n)
+        for (size_t b = 0; b < nb; ++b) {
+            const float* v = w + n * K + b * MXO_BLOCK;
+            float max_abs = 0.0f;
+            for (int i = 0; i < MXO_BLOCK; ++i) {
+                float a = fabsf(v[i]);
+                if (a > max_abs) max_abs = a;
+            }
+            uint8_t sb = mxo_e8m0_from_absmax(max_abs, qmax);
+            scales[n * nb + b] = sb;
+            float inv = pow2i(127 - (int)sb);
+            int32_t sum = 0;
+            for (int i = 0; i < MXO_BLOCK; ++i) {
+                int qv = (int)rintf(v[i] * inv);
+                if (qv > qmax) qv = qmax;
+                if (qv < -qmax) qv = -qmax;
+                sum += qv;
+                size_t k = b * MXO_BLOCK + i;
+                if (fmt == MXO_FMT_INT8) {
+                    ((int8_t*)data)[n * K + k] = (int8_t)qv;
+                } else {
+                    uint8_t* p = (uint8_t*)data + n * (K / 2) + k / 2;
+                    uint8_t nib = (uint8_t)(qv & 0xF);
+                    *p |= (k & 1) ? (uint8_t)(nib << 4) : nib;
+                }
+            }
+            if (w_sums) w_sums[n * nb + b] = sum;
+        }
+}
+
+/* --------------------------------------------------------------- dots --- */
+
+/* The VNNI contract: dpbusd(u8 = q+128, s8 w) - 128 * w_sum == sum q*w.
+ * The restatement computes sum q*w directly (identical integer). */
+static int32_t block_dot(int fmt, const uint8_t* xq, const void* w, size_t K,
+                         size_t n, size_t b)
+{
+    int32_t acc = 0;
+    for (int i = 0; i < MXO_BLOCK; ++i) {
+        size_t k = b * MXO_BLOCK + i;
+        acc += ((int32_t)xq[k] - 128) * mxo_weight_at(fmt, w, K, n, k);
+    }
+    return acc;
+}
+
+void mxo_block_dots(int fmt, const uint8_t* xq, const void* w, size_t B,
+                    size_t N, size_t K, int32_t* out)
+{
+    size_t nb = K / MXO_BLOCK;
+    for (size_t r = 0; r < B; ++r)
+        for (size_t n = 0; n < N; ++n)
+            for (size_t b = 0; b < nb; ++b)
+                out[(r * N + n) * nb + b] = block_dot(fmt, xq + r * K, w, K, n, b);
+}
+
+static float row_dot(int fmt, const uint8_t* xq, const uint8_t* xs,
+                     const void* w, const uint8_t* ws, size_t K, size_t n)
+{
+    size_t nb = K / MXO_BLOCK;
+    double acc = 0.0;
+    for (size_t b = 0; b < nb; ++b) {
+        uint8_t sx = xs[b], sw = ws[n * nb + b];
+        int32_t d = block_dot(fmt, xq, w, K, n, b);
+        if (sx == 0xFF || sw == 0xFF) { acc = NAN; continue; }
+        acc += ldexp((double)d, (int)sx + (int)sw - 254);
+    }
+    return (float)acc;
+}
+
+void mxo_gemv(int fmt, const uint8_t* xq, const uint8_t* xs, const void* w,
+              const uint8_t* ws, size_t B, size_t N, size_t K, float* y)
+{
+    size_t nb = K / MXO_BLOCK;
+    for (size_t r = 0; r < B; ++r)
+        for (size_t n = 0; n < N; ++n)
+            y[r * N + n] = row_dot(fmt, xq + r * K, xs + r * nb, w, ws, K, n);
+}
+
+void mxo_gather_dot(int fmt, const uint8_t* xq, const uint8_t* xs,
+                    const void* w, const uint8_t* ws, size_t K,
+                    const int32_t* rows, size_t nrows, size_t B, float* y)
+{
+    size_t nb = K / MXO_BLOCK;
+    for (size_t r = 0; r < B; ++r)
+        for (size_t j = 0; j < nrows; ++j)
+            y[r * nrows + j] = row_dot(fmt, xq + r * K, xs + r * nb, w, ws, K,
+                                       (size_t)rows[j]);
+}
+
+/* ---------------------------------------------------------------- MLP --- */
+
+static void mlp_from_q(int fmt, const uint8_t* xq, const uint8_t* xs, size_t B,
+                       size_t D, size_t F, const void* wg, const uint8_t* sg,
+                       const void* wu, const uint8_t* su, const void* wd,
+                       const uint8_t* sd, float* y, uint8_t* mid_q,
+                       uint8_t* mid_s)
+{
+    float* g = (float*)malloc(B * F * sizeof(float));
+    float* u = (float*)malloc(B * F * sizeof(float));
+    uint8_t* hq = mid_q ? mid_q : (uint8_t*)malloc(B * F);
+    uint8_t* hs = mid_s ? mid_s : (uint8_t*)malloc(B * F / MXO_BLOCK);
+    mxo_gemv(fmt, xq, xs, wg, sg, B, F, D, g);
+    mxo_gemv(fmt, xq, xs, wu, su, B, F, D, u);
+    mxo_swiglu_quantize(g, u, B, F, hq, hs);
+    mxo_gemv(fmt, hq, hs, wd, sd, B, D, F, y);
+    free(g);
+    free(u);
+    if (!mid_q) free(hq);
+    if (!mid_s) free(hs);
+}
+
+void mxo_mlp_swiglu(int fmt, const float* x, size_t B, size_t D, size_t F,
+                    const void* wg, const uint8_t* sg, const void* wu,
+                    const uint8_t* su, const void* wd, const uint8_t* sd,
+                    float* y, uint8_t* mid_q, uint8_t* mid_s)
+{
+    uint8_t* xq = (uint8_t*)malloc(B * D);
+    uint8_t* xs = (uint8_t*)malloc(B * D / MXO_BLOCK);
+    mxo_quantize_x(x, B, D, 0, xq, xs);
+    mlp_from_q(fmt, xq, xs, B, D, F, wg, sg, wu, su, wd, sd, y, mid_q, mid_s);
+    free(xq);
+    free(xs);
+}
+
+/* ------------------------------------------------------------ routing --- */
+
+int mxo_route_topk(const float* logits, size_t T, size_t E, size_t k,
+                   int32_t* idx, float* gate)
+{
+    if (k == 0 || k > E || k > 64) return -1;
+    for (size_t t = 0; t < T; ++t) {
+        const float* l = logits + t * E;
+        int32_t* id = idx + t * k;
+        for (size_t j = 0; j < k; ++j) {
+            int best = -1;
+            for (size_t e = 0; e < E; ++e) {
+                int used = 0;
+                for (size_t p = 0; p < j; ++p) used |= id[p] == (int32_t)e;
+                if (used) continue;
+                if (best < 0 || l[e] > l[best]) best = (int)e;
+            }
+            id[j] = best;
+        }
+        /* softmax over the chosen logits; the first is the maximum */
+        float mx = l[id[0]];
+        float ex[64];
+        float den = 0.0f;
+        for (size_t j = 0; j < k; ++j) {
+            ex[j] = mxo_expf(l[id[j]] - mx);
+            den = den + ex[j];
+        }
+        for (size_t j = 0; j < k; ++j) gate[t * k + j] = ex[j] / den;
+    }
+    return 0;
+}
+
+/* ---------------------------------------------------------------- MoE --- */
+
+int mxo_moe(int fmt, const float* x, const float* logits, size_t T, size_t D,
+            size_t F, size_t E, size_t k, const void* const* wg,
+            const uint8_t* const* sg, const void* const* wu,
+            const uint8_t* const* su, const void* const* wd,
+            const uint8_t* const* sd, float* y)
+{
+    int32_t* idx = (int32_t*)malloc(T * k * sizeof(int32_t));
+    float* gate = (float*)malloc(T * k * sizeof(float));
+    if (mxo_route_topk(logits, T, E, k, idx, gate) != 0) {
+        free(idx);
+        free(gate);
+        return -1;
+    }
+    uint8_t* xq = (uint8_t*)malloc(D);
+    uint8_t* xs = (uint8_t*)malloc(D / MXO_BLOCK);
+    float* out = (float*)malloc(D * sizeof(float));
+    double* acc = (double*)malloc(D * sizeof(double));
+    for (size_t t = 0; t < T; ++t) {
+        mxo_quantize_x(x + t * D, 1, D, 0, xq, xs);
+        for (size_t d = 0; d < D; ++d) acc[d] = 0.0;
+        for (size_t j = 0; j < k; ++j) {
+            int e = idx[t * k + j];
+            mlp_from_q(fmt, xq, xs, 1, D, F, wg[e], sg[e], wu[e], su[e], wd[e],
+                       sd[e], out, NULL, NULL);
+            for (size_t d = 0; d < D; ++d)
+                acc[d] += (double)gate[t * k + j] * (double)out[d];
+        }
+        for (size_t d = 0; d < D; ++d) y[t * D + d] = (float)acc[d];
+    }
+    free(idx);
+    free(gate);
+    free(xq);
+    free(xs);
+    free(out);
+    free(acc);
+    return 0;
+}
+
+/* ---------------------------------------------------------------- GAE --- */
+
+/* agentic_env/replay_memory.cpp:204-253, same operation order per element. */
+void mxo_gae(const float* rewards, const float* values, const uint8_t* dones,
+             const float* next_values, size_t T, size_t E, float gamma,
+             float lambda, float* adv, float* ret)
+{
+    float gl = gamma * lambda;
+    float* acc = (float*)calloc(E, sizeof(float));
+    float* vn = (float*)malloc(E * sizeof(float));
+    memcpy(vn, next_values, E * sizeof(float));
+    for (size_t tt = T; tt-- > 0;) {
+        for (size_t k = 0; k < E; ++k) {
+            size_t i = tt * E + k;
+            float done_f = dones[i] ? 0.0f : 1.0f;
+            float delta = rewards[i] + gamma * vn[k] * done_f - values[i];
+            acc[k] = delta + gl * acc[k] * done_f;
+            adv[i] = acc[k];
+            ret[i] = acc[k] + values[i];
+            vn[k] = values[i];
+        }
+    }
+    free(acc);
+    free(vn);
+}

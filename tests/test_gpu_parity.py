@@ -1,0 +1,277 @@
+"""GPU parity tests: every call goes through libmxq.so (the C-ABI) and is
+checked against the CPU oracle on the same seeded inputs.
+
+Bars: quantised bytes, E8M0 scales, per-block int32 dots, routing and GAE are
+bit-exact; fp32 linear outputs agree with the oracle's exactly-rounded
+result within relative L2 error <= 1e-5 (REL_TOL).
+"""
+import numpy as np
+import pytest
+import torch
+
+from oracle import oracle
+from cpu_model_b200 import mx, synth
+
+pytestmark = pytest.mark.gpu
+
+REL_TOL = 1e-5
+
+
+def rel_l2(a, b):
+    a = np.asarray(a, np.float64)
+    b = np.asarray(b, np.float64)
+    den = np.linalg.norm(b)
+    return np.linalg.norm(a - b) / (den if den > 0 else 1.0)
+
+
+def cuda(a):
+    return torch.from_numpy(np.ascontiguousarray(a)).cuda()
+
+
+def host(t):
+    torch.cuda.synchronize()
+    return t.cpu().numpy()
+
+
+def weight(ctx, fmt, n, k, seed, emin=-10, emax=-4):
+    w, ws = synth.weights(fmt, n, k, emin, emax, seed)
+    return w, ws, mx.MXWeight(torch.from_numpy(w), torch.from_numpy(ws), fmt, n, k, ctx)
+
+
+def edge_inputs(b, k, seed):
+    x = synth.normal((b, k), seed)
+    x[0, :32] = 0.0
+    if k >= 96:
+        x[0, 32:64] *= 1e-30
+        x[0, 64:96] *= 1e30
+    if b > 1 and k >= 64:
+        x[1, 40] = 0.5 * 2.0 ** -6        # exact tie after scaling
+        x[1, 33] = 127.0 * 2.0 ** -6
+    return x
+
+
+# ----------------------------------------------------------- quantisers ---
+@pytest.mark.parametrize("b,k", [(1, 32), (3, 96), (5, 4096), (2, 11008)])
+@pytest.mark.parametrize("act", [0, 1])
+def test_quantize_bit_exact(ctx, b, k, act):
+    x = edge_inputs(b, k, 10 + b)
+    q, s = oracle.quantize_x(x, act)
+    a = (mx.mx_quantize_x if act == 0 else mx.mx_fused_silu_quantize_x)(cuda(x), ctx)
+    ctx.synchronize()
+    assert np.array_equal(host(a.q), q)
+    assert np.array_equal(host(a.s), s)
+
+
+def test_quantize_nonfinite_blocks(ctx):
+    x = synth.normal((2, 128), 3)
+    x[0, 5] = np.inf
+    x[1, 70] = np.nan
+    q, s = oracle.quantize_x(x)
+    a = mx.mx_quantize_x(cuda(x), ctx)
+    assert np.array_equal(host(a.q), q) and np.array_equal(host(a.s), s)
+    assert s[0, 0] == 255 and s[1, 2] == 255
+
+
+@pytest.mark.parametrize("b,k", [(1, 64), (4, 11008)])
+def test_swiglu_quantize_bit_exact(ctx, b, k):
+    g = synth.normal((b, k), 21) * 4
+    u = synth.normal((b, k), 22)
+    q, s = oracle.swiglu_quantize(g, u)
+    a = mx.fused_gated_silu_quantize(cuda(g), cuda(u), ctx)
+    assert np.array_equal(host(a.q), q) and np.array_equal(host(a.s), s)
+
+
+# ----------------------------------------------------------- block dots ---
+@pytest.mark.parametrize("fmt", [8, 4])
+@pytest.mark.parametrize("b,n,k", [(1, 1, 32), (3, 33, 96), (2, 300, 4096)])
+def test_block_dots_bit_exact(ctx, fmt, b, n, k):
+    w, ws, W = weight(ctx, fmt, n, k, 30 + n)
+    xq, xs = oracle.quantize_x(synth.normal((b, k), 31))
+    d = mx.mx_block_dots(mx.MXActivation(cuda(xq), cuda(xs)), W, ctx)
+    assert np.array_equal(host(d), oracle.block_dots(fmt, xq, w, n, k))
+
+
+def test_block_dots_extremes(ctx):
+    """Largest |dot| per format: int8 127*127*32, int4 127*8*32."""
+    for fmt, wv in ((8, -127), (4, -8)):
+        n, k = 4, 64
+        wvals = np.full((n, k), wv, np.int8)
+        w = synth.pack_int4(wvals) if fmt == 4 else wvals
+        ws = np.full((n, k // 32), 127, np.uint8)
+        W = mx.MXWeight(torch.from_numpy(w), torch.from_numpy(ws), fmt, n, k, ctx)
+        xq = np.full((2, k), 128 + 127, np.uint8)
+        xq[1] = 1                                   # q = -127
+        d = host(mx.mx_block_dots(mx.MXActivation(cuda(xq), cuda(np.full((2, 2), 127, np.uint8))), W, ctx))
+        assert np.array_equal(d, oracle.block_dots(fmt, xq, w, n, k))
+        assert abs(int(d[0, 0, 0])) == 127 * abs(wv) * 32
+
+
+# --------------------------------------------------------------- GEMV ---
+@pytest.mark.parametrize("fmt", [8, 4])
+@pytest.mark.parametrize("b", [1, 2, 3, 4, 5, 8])
+@pytest.mark.parametrize("n,k", [(1, 32), (33, 96), (1000, 4096), (256, 11008)])
+def test_gemv_parity(ctx, fmt, b, n, k):
+    w, ws, W = weight(ctx, fmt, n, k, 40 + n + k)
+    x = edge_inputs(b, k, 41 + b)
+    xq, xs = oracle.quantize_x(x)
+    ref = oracle.gemv(fmt, xq, xs, w, ws, n, k)
+    ctx.set_path(mx.PATH_GEMV)
+    try:
+        y = host(mx.mx_gemv(mx.MXActivation(cuda(xq), cuda(xs)), W, ctx))
+        ctx.synchronize()
+    finally:
+        ctx.set_path(mx.PATH_AUTO)
+    assert rel_l2(y, ref) <= REL_TOL
+
+
+# ---------------------------------------------------- tensor-core GEMM ---
+@pytest.mark.parametrize("fmt", [8, 4])
+@pytest.mark.parametrize("b", [1, 9, 16, 40, 64, 100, 256, 300])
+@pytest.mark.parametrize("n,k", [(33, 96), (384, 4096), (256, 11008)])
+def test_gemm_parity(ctx, fmt, b, n, k):
+    w, ws, W = weight(ctx, fmt, n, k, 50 + n + k)
+    x = edge_inputs(b, k, 51 + b)
+    xq, xs = oracle.quantize_x(x)
+    ref = oracle.gemv(fmt, xq, xs, w, ws, n, k)
+    ctx.set_path(mx.PATH_GEMM)
+    try:
+        y = host(mx.mx_gemv(mx.MXActivation(cuda(xq), cuda(xs)), W, ctx))
+        ctx.synchronize()
+        y2 = host(mx.mx_linear(cuda(x), W, ctx))
+        ctx.synchronize()
+    finally:
+        ctx.set_path(mx.PATH_AUTO)
+    assert rel_l2(y, ref) <= REL_TOL
+    assert np.array_equal(y, y2)
+
+
+def test_golden_fixture_on_gpu(ctx):
+    import os
+    d = np.load(os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden", "mx_oracle.npz"))
+    names = sorted({k.rsplit("_", 1)[0] for k in d.files if k.endswith("_shape")})
+    for nm in names:
+        fmt, b, n, k = (int(v) for v in d[nm + "_shape"])
+        W = mx.MXWeight(torch.from_numpy(d[nm + "_w"]), torch.from_numpy(d[nm + "_ws"]), fmt, n, k, ctx)
+        a = mx.mx_quantize_x(cuda(d[nm + "_x"]), ctx)
+        assert np.array_equal(host(a.q), d[nm + "_xq"]) and np.array_equal(host(a.s), d[nm + "_xs"])
+        assert np.array_equal(host(mx.mx_block_dots(a, W, ctx)), d[nm + "_dots"])
+        for path in (mx.PATH_GEMV, mx.PATH_GEMM):
+            if path == mx.PATH_GEMV and b > 8:
+                continue
+            ctx.set_path(path)
+            try:
+                y = host(mx.mx_gemv(a, W, ctx))
+            finally:
+                ctx.set_path(mx.PATH_AUTO)
+            assert rel_l2(y, d[nm + "_y"]) <= REL_TOL, (nm, path)
+
+
+# -------------------------------------------------- full-size workloads ---
+def test_single_int8_linear_4096(ctx):
+    """4096x4096 MX-int8 GEMV, exponents [-10,-4], x ~ N(0,1), batch 1,
+    seed 0 (the reference's CPU-runnable linear)."""
+    w, ws, W = weight(ctx, 8, 4096, 4096, 0, -10, -4)
+    x = synth.normal((1, 4096), 0)
+    xq, xs = oracle.quantize_x(x)
+    ref = oracle.gemv(8, xq, xs, w, ws, 4096, 4096)
+    y = host(mx.mx_linear(cuda(x), W, ctx))
+    ctx.synchronize()
+    assert rel_l2(y, ref) <= REL_TOL
+
+
+@pytest.mark.parametrize("b", [1, 8, 64, 512])
+def test_int4_mlp_pair_7b_shape(ctx, b):
+    """MX-int4 up 4096->11008 then down 11008->4096 at batch 1/8/64/512.
+    Stage-wise: up vs oracle (rows sampled at b=512), the requantised
+    intermediate bit-exact against the oracle's quantiser applied to the GPU's
+    own up output, down vs oracle on that intermediate."""
+    wu, su, Wu = weight(ctx, 4, 11008, 4096, 1, -8, -3)
+    wd, sd, Wd = weight(ctx, 4, 4096, 11008, 2, -8, -3)
+    x = synth.normal((b, 4096), 3 + b)
+    xq, xs = oracle.quantize_x(x)
+    y1 = host(mx.mx_linear(cuda(x), Wu, ctx))
+    ctx.synchronize()
+    rows = np.arange(11008) if b <= 64 else np.random.default_rng(5).choice(11008, 96, replace=False).astype(np.int32)
+    ref1 = oracle.gather_dot(4, xq, xs, wu, su, 4096, rows)
+    assert rel_l2(y1[:, rows], ref1) <= REL_TOL
+    hq, hs = oracle.quantize_x(y1)
+    y2 = host(mx.mx_linear(cuda(y1), Wd, ctx))
+    ctx.synchronize()
+    rows2 = np.arange(4096) if b <= 64 else np.random.default_rng(6).choice(4096, 96, replace=False).astype(np.int32)
+    ref2 = oracle.gather_dot(4, hq, hs, wd, sd, 11008, rows2)
+    assert rel_l2(y2[:, rows2], ref2) <= REL_TOL
+    yp = host(mx.mx_linear_pair(cuda(x), Wu, Wd, ctx))
+    ctx.synchronize()
+    assert np.array_equal(yp, y2)
+
+
+# ---------------------------------------------------- gather / MLP ---
+@pytest.mark.parametrize("fmt", [8, 4])
+def test_rank16_dot_ptrs(ctx, fmt):
+    n, k = 1024, 2048
+    w, ws, W = weight(ctx, fmt, n, k, 60)
+    x = synth.normal((2, k), 61)
+    xq, xs = oracle.quantize_x(x)
+    rows = np.array([5, 1023, 0, 77, 77, 512, 3, 900, 1, 2, 4, 6, 8, 10, 12, 14], np.int32)
+    ref = oracle.gather_dot(fmt, xq, xs, w, ws, k, rows)
+    y = host(mx.mx_rank16_dot_ptrs(mx.MXActivation(cuda(xq), cuda(xs)), W, cuda(rows), ctx))
+    assert rel_l2(y, ref) <= REL_TOL
+
+
+@pytest.mark.parametrize("b", [1, 3, 24])
+def test_gated_mlp_step(ctx, b):
+    d, f = 256, 704
+    wg, sg, Wg = weight(ctx, 4, f, d, 70)
+    wu, su, Wu = weight(ctx, 4, f, d, 71)
+    wd, sd, Wd = weight(ctx, 4, d, f, 72)
+    x = synth.normal((b, d), 73)
+    y = host(mx.gated_mlp_step(cuda(x), Wg, Wu, Wd, ctx))
+    ctx.synchronize()
+    ref, _, _ = oracle.mlp_swiglu(4, x, d, f, wg, sg, wu, su, wd, sd)
+    assert rel_l2(y, ref) <= 1e-4   # one rounding of the intermediate may flip
+
+
+def test_fixed_size_checks(ctx):
+    """Shapes the API must reject (the reference throws invalid_argument)."""
+    w, ws, W = weight(ctx, 8, 64, 64, 80)
+    with pytest.raises(ValueError):
+        mx.mx_linear(cuda(synth.normal((1, 96), 1)), W, ctx)
+    with pytest.raises(ValueError):
+        mx.MXWeight(torch.from_numpy(np.zeros((4, 48), np.int8)), torch.from_numpy(np.zeros((4, 1), np.uint8)),
+                    8, 4, 48, ctx)
+    with pytest.raises(ValueError):
+        mx.mx_dot(mx.mx_quantize_x(cuda(synth.normal((1, 64), 2)), ctx), W, ctx)
+
+
+# ------------------------------------------------------ routing / GAE ---
+def test_route_topk_bit_exact(ctx):
+    logits = synth.normal((4096, 8), 90)
+    logits[7, 3] = logits[7, 5] = 9.0        # tie
+    idx, gate = oracle.route_topk(logits, 2)
+    gi, gg = mx.route_topk(cuda(logits), 2, ctx)
+    assert np.array_equal(host(gi), idx) and np.array_equal(host(gg), gate)
+    with pytest.raises(ValueError):
+        mx.HashedRouter(1024, 10, 20)
+    with pytest.raises(ValueError):
+        mx.route_topk(cuda(logits), 9, ctx)
+
+
+def test_gae_bit_exact(ctx):
+    import os
+    d = np.load(os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden", "gae_reference.npz"))
+    for case in ("kat", "rand"):
+        a, r = mx.fused_compute_gae(cuda(d[case + "_r"]), cuda(d[case + "_v"]), cuda(d[case + "_d"]),
+                                    cuda(d[case + "_nv"]), 0.99, 0.95, ctx)
+        assert np.array_equal(host(a), d[case + "_adv"])
+        assert np.array_equal(host(r), d[case + "_ret"])
+    T, E = 512, 256
+    g = synth.rng(91)
+    rr = np.zeros((T, E), np.float32)
+    done = np.zeros((T, E), np.uint8)
+    done[-1] = 1
+    rr[-1] = g.standard_normal(E, dtype=np.float32)
+    v = g.standard_normal((T, E), dtype=np.float32)
+    nv = np.zeros(E, np.float32)
+    a0, r0 = oracle.gae(rr, v, done, nv, 0.99, 0.95)
+    a1, r1 = mx.fused_compute_gae(cuda(rr), cuda(v), cuda(done), cuda(nv), 0.99, 0.95, ctx)
+    assert np.array_equal(host(a1), a0) and np.array_equal(host(r1), r0)

@@ -1,0 +1,247 @@
+"""CPU tests of the oracle (the checker) -- pins it before it judges the GPU.
+
+- GAE: against the reference's own compiled fused_compute_gae
+  (oracle/_ref, and the committed fixture it produced) and the known answers
+  of agentic_env/test_memory.cpp:47-83.
+- MX: the reference's MX kernels are absent (parity unpinned), so the
+  restatement is checked against hand-computed cases, an independent numpy
+  implementation, the dpbusd / w_sums identity of the removed VNNI kernel,
+  and the committed self-fixtures.
+"""
+import math
+import os
+import struct
+
+import numpy as np
+import pytest
+
+from oracle import oracle
+from cpu_model_b200 import synth
+
+GOLD = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
+
+
+# ----------------------------------------------------------------- E8M0 ---
+@pytest.mark.parametrize("m,qmax,byte", [
+    (0.0, 127, 0),
+    (127.0, 127, 127),
+    (127.00001, 127, 128),
+    (1.0, 127, 121),          # 1 <= 127 * 2^-6, 1 > 127 * 2^-7
+    (63.5, 127, 126),         # exactly 127 * 2^-1
+    (7.0, 7, 127),
+    (8.0, 7, 128),
+    (1e-45, 127, 0),          # denormal -> clamp to 2^-127
+    (3.4e38, 127, 122 + 127),
+    (float("inf"), 127, 255),
+    (float("nan"), 127, 255),
+])
+def test_e8m0_known_answers(m, qmax, byte):
+    assert oracle.e8m0_from_absmax(m, qmax) == byte
+
+
+def _bits_exponent(m, qmax):
+    """The GPU kernels' bit formula (mxq_common.cuh: e8m0_exponent)."""
+    bits = struct.unpack("<I", struct.pack("<f", m))[0]
+    kexp = (bits >> 23) & 0xFF
+    if kexp == 0:
+        return -127
+    k = kexp - 127
+    frac = bits & 0x7FFFFF
+    if qmax == 127:
+        e = k - 6 + (1 if frac > 0x7E0000 else 0)
+    else:
+        e = k - 2 + (1 if frac > 0x600000 else 0)
+    return max(e, -127)
+
+
+@pytest.mark.parametrize("qmax", [127, 7])
+def test_e8m0_bit_formula_matches_oracle(qmax):
+    g = synth.rng(11)
+    vals = np.concatenate([
+        np.exp(g.uniform(-90, 88, 4000)).astype(np.float32),
+        (np.float32(qmax) * np.exp2(np.arange(-120, 120)).astype(np.float32)),   # exact thresholds
+        np.nextafter(np.float32(qmax) * np.exp2(np.arange(-120, 120)).astype(np.float32), np.float32(np.inf)),
+    ])
+    for m in vals:
+        m = float(np.float32(m))
+        if m == 0.0 or not math.isfinite(m):
+            continue
+        assert oracle.e8m0_from_absmax(m, qmax) - 127 == _bits_exponent(m, qmax), m
+
+
+def test_e8m0_decode():
+    assert oracle.e8m0_decode(127) == 1.0
+    assert oracle.e8m0_decode(0) == 2.0 ** -127
+    assert oracle.e8m0_decode(254) == 2.0 ** 127
+    assert math.isnan(oracle.e8m0_decode(255))
+
+
+# ------------------------------------------------------------ quantiser ---
+def test_quantize_hand_block():
+    x = np.zeros((1, 32), np.float32)
+    x[0, :6] = [1.0, -0.5, 0.25, 0.0234375, -1.0, 0.0078125]
+    q, s = oracle.quantize_x(x)
+    # max 1.0 -> e = -6 -> x * 64
+    assert s[0, 0] == 121
+    assert list(q[0, :6].astype(int) - 128) == [64, -32, 16, 2, -64, 0]   # 1.5 -> 2, 0.5 -> 0 (half-even)
+    assert np.all(q[0, 6:] == 128)
+
+
+def test_quantize_ties_round_half_even():
+    x = np.zeros((1, 32), np.float32)
+    x[0, 0] = 127.0                       # e = 0 -> identity scale
+    x[0, 1:6] = [0.5, 1.5, 2.5, -0.5, -2.5]
+    q, s = oracle.quantize_x(x)
+    assert s[0, 0] == 127
+    assert list(q[0, 1:6].astype(int) - 128) == [0, 2, 2, 0, -2]
+
+
+def test_quantize_zero_and_nonfinite_blocks():
+    x = np.ones((1, 96), np.float32)
+    x[0, :32] = 0.0
+    x[0, 40] = np.inf
+    q, s = oracle.quantize_x(x)
+    assert s[0, 0] == 0 and np.all(q[0, :32] == 128)
+    assert s[0, 1] == 255 and np.all(q[0, 32:64] == 128)
+    assert s[0, 2] == 121
+
+
+def test_quantize_range_and_reconstruction():
+    x = synth.normal((8, 4096), 3)
+    q, s = oracle.quantize_x(x)
+    v = q.astype(np.int32) - 128
+    assert v.min() >= -127 and v.max() <= 127
+    scale = np.exp2(s.astype(np.float64) - 127).repeat(32, axis=1)
+    err = np.abs(v * scale - x)
+    assert np.all(err <= 0.5 * scale + 1e-30)
+
+
+def test_exp_and_silu_accuracy():
+    xs = np.linspace(-100, 88, 20001).astype(np.float32)
+    ours = np.array([oracle.expf(float(v)) for v in xs], np.float64)
+    ref = np.exp(xs.astype(np.float64))
+    rel = np.abs(ours - ref) / np.maximum(ref, 1e-300)
+    assert np.max(rel[ref > 1e-37]) < 4e-7
+    for v in [-30.0, -1.0, 0.0, 0.5, 3.0, 20.0]:
+        want = v / (1 + math.exp(-v))
+        assert abs(oracle.silu(v) - want) <= 3e-7 * max(1.0, abs(want))
+
+
+# ----------------------------------------------------------- dots/GEMV ---
+def _numpy_gemv(fmt, xq, xs, w, ws, n, k):
+    wv = synth.unpack_int4(w) if fmt == 4 else w.astype(np.int8)
+    xv = xq.astype(np.int64) - 128
+    b = xq.shape[0]
+    nb = k // 32
+    dots = np.einsum("bkj,nkj->bnk", xv.reshape(b, nb, 32), wv.astype(np.int64).reshape(n, nb, 32))
+    sc = (xs.astype(np.int64)[:, None, :] + ws.astype(np.int64)[None, :, :] - 254)
+    y = np.sum(np.ldexp(dots.astype(np.float64), sc), axis=2).astype(np.float32)
+    return dots, y
+
+
+@pytest.mark.parametrize("fmt", [8, 4])
+def test_gemv_matches_numpy(fmt):
+    n, k, b = 48, 256, 3
+    w, ws = synth.weights(fmt, n, k, -10, -4, 5)
+    xq, xs = oracle.quantize_x(synth.normal((b, k), 6))
+    dots, y = _numpy_gemv(fmt, xq, xs, w, ws, n, k)
+    assert np.array_equal(oracle.block_dots(fmt, xq, w, n, k), dots)
+    assert np.array_equal(oracle.gemv(fmt, xq, xs, w, ws, n, k), y)
+
+
+@pytest.mark.parametrize("fmt", [8, 4])
+def test_vnni_identity_and_baseline(fmt):
+    """dpbusd(u8 = q+128, s8 w) - 128 * w_sum == sum q*w: the CPU baseline
+    (multi-threaded restatement of the removed VNNI kernel) agrees with the
+    oracle to fp32 summation error."""
+    n, k, b = 64, 512, 2
+    w, ws = synth.weights(fmt, n, k, -10, -4, 8)
+    xq, xs = oracle.quantize_x(synth.normal((b, k), 9))
+    sums = oracle.weight_sums(fmt, w, n, k)
+    wv = synth.unpack_int4(w) if fmt == 4 else w
+    assert np.array_equal(sums, wv.astype(np.int32).reshape(n, k // 32, 32).sum(-1))
+    y, _ = oracle.baseline_gemv(fmt, xq, xs, w, ws, sums, n, k)
+    ref = oracle.gemv(fmt, xq, xs, w, ws, n, k)
+    assert np.linalg.norm(y - ref) / np.linalg.norm(ref) < 1e-6
+
+
+def test_quantize_w_roundtrip():
+    g = synth.rng(4)
+    wf = g.standard_normal((16, 128)).astype(np.float32)
+    for fmt, qmax in ((8, 127), (4, 7)):
+        data, scales, sums = oracle.quantize_w(fmt, wf)
+        wv = synth.unpack_int4(data) if fmt == 4 else data
+        assert np.abs(wv).max() <= qmax
+        rec = wv.astype(np.float64) * np.exp2(scales.astype(np.float64) - 127).repeat(32, axis=1)
+        assert np.all(np.abs(rec - wf) <= 0.5 * np.exp2(scales.astype(np.float64) - 127).repeat(32, axis=1) + 1e-12)
+        assert np.array_equal(sums, wv.astype(np.int32).reshape(16, 4, 32).sum(-1))
+
+
+def test_reference_ami_fixture_shape():
+    """The reference AMI harness's MX fixture (nn/tests/autotest.hpp:93-116):
+    weights memset to seed%127 (seed 42), scale bytes 1, activations 128.
+    Activations 128 encode q = 0, so every block dot is 0 and mx_gemv is 0."""
+    D = 1024
+    w = np.full((D, D), 42, np.int8)
+    ws = np.ones((D, D // 32), np.uint8)
+    xq = np.full((1, D), 128, np.uint8)
+    xs = np.ones((1, D // 32), np.uint8)
+    assert np.all(oracle.block_dots(8, xq, w, D, D) == 0)
+    assert np.all(oracle.gemv(8, xq, xs, w, ws, D, D) == 0.0)
+
+
+def test_golden_mx_self_fixture():
+    d = np.load(os.path.join(GOLD, "mx_oracle.npz"))
+    names = sorted({k.rsplit("_", 1)[0] for k in d.files if k.endswith("_shape")})
+    assert names
+    for nm in names:
+        fmt, b, n, k = (int(v) for v in d[nm + "_shape"])
+        xq, xs = oracle.quantize_x(d[nm + "_x"])
+        assert np.array_equal(xq, d[nm + "_xq"]) and np.array_equal(xs, d[nm + "_xs"])
+        assert np.array_equal(oracle.block_dots(fmt, xq, d[nm + "_w"], n, k), d[nm + "_dots"])
+        assert np.array_equal(oracle.gemv(fmt, xq, xs, d[nm + "_w"], d[nm + "_ws"], n, k), d[nm + "_y"])
+
+
+# -------------------------------------------------------------- routing ---
+def test_route_topk_contract():
+    logits = np.array([[0.1, 2.0, 2.0, -1.0], [3.0, 1.0, 2.0, 0.0]], np.float32)
+    idx, gate = oracle.route_topk(logits, 2)
+    assert idx.tolist() == [[1, 2], [0, 2]]            # tie -> lower id first
+    assert abs(gate[0, 0] - 0.5) < 1e-7
+    assert np.allclose(gate.sum(1), 1.0, atol=1e-6)
+    with pytest.raises(ValueError):                     # HashedRouter K > N
+        oracle.route_topk(logits, 5)
+    with pytest.raises(ValueError):
+        oracle.route_topk(logits, 0)
+
+
+# ------------------------------------------------------------------ GAE ---
+def test_gae_known_answers():
+    """agentic_env/test_memory.cpp:47-83."""
+    d = np.load(os.path.join(GOLD, "gae_reference.npz"))
+    adv, ret = oracle.gae(d["kat_r"], d["kat_v"], d["kat_d"], d["kat_nv"], 0.99, 0.95)
+    flat = adv.ravel()
+    assert abs(flat[5] - 4.83) < 0.01
+    assert abs(flat[3] - 8.36) < 0.01
+    assert abs(flat[1] - 10.67) < 0.01
+
+
+@pytest.mark.parametrize("case", ["kat", "rand"])
+def test_gae_matches_reference_fixture(case):
+    d = np.load(os.path.join(GOLD, "gae_reference.npz"))
+    adv, ret = oracle.gae(d[case + "_r"], d[case + "_v"], d[case + "_d"], d[case + "_nv"], 0.99, 0.95)
+    assert np.array_equal(adv, d[case + "_adv"])
+    assert np.array_equal(ret, d[case + "_ret"])
+
+
+@pytest.mark.skipif(not oracle.ref_gae_available(), reason="reference GAE not built here")
+def test_gae_matches_reference_build_live():
+    g = synth.rng(99)
+    T, E = 37, 19
+    r = g.standard_normal((T, E), dtype=np.float32)
+    v = g.standard_normal((T, E), dtype=np.float32)
+    dn = (g.random((T, E)) < 0.1).astype(np.uint8)
+    nv = g.standard_normal(E, dtype=np.float32)
+    a0, r0 = oracle.gae(r, v, dn, nv, 0.97, 0.9)
+    a1, r1 = oracle.ref_gae(r, v, dn, nv, 0.97, 0.9)
+    assert np.array_equal(a0, a1) and np.array_equal(r0, r1)
