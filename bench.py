@@ -182,10 +182,10 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
-def workload_config(batch):
+def workload_config(batch, copies=COPIES):
     return {"workload": "mx_int4_mlp_pair_7b", "up": "4096->11008", "down": "11008->4096",
             "batch": batch, "weights": "int4 [-8,7], E8M0 exp [-8,-3]", "activations": "fp32 N(0,1) -> MX-int8",
-            "l2": "rotating %d weight copies (%.0f MB) > 126 MB L2" % (COPIES, COPIES * pair_bytes(0) / 1e6),
+            "l2": "rotating %d weight copies (%.0f MB) vs 126 MB L2" % (copies, copies * pair_bytes(0) / 1e6),
             "parallelism": "replicas"}
 
 
@@ -207,7 +207,7 @@ def run_ours(args):
 
     # weights: COPIES distinct pairs (seeded per copy), uploaded once
     pairs = []
-    for c in range(COPIES):
+    for c in range(args.copies):
         wu, su = synth.weights(4, UP[0], UP[1], EMIN, EMAX, 1000 + 2 * c)
         wd, sd = synth.weights(4, DOWN[0], DOWN[1], EMIN, EMAX, 1001 + 2 * c)
         pairs.append((mx.MXWeight(torch.from_numpy(wu), torch.from_numpy(su), 4, UP[0], UP[1], ctx),
@@ -227,51 +227,81 @@ def run_ours(args):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return float(t.item())
 
+    def capture(fn):
+        """Record fn() (a sequence of library calls on the current stream) into
+        a CUDA graph; the library's launches become graph nodes, with their
+        programmatic (PDL) dependencies kept as graph edges."""
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            ctx._bind()
+            fn()
+        ctx._bind()
+        return g
+
     def time_pairs(batch, steps, warmup):
+        """K pair steps, rotating the weight copies, replayed as one CUDA graph
+        (a decode loop launches its step graph once per token); timed with
+        CUDA events around the replay."""
         x = torch.from_numpy(synth.normal((batch, UP[1]), 7 + rank)).to(dev)
         y = torch.empty((batch, DOWN[0]), dtype=torch.float32, device=dev)
         ctx._bind()
         lib = ctx.lib
-        for i in range(warmup):
-            wu, wd = pairs[i % COPIES]
+
+        def step(i):
+            wu, wd = pairs[i % len(pairs)]
             mx.check(lib.mxq_linear_pair(ctx.h, wu.h, wd.h, mx._ptr(x), batch, mx._ptr(y)), ctx.h)
+
+        for i in range(warmup):
+            step(i)
         ctx.synchronize()
+        l0 = ctx.launch_count()
+        g = capture(lambda: [step(i) for i in range(steps)])
+        launches = ctx.launch_count() - l0
+        g.replay()                      # untimed graph warm-up
+        torch.cuda.synchronize()
         barrier()
         torch.cuda.synchronize()
-        l0 = ctx.launch_count()
         e0 = torch.cuda.Event(enable_timing=True)
         e1 = torch.cuda.Event(enable_timing=True)
         e0.record(stream)
-        for i in range(steps):
-            wu, wd = pairs[(warmup + i) % COPIES]
-            mx.check(lib.mxq_linear_pair(ctx.h, wu.h, wd.h, mx._ptr(x), batch, mx._ptr(y)), ctx.h)
+        g.replay()
         e1.record(stream)
         torch.cuda.synchronize()
         barrier()
         ms = max_over_ranks(e0.elapsed_time(e1))
         ctx.synchronize()
-        return ms / steps, ctx.launch_count() - l0
+        del g
+        return ms / steps, launches
 
     def time_gemv(batch, steps):
         """The dominant kernel alone: the up-projection linear kernel (GEMV or
         tensor-core GEMM by batch) on pre-quantised activations, rotating
-        weight copies; CUDA events on the launching stream."""
+        weight copies, as one CUDA graph; CUDA events on the launching
+        stream."""
         x = torch.from_numpy(synth.normal((batch, UP[1]), 9)).to(dev)
         a = mx.mx_quantize_x(x, ctx)
         y = torch.empty((batch, UP[0]), dtype=torch.float32, device=dev)
         lib = ctx.lib
         ctx._bind()
+
+        def one(i):
+            mx.check(lib.mxq_gemv(ctx.h, pairs[i % len(pairs)][0].h, mx._ptr(a.q), mx._ptr(a.s), batch,
+                                  mx._ptr(y)), ctx.h)
+
         for i in range(3):
-            mx.check(lib.mxq_gemv(ctx.h, pairs[i % COPIES][0].h, mx._ptr(a.q), mx._ptr(a.s), batch, mx._ptr(y)), ctx.h)
+            one(i)
+        ctx.synchronize()
+        g = capture(lambda: [one(i) for i in range(steps)])
+        g.replay()
         torch.cuda.synchronize()
         e0 = torch.cuda.Event(enable_timing=True)
         e1 = torch.cuda.Event(enable_timing=True)
         e0.record(stream)
-        for i in range(steps):
-            mx.check(lib.mxq_gemv(ctx.h, pairs[i % COPIES][0].h, mx._ptr(a.q), mx._ptr(a.s), batch, mx._ptr(y)), ctx.h)
+        g.replay()
         e1.record(stream)
         torch.cuda.synchronize()
         ctx.synchronize()
+        del g
         return e0.elapsed_time(e1) / steps
 
     def time_e2e(batch, steps):
@@ -282,14 +312,14 @@ def run_ours(args):
         lib = ctx.lib
         ctx._bind()
         for i in range(3):
-            wu, wd = pairs[i % COPIES]
+            wu, wd = pairs[i % len(pairs)]
             mx.check(lib.mxq_linear_pair_host(ctx.h, wu.h, wd.h, mx._ptr(xh), batch, mx._ptr(yh)), ctx.h)
         barrier()
         e0 = torch.cuda.Event(enable_timing=True)
         e1 = torch.cuda.Event(enable_timing=True)
         e0.record(stream)
         for i in range(steps):
-            wu, wd = pairs[i % COPIES]
+            wu, wd = pairs[i % len(pairs)]
             mx.check(lib.mxq_linear_pair_host(ctx.h, wu.h, wd.h, mx._ptr(xh), batch, mx._ptr(yh)), ctx.h)
         e1.record(stream)
         torch.cuda.synchronize()
@@ -325,7 +355,7 @@ def run_ours(args):
             "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "mx-int4 (int4 w, int8 a, int32 dot, fp32 sum)",
-            "data": "synthetic", "config": workload_config(b),
+            "data": "synthetic", "config": workload_config(b, args.copies),
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
                          "frac": achieved / peaks["hbm_gbs"], "traffic": None,
                          "kernel": "gemv_kernel<int4> (up 4096->11008)",
@@ -361,6 +391,8 @@ def main():
     ap.add_argument("--no-sweep", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--copies", type=int, default=COPIES,
+                    help="distinct weight-pair copies rotated per step (default 8 = 383 MB)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

@@ -18,6 +18,7 @@ struct mxq_context {
   cudaStream_t stream = nullptr;
   int path = MXQ_PATH_AUTO;
   uint32_t* status = nullptr;  // device status word
+  uint32_t* status_host = nullptr;  // pinned mirror, read after one stream sync
   uint64_t launches = 0;
   std::string err;
   // workspace (device)
@@ -108,6 +109,24 @@ __global__ void repack_kernel(const uint8_t* __restrict__ data,
   }
 }
 
+// Range of the weight scale bytes (selects the GEMV's fast scale path).
+__global__ void scale_range_kernel(const uint8_t* __restrict__ s, size_t n, uint32_t* out) {
+  uint32_t lo = 255, hi = 0;
+  for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
+    const uint32_t v = s[i];
+    lo = min(lo, v);
+    hi = max(hi, v);
+  }
+  for (int o = 16; o > 0; o >>= 1) {
+    lo = min(lo, __shfl_xor_sync(0xffffffffu, lo, o));
+    hi = max(hi, __shfl_xor_sync(0xffffffffu, hi, o));
+  }
+  if ((threadIdx.x & 31) == 0) {
+    atomicMin(&out[0], lo);
+    atomicMax(&out[1], hi);
+  }
+}
+
 // ------------------------------------------------------------ routing ---
 __global__ void route_topk_kernel(const float* __restrict__ logits, int T, int E,
                                   int k, int32_t* __restrict__ idx,
@@ -173,13 +192,32 @@ int check_weight(mxq_context* c, mxq_weight w) {
 int use_gemv(mxq_context* c, size_t b) {
   if (c->path == MXQ_PATH_GEMV) return 1;
   if (c->path == MXQ_PATH_GEMM) return 0;
-  return b <= (size_t)gemv_max_batch();
+  return b <= (size_t)kGemvAutoBatch;
 }
 
 int after_launch(mxq_context* c, cudaError_t e, const char* what) {
   if (e != cudaSuccess) return cuda_fail(c, e, what);
   c->launches++;
   return MXQ_OK;
+}
+
+// Decode GEMV straight from fp32 rows (quantised inside the kernel).  `next`
+// (optional) is the weight the following call will read: its bytes are
+// prefetched into L2 while this GEMV streams, so the next layer starts warm.
+int gemv_f32(mxq_context* c, mxq_weight w, const float* x, size_t b, float* y, mxq_weight next) {
+  GemvArgs ga{};
+  ga.w = w->v;
+  ga.xf = x;
+  ga.y = y;
+  ga.B = (int)b;
+  if (next) {
+    ga.pf_ptr = next->data;
+    ga.pf_bytes = (size_t)next->v.Npad * next->v.Kpad / (next->v.fmt == 4 ? 2 : 1);
+    ga.pf_ptr2 = next->scales;
+    ga.pf_bytes2 = (size_t)next->v.Npad * next->v.Kpad / kBlock;
+  }
+  if (rgemv_supported(w->v, (int)b)) return after_launch(c, launch_rgemv(ga, c->stream, true), "gemv");
+  return after_launch(c, launch_gemv(ga, c->stream, true), "gemv");
 }
 
 // fp32 x [B][K] (device) -> y [B][N] through quantise + GEMV or GEMM.
@@ -190,6 +228,7 @@ int linear_dev(mxq_context* c, mxq_weight w, const float* x, size_t b, float* y,
   if (use_gemv(c, b)) {
     if (b > (size_t)gemv_max_batch())
       return fail(c, MXQ_ERR_INVALID_ARGUMENT, "GEMV path supports batch <= %d", gemv_max_batch());
+    if (act == MXQ_ACT_NONE) return gemv_f32(c, w, x, b, y, nullptr);
     if ((rc = ensure(c, c->ws_q, c->ws_q_bytes, b * K, "workspace q"))) return rc;
     if ((rc = ensure(c, c->ws_s, c->ws_s_bytes, b * K / kBlock, "workspace s"))) return rc;
     QuantArgs qa{};
@@ -245,6 +284,7 @@ int gemv_dev(mxq_context* c, mxq_weight w, const uint8_t* xq, const uint8_t* xs,
     ga.xs = xs;
     ga.y = y;
     ga.B = (int)b;
+    if (rgemv_supported(w->v, (int)b)) return after_launch(c, launch_rgemv(ga, c->stream, true), "gemv");
     return after_launch(c, launch_gemv(ga, c->stream, true), "gemv");
   }
   const int BN = gemm_pick_bn((int)b);
@@ -312,6 +352,7 @@ int mxq_create(int device, mxq_ctx* out) {
     c->device = device;
     e = cudaMalloc(&c->status, sizeof(uint32_t));
     if (e == cudaSuccess) e = cudaMemset(c->status, 0, sizeof(uint32_t));
+    if (e == cudaSuccess) e = cudaHostAlloc(&c->status_host, sizeof(uint32_t), cudaHostAllocDefault);
     if (e != cudaSuccess) {
       delete c;
       return cuda_fail(nullptr, e, "status word");
@@ -327,6 +368,7 @@ int mxq_destroy(mxq_ctx c) {
     DeviceGuard g(c->device);
     cudaStreamSynchronize(c->stream);
     cudaFree(c->status);
+    cudaFreeHost(c->status_host);
     cudaFree(c->ws_q);
     cudaFree(c->ws_s);
     cudaFree(c->ws_op);
@@ -383,11 +425,12 @@ int mxq_reserve(mxq_ctx c, size_t max_batch, size_t max_k) {
 int mxq_synchronize(mxq_ctx c) {
   if (int rc = check_ctx(c)) return rc;
   DeviceGuard g(c->device);
-  cudaError_t e = cudaStreamSynchronize(c->stream);
+  // one round trip: the status word rides the stream into pinned memory
+  cudaError_t e = cudaMemcpyAsync(c->status_host, c->status, sizeof(uint32_t),
+                                  cudaMemcpyDeviceToHost, c->stream);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(c->stream);
   if (e != cudaSuccess) return cuda_fail(c, e, "synchronize");
-  uint32_t st = 0;
-  e = cudaMemcpy(&st, c->status, sizeof(st), cudaMemcpyDeviceToHost);
-  if (e != cudaSuccess) return cuda_fail(c, e, "status read");
+  const uint32_t st = *c->status_host;
   if (st) {
     cudaMemset(c->status, 0, sizeof(uint32_t));
     return fail(c, MXQ_ERR_TIMEOUT, "a device-side bounded wait gave up (status 0x%x)", st);
@@ -430,7 +473,14 @@ int mxq_weight_create(mxq_ctx c, int fmt, size_t n, size_t k, const void* data,
       src_s = tmp + src_bytes;
     }
     if (e == cudaSuccess) e = launch_repack(src_d, src_s, fmt, N, K, Npad, Kpad, w->data, w->scales, c->stream);
+    uint32_t range[2] = {255, 0};
+    uint32_t* drange = nullptr;
+    if (e == cudaSuccess) e = cudaMalloc(&drange, sizeof(range));
+    if (e == cudaSuccess) e = cudaMemcpyAsync(drange, range, sizeof(range), cudaMemcpyHostToDevice, c->stream);
+    if (e == cudaSuccess) e = launch_scale_range(src_s, sc_bytes, drange, c->stream);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(range, drange, sizeof(range), cudaMemcpyDeviceToHost, c->stream);
     if (e == cudaSuccess) e = cudaStreamSynchronize(c->stream);
+    if (drange) cudaFree(drange);
     if (tmp) cudaFree(tmp);
     if (e != cudaSuccess) {
       cudaFree(w->data);
@@ -445,6 +495,8 @@ int mxq_weight_create(mxq_ctx c, int fmt, size_t n, size_t k, const void* data,
     w->v.Kpad = Kpad;
     w->v.data = w->data;
     w->v.scales = w->scales;
+    w->v.scale_lo = (int)range[0];
+    w->v.scale_hi = (int)range[1];
     *out = w;
     return MXQ_OK;
   })
@@ -571,6 +623,12 @@ int mxq_linear_pair(mxq_ctx c, mxq_weight w1, mxq_weight w2, const float* x,
     DeviceGuard g(c->device);
     int rc;
     if ((rc = ensure(c, c->ws_f0, c->ws_f0_bytes, b * w1->v.N * 4, "workspace mid"))) return rc;
+    if (use_gemv(c, b)) {
+      // decode: two launches; each GEMV quantises its fp32 input itself and
+      // the first warms L2 with the second's weights while it streams
+      if ((rc = gemv_f32(c, w1, x, b, c->ws_f0, w2))) return rc;
+      return gemv_f32(c, w2, c->ws_f0, b, y, nullptr);
+    }
     if ((rc = linear_dev(c, w1, x, b, c->ws_f0, MXQ_ACT_NONE))) return rc;
     return linear_dev(c, w2, c->ws_f0, b, y, MXQ_ACT_NONE);
   })
@@ -693,6 +751,14 @@ int mxq_gae(mxq_ctx c, const float* rewards, const float* values, const uint8_t*
 }  // extern "C"
 
 namespace mxq {
+cudaError_t launch_scale_range(const uint8_t* scales, size_t count, uint32_t* out2, cudaStream_t st) {
+  size_t ctas = (count + 255) / 256;
+  if (ctas > 1024) ctas = 1024;
+  if (ctas < 1) ctas = 1;
+  scale_range_kernel<<<(unsigned)ctas, 256, 0, st>>>(scales, count, out2);
+  return cudaGetLastError();
+}
+
 cudaError_t launch_repack(const uint8_t* data, const uint8_t* scales, int fmt, int N, int K,
                           int Npad, int Kpad, uint8_t* od, uint8_t* os, cudaStream_t st) {
   const long total = (long)Npad * (Kpad / kTileK);

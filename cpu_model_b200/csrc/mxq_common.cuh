@@ -176,6 +176,23 @@ __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
+// One CTA's slice of an L2 prefetch (bulk prefetch wants 16-byte multiples).
+__device__ __forceinline__ void prefetch_l2_share(const void* p, size_t bytes, int cta, int ctas) {
+  if (!p || !bytes) return;
+  const size_t chunk = ((bytes + ctas - 1) / ctas + 15) / 16 * 16;
+  const size_t lo = (size_t)cta * chunk;
+  if (lo >= bytes) return;
+  size_t n = bytes - lo < chunk ? bytes - lo : chunk;
+  const uint8_t* q = static_cast<const uint8_t*>(p) + lo;
+  while (n) {
+    const uint32_t piece = (uint32_t)(n > 65536 ? 65536 : n);
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(q), "r"(piece) : "memory");
+    q += piece;
+    n -= piece;
+  }
+}
+
+
 // ------------------------------------------------------------- tcgen05 --
 __device__ __forceinline__ void tmem_alloc(uint32_t* dst_smem, uint32_t ncols) {
   asm volatile(

@@ -33,23 +33,26 @@ namespace mxq {
 namespace {
 
 constexpr int kGemmThreads = 384;
-constexpr int kRawStages = 8;
 constexpr uint32_t kWaitLimit = 1u << 22;
 
+// Raw (packed weight) ring sized by bytes in flight: small token tiles are
+// HBM-streaming (deep ring, ~100 KB per SM); large ones are MMA-bound.
 template <int WFMT, int BN>
 struct Cfg {
   static constexpr int TB = WFMT == 4 ? 32 : 64;
   static constexpr int RAW_W = 128 * TB;
   static constexpr int RAW_STAGE = RAW_W + 256;
+  static constexpr int RAW_TARGET = BN <= 64 ? 104 * 1024 : (BN <= 128 ? 64 * 1024 : 36 * 1024);
+  static constexpr int RS = RAW_TARGET / RAW_STAGE;
   static constexpr int W_TILE = 128 * 128;
   static constexpr int X_TILE = BN * 128;
   static constexpr int OP_STAGE = W_TILE + X_TILE;
   static constexpr int BUDGET = 222 * 1024;
-  static constexpr int OS_FIT = (BUDGET - 2048 - kRawStages * RAW_STAGE) / OP_STAGE;
+  static constexpr int OS_FIT = (BUDGET - 2048 - RS * RAW_STAGE) / OP_STAGE;
   static constexpr int OS = OS_FIT > 4 ? 4 : OS_FIT;
   static constexpr int TMEM_COLS = BN <= 32 ? 32 : (BN <= 64 ? 64 : (BN <= 128 ? 128 : 256));
-  static constexpr size_t SMEM = 1024 + (size_t)OS * OP_STAGE + (size_t)kRawStages * RAW_STAGE + 512;
-  static_assert(OS >= 2, "operand ring too shallow");
+  static constexpr size_t SMEM = 1024 + (size_t)OS * OP_STAGE + (size_t)RS * RAW_STAGE + 1024;
+  static_assert(OS >= 2 && RS >= 4, "rings too shallow");
 };
 
 __device__ __forceinline__ uint32_t bf16x2_scale(uint32_t s) {
@@ -97,7 +100,7 @@ template <int WFMT, int BN>
 __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tc_kernel(GemmArgs a) {
   using C = Cfg<WFMT, BN>;
   constexpr int OS = C::OS;
-  constexpr int RS = kRawStages;
+  constexpr int RS = C::RS;
   extern __shared__ uint8_t smem_raw[];
   // 1024-byte alignment for the 128B-swizzled operand tiles
   const uint32_t base_u32 = smem_u32(smem_raw);
@@ -204,6 +207,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tc_kernel(GemmArgs a) {
       const int r = kt % RS, s = kt % OS;
       ok = mbar_wait(&raw_full[r], (kt / RS) & 1, status, kWaitLimit);
       if (ok && kt >= OS) ok = mbar_wait(&op_empty[s], ((kt / OS) - 1) & 1, status, kWaitLimit);
+      ok = __all_sync(0xffffffffu, ok);   // keep each warp's lanes together
       if (!ok) break;
       const uint8_t* raw = raw_ring + r * C::RAW_STAGE;
       const uint8_t* rsc = raw + C::RAW_W;
@@ -237,7 +241,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tc_kernel(GemmArgs a) {
       mbar_arrive(&w_full[s]);
     }
     // epilogue
-    ok = mbar_wait(acc_full, 0, status, kWaitLimit);
+    if (ok) ok = mbar_wait(acc_full, 0, status, kWaitLimit);
+    ok = __all_sync(0xffffffffu, ok);     // tcgen05.ld is warp-collective
     tc_fence_after();
     if (ok) {
       const int q = warp & 3, h = (warp - 4) >> 2;

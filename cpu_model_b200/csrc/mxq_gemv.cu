@@ -100,8 +100,8 @@ __device__ __forceinline__ float wscale(uint32_t s) {
                    : pow2_exact((int)s - 127 - SHIFT);
 }
 
-template <int WFMT, int NB, bool GATHER>
-__global__ void __launch_bounds__(256) gemv_kernel(GemvArgs a) {
+template <int WFMT, int NB, bool GATHER, bool INF32>
+__global__ void __launch_bounds__(256, 2) gemv_kernel(GemvArgs a) {
   constexpr int LPR = WFMT == 4 ? 2 : 4;  // lanes per row
   constexpr int ROWS = 32 / LPR;          // rows per warp (and per CTA)
   constexpr int TB = WFMT == 4 ? 32 : 64; // bytes per row per k-tile
@@ -145,6 +145,12 @@ __global__ void __launch_bounds__(256) gemv_kernel(GemvArgs a) {
       sa[u] = __ldg(sbase + u * 256);
     }
   }
+  if (a.pf_bytes && threadIdx.x == 0) {
+    // warm L2 with this CTA's share of the next layer's weights: their HBM
+    // reads overlap this kernel instead of waiting for the next launch
+    prefetch_l2_share(a.pf_ptr, a.pf_bytes, blockIdx.x, gridDim.x);
+    prefetch_l2_share(a.pf_ptr2, a.pf_bytes2, blockIdx.x, gridDim.x);
+  }
 
   asm volatile("griddepcontrol.wait;" ::: "memory");
 
@@ -153,24 +159,82 @@ __global__ void __launch_bounds__(256) gemv_kernel(GemvArgs a) {
   uint8_t* act = smem + warp * per_warp;
   float* fa = reinterpret_cast<float*>(act + NB * S * 64);
   const int kb = a.w.K / kBlock;
+  if (INF32) {
+    // fp32 rows quantised here with quantize_kernel's arithmetic (bytes are
+    // identical): 8 lanes per 32-element block, one float4 each, all of a
+    // batch's loads in flight before use
+    constexpr int QB = 6;
+    const int nblk = nkt * 2;
+    const int items = NB * nblk * 8;
+    for (int base = lane; base < items; base += 32 * QB) {
+      float4 v[QB];
 #pragma unroll
-  for (int t = 0; t < NB; ++t) {
-    if (t < a.B) {
-      for (int c = lane; c < nkt * 4; c += 32) {
-        const int k = kt0 * kTileK + c * 16;
-        uint4 v = make_uint4(0, 0, 0, 0);
-        if (k < a.w.K)
-          v = xor80(*reinterpret_cast<const uint4*>(a.xq + (size_t)t * a.w.K + k));
-        *reinterpret_cast<uint4*>(act + t * S * 64 + c * 16) = v;
+      for (int i = 0; i < QB; ++i) {
+        const int c = base + i * 32;
+        const int t = c / (nblk * 8), bl = (c / 8) % nblk, part = c % 8;
+        const int b = kt0 * 2 + bl;
+        v[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (c < items && t < a.B && b < kb)
+          v[i] = *reinterpret_cast<const float4*>(a.xf + (size_t)t * a.w.K + b * kBlock + part * 4);
       }
-      for (int bb = lane; bb < nkt * 2; bb += 32) {
-        const int b = kt0 * 2 + bb;
-        fa[t * S * 2 + bb] = b < kb ? e8m0_to_float(a.xs[(size_t)t * kb + b]) : 0.0f;
+#pragma unroll
+      for (int i = 0; i < QB; ++i) {
+        const int c = base + i * 32;          // 8-lane groups share (t, block)
+        const int t = c / (nblk * 8), bl = (c / 8) % nblk, part = c % 8;
+        const int b = kt0 * 2 + bl;
+        const float e4[4] = {v[i].x, v[i].y, v[i].z, v[i].w};
+        float m = 0.0f;
+        bool nf = false;
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float av = fabsf(e4[e]);
+          nf |= !(av <= 3.402823466e38f);
+          m = fmaxf(m, nf ? 0.0f : av);
+        }
+#pragma unroll
+        for (int o = 4; o > 0; o >>= 1) {
+          m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+          nf |= __shfl_xor_sync(0xffffffffu, (int)nf, o) != 0;
+        }
+        if (c < items) {
+          uint32_t sb = 0;
+          int e = 0;
+          const bool live = t < a.B && b < kb;
+          if (live) {
+            if (nf) sb = 255;
+            else if (m != 0.0f) { e = e8m0_exponent<127>(m); sb = (uint32_t)(e + 127); }
+          }
+          uint32_t packed = 0;
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            const int q = (sb != 0 && sb != 255) ? quant_value(e4[k], e) : 0;
+            packed |= ((uint32_t)q & 0xFFu) << (8 * k);
+          }
+          *reinterpret_cast<uint32_t*>(act + t * S * 64 + bl * kBlock + part * 4) = packed;
+          if (part == 0) fa[t * S * 2 + bl] = live ? e8m0_to_float(sb) : 0.0f;
+        }
       }
-    } else {
-      for (int c = lane; c < nkt * 4; c += 32)
-        *reinterpret_cast<uint4*>(act + t * S * 64 + c * 16) = make_uint4(0, 0, 0, 0);
-      for (int bb = lane; bb < nkt * 2; bb += 32) fa[t * S * 2 + bb] = 0.0f;
+    }
+  } else {
+#pragma unroll
+    for (int t = 0; t < NB; ++t) {
+      if (t < a.B) {
+        for (int c = lane; c < nkt * 4; c += 32) {
+          const int k = kt0 * kTileK + c * 16;
+          uint4 v = make_uint4(0, 0, 0, 0);
+          if (k < a.w.K)
+            v = xor80(*reinterpret_cast<const uint4*>(a.xq + (size_t)t * a.w.K + k));
+          *reinterpret_cast<uint4*>(act + t * S * 64 + c * 16) = v;
+        }
+        for (int bb = lane; bb < nkt * 2; bb += 32) {
+          const int b = kt0 * 2 + bb;
+          fa[t * S * 2 + bb] = b < kb ? e8m0_to_float(a.xs[(size_t)t * kb + b]) : 0.0f;
+        }
+      } else {
+        for (int c = lane; c < nkt * 4; c += 32)
+          *reinterpret_cast<uint4*>(act + t * S * 64 + c * 16) = make_uint4(0, 0, 0, 0);
+        for (int bb = lane; bb < nkt * 2; bb += 32) fa[t * S * 2 + bb] = 0.0f;
+      }
     }
   }
   __syncwarp();
@@ -289,7 +353,7 @@ __global__ void block_dots_kernel(GemvArgs a) {
   }
 }
 
-template <int WFMT, int NB, bool GATHER>
+template <int WFMT, int NB, bool GATHER, bool INF32>
 cudaError_t launch_t(const GemvArgs& a, cudaStream_t st, bool pdl) {
   constexpr int LPR = WFMT == 4 ? 2 : 4;
   constexpr int ROWS = 32 / LPR;
@@ -300,7 +364,7 @@ cudaError_t launch_t(const GemvArgs& a, cudaStream_t st, bool pdl) {
   if (smem > 227 * 1024) return cudaErrorInvalidValue;
   static size_t configured = 0;
   if (smem > 48 * 1024 && smem > configured) {
-    cudaError_t e = cudaFuncSetAttribute(gemv_kernel<WFMT, NB, GATHER>,
+    cudaError_t e = cudaFuncSetAttribute(gemv_kernel<WFMT, NB, GATHER, INF32>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          (int)smem);
     if (e != cudaSuccess) return e;
@@ -317,18 +381,18 @@ cudaError_t launch_t(const GemvArgs& a, cudaStream_t st, bool pdl) {
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = pdl ? 1 : 0;
-  return cudaLaunchKernelEx(&cfg, gemv_kernel<WFMT, NB, GATHER>, a);
+  return cudaLaunchKernelEx(&cfg, gemv_kernel<WFMT, NB, GATHER, INF32>, a);
 }
 
-template <int WFMT, bool GATHER>
+template <int WFMT, bool GATHER, bool INF32>
 cudaError_t launch_fmt(const GemvArgs& a, cudaStream_t st, bool pdl) {
   switch (a.B) {
-    case 1: return launch_t<WFMT, 1, GATHER>(a, st, pdl);
-    case 2: return launch_t<WFMT, 2, GATHER>(a, st, pdl);
-    case 3: return launch_t<WFMT, 3, GATHER>(a, st, pdl);
-    case 4: return launch_t<WFMT, 4, GATHER>(a, st, pdl);
-    case 5: case 6: return launch_t<WFMT, 6, GATHER>(a, st, pdl);
-    case 7: case 8: return launch_t<WFMT, 8, GATHER>(a, st, pdl);
+    case 1: return launch_t<WFMT, 1, GATHER, INF32>(a, st, pdl);
+    case 2: return launch_t<WFMT, 2, GATHER, INF32>(a, st, pdl);
+    case 3: return launch_t<WFMT, 3, GATHER, INF32>(a, st, pdl);
+    case 4: return launch_t<WFMT, 4, GATHER, INF32>(a, st, pdl);
+    case 5: case 6: return launch_t<WFMT, 6, GATHER, INF32>(a, st, pdl);
+    case 7: case 8: return launch_t<WFMT, 8, GATHER, INF32>(a, st, pdl);
   }
   return cudaErrorInvalidValue;
 }
@@ -348,9 +412,9 @@ cudaError_t launch_gemv(const GemvArgs& a, cudaStream_t st, bool pdl) {
     return cudaGetLastError();
   }
   if (a.B < 1 || a.B > gemv_max_batch()) return cudaErrorInvalidValue;
-  const bool g = a.rows != nullptr;
-  if (a.w.fmt == 4) return g ? launch_fmt<4, true>(a, st, pdl) : launch_fmt<4, false>(a, st, pdl);
-  return g ? launch_fmt<8, true>(a, st, pdl) : launch_fmt<8, false>(a, st, pdl);
+  if (a.rows) return a.w.fmt == 4 ? launch_fmt<4, true, false>(a, st, pdl) : launch_fmt<8, true, false>(a, st, pdl);
+  if (a.xf) return a.w.fmt == 4 ? launch_fmt<4, false, true>(a, st, pdl) : launch_fmt<8, false, true>(a, st, pdl);
+  return a.w.fmt == 4 ? launch_fmt<4, false, false>(a, st, pdl) : launch_fmt<8, false, false>(a, st, pdl);
 }
 
 }  // namespace mxq

@@ -17,6 +17,7 @@ struct WeightView {
   int Npad, Kpad; // Npad multiple of 256, Kpad multiple of 64
   const uint8_t* data;
   const uint8_t* scales;
+  int scale_lo, scale_hi;  // range of the logical weight scale bytes
 };
 
 struct QuantArgs {
@@ -37,8 +38,13 @@ cudaError_t launch_quantize(const QuantArgs& a, int mode, cudaStream_t st, bool 
 
 struct GemvArgs {
   WeightView w;
-  const uint8_t* xq;     // MX activations [B][K]
+  const uint8_t* xq;     // MX activations [B][K] ...
   const uint8_t* xs;     // [B][K/32]
+  const float* xf;       // ... or fp32 rows [B][K], quantised in the kernel
+  const void* pf_ptr;    // optional: bytes to prefetch into L2 (next layer's
+  size_t pf_bytes;       //   weights and scales), spread over the CTAs
+  const void* pf_ptr2;
+  size_t pf_bytes2;
   float* y;              // [B][N]   (or [B][nrows] when gathering)
   int B;
   const int32_t* rows;   // optional gathered row ids (mx_rank16_dot_ptrs)
@@ -59,6 +65,18 @@ struct GemmArgs {
 
 cudaError_t launch_gemm(const GemmArgs& a, cudaStream_t st, bool pdl);
 int gemm_pick_bn(int B);
+
+// Batches up to this size take the GEMV in MXQ_PATH_AUTO.
+constexpr int kGemvAutoBatch = 4;
+
+// Persistent decode GEMV (mxq_rgemv.cu), batch <= kRgemvMaxBatch: MX or fp32
+// input (GemvArgs.xq/xs or .xf), optional L2 prefetch; no gather/dots.
+constexpr int kRgemvMaxBatch = 4;
+bool rgemv_supported(const WeightView& w, int B);
+cudaError_t launch_rgemv(const GemvArgs& a, cudaStream_t st, bool pdl);
+
+cudaError_t launch_scale_range(const uint8_t* scales, size_t count, uint32_t* out2,
+                               cudaStream_t st);
 
 cudaError_t launch_repack(const uint8_t* data, const uint8_t* scales, int fmt,
                           int N, int K, int Npad, int Kpad, uint8_t* out_data,

@@ -1,0 +1,407 @@
+// mxq_rgemv.cu -- persistent decode GEMV (batch <= 4): the HBM-bound mx_gemv
+// of the reference (nn/tests/test_auto_generated.cpp:56; dpbusd design
+// nn/user.md:17).
+//
+// One CTA per SM, 16 warps, one wave: fixed per-CTA costs (activation
+// staging, pipeline ramp) are paid once per launch, not once per wave.
+//
+// Work split.  Output rows are taken in groups of 4; each CTA owns a
+// contiguous, balanced range of groups (ranges differ by one group: for a
+// 7B MLP 18-19 groups of the up projection, 6-7 of the down projection per
+// CTA).  Inside a CTA the 16 warps split K; a warp streams its K-slice of
+// every group it owns, straight from HBM into registers (128-bit
+// ld.global.nc, no L1 allocation), with two batches of loads in flight
+// (64 KB per SM).  In the tiled weight layout a group's k-tile is 128 (int4)
+// or 256 (int8) contiguous bytes, so one warp load covers 4 (2) k-tiles of the
+// group in full 128-byte lines.  Partial sums stay inside the CTA: each warp
+// folds its lanes with shuffles, writes one value per row to shared memory,
+// and after the last group the CTA adds the 16 warps' values in warp order
+// -- no cross-CTA reduction, deterministic results.
+//
+// Activations (an MX activation, or fp32 rows quantised here with
+// quantize_kernel's arithmetic -- identical bytes) are staged once per warp
+// for its K-slice as signed int8 plus a float block scale.  int4 nibbles are
+// widened to int8 in place (16*w by a shift and a mask, re-interleaved with
+// two byte-permutes), eight dp4a give the exact int32 block dot (x16), and
+// 2^(e_x + e_w - 4) scales it into the fp32 sum.
+#include "mxq_internal.h"
+
+namespace mxq {
+
+namespace {
+
+constexpr int kWarps = 16;
+constexpr int kThreads = kWarps * 32;
+constexpr int kD = 4;   // loads per batch (two batches in flight)
+
+template <int WFMT>
+struct RCfg {
+  static constexpr int TB = WFMT == 4 ? 32 : 64;   // bytes per row per k-tile
+  static constexpr int TPL = TB / 16;              // lanes per row per k-tile (2 / 4)
+  static constexpr int LPK = 4 * TPL;              // lanes per k-tile of a 4-row group (8 / 16)
+  static constexpr int KPL = 32 / LPK;             // k-tiles per warp load (4 / 2)
+  static constexpr int SHIFT = WFMT == 4 ? 4 : 0;  // int4 dots come out x16
+};
+
+__device__ __forceinline__ uint4 ldg_stream(const void* p) {
+  uint4 v;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p));
+  return v;
+}
+
+// geometry shared by host and device
+struct RGeom {
+  int KT;      // k-tiles
+  int kts;     // k-tiles per warp (multiple of KPL)
+  int nload;   // warp loads per group
+  int G4;      // 4-row groups
+};
+
+template <int WFMT>
+__host__ __device__ __forceinline__ RGeom rgeom(const WeightView& w) {
+  using C = RCfg<WFMT>;
+  RGeom g;
+  g.KT = w.Kpad / kTileK;
+  const int per = (g.KT + kWarps - 1) / kWarps;
+  g.kts = (per + C::KPL - 1) / C::KPL * C::KPL;
+  g.nload = g.kts / C::KPL;
+  g.G4 = (w.N + 3) / 4;
+  return g;
+}
+
+template <int WFMT, int NB, bool FAST, bool INF32>
+__global__ void __launch_bounds__(kThreads, 1) rgemv_kernel(GemvArgs a) {
+  using C = RCfg<WFMT>;
+  extern __shared__ __align__(16) uint8_t smem[];
+  const RGeom g = rgeom<WFMT>(a.w);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int G = gridDim.x;
+  const int g_lo = (int)((long)blockIdx.x * g.G4 / G);
+  const int g_hi = (int)((long)(blockIdx.x + 1) * g.G4 / G);
+  const int ng = g_hi - g_lo;
+  const int kt0 = warp * g.kts;
+
+  // lane -> (k-tile within a load, row within the group, sub-slice)
+  const int kto = lane / C::LPK;
+  const int rr = (lane % C::LPK) / C::TPL;
+  const int sub = lane % C::TPL;
+  const int bh = WFMT == 4 ? sub : (sub >> 1);   // block within the k-tile
+
+  // shared memory: per warp its activation slice, then the partial sums
+  const int slice = g.kts * kTileK;                      // activation bytes per token
+  const int per_warp = (NB * slice + NB * g.kts * 2 * 4 + 15) / 16 * 16;
+  int8_t* act = reinterpret_cast<int8_t*>(smem + warp * per_warp);
+  float* fa = reinterpret_cast<float*>(act + NB * slice);
+  float* part = reinterpret_cast<float*>(smem + kWarps * per_warp);   // [warp][group][4 rows][NB]
+  const int max_ng = (g.G4 + G - 1) / G;
+
+  // The lane streams the sequence (group gi, load li) with li fastest; two
+  // cursors walk it -- one issuing loads, one computing -- by pointer bumps,
+  // with the row address recomputed once per group.
+  const int Q = ng * g.nload;
+  const size_t kstep_w = (size_t)C::KPL * 128 * C::TB;   // next load of the same row
+  const size_t kstep_s = (size_t)C::KPL * 256;
+  uint32_t kmask = 0;                                    // loads whose k-tile exists
+  for (int li = 0; li < g.nload && li < 32; ++li)
+    if (kt0 + li * C::KPL + kto < g.KT) kmask |= 1u << li;
+  struct Cursor {
+    int gi, li;
+    const uint8_t* wp;
+    const uint8_t* sp;
+  };
+  auto row_base = [&](Cursor& cu) {
+    const int n = (g_lo + cu.gi) * 4 + rr;
+    const size_t rowoff = ((size_t)(n >> 7) * g.KT + kt0 + kto) * 128 + (n & 127);
+    cu.wp = a.w.data + rowoff * C::TB + sub * 16;
+    cu.sp = a.w.scales + rowoff * 2 + bh;
+  };
+  auto step = [&](Cursor& cu) {
+    if (++cu.li == g.nload) {
+      cu.li = 0;
+      ++cu.gi;
+      row_base(cu);
+    } else {
+      cu.wp += kstep_w;
+      cu.sp += kstep_s;
+    }
+  };
+  Cursor ic{0, 0, nullptr, nullptr};
+  row_base(ic);
+  int issued = 0;
+
+  uint4 wa[kD], wb[kD];
+  uint32_t sa[kD], sb[kD];
+  auto issue = [&](uint4 (&w)[kD], uint32_t (&s)[kD]) {
+#pragma unroll
+    for (int d = 0; d < kD; ++d) {
+      if (issued < Q) {
+        if ((kmask >> ic.li) & 1u) {
+          w[d] = ldg_stream(ic.wp);
+          s[d] = __ldg(ic.sp);
+        } else {
+          w[d] = make_uint4(0, 0, 0, 0);
+          s[d] = 127;
+        }
+        step(ic);
+        ++issued;
+      }
+    }
+  };
+  issue(wa, sa);
+  if (a.pf_bytes && threadIdx.x == 0) {
+    prefetch_l2_share(a.pf_ptr, a.pf_bytes, blockIdx.x, gridDim.x);
+    prefetch_l2_share(a.pf_ptr2, a.pf_bytes2, blockIdx.x, gridDim.x);
+  }
+
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+
+  // ---- stage this warp's K-slice of the activation
+  const int kb = a.w.K / kBlock;
+  const int nblk = g.kts * 2;
+  if (INF32) {
+    constexpr int QB = 4;
+    const int items = NB * nblk * 8;   // float4 chunks, 8 per block
+    for (int base = lane; base < items; base += 32 * QB) {
+      float4 v[QB];
+#pragma unroll
+      for (int i = 0; i < QB; ++i) {
+        const int c = base + i * 32;
+        const int t = c / (nblk * 8), bl = (c / 8) % nblk, p4 = c % 8;
+        const int b = kt0 * 2 + bl;
+        v[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (c < items && t < a.B && b < kb)
+          v[i] = *reinterpret_cast<const float4*>(a.xf + (size_t)t * a.w.K + b * kBlock + p4 * 4);
+      }
+#pragma unroll
+      for (int i = 0; i < QB; ++i) {
+        const int c = base + i * 32;          // 8-lane groups share (t, block)
+        const int t = c / (nblk * 8), bl = (c / 8) % nblk, p4 = c % 8;
+        const int b = kt0 * 2 + bl;
+        const float e4[4] = {v[i].x, v[i].y, v[i].z, v[i].w};
+        float m = 0.0f;
+        bool nf = false;
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float av = fabsf(e4[e]);
+          nf |= !(av <= 3.402823466e38f);
+          m = fmaxf(m, nf ? 0.0f : av);
+        }
+#pragma unroll
+        for (int o = 4; o > 0; o >>= 1) {
+          m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+          nf |= __shfl_xor_sync(0xffffffffu, (int)nf, o) != 0;
+        }
+        if (c < items) {
+          uint32_t s8 = 0;
+          int e = 0;
+          const bool live = t < a.B && b < kb;
+          if (live) {
+            if (nf) s8 = 255;
+            else if (m != 0.0f) { e = e8m0_exponent<127>(m); s8 = (uint32_t)(e + 127); }
+          }
+          uint32_t packed = 0;
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            const int q = (s8 != 0 && s8 != 255) ? quant_value(e4[k], e) : 0;
+            packed |= ((uint32_t)q & 0xFFu) << (8 * k);
+          }
+          *reinterpret_cast<uint32_t*>(act + t * slice + bl * kBlock + p4 * 4) = packed;
+          if (p4 == 0) fa[t * nblk + bl] = live ? e8m0_to_float(s8) : 0.0f;
+        }
+      }
+    }
+  } else {
+    for (int t = 0; t < NB; ++t) {
+      for (int c = lane; c < g.kts * 4; c += 32) {
+        const int k = kt0 * kTileK + c * 16;
+        uint4 v = make_uint4(0, 0, 0, 0);
+        if (t < a.B && k < a.w.K) {
+          v = *reinterpret_cast<const uint4*>(a.xq + (size_t)t * a.w.K + k);
+          v.x ^= 0x80808080u; v.y ^= 0x80808080u; v.z ^= 0x80808080u; v.w ^= 0x80808080u;
+        }
+        *reinterpret_cast<uint4*>(act + t * slice + c * 16) = v;
+      }
+      for (int bb = lane; bb < nblk; bb += 32) {
+        const int b = kt0 * 2 + bb;
+        fa[t * nblk + bb] = (t < a.B && b < kb) ? e8m0_to_float(a.xs[(size_t)t * kb + b]) : 0.0f;
+      }
+    }
+  }
+  __syncwarp();
+
+  float acc[NB];
+#pragma unroll
+  for (int t = 0; t < NB; ++t) acc[t] = 0.0f;
+  int cgi = 0, cli = 0;                                 // compute cursor
+  const int8_t* xrow = act + kto * kTileK + (WFMT == 4 ? sub * 32 : sub * 16);
+  const float* frow = fa + kto * 2 + bh;
+
+  auto compute = [&](const uint4& w, uint32_t s) {
+    const int j = cli * C::KPL;                       // k-tile offset of this load (minus kto)
+    float fw;
+    if (FAST) fw = __int_as_float((int)((s - C::SHIFT) << 23));
+    else fw = s == 255u ? __int_as_float(0x7fc00000) : pow2_exact((int)s - 127 - C::SHIFT);
+    if (WFMT == 4) {
+      uint32_t n[8];
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const uint32_t ww = k == 0 ? w.x : (k == 1 ? w.y : (k == 2 ? w.z : w.w));
+        const uint32_t lo = (ww << 4) & 0xF0F0F0F0u, hi = ww & 0xF0F0F0F0u;
+        n[2 * k] = __byte_perm(lo, hi, 0x5140);
+        n[2 * k + 1] = __byte_perm(lo, hi, 0x7362);
+      }
+#pragma unroll
+      for (int t = 0; t < NB; ++t) {
+        const uint4* xp = reinterpret_cast<const uint4*>(xrow + t * slice + j * kTileK);
+        const uint4 x0 = xp[0], x1 = xp[1];
+        int d0 = __dp4a((int)x0.x, (int)n[0], 0);
+        int d1 = __dp4a((int)x0.y, (int)n[1], 0);
+        d0 = __dp4a((int)x0.z, (int)n[2], d0);
+        d1 = __dp4a((int)x0.w, (int)n[3], d1);
+        d0 = __dp4a((int)x1.x, (int)n[4], d0);
+        d1 = __dp4a((int)x1.y, (int)n[5], d1);
+        d0 = __dp4a((int)x1.z, (int)n[6], d0);
+        d1 = __dp4a((int)x1.w, (int)n[7], d1);
+        acc[t] = __fmaf_rn((float)(d0 + d1), __fmul_rn(frow[t * nblk + j * 2], fw), acc[t]);
+      }
+    } else {
+#pragma unroll
+      for (int t = 0; t < NB; ++t) {
+        const uint4 x = *reinterpret_cast<const uint4*>(xrow + t * slice + j * kTileK);
+        int d0 = __dp4a((int)x.x, (int)w.x, 0);
+        int d1 = __dp4a((int)x.y, (int)w.y, 0);
+        d0 = __dp4a((int)x.z, (int)w.z, d0);
+        d1 = __dp4a((int)x.w, (int)w.w, d1);
+        acc[t] = __fmaf_rn((float)(d0 + d1), __fmul_rn(frow[t * nblk + j * 2], fw), acc[t]);
+      }
+    }
+    if (++cli == g.nload) {
+      // group done: fold the lanes of each row (k-tiles x sub-slices), keep
+      // the row's warp total in shared memory
+#pragma unroll
+      for (int t = 0; t < NB; ++t) {
+#pragma unroll
+        for (int o = 1; o < C::TPL; o <<= 1) acc[t] += __shfl_xor_sync(0xffffffffu, acc[t], o);
+#pragma unroll
+        for (int o = C::LPK; o < 32; o <<= 1) acc[t] += __shfl_xor_sync(0xffffffffu, acc[t], o);
+      }
+      if (kto == 0 && sub == 0)
+#pragma unroll
+        for (int t = 0; t < NB; ++t) part[((warp * max_ng + cgi) * 4 + rr) * NB + t] = acc[t];
+#pragma unroll
+      for (int t = 0; t < NB; ++t) acc[t] = 0.0f;
+      cli = 0;
+      ++cgi;
+    }
+  };
+
+  // every lane runs the same number of steps (Q is CTA-uniform), so the
+  // shuffles above are never divergent
+  for (int q0 = 0; q0 < Q; q0 += 2 * kD) {
+    issue(wb, sb);
+#pragma unroll
+    for (int d = 0; d < kD; ++d)
+      if (q0 + d < Q) compute(wa[d], sa[d]);
+    issue(wa, sa);
+#pragma unroll
+    for (int d = 0; d < kD; ++d)
+      if (q0 + kD + d < Q) compute(wb[d], sb[d]);
+  }
+
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  __syncthreads();
+  // y = sum over the 16 warps, in warp order
+  for (int e = threadIdx.x; e < ng * 4 * NB; e += kThreads) {
+    const int t = e % NB, row = e / NB;          // row within this CTA's range
+    const int gi = row / 4, r4 = row % 4;
+    const int n = (g_lo + gi) * 4 + r4;
+    float s = 0.0f;
+#pragma unroll
+    for (int w = 0; w < kWarps; ++w) s += part[((w * max_ng + gi) * 4 + r4) * NB + t];
+    if (t < a.B && n < a.w.N) a.y[(size_t)t * a.w.N + n] = s;
+  }
+}
+
+int g_sms = 0;
+
+int sms() {
+  if (g_sms == 0) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (cudaDeviceGetAttribute(&g_sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || g_sms <= 0)
+      g_sms = 148;
+  }
+  return g_sms;
+}
+
+template <int WFMT>
+size_t smem_bytes(const WeightView& w, int nb) {
+  const RGeom g = rgeom<WFMT>(w);
+  const int per_warp = (nb * g.kts * kTileK + nb * g.kts * 2 * 4 + 15) / 16 * 16;
+  const int G = sms();
+  const int max_ng = (g.G4 + G - 1) / G;
+  return (size_t)kWarps * per_warp + (size_t)kWarps * max_ng * 4 * nb * 4;
+}
+
+template <int WFMT, int NB, bool FAST, bool INF32>
+cudaError_t launch_t(const GemvArgs& a, cudaStream_t st, bool pdl) {
+  const size_t smem = smem_bytes<WFMT>(a.w, NB);
+  if (smem > 220 * 1024) return cudaErrorInvalidValue;
+  static size_t configured = 0;
+  if (smem > 48 * 1024 && smem > configured) {
+    cudaError_t e = cudaFuncSetAttribute(rgemv_kernel<WFMT, NB, FAST, INF32>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    configured = smem;
+  }
+  const int G4 = (a.w.N + 3) / 4;
+  const int grid = G4 < sms() ? G4 : sms();
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)grid);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, rgemv_kernel<WFMT, NB, FAST, INF32>, a);
+}
+
+template <int WFMT, bool FAST, bool INF32>
+cudaError_t launch_nb(const GemvArgs& a, cudaStream_t st, bool pdl) {
+  switch (a.B) {
+    case 1: return launch_t<WFMT, 1, FAST, INF32>(a, st, pdl);
+    case 2: return launch_t<WFMT, 2, FAST, INF32>(a, st, pdl);
+    case 3: return launch_t<WFMT, 3, FAST, INF32>(a, st, pdl);
+    case 4: return launch_t<WFMT, 4, FAST, INF32>(a, st, pdl);
+  }
+  return cudaErrorInvalidValue;
+}
+
+template <int WFMT, bool INF32>
+cudaError_t launch_fast(const GemvArgs& a, cudaStream_t st, bool pdl) {
+  // fast scale path when every weight scale byte is in [SHIFT+1, 254]
+  return a.w.scale_lo >= (WFMT == 4 ? 5 : 1) && a.w.scale_hi <= 254 ? launch_nb<WFMT, true, INF32>(a, st, pdl)
+                                                                      : launch_nb<WFMT, false, INF32>(a, st, pdl);
+}
+
+}  // namespace
+
+bool rgemv_supported(const WeightView& w, int B) {
+  if (B < 1 || B > kRgemvMaxBatch) return false;
+  const size_t smem = w.fmt == 4 ? smem_bytes<4>(w, B) : smem_bytes<8>(w, B);
+  return smem <= 220 * 1024;
+}
+
+cudaError_t launch_rgemv(const GemvArgs& a, cudaStream_t st, bool pdl) {
+  if (!rgemv_supported(a.w, a.B) || a.rows || a.block_dots) return cudaErrorInvalidValue;
+  const bool f32 = a.xf != nullptr;
+  if (a.w.fmt == 4) return f32 ? launch_fast<4, true>(a, st, pdl) : launch_fast<4, false>(a, st, pdl);
+  return f32 ? launch_fast<8, true>(a, st, pdl) : launch_fast<8, false>(a, st, pdl);
+}
+
+}  // namespace mxq

@@ -65,7 +65,7 @@ extern "C" {
 #define MXQ_ACT_NONE 0
 #define MXQ_ACT_SILU 1
 
-#define MXQ_PATH_AUTO 0 /* GEMV for batch <= 8, tensor-core GEMM above */
+#define MXQ_PATH_AUTO 0 /* streaming GEMV for batch <= 4, tensor-core GEMM above */
 #define MXQ_PATH_GEMV 1
 #define MXQ_PATH_GEMM 2
 
@@ -79,7 +79,8 @@ MXQ_API int mxq_create(int device, mxq_ctx* out);
 MXQ_API int mxq_destroy(mxq_ctx ctx);
 MXQ_API int mxq_set_stream(mxq_ctx ctx, void* cuda_stream);
 /* Regime override, the counterpart of nca::simd::set_override_backend
- * (nn/core/simd/dispatch.cpp:83-87): MXQ_PATH_*. */
+ * (nn/core/simd/dispatch.cpp:83-87): MXQ_PATH_*.  MXQ_PATH_GEMV accepts
+ * batch <= 8 (streaming split-K kernel up to 4, register-blocked above). */
 MXQ_API int mxq_set_path(mxq_ctx ctx, int path);
 MXQ_API int mxq_reserve(mxq_ctx ctx, size_t max_batch, size_t max_k);
 MXQ_API int mxq_synchronize(mxq_ctx ctx);

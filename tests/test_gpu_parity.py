@@ -275,3 +275,21 @@ def test_gae_bit_exact(ctx):
     a0, r0 = oracle.gae(rr, v, done, nv, 0.99, 0.95)
     a1, r1 = mx.fused_compute_gae(cuda(rr), cuda(v), cuda(done), cuda(nv), 0.99, 0.95, ctx)
     assert np.array_equal(host(a1), a0) and np.array_equal(host(r1), r0)
+
+
+@pytest.mark.parametrize("fmt", [8, 4])
+@pytest.mark.parametrize("b", [1, 4, 16])
+def test_repeat_calls_bit_identical(ctx, fmt, b):
+    """Split-K reductions (streaming GEMV) and the GEMM are deterministic:
+    repeated calls, interleaved with other shapes, give identical bits."""
+    w, ws, W = weight(ctx, fmt, 2000, 4096, 95)
+    w2, ws2, W2 = weight(ctx, fmt, 300, 11008, 96)
+    x = cuda(synth.normal((b, 4096), 97))
+    x2 = cuda(synth.normal((b, 11008), 98))
+    ys = []
+    for _ in range(4):
+        ys.append(host(mx.mx_linear(x, W, ctx)))
+        mx.mx_linear(x2, W2, ctx)
+    ctx.synchronize()
+    for y in ys[1:]:
+        assert np.array_equal(y, ys[0])
