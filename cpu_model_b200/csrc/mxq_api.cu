@@ -768,3 +768,79 @@ cudaError_t launch_repack(const uint8_t* data, const uint8_t* scales, int fmt, i
   return cudaGetLastError();
 }
 }  // namespace mxq
+
+// ------------------------------------------------ linear without allocation
+// mxq_linear_noalloc: the tensor-core linear (quantiser -> bf16 operand ->
+// tcgen05 GEMM) with its operand scratch in a fixed device array instead of
+// the context workspace, for callers that may not allocate device memory.
+#include <mutex>
+
+namespace {
+
+// Operand scratch: Bpad x Kpad bf16 values.  Every GPU that loads this
+// library holds it until the process exits.
+constexpr size_t kNoallocScratchBytes = (size_t)4 << 20;   // 4 MiB
+static __device__ __align__(256) uint8_t g_noalloc_scratch[kNoallocScratchBytes];
+
+constexpr int kNoallocMaxDevices = 64;
+std::mutex g_noalloc_mu;
+void* g_noalloc_addr[kNoallocMaxDevices] = {};
+
+// Device address of g_noalloc_scratch on the context's device, looked up once
+// per device with that device current.  In host code the symbol's name is
+// only a host-side stand-in, so the kernels get this address instead.
+int noalloc_scratch(mxq_context* c, void** out) {
+  if (c->device < 0 || c->device >= kNoallocMaxDevices)
+    return fail(c, MXQ_ERR_UNSUPPORTED, "mxq_linear_noalloc: device %d beyond %d", c->device, kNoallocMaxDevices);
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (!g_noalloc_addr[c->device]) {
+    void* p = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess || !p) return cuda_fail(c, e, "mxq_linear_noalloc: scratch address");
+    g_noalloc_addr[c->device] = p;
+  }
+  *out = g_noalloc_addr[c->device];
+  return MXQ_OK;
+}
+
+}  // namespace
+
+extern "C" int mxq_linear_noalloc(mxq_ctx c, mxq_weight w, const float* x, size_t b, float* y) {
+  MXQ_TRY({
+    if (int rc = check_ctx(c)) return rc;
+    if (int rc = check_weight(c, w)) return rc;
+    if (!x || !y || b == 0) return fail(c, MXQ_ERR_INVALID_ARGUMENT, "null pointer or empty batch");
+    if (b > (size_t)(1 << 20)) return fail(c, MXQ_ERR_INVALID_ARGUMENT, "mxq_linear_noalloc: batch %zu too large", b);
+    DeviceGuard g(c->device);   // the scratch address is per device: look it up with the device current
+    const int BN = gemm_pick_bn((int)b);
+    const size_t Bpad = (b + BN - 1) / BN * BN;
+    const size_t need = Bpad * (size_t)w->v.Kpad * 2;
+    if (need > kNoallocScratchBytes)
+      return fail(c, MXQ_ERR_INVALID_ARGUMENT,
+                  "mxq_linear_noalloc: batch %zu x K %d needs %zu bytes of scratch, more than the fixed %zu",
+                  b, w->v.K, need, kNoallocScratchBytes);
+    void* scratch = nullptr;
+    if (int rc = noalloc_scratch(c, &scratch)) return rc;
+    // the quantiser writes every element of the Bpad x Kpad operand (padding
+    // included), so nothing left in the shared array from an earlier call is read
+    QuantArgs qa{};
+    qa.x = x;
+    qa.B = (int)b;
+    qa.K = w->v.K;
+    qa.opnd = static_cast<__nv_bfloat16*>(scratch);
+    qa.Bpad = (int)Bpad;
+    qa.Kpad = w->v.Kpad;
+    qa.BN = BN;
+    qa.int4_order = w->v.fmt == 4;
+    if (int rc = after_launch(c, launch_quantize(qa, MXQ_ACT_NONE, c->stream, true), "quantize")) return rc;
+    GemmArgs ga{};
+    ga.w = w->v;
+    ga.opnd = qa.opnd;
+    ga.y = y;
+    ga.B = (int)b;
+    ga.Bpad = (int)Bpad;
+    ga.BN = BN;
+    ga.status = c->status;
+    return after_launch(c, launch_gemm(ga, c->stream, true), "gemm");
+  })
+}

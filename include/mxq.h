@@ -147,6 +147,23 @@ MXQ_API int mxq_mlp_swiglu(mxq_ctx ctx, mxq_weight gate, mxq_weight up,
                            mxq_weight down, const float* x, size_t b,
                            float* y);
 
+/* Same result as mxq_linear on the tensor-core path (quantise -> GEMM), but
+ * the call allocates nothing: the quantised-activation operand lives in a
+ * fixed 4 MiB device array inside this library, not in the context
+ * workspace.  No counterpart in the reference.  It is for callers that may
+ * not allocate device memory -- an engine whose device memory is owned by its
+ * own pool allocator, or a serving loop held to a no-allocation rule -- and
+ * who cannot rely on mxq_reserve having sized the workspace.
+ * Limit: 2 * Bpad * Kpad bytes <= 4 MiB (Bpad = batch rounded up to the
+ * GEMM's token tile, Kpad = K rounded up to 64), e.g. batch 512 at K 4096;
+ * larger shapes return MXQ_ERR_INVALID_ARGUMENT.  The first call on a device
+ * looks up the array's device address (once per device, with that device
+ * current); make that first call before any stream capture.  All calls, on
+ * every context and stream of a device, share the one array: calls that
+ * overlap on the GPU race and must be serialised by the caller. */
+MXQ_API int mxq_linear_noalloc(mxq_ctx ctx, mxq_weight w, const float* x,
+                               size_t b, float* y);
+
 /* ------------------------------------------------------------ routing --- */
 /* Top-k expert selection with the HashedRouter contract
  * (nn/tests/test_robustness.cpp:13-35: k > n_experts is an invalid
