@@ -346,7 +346,7 @@ def run_ours(args):
                  "up_kernel_ms": kms,
                  "up_kernel_hbm_gbs": gemv_bytes(UP[0], UP[1], sb) / (kms / 1e3) / 1e9,
                  "up_kernel_tflops": fl / (kms / 1e3) / 1e12}
-        entry["path"] = "gemv-dp4a" if sb <= 8 else "tcgen05-bf16"
+        entry["path"] = "gemv-dp4a" if sb <= 4 else "tcgen05-bf16"
         sweep[str(sb)] = entry
 
     if rank == 0:
@@ -358,7 +358,7 @@ def run_ours(args):
             "data": "synthetic", "config": workload_config(b, args.copies),
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
                          "frac": achieved / peaks["hbm_gbs"], "traffic": None,
-                         "kernel": "gemv_kernel<int4> (up 4096->11008)",
+                         "kernel": "rgemv_kernel<int4> (up 4096->11008)" if b <= 4 else "gemm_tc_kernel<int4> (up 4096->11008)",
                          "algorithmic_bytes_per_launch": gbytes, "launch_ms": gemv_ms,
                          "peak_src": peaks["src"] + " hbm_gbs (burst copy)"},
             "pair_hbm_gbs": pair_bytes(b) / (ms / 1e3) / 1e9,
