@@ -109,21 +109,25 @@ __global__ void repack_kernel(const uint8_t* __restrict__ data,
   }
 }
 
-// Range of the weight scale bytes (selects the GEMV's fast scale path).
+// Range of the weight scale bytes (selects the GEMV's fast scale path) and
+// the largest finite one (sets the tensor-core path's exponent shift).
 __global__ void scale_range_kernel(const uint8_t* __restrict__ s, size_t n, uint32_t* out) {
-  uint32_t lo = 255, hi = 0;
+  uint32_t lo = 255, hi = 0, hif = 0;
   for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
     const uint32_t v = s[i];
     lo = min(lo, v);
     hi = max(hi, v);
+    if (v != 255u) hif = max(hif, v);
   }
   for (int o = 16; o > 0; o >>= 1) {
     lo = min(lo, __shfl_xor_sync(0xffffffffu, lo, o));
     hi = max(hi, __shfl_xor_sync(0xffffffffu, hi, o));
+    hif = max(hif, __shfl_xor_sync(0xffffffffu, hif, o));
   }
   if ((threadIdx.x & 31) == 0) {
     atomicMin(&out[0], lo);
     atomicMax(&out[1], hi);
+    atomicMax(&out[2], hif);
   }
 }
 
@@ -259,6 +263,7 @@ int linear_dev(mxq_context* c, mxq_weight w, const float* x, size_t b, float* y,
   qa.Kpad = w->v.Kpad;
   qa.BN = BN;
   qa.int4_order = w->v.fmt == 4;
+  qa.shift = w->v.gemm_shift;
   if ((rc = after_launch(c, launch_quantize(qa, act, c->stream, true), "quantize"))) return rc;
   GemmArgs ga{};
   ga.w = w->v;
@@ -301,6 +306,7 @@ int gemv_dev(mxq_context* c, mxq_weight w, const uint8_t* xq, const uint8_t* xs,
   qa.Kpad = w->v.Kpad;
   qa.BN = BN;
   qa.int4_order = w->v.fmt == 4;
+  qa.shift = w->v.gemm_shift;
   if ((rc = after_launch(c, launch_quantize(qa, 3, c->stream, true), "operand"))) return rc;
   GemmArgs ga{};
   ga.w = w->v;
@@ -473,7 +479,7 @@ int mxq_weight_create(mxq_ctx c, int fmt, size_t n, size_t k, const void* data,
       src_s = tmp + src_bytes;
     }
     if (e == cudaSuccess) e = launch_repack(src_d, src_s, fmt, N, K, Npad, Kpad, w->data, w->scales, c->stream);
-    uint32_t range[2] = {255, 0};
+    uint32_t range[3] = {255, 0, 0};
     uint32_t* drange = nullptr;
     if (e == cudaSuccess) e = cudaMalloc(&drange, sizeof(range));
     if (e == cudaSuccess) e = cudaMemcpyAsync(drange, range, sizeof(range), cudaMemcpyHostToDevice, c->stream);
@@ -497,6 +503,12 @@ int mxq_weight_create(mxq_ctx c, int fmt, size_t n, size_t k, const void* data,
     w->v.scales = w->scales;
     w->v.scale_lo = (int)range[0];
     w->v.scale_hi = (int)range[1];
+    {
+      // bf16 holds |q| * 2^n up to n = 120 (int8) / 124 (int4)
+      const int emax = (int)range[2] - 127, lim = fmt == 8 ? 120 : 124;
+      w->v.gemm_shift = emax > lim ? emax - lim : 0;
+      w->v.gemm_fused = (int)range[2] - w->v.gemm_shift <= (fmt == 8 ? 231 : 246);
+    }
     *out = w;
     return MXQ_OK;
   })
@@ -832,6 +844,7 @@ extern "C" int mxq_linear_noalloc(mxq_ctx c, mxq_weight w, const float* x, size_
     qa.Kpad = w->v.Kpad;
     qa.BN = BN;
     qa.int4_order = w->v.fmt == 4;
+    qa.shift = w->v.gemm_shift;
     if (int rc = after_launch(c, launch_quantize(qa, MXQ_ACT_NONE, c->stream, true), "quantize")) return rc;
     GemmArgs ga{};
     ga.w = w->v;

@@ -18,6 +18,14 @@ struct WeightView {
   const uint8_t* data;
   const uint8_t* scales;
   int scale_lo, scale_hi;  // range of the logical weight scale bytes
+  // Tensor-core path: weights enter the bf16 operand as q*2^(e-gemm_shift)
+  // and activations as q*2^(e+gemm_shift), so the largest finite weight
+  // scale still fits bf16 (0 unless a weight exponent exceeds 120 / 124).
+  int gemm_shift;
+  // The converter's one-fma form needs its offset term (136 or 2^23+128
+  // times the scale) finite: every finite scale byte minus gemm_shift
+  // <= 246 (int4) / 231 (int8).  A NaN scale byte gives NaN on either form.
+  int gemm_fused;
 };
 
 struct QuantArgs {
@@ -31,6 +39,7 @@ struct QuantArgs {
   __nv_bfloat16* opnd;   // optional GEMM operand (tiled, swizzled)
   int Bpad, Kpad, BN;
   int int4_order;        // operand K order for int4 weights
+  int shift;             // operand exponent shift (WeightView::gemm_shift)
 };
 
 // mode: 0 = plain, 1 = SiLU, 2 = SwiGLU(x, up), 3 = MX input -> operand
@@ -61,6 +70,7 @@ struct GemmArgs {
   float* y;                  // [B][N]
   int B, Bpad, BN;
   uint32_t* status;          // device status word (bounded waits)
+  int splits;                // K splits over a cluster; 0 = chosen by occupancy
 };
 
 cudaError_t launch_gemm(const GemmArgs& a, cudaStream_t st, bool pdl);

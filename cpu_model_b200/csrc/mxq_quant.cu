@@ -21,6 +21,16 @@ namespace mxq {
 // in-group position -> slot, for the int4 operand order
 __device__ __forceinline__ int int4_slot(int j) { return (j >> 1) + ((j & 1) << 2); }
 
+// q * 2^(s - 127 + shift) for the bf16 GEMM operand (exact when in range;
+// NaN for scale 0xFF; a zero q stays zero whatever the exponent).
+__device__ __forceinline__ float operand_value(int q, uint32_t s, int shift) {
+  if (s == 255u) return __int_as_float(0x7fc00000);
+  if (q == 0) return 0.0f;
+  const int n = (int)s - 127 + shift;
+  if (n > 127) return q > 0 ? __int_as_float(0x7f800000) : __int_as_float(0xff800000);
+  return __fmul_rn((float)q, pow2_exact(n));
+}
+
 template <int MODE>
 __global__ void __launch_bounds__(256) quantize_kernel(QuantArgs a) {
   asm volatile("griddepcontrol.wait;" ::: "memory");
@@ -67,7 +77,7 @@ __global__ void __launch_bounds__(256) quantize_kernel(QuantArgs a) {
       if (a.out_s && lane == 0) a.out_s[(long)t * kb + b] = (uint8_t)sb;
     }
     if (a.opnd) {
-      const float f = valid ? __fmul_rn((float)q, e8m0_to_float(sb)) : 0.0f;
+      const float f = valid ? operand_value(q, sb, a.shift) : 0.0f;
       const int k = b * kBlock + lane;
       const int kt = k / kTileK;
       const int kin = k % kTileK;

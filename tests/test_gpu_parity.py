@@ -145,6 +145,26 @@ def test_gemm_parity(ctx, fmt, b, n, k):
     assert np.array_equal(y, y2)
 
 
+@pytest.mark.parametrize("fmt", [8, 4])
+def test_gemm_extreme_weight_scales(ctx, fmt):
+    """Weight scale bytes 245..249 (exponents 118..122): past the range where
+    the converter folds the int4/int8 offset into one fma, so the two-step
+    conversion runs; activations scaled by 2^-40 keep the products finite."""
+    n, k, b = 384, 2048, 40
+    w, ws, W = weight(ctx, fmt, n, k, 61, 118, 122)
+    x = synth.normal((b, k), 62) * np.float32(2.0 ** -40)
+    xq, xs = oracle.quantize_x(x)
+    ref = oracle.gemv(fmt, xq, xs, w, ws, n, k)
+    assert np.all(np.isfinite(ref))
+    ctx.set_path(mx.PATH_GEMM)
+    try:
+        y = host(mx.mx_gemv(mx.MXActivation(cuda(xq), cuda(xs)), W, ctx))
+        ctx.synchronize()
+    finally:
+        ctx.set_path(mx.PATH_AUTO)
+    assert rel_l2(y, ref) <= REL_TOL
+
+
 def test_golden_fixture_on_gpu(ctx):
     import os
     d = np.load(os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden", "mx_oracle.npz"))
