@@ -60,24 +60,34 @@ struct Cfg {
   static constexpr int NG = BN <= 64 ? 4 : 2;
   static constexpr int GW = kConvWarps / NG;             // warps per group
   static constexpr int GT = GW * 32;
+  static constexpr int KPS = NG;                         // k-tiles per chunk (one per group)
   static constexpr int TB = WFMT == 4 ? 32 : 64;
-  static constexpr int RAW_W = 128 * TB;
-  static constexpr int RAW_STAGE = RAW_W + 256;
+  static constexpr int RAW_W = 128 * TB;                 // packed weights of one k-tile
+  static constexpr int RAW_CHUNK = KPS * RAW_W;          // scales are read per thread
   static constexpr int RAW_TARGET = WFMT == 8 ? (BN <= 64 ? 68 * 1024 : 34 * 1024)
-                                              : (BN <= 64 ? 64 * 1024 : (BN <= 128 ? 40 * 1024 : 26 * 1024));
-  static constexpr int RS = RAW_TARGET / RAW_STAGE / NG * NG;
+                                              : (BN <= 64 ? 48 * 1024 : (BN <= 128 ? 40 * 1024 : 26 * 1024));
+  static constexpr int RSC = RAW_TARGET / RAW_CHUNK < 2 ? 2 : RAW_TARGET / RAW_CHUNK;
   static constexpr int W_TILE = 128 * 128;
-  static constexpr int WS = 4;
+  static constexpr int WS = NG;                          // one weight stage per group
   static constexpr int X_TILE = BN * 128;
+  // activation chunks of XK k-tiles, about 32 KB per copy (a multiple of KPS)
+  static constexpr int XM = KPS * X_TILE >= 32768 ? 1 : 32768 / (KPS * X_TILE);
+  static constexpr int XK = XM * KPS;
+  static constexpr int X_CHUNK = XK * X_TILE;
   static constexpr int BUDGET = 222 * 1024;
-  static constexpr int XS_FIT = (BUDGET - 2048 - RS * RAW_STAGE - WS * W_TILE) / X_TILE;
-  static constexpr int XS = XS_FIT > 16 ? 16 : XS_FIT;
-  static constexpr int TMEM_COLS = BN <= 32 ? 32 : (BN <= 64 ? 64 : (BN <= 128 ? 128 : 256));
-  static constexpr size_t OP_BYTES = (size_t)WS * W_TILE + (size_t)XS * X_TILE;
-  static constexpr size_t SMEM = 1024 + OP_BYTES + (size_t)RS * RAW_STAGE + 1024;
-  // converter work per k-tile: 32-bit words of packed weights per thread
+  static constexpr int XS_FIT = (BUDGET - 2048 - RSC * RAW_CHUNK - WS * W_TILE) / X_CHUNK;
+  static constexpr int XSC = XS_FIT > 8 ? 8 : XS_FIT;
+  // one accumulator of BN columns per group
+  static constexpr int ACC_COLS = NG * BN;
+  static constexpr int TMEM_COLS = ACC_COLS <= 32 ? 32 : (ACC_COLS <= 64 ? 64 : (ACC_COLS <= 128 ? 128 : (ACC_COLS <= 256 ? 256 : 512)));
+  static constexpr size_t OP_BYTES = (size_t)WS * W_TILE + (size_t)XSC * X_CHUNK;
+  static constexpr size_t SMEM = 1024 + OP_BYTES + (size_t)RSC * RAW_CHUNK + 1024;
+  // converter work per k-tile: 32-bit words of packed weights per thread,
+  // and the 16-byte bf16 chunks they become
   static constexpr int WORDS = 128 * TB / 4 / GT;
-  static_assert(XS >= 3 && RS >= NG && RS % NG == 0 && WS % NG == 0, "ring depths");
+  static constexpr int NCH = WFMT == 4 ? WORDS : WORDS / 2;
+  static_assert(XSC >= 2, "activation ring");
+  static_assert(ACC_COLS <= 512, "tensor memory");
   static_assert(SMEM <= 227 * 1024, "shared memory");
   static_assert(WORDS == 4 || WORDS == 8 || WORDS == 16, "converter split");
   // the split-K partial tile [BN][128] fp32 reuses the w and x rings
@@ -144,64 +154,70 @@ __device__ __forceinline__ uint2 cvt_int8_word(uint32_t w, float sc, float nb) {
   return make_uint2(*reinterpret_cast<uint32_t*>(&a), *reinterpret_cast<uint32_t*>(&b));
 }
 
-// One thread's share of one 128x64 k-tile: WORDS consecutive 32-bit words of
-// one row (int4: 4 words per 32-element scale block, 8 per row; int8: 8 per
-// block, 16 per row), converted and stored to the swizzled bf16 tile.
-template <int WFMT, int WORDS, bool FUSED>
-__device__ __forceinline__ void convert_share(const uint8_t* raw, const uint8_t* rsc, uint8_t* wt,
-                                              int row, int w0, int shift) {
+// One thread's share of one 128x64 k-tile, converted into registers: WORDS
+// consecutive 32-bit words of one row (int4: 4 words per 32-element scale
+// block; int8: 8), giving NCH 16-byte bf16 chunks starting at chunk c0 of the
+// row (int4: word i -> chunk i; int8: words 2j, 2j+1 -> chunk j).
+template <int WFMT, int WORDS, int NCH, bool FUSED>
+__device__ __forceinline__ void convert_share(const uint8_t* raw, uint32_t sc2, int row, int w0,
+                                              int shift, uint4 (&out)[NCH]) {
   if (WFMT == 4) {
-    // 32 bytes per row; word i -> output chunk i
 #pragma unroll
     for (int q = 0; q < WORDS; q += 4) {
-      const uint32_t sb = bf16x2_scale(rsc[row * 2 + ((w0 + q) >> 2)], shift);
+      const uint32_t sb = bf16x2_scale((sc2 >> (8 * ((w0 + q) >> 2))) & 0xFFu, shift);
       const __nv_bfloat162 sc = *reinterpret_cast<const __nv_bfloat162*>(&sb);
       const __nv_bfloat162 nb = FUSED ? __hmul2(__floats2bfloat162_rn(-136.0f, -136.0f), sc)
                                       : __floats2bfloat162_rn(136.0f, 136.0f);
       const uint4 v = *reinterpret_cast<const uint4*>(raw + row * 32 + (w0 + q) * 4);
-      const uint32_t words[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const uint4 o = cvt_int4_word<FUSED>(words[i], sc, nb);
-        *reinterpret_cast<uint4*>(wt + sw128_offset(row, w0 + q + i)) = o;
-      }
+      out[q + 0] = cvt_int4_word<FUSED>(v.x, sc, nb);
+      out[q + 1] = cvt_int4_word<FUSED>(v.y, sc, nb);
+      out[q + 2] = cvt_int4_word<FUSED>(v.z, sc, nb);
+      out[q + 3] = cvt_int4_word<FUSED>(v.w, sc, nb);
     }
   } else {
-    // 64 bytes per row; word pair (2j, 2j+1) -> chunk j
 #pragma unroll
     for (int q = 0; q < WORDS; q += 4) {
-      const float sc = f32_scale(rsc[row * 2 + ((w0 + q) >> 3)], shift);
+      const float sc = f32_scale((sc2 >> (8 * ((w0 + q) >> 3))) & 0xFFu, shift);
       const float nb = FUSED ? -8388736.0f * sc : 0.0f;
       const uint4 v = *reinterpret_cast<const uint4*>(raw + row * 64 + (w0 + q) * 4);
       const uint2 c0 = cvt_int8_word<FUSED>(v.x, sc, nb), c1 = cvt_int8_word<FUSED>(v.y, sc, nb);
       const uint2 c2 = cvt_int8_word<FUSED>(v.z, sc, nb), c3 = cvt_int8_word<FUSED>(v.w, sc, nb);
-      const int ch = (w0 + q) >> 1;
-      *reinterpret_cast<uint4*>(wt + sw128_offset(row, ch)) = make_uint4(c0.x, c0.y, c1.x, c1.y);
-      *reinterpret_cast<uint4*>(wt + sw128_offset(row, ch + 1)) = make_uint4(c2.x, c2.y, c3.x, c3.y);
+      out[q / 2 + 0] = make_uint4(c0.x, c0.y, c1.x, c1.y);
+      out[q / 2 + 1] = make_uint4(c2.x, c2.y, c3.x, c3.y);
     }
   }
+}
+
+__device__ __forceinline__ uint32_t ldg_u16(const uint16_t* p) {
+  unsigned short v;
+  asm volatile("ld.global.nc.u16 %0, [%1];" : "=h"(v) : "l"(p));
+  return v;
+}
+
+__device__ __forceinline__ void named_bar_sync(int id, int nthreads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
 }
 
 template <int WFMT, int BN>
 __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tc_kernel(GemmArgs a) {
   using C = Cfg<WFMT, BN>;
   constexpr int WS = C::WS;
-  constexpr int XS = C::XS;
-  constexpr int RS = C::RS;
+  constexpr int XSC = C::XSC;
+  constexpr int RSC = C::RSC;
+  constexpr int KPS = C::KPS;
   extern __shared__ uint8_t smem_raw[];
   // 1024-byte alignment for the 128B-swizzled operand tiles
   const uint32_t base_u32 = smem_u32(smem_raw);
   uint8_t* smem = smem_raw + ((1024 - (base_u32 & 1023)) & 1023);
   uint8_t* w_ring = smem;                                    // WS x W_TILE
-  uint8_t* x_ring = w_ring + WS * C::W_TILE;                 // XS x X_TILE
-  uint8_t* raw_ring = smem + C::OP_BYTES;                    // RS x RAW_STAGE
-  uint64_t* bars = reinterpret_cast<uint64_t*>(raw_ring + RS * C::RAW_STAGE);
+  uint8_t* x_ring = w_ring + WS * C::W_TILE;                 // XSC x X_CHUNK
+  uint8_t* raw_ring = smem + C::OP_BYTES;                    // RSC x RAW_CHUNK
+  uint64_t* bars = reinterpret_cast<uint64_t*>(raw_ring + RSC * C::RAW_CHUNK);
   uint64_t* raw_full = bars;
-  uint64_t* raw_empty = raw_full + RS;
-  uint64_t* x_full = raw_empty + RS;
-  uint64_t* x_empty = x_full + XS;
-  uint64_t* w_full = x_empty + XS;
-  uint64_t* w_empty = w_full + WS;
+  uint64_t* raw_empty = raw_full + RSC;
+  uint64_t* x_full = raw_empty + RSC;
+  uint64_t* x_empty = x_full + XSC;
+  uint64_t* w_empty = x_empty + XSC;
   uint64_t* acc_full = w_empty + WS;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_full + 1);
   float* part = reinterpret_cast<float*>(w_ring);            // split-K partial [BN][128]
@@ -212,23 +228,22 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tc_kernel(GemmArgs a) {
   const int S = gridDim.z;         // K splits (= cluster size)
   const int KT = a.w.Kpad / kTileK;
   const int kb = (int)blockIdx.z * KT / S;
-  const int nk = ((int)blockIdx.z + 1) * KT / S - kb;
+  const int nk = ((int)blockIdx.z + 1) * KT / S - kb;      // k-tiles of this CTA
+  const int nch = (nk + KPS - 1) / KPS;                      // chunks (the last may be short)
+  const int ngrp = nk < C::NG ? nk : C::NG;                   // groups that own k-tiles
   uint32_t* status = a.status;
 
   if (threadIdx.x == 0) {
-    for (int i = 0; i < RS; ++i) {
+    for (int i = 0; i < RSC; ++i) {
       mbar_init(&raw_full[i], 1);
-      mbar_init(&raw_empty[i], C::GW);
+      mbar_init(&raw_empty[i], kConvWarps);
     }
-    for (int i = 0; i < XS; ++i) {
+    for (int i = 0; i < XSC; ++i) {
       mbar_init(&x_full[i], 1);
-      mbar_init(&x_empty[i], 1);
+      mbar_init(&x_empty[i], C::XK);
     }
-    for (int i = 0; i < WS; ++i) {
-      mbar_init(&w_full[i], C::GW);
-      mbar_init(&w_empty[i], 1);
-    }
-    mbar_init(acc_full, 1);
+    for (int i = 0; i < WS; ++i) mbar_init(&w_empty[i], 1);
+    mbar_init(acc_full, ngrp > 0 ? ngrp : 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   if (warp == 1) tmem_alloc(tmem_slot, C::TMEM_COLS);
@@ -237,116 +252,136 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tc_kernel(GemmArgs a) {
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  // Role warps 0-2 run their loops warp-uniformly (every lane waits, the
-  // elected lane issues the copies / MMAs), so the tcgen05 and bulk-copy
-  // operands stay warp-uniform.
+  // Chunks of KPS consecutive k-tiles move as one bulk copy each (weights,
+  // scales, activations): large copies stream far better than per-tile ones.
+  // The producer warps run their loops warp-uniformly (every lane waits, the
+  // elected lane issues the copies).  Warp 1 owns the TMEM allocation.
   if (warp == 0) {
     // ------------------------------------------------ raw weight producer
     const uint8_t* wsrc = a.w.data + ((size_t)rt * KT + kb) * C::RAW_W;
-    const uint8_t* ssrc = a.w.scales + ((size_t)rt * KT + kb) * 256;
     bool ok = true;
-    int r = 0;
-    uint32_t ph = 0;
-    for (int i = 0; i < nk && ok; ++i) {
-      if (i >= RS) ok = mbar_wait(&raw_empty[r], ph ^ 1u, status);
+    for (int c = 0; c < nch && ok; ++c) {
+      const int st = c % RSC;
+      if (c >= RSC) ok = mbar_wait(&raw_empty[st], ((c / RSC) - 1) & 1, status);
       ok = __all_sync(0xffffffffu, ok);
       if (!ok) break;
       if (elect_one()) {
-        uint8_t* dst = raw_ring + r * C::RAW_STAGE;
-        mbar_arrive_expect_tx(&raw_full[r], C::RAW_STAGE);
-        bulk_g2s(dst, wsrc + (size_t)i * C::RAW_W, C::RAW_W, &raw_full[r]);
-        bulk_g2s(dst + C::RAW_W, ssrc + (size_t)i * 256, 256, &raw_full[r]);
+        const int nt_c = nk - c * KPS < KPS ? nk - c * KPS : KPS;
+        uint8_t* dst = raw_ring + st * C::RAW_CHUNK;
+        mbar_arrive_expect_tx(&raw_full[st], (uint32_t)(nt_c * C::RAW_W));
+        bulk_g2s(dst, wsrc + (size_t)c * KPS * C::RAW_W, (uint32_t)(nt_c * C::RAW_W), &raw_full[st]);
       }
       __syncwarp();
-      if (++r == RS) { r = 0; ph ^= 1u; }
     }
     // drain: the last issued copies have landed before shared memory is released
-    for (int i = nk - (nk < RS ? nk : RS); i < nk && ok; ++i)
-      ok = mbar_wait(&raw_full[i % RS], (i / RS) & 1, status);
+    for (int c = nch - (nch < RSC ? nch : RSC); c < nch && ok; ++c)
+      ok = mbar_wait(&raw_full[c % RSC], (c / RSC) & 1, status);
   } else if (warp == 2) {
     // ------------------------------------------- activation tile producer
     asm volatile("griddepcontrol.wait;" ::: "memory");
     const uint8_t* xsrc =
         reinterpret_cast<const uint8_t*>(a.opnd) + ((size_t)nt * KT + kb) * C::X_TILE;
+    const int nxc = (nk + C::XK - 1) / C::XK;
     bool ok = true;
-    int s = 0;
-    uint32_t ph = 0;
-    for (int i = 0; i < nk && ok; ++i) {
-      if (i >= XS) ok = mbar_wait(&x_empty[s], ph ^ 1u, status);
+    for (int c = 0; c < nxc && ok; ++c) {
+      const int st = c % XSC;
+      if (c >= XSC) ok = mbar_wait(&x_empty[st], ((c / XSC) - 1) & 1, status);
       ok = __all_sync(0xffffffffu, ok);
       if (!ok) break;
       if (elect_one()) {
-        mbar_arrive_expect_tx(&x_full[s], C::X_TILE);
-        bulk_g2s(x_ring + s * C::X_TILE, xsrc + (size_t)i * C::X_TILE, C::X_TILE, &x_full[s]);
+        const int nt_c = nk - c * C::XK < C::XK ? nk - c * C::XK : C::XK;
+        mbar_arrive_expect_tx(&x_full[st], (uint32_t)(nt_c * C::X_TILE));
+        bulk_g2s(x_ring + st * C::X_CHUNK, xsrc + (size_t)c * C::X_CHUNK, (uint32_t)(nt_c * C::X_TILE),
+                 &x_full[st]);
       }
       __syncwarp();
-      if (++s == XS) { s = 0; ph ^= 1u; }
     }
-    for (int i = nk - (nk < XS ? nk : XS); i < nk && ok; ++i)
-      ok = mbar_wait(&x_full[i % XS], (i / XS) & 1, status);
-  } else if (warp == 1) {
-    // ------------------------------------------------------- MMA issuer
-    const uint32_t idesc = idesc_bf16(128, BN);
-    // descriptor start-address field is address >> 4: stage and K offsets
-    // add to the prebuilt descriptors directly
-    const uint64_t wdesc = sw128_kmajor_desc(smem_u32(w_ring));
-    const uint64_t xdesc = sw128_kmajor_desc(smem_u32(x_ring));
-    bool ok = true;
-    int s = 0, sx = 0;
-    uint32_t ph = 0, phx = 0;
-    for (int i = 0; i < nk && ok; ++i) {
-      ok = mbar_wait(&w_full[s], ph, status) && mbar_wait(&x_full[sx], phx, status);
-      ok = __all_sync(0xffffffffu, ok);
-      if (!ok) break;
-      tc_fence_after();
-      const uint64_t wd = wdesc + (uint64_t)((s * C::W_TILE) >> 4);
-      const uint64_t xd = xdesc + (uint64_t)((sx * C::X_TILE) >> 4);
-      if (elect_one()) {
-#pragma unroll
-        for (int kk = 0; kk < 4; ++kk)
-          mma_bf16_ss(tmem, wd + 2 * kk, xd + 2 * kk, idesc, (i | kk) != 0 ? 1u : 0u);
-        mma_commit(&w_empty[s]);
-        mma_commit(&x_empty[sx]);
-      }
-      __syncwarp();
-      if (++s == WS) { s = 0; ph ^= 1u; }
-      if (++sx == XS) { sx = 0; phx ^= 1u; }
-    }
-    if (ok && elect_one()) mma_commit(acc_full);
-    __syncwarp();
+    for (int c = nxc - (nxc < XSC ? nxc : XSC); c < nxc && ok; ++c)
+      ok = mbar_wait(&x_full[c % XSC], (c / XSC) & 1, status);
   } else if (warp >= kRoleWarps) {
-    // ------------------------------------------ converters, then epilogue
+    // --------------------- converter groups: convert, issue MMAs, epilogue
+    // Group g takes k-tile g of every chunk and issues its MMAs into its own
+    // accumulator (TMEM columns g*BN ..), so each accumulator sums its tiles
+    // in a fixed order.  Per chunk: wait for the raw chunk, convert the
+    // group's tile into registers, release the raw chunk (every converter
+    // warp arrives once per chunk, tile or not), wait for the group's weight
+    // stage, store, fence to the async proxy, group barrier, then one elected
+    // lane of the group's issuing warp waits for the activation chunk and
+    // issues 4 MMAs.  Every warp of a group passes the group barrier once per
+    // chunk whatever happened, so a timed-out wait cannot strand the others.
     const int cw = warp - kRoleWarps;
     const int grp = cw / C::GW;
     const int gt = (cw % C::GW) * 32 + lane;           // thread within the group
+    const bool issuer = (cw % C::GW) == (grp & 3);     // spread over the SM's 4 schedulers
     constexpr int WPR = C::TB / 4;                     // words per row
     const int row = (gt * C::WORDS) / WPR, w0 = (gt * C::WORDS) % WPR;
+    const int c0 = WFMT == 4 ? w0 : w0 / 2;
     const int shift = a.w.gemm_shift;
     const bool fused = a.w.gemm_fused != 0;
+    const uint32_t idesc = idesc_bf16(128, BN);
+    uint8_t* wt = w_ring + grp * C::W_TILE;
+    const uint64_t wd = sw128_kmajor_desc(smem_u32(wt));
+    const uint64_t xdesc = sw128_kmajor_desc(smem_u32(x_ring));
+    // this thread's row's two E8M0 bytes per k-tile, straight from global
+    // memory (2 bytes per row per tile; a bulk copy of them would cost as
+    // much as a weight chunk), one chunk ahead
+    const uint16_t* srow = reinterpret_cast<const uint16_t*>(a.w.scales) + ((size_t)rt * KT + kb) * 128 + row;
+    uint32_t sc_next = grp < nk ? ldg_u16(srow + (size_t)grp * 128) : 0u;
+    const uint32_t acc = tmem + (uint32_t)(grp * BN);
     bool ok = true;
-    for (int i = grp; i < nk && ok; i += C::NG) {
-      const int r = i % RS, s = i % WS;
-      ok = mbar_wait(&raw_full[r], (i / RS) & 1, status);
-      if (ok && i >= WS) ok = mbar_wait(&w_empty[s], ((i / WS) - 1) & 1, status);
-      ok = __all_sync(0xffffffffu, ok);   // keep each warp's lanes together
-      if (!ok) break;
-      const uint8_t* raw = raw_ring + r * C::RAW_STAGE;
-      uint8_t* wt = w_ring + s * C::W_TILE;
-      if (fused)
-        convert_share<WFMT, C::WORDS, true>(raw, raw + C::RAW_W, wt, row, w0, shift);
-      else
-        convert_share<WFMT, C::WORDS, false>(raw, raw + C::RAW_W, wt, row, w0, shift);
-      // each writer makes its stores visible to the tensor core's async
-      // proxy; after the warp converges one lane arrives for all 32
-      fence_proxy_async_smem();
+    for (int c = 0; c < nch; ++c) {
+      const int rs = c % RSC;
+      const int i = c * KPS + grp;                     // this group's k-tile
+      const bool has = i < nk;                         // group-uniform
+      const uint32_t sc2 = sc_next;
+      if (i + KPS < nk) sc_next = ldg_u16(srow + (size_t)(i + KPS) * 128);
+      if (ok) ok = mbar_wait(&raw_full[rs], (c / RSC) & 1, status);
+      ok = __all_sync(0xffffffffu, ok);
+      uint4 out[C::NCH];
+      if (ok && has) {
+        const uint8_t* raw = raw_ring + rs * C::RAW_CHUNK;
+        const uint8_t* tile = raw + grp * C::RAW_W;
+        if (fused)
+          convert_share<WFMT, C::WORDS, C::NCH, true>(tile, sc2, row, w0, shift, out);
+        else
+          convert_share<WFMT, C::WORDS, C::NCH, false>(tile, sc2, row, w0, shift, out);
+      }
       __syncwarp();
-      if (lane == 0) {
-        mbar_arrive(&raw_empty[r]);
-        mbar_arrive(&w_full[s]);
+      if (ok && lane == 0) mbar_arrive(&raw_empty[rs]);
+      if (ok && has && c > 0) ok = mbar_wait(&w_empty[grp], (c - 1) & 1, status);
+      ok = __all_sync(0xffffffffu, ok);
+      if (ok && has) {
+#pragma unroll
+        for (int j = 0; j < C::NCH; ++j)
+          *reinterpret_cast<uint4*>(wt + sw128_offset(row, c0 + j)) = out[j];
+        // each writer makes its stores visible to the tensor core's async proxy
+        fence_proxy_async_smem();
+      }
+      named_bar_sync(1 + grp, C::GT);
+      if (issuer && has) {
+        const int cx = i / C::XK, xs = cx % XSC;
+        if (ok) ok = mbar_wait(&x_full[xs], (cx / XSC) & 1, status);
+        ok = __all_sync(0xffffffffu, ok);
+        if (ok) {
+          tc_fence_after();
+          const uint64_t xd = xdesc + (uint64_t)((xs * C::X_CHUNK + (i % C::XK) * C::X_TILE) >> 4);
+          if (elect_one()) {
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk)
+              mma_bf16_ss(acc, wd + 2 * kk, xd + 2 * kk, idesc, (c != 0 || kk != 0) ? 1u : 0u);
+            mma_commit(&w_empty[grp]);
+            mma_commit(&x_empty[xs]);
+          }
+          __syncwarp();
+        }
       }
     }
-    // epilogue
-    if (ok) ok = mbar_wait(acc_full, 0, status);
+    if (issuer && ok && grp < ngrp) {
+      if (elect_one()) mma_commit(acc_full);
+      __syncwarp();
+    }
+    // epilogue: sum the group accumulators in group order
+    ok = mbar_wait(acc_full, 0, status);
     ok = __all_sync(0xffffffffu, ok);     // tcgen05.ld is warp-collective
     tc_fence_after();
     if (ok) {
@@ -360,18 +395,30 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tc_kernel(GemmArgs a) {
       const uint32_t lane_base = tmem + ((uint32_t)(q * 32) << 16);
       if (h * CPG < BN) {
 #pragma unroll 1
-        for (int c = h * CPG; c < (h + 1) * CPG; c += 8) {
-          uint32_t v[8];
-          tmem_ld8(lane_base + (uint32_t)c, v);
-          tmem_ld_wait();
+        for (int cc = h * CPG; cc < (h + 1) * CPG; cc += 8) {
+          float f[8];
+          {
+            uint32_t v[8];
+            tmem_ld8(lane_base + (uint32_t)cc, v);
+            tmem_ld_wait();
+#pragma unroll
+            for (int j = 0; j < 8; ++j) f[j] = __uint_as_float(v[j]);
+          }
+          for (int g = 1; g < ngrp; ++g) {
+            uint32_t v[8];
+            tmem_ld8(lane_base + (uint32_t)(g * BN + cc), v);
+            tmem_ld_wait();
+#pragma unroll
+            for (int j = 0; j < 8; ++j) f[j] += __uint_as_float(v[j]);
+          }
           if (S > 1) {
 #pragma unroll
-            for (int j = 0; j < 8; ++j) part[(c + j) * 128 + trow] = __uint_as_float(v[j]);
+            for (int j = 0; j < 8; ++j) part[(cc + j) * 128 + trow] = f[j];
           } else {
 #pragma unroll
             for (int j = 0; j < 8; ++j) {
-              const int tok = nt * BN + c + j;
-              if (tok < a.B && row_g < a.w.N) a.y[(size_t)tok * a.w.N + row_g] = __uint_as_float(v[j]);
+              const int tok = nt * BN + cc + j;
+              if (tok < a.B && row_g < a.w.N) a.y[(size_t)tok * a.w.N + row_g] = f[j];
             }
           }
         }
