@@ -42,6 +42,7 @@ SIGNATURES = {
     "mxq_last_error": [_vp],
     "mxq_launch_count": [_vp, ctypes.POINTER(ctypes.c_uint64)],
     "mxq_weight_create": [_vp, _i, _sz, _sz, _vp, _vp, _i, ctypes.POINTER(_vp)],
+    "mxq_weight_create_bsr": [_vp, _i, _sz, _sz, _vp, _vp, _vp, _i, ctypes.POINTER(_vp)],
     "mxq_weight_destroy": [_vp],
     "mxq_weight_shape": [_vp, ctypes.POINTER(_i), ctypes.POINTER(_sz), ctypes.POINTER(_sz)],
     "mxq_quantize_x": [_vp, _vp, _sz, _sz, _i, _vp, _vp],
@@ -56,6 +57,7 @@ SIGNATURES = {
     "mxq_mlp_swiglu": [_vp, _vp, _vp, _vp, _vp, _sz, _vp],
     "mxq_linear_noalloc": [_vp, _vp, _vp, _sz, _vp],
     "mxq_route_topk": [_vp, _vp, _sz, _sz, _sz, _vp, _vp],
+    "mxq_moe_swiglu": [_vp, _vp, _vp, _vp, _sz, _vp, _vp, _sz, _sz, _vp],
     "mxq_gae": [_vp, _vp, _vp, _vp, _vp, _sz, _sz, _f, _f, _vp, _vp],
 }
 

@@ -7,6 +7,7 @@
 #include <cstdarg>
 #include <new>
 #include <string>
+#include <vector>
 
 #include "../../include/mxq.h"
 #include "mxq_internal.h"
@@ -29,6 +30,10 @@ struct mxq_context {
   float* ws_f1 = nullptr;    size_t ws_f1_bytes = 0;
   float* ws_in = nullptr;    size_t ws_in_bytes = 0;   // host-call staging
   float* ws_out = nullptr;   size_t ws_out_bytes = 0;
+  // MoE: routing bookkeeping, per-route expert outputs, pinned route counts
+  int32_t* ws_moe = nullptr; size_t ws_moe_bytes = 0;
+  float* ws_yr = nullptr;    size_t ws_yr_bytes = 0;
+  int32_t* moe_counts_host = nullptr; size_t moe_counts_cap = 0;
 };
 
 struct mxq_weight_s {
@@ -36,6 +41,7 @@ struct mxq_weight_s {
   WeightView v{};
   uint8_t* data = nullptr;
   uint8_t* scales = nullptr;
+  int32_t* tiles = nullptr;   // block-sparse: kt_ptr then kt_idx (device)
 };
 
 namespace {
@@ -106,6 +112,30 @@ __global__ void repack_kernel(const uint8_t* __restrict__ data,
       const int b = kt * 2 + h;
       os[dst * 2 + h] = (n < N && b < K / kBlock) ? scales[(long)n * (K / kBlock) + b] : 127;
     }
+  }
+}
+
+// Block-sparse repack: one thread per (stored tile, row).  Stored tile ti
+// holds k-tile tile_kt[ti] of row tile tile_rt[ti]; rows whose 64x64 block
+// is masked out (or beyond N) are stored as zero weights with scale 127.
+__global__ void repack_bsr_kernel(const uint8_t* __restrict__ data,
+                                  const uint8_t* __restrict__ scales,
+                                  const uint8_t* __restrict__ mask, int fmt, int N, int K,
+                                  const int32_t* __restrict__ tile_rt, const int32_t* __restrict__ tile_kt,
+                                  long ntiles, uint8_t* __restrict__ od, uint8_t* __restrict__ os) {
+  const int TB = fmt == 4 ? 32 : 64;
+  const int row_bytes = fmt == 4 ? K / 2 : K;
+  const int KB = K / kTileK;
+  for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < ntiles * 128;
+       i += (long)gridDim.x * blockDim.x) {
+    const long ti = i / 128;
+    const int r = (int)(i % 128);
+    const int n = tile_rt[ti] * 128 + r, kt = tile_kt[ti];
+    const bool keep = n < N && mask[(long)(n / 64) * KB + kt] != 0;
+    for (int j = 0; j < TB; ++j)
+      od[i * TB + j] = keep ? data[(long)n * row_bytes + (long)kt * TB + j] : 0;
+    for (int h = 0; h < 2; ++h)
+      os[i * 2 + h] = keep ? scales[(long)n * (K / kBlock) + kt * 2 + h] : 127;
   }
 }
 
@@ -193,7 +223,8 @@ int check_weight(mxq_context* c, mxq_weight w) {
   return MXQ_OK;
 }
 
-int use_gemv(mxq_context* c, size_t b) {
+int use_gemv(mxq_context* c, size_t b, const mxq_weight_s* w) {
+  if (w->v.kt_ptr) return 0;   // block-sparse: the GEMM walks the tile list
   if (c->path == MXQ_PATH_GEMV) return 1;
   if (c->path == MXQ_PATH_GEMM) return 0;
   return b <= (size_t)kGemvAutoBatch;
@@ -229,7 +260,7 @@ int linear_dev(mxq_context* c, mxq_weight w, const float* x, size_t b, float* y,
                int act) {
   const int K = w->v.K;
   int rc;
-  if (use_gemv(c, b)) {
+  if (use_gemv(c, b, w)) {
     if (b > (size_t)gemv_max_batch())
       return fail(c, MXQ_ERR_INVALID_ARGUMENT, "GEMV path supports batch <= %d", gemv_max_batch());
     if (act == MXQ_ACT_NONE) return gemv_f32(c, w, x, b, y, nullptr);
@@ -280,7 +311,7 @@ int linear_dev(mxq_context* c, mxq_weight w, const float* x, size_t b, float* y,
 int gemv_dev(mxq_context* c, mxq_weight w, const uint8_t* xq, const uint8_t* xs,
              size_t b, float* y) {
   int rc;
-  if (use_gemv(c, b)) {
+  if (use_gemv(c, b, w)) {
     if (b > (size_t)gemv_max_batch())
       return fail(c, MXQ_ERR_INVALID_ARGUMENT, "GEMV path supports batch <= %d", gemv_max_batch());
     GemvArgs ga{};
@@ -382,6 +413,9 @@ int mxq_destroy(mxq_ctx c) {
     cudaFree(c->ws_f1);
     cudaFree(c->ws_in);
     cudaFree(c->ws_out);
+    cudaFree(c->ws_moe);
+    cudaFree(c->ws_yr);
+    if (c->moe_counts_host) cudaFreeHost(c->moe_counts_host);
     delete c;
     return MXQ_OK;
   })
@@ -514,11 +548,126 @@ int mxq_weight_create(mxq_ctx c, int fmt, size_t n, size_t k, const void* data,
   })
 }
 
+int mxq_weight_create_bsr(mxq_ctx c, int fmt, size_t n, size_t k, const void* data,
+                          const uint8_t* scales, const uint8_t* block_mask, int on_device,
+                          mxq_weight* out) {
+  MXQ_TRY({
+    if (int rc = check_ctx(c)) return rc;
+    if (!out || !data || !scales || !block_mask) return fail(c, MXQ_ERR_INVALID_ARGUMENT, "null pointer");
+    *out = nullptr;
+    if (fmt != MXQ_FMT_INT4 && fmt != MXQ_FMT_INT8)
+      return fail(c, MXQ_ERR_INVALID_ARGUMENT, "unknown weight format %d", fmt);
+    if (n == 0 || k == 0 || k % kTileK)
+      return fail(c, MXQ_ERR_INVALID_ARGUMENT, "block-sparse weight %zux%zu: K must be a positive multiple of 64", n, k);
+    if (n > (1u << 24) || k > (1u << 24))
+      return fail(c, MXQ_ERR_INVALID_ARGUMENT, "weight shape %zux%zu too large", n, k);
+    DeviceGuard g(c->device);
+    const int N = (int)n, K = (int)k;
+    const int Npad = (N + 255) / 256 * 256, Kpad = K;
+    const int T = Npad / 128, KB = K / kTileK, NB = (N + 63) / 64;
+    // host-side tile list: a 128x64 tile is stored when either 64-row half
+    // has its block present
+    std::vector<int32_t> ptr(T + 1, 0), rt_of, kt_of;
+    for (int rt = 0; rt < T; ++rt) {
+      for (int kt = 0; kt < KB; ++kt) {
+        bool any = false;
+        for (int h = 0; h < 2; ++h) {
+          const int br = rt * 2 + h;
+          if (br < NB && block_mask[(size_t)br * KB + kt]) any = true;
+        }
+        if (any) {
+          rt_of.push_back(rt);
+          kt_of.push_back(kt);
+        }
+      }
+      ptr[rt + 1] = (int32_t)rt_of.size();
+    }
+    const long ntiles = (long)rt_of.size();
+    const int TB = fmt == 4 ? 32 : 64;
+    const size_t src_bytes = fmt == 4 ? n * k / 2 : n * k;
+    const size_t sc_bytes = n * k / kBlock;
+    const size_t mask_bytes = (size_t)NB * KB;
+    auto* w = new mxq_weight_s();
+    w->ctx = c;
+    const size_t nt_alloc = ntiles > 0 ? (size_t)ntiles : 1;
+    cudaError_t e = cudaMalloc(&w->data, nt_alloc * 128 * TB);
+    if (e == cudaSuccess) e = cudaMalloc(&w->scales, nt_alloc * 256);
+    if (e == cudaSuccess) e = cudaMalloc(&w->tiles, (T + 1 + nt_alloc) * sizeof(int32_t));
+    uint8_t* tmp = nullptr;
+    int32_t* dlist = nullptr;
+    const size_t tmp_bytes = (on_device ? 0 : src_bytes + sc_bytes) + mask_bytes;
+    if (e == cudaSuccess) e = cudaMalloc(&tmp, tmp_bytes);
+    if (e == cudaSuccess) e = cudaMalloc(&dlist, 2 * nt_alloc * sizeof(int32_t));
+    const uint8_t* src_d = static_cast<const uint8_t*>(data);
+    const uint8_t* src_s = scales;
+    uint8_t* dmask = tmp + (on_device ? 0 : src_bytes + sc_bytes);
+    if (e == cudaSuccess && !on_device) {
+      e = cudaMemcpy(tmp, data, src_bytes, cudaMemcpyHostToDevice);
+      if (e == cudaSuccess) e = cudaMemcpy(tmp + src_bytes, scales, sc_bytes, cudaMemcpyHostToDevice);
+      src_d = tmp;
+      src_s = tmp + src_bytes;
+    }
+    if (e == cudaSuccess) e = cudaMemcpy(dmask, block_mask, mask_bytes, cudaMemcpyHostToDevice);
+    if (e == cudaSuccess) e = cudaMemcpy(w->tiles, ptr.data(), (T + 1) * sizeof(int32_t), cudaMemcpyHostToDevice);
+    if (e == cudaSuccess && ntiles > 0) {
+      e = cudaMemcpy(w->tiles + T + 1, kt_of.data(), ntiles * sizeof(int32_t), cudaMemcpyHostToDevice);
+      if (e == cudaSuccess) e = cudaMemcpy(dlist, rt_of.data(), ntiles * sizeof(int32_t), cudaMemcpyHostToDevice);
+      if (e == cudaSuccess)
+        e = cudaMemcpy(dlist + ntiles, kt_of.data(), ntiles * sizeof(int32_t), cudaMemcpyHostToDevice);
+      if (e == cudaSuccess) {
+        long ctas = (ntiles * 128 + 255) / 256;
+        if (ctas > 148L * 32) ctas = 148L * 32;
+        repack_bsr_kernel<<<(unsigned)ctas, 256, 0, c->stream>>>(src_d, src_s, dmask, fmt, N, K, dlist,
+                                                                 dlist + ntiles, ntiles, w->data, w->scales);
+        e = cudaGetLastError();
+      }
+    }
+    uint32_t range[3] = {255, 0, 0};
+    uint32_t* drange = nullptr;
+    if (e == cudaSuccess) e = cudaMalloc(&drange, sizeof(range));
+    if (e == cudaSuccess) e = cudaMemcpyAsync(drange, range, sizeof(range), cudaMemcpyHostToDevice, c->stream);
+    if (e == cudaSuccess && ntiles > 0) e = launch_scale_range(w->scales, (size_t)ntiles * 256, drange, c->stream);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(range, drange, sizeof(range), cudaMemcpyDeviceToHost, c->stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(c->stream);
+    if (drange) cudaFree(drange);
+    if (dlist) cudaFree(dlist);
+    if (tmp) cudaFree(tmp);
+    if (e != cudaSuccess) {
+      cudaFree(w->data);
+      cudaFree(w->scales);
+      cudaFree(w->tiles);
+      delete w;
+      return cuda_fail(c, e, "block-sparse weight upload");
+    }
+    if (ntiles == 0) range[0] = range[1] = range[2] = 127;
+    w->v.fmt = fmt;
+    w->v.N = N;
+    w->v.K = K;
+    w->v.Npad = Npad;
+    w->v.Kpad = Kpad;
+    w->v.data = w->data;
+    w->v.scales = w->scales;
+    w->v.scale_lo = (int)range[0];
+    w->v.scale_hi = (int)range[1];
+    {
+      const int emax = (int)range[2] - 127, lim = fmt == 8 ? 120 : 124;
+      w->v.gemm_shift = emax > lim ? emax - lim : 0;
+      w->v.gemm_fused = (int)range[2] - w->v.gemm_shift <= (fmt == 8 ? 231 : 246);
+    }
+    w->v.kt_ptr = w->tiles;
+    w->v.kt_idx = w->tiles + T + 1;
+    w->v.nnz_tiles = (int)ntiles;
+    *out = w;
+    return MXQ_OK;
+  })
+}
+
 int mxq_weight_destroy(mxq_weight w) {
   if (!w) return fail(nullptr, MXQ_ERR_INVALID_ARGUMENT, "null weight handle");
   DeviceGuard g(w->ctx->device);
   cudaFree(w->data);
   cudaFree(w->scales);
+  if (w->tiles) cudaFree(w->tiles);
   delete w;
   return MXQ_OK;
 }
@@ -578,12 +727,17 @@ int mxq_gemv(mxq_ctx c, mxq_weight w, const uint8_t* xq, const uint8_t* xs,
   })
 }
 
+static int reject_sparse(mxq_context* c, mxq_weight w, const char* what) {
+  return w->v.kt_ptr ? fail(c, MXQ_ERR_UNSUPPORTED, "%s: not available for block-sparse weights", what) : MXQ_OK;
+}
+
 int mxq_gather_dot(mxq_ctx c, mxq_weight w, const uint8_t* xq, const uint8_t* xs,
                    size_t b, const int32_t* rows, size_t nrows, float* y) {
   if (int rc = check_ctx(c)) return rc;
   if (int rc = check_weight(c, w)) return rc;
   if (!xq || !xs || !rows || !y || b == 0 || nrows == 0)
     return fail(c, MXQ_ERR_INVALID_ARGUMENT, "null pointer or empty input");
+  if (int rc = reject_sparse(c, w, "gather_dot")) return rc;
   if (b > (size_t)gemv_max_batch())
     return fail(c, MXQ_ERR_INVALID_ARGUMENT, "gather_dot supports batch <= %d", gemv_max_batch());
   if (!aligned16(xq)) return fail(c, MXQ_ERR_INVALID_ARGUMENT, "activation must be 16-byte aligned");
@@ -603,6 +757,7 @@ int mxq_block_dots(mxq_ctx c, mxq_weight w, const uint8_t* xq, size_t b, int32_t
   if (int rc = check_ctx(c)) return rc;
   if (int rc = check_weight(c, w)) return rc;
   if (!xq || !dots || b == 0) return fail(c, MXQ_ERR_INVALID_ARGUMENT, "null pointer or empty batch");
+  if (int rc = reject_sparse(c, w, "block_dots")) return rc;
   if (!aligned16(xq)) return fail(c, MXQ_ERR_INVALID_ARGUMENT, "activation must be 16-byte aligned");
   DeviceGuard g(c->device);
   GemvArgs ga{};
@@ -635,7 +790,7 @@ int mxq_linear_pair(mxq_ctx c, mxq_weight w1, mxq_weight w2, const float* x,
     DeviceGuard g(c->device);
     int rc;
     if ((rc = ensure(c, c->ws_f0, c->ws_f0_bytes, b * w1->v.N * 4, "workspace mid"))) return rc;
-    if (use_gemv(c, b)) {
+    if (use_gemv(c, b, w1) && use_gemv(c, b, w2)) {
       // decode: two launches; each GEMV quantises its fp32 input itself and
       // the first warms L2 with the second's weights while it streams
       if ((rc = gemv_f32(c, w1, x, b, c->ws_f0, w2))) return rc;
@@ -729,6 +884,138 @@ int mxq_mlp_swiglu(mxq_ctx c, mxq_weight wg, mxq_weight wu, mxq_weight wd,
     qa.out_s = hs;
     if ((rc = after_launch(c, launch_quantize(qa, 2, c->stream, true), "swiglu quantize"))) return rc;
     return gemv_dev(c, wd, hq, hs, b, y);
+  })
+}
+
+// Expert layer operand: rows gathered from x (slot -> token row), quantised
+// per 32-block into the tensor-core operand for weight w.
+static int moe_operand(mxq_context* c, mxq_weight w, const float* x, const int32_t* gather, int b, int K,
+                       int BN, int Bpad) {
+  QuantArgs qa{};
+  qa.x = x;
+  qa.gather = gather;
+  qa.B = b;
+  qa.K = K;
+  qa.opnd = reinterpret_cast<__nv_bfloat16*>(c->ws_op);
+  qa.Bpad = Bpad;
+  qa.Kpad = w->v.Kpad;
+  qa.BN = BN;
+  qa.int4_order = w->v.fmt == 4;
+  qa.shift = w->v.gemm_shift;
+  return after_launch(c, launch_quantize(qa, 0, c->stream, true), "moe operand");
+}
+
+static int moe_gemm(mxq_context* c, mxq_weight w, int b, int BN, int Bpad, float* y) {
+  GemmArgs ga{};
+  ga.w = w->v;
+  ga.opnd = reinterpret_cast<const __nv_bfloat16*>(c->ws_op);
+  ga.y = y;
+  ga.B = b;
+  ga.Bpad = Bpad;
+  ga.BN = BN;
+  ga.status = c->status;
+  return after_launch(c, launch_gemm(ga, c->stream, true), "moe gemm");
+}
+
+int mxq_moe_swiglu(mxq_ctx c, const mxq_weight* w_gate, const mxq_weight* w_up,
+                   const mxq_weight* w_down, size_t n_experts, const float* x,
+                   const float* logits, size_t t, size_t k, float* y) {
+  MXQ_TRY({
+    if (int rc = check_ctx(c)) return rc;
+    if (!w_gate || !w_up || !w_down || !x || !logits || !y || n_experts == 0)
+      return fail(c, MXQ_ERR_INVALID_ARGUMENT, "null pointer or no experts");
+    if (k == 0 || k > n_experts)
+      return fail(c, MXQ_ERR_INVALID_ARGUMENT, "top-k: k=%zu must be in [1, n_experts=%zu]", k, n_experts);
+    if (k > 64 || n_experts > 4096) return fail(c, MXQ_ERR_UNSUPPORTED, "top-k: k <= 64 and n_experts <= 4096");
+    const int E = (int)n_experts;
+    for (int e = 0; e < E; ++e) {
+      if (int rc = check_weight(c, w_gate[e])) return rc;
+      if (int rc = check_weight(c, w_up[e])) return rc;
+      if (int rc = check_weight(c, w_down[e])) return rc;
+    }
+    const int D = w_gate[0]->v.K, F = w_gate[0]->v.N;
+    for (int e = 0; e < E; ++e) {
+      const WeightView &g = w_gate[e]->v, &u = w_up[e]->v, &d = w_down[e]->v;
+      if (g.K != D || g.N != F || u.K != D || u.N != F || d.K != F || d.N != D)
+        return fail(c, MXQ_ERR_INVALID_ARGUMENT,
+                    "expert %d shapes: gate/up must be [%d][%d] and down [%d][%d]", e, F, D, D, F);
+    }
+    if (t == 0) return MXQ_OK;
+    if (t > (1u << 24) || t * k > (1u << 26)) return fail(c, MXQ_ERR_INVALID_ARGUMENT, "too many tokens");
+    DeviceGuard g(c->device);
+    const int T = (int)t, K = (int)k, R = T * K;
+    int rc;
+    // bookkeeping: idx[R] gate[R] counts[E] offsets[E+1] slot_token[R] route_pos[R]
+    const size_t moe_ints = (size_t)4 * R + 2 * E + 1;
+    if ((rc = ensure(c, c->ws_moe, c->ws_moe_bytes, moe_ints * 4, "workspace moe"))) return rc;
+    int32_t* idx = c->ws_moe;
+    float* gate = reinterpret_cast<float*>(idx + R);
+    int32_t* counts = idx + 2 * R;
+    int32_t* offsets = counts + E;
+    int32_t* slot_token = offsets + E + 1;
+    int32_t* route_pos = slot_token + R;
+    route_topk_kernel<<<(unsigned)((T + 127) / 128), 128, 0, c->stream>>>(logits, T, E, K, idx, gate);
+    if ((rc = after_launch(c, cudaGetLastError(), "moe route"))) return rc;
+    if ((rc = after_launch(c, launch_moe_assign(idx, T, K, E, counts, offsets, slot_token, route_pos,
+                                                c->stream), "moe assign")))
+      return rc;
+    // the per-expert launches are sized on the host: one small read-back
+    if ((size_t)E > c->moe_counts_cap) {
+      if (c->moe_counts_host) cudaFreeHost(c->moe_counts_host);
+      c->moe_counts_host = nullptr;
+      c->moe_counts_cap = 0;
+      if (cudaError_t e = cudaHostAlloc(&c->moe_counts_host, (size_t)E * 4, cudaHostAllocDefault))
+        return cuda_fail(c, e, "moe counts");
+      c->moe_counts_cap = (size_t)E;
+    }
+    if (cudaError_t e = cudaMemcpyAsync(c->moe_counts_host, counts, (size_t)E * 4, cudaMemcpyDeviceToHost,
+                                        c->stream))
+      return cuda_fail(c, e, "moe counts");
+    if (cudaError_t e = cudaStreamSynchronize(c->stream)) return cuda_fail(c, e, "moe counts");
+    int nmax = 0;
+    for (int e = 0; e < E; ++e) nmax = c->moe_counts_host[e] > nmax ? c->moe_counts_host[e] : nmax;
+    if (nmax > 0) {
+      const int BNm = gemm_pick_bn(nmax);
+      const size_t Bpm = (size_t)(nmax + BNm - 1) / BNm * BNm;
+      int kmax = 0;
+      for (int e = 0; e < E; ++e) {
+        kmax = w_gate[e]->v.Kpad > kmax ? w_gate[e]->v.Kpad : kmax;
+        kmax = w_up[e]->v.Kpad > kmax ? w_up[e]->v.Kpad : kmax;
+        kmax = w_down[e]->v.Kpad > kmax ? w_down[e]->v.Kpad : kmax;
+      }
+      if ((rc = ensure(c, c->ws_op, c->ws_op_bytes, Bpm * kmax * 2, "workspace operand"))) return rc;
+      if ((rc = ensure(c, c->ws_f0, c->ws_f0_bytes, (size_t)nmax * F * 4, "workspace gate"))) return rc;
+      if ((rc = ensure(c, c->ws_f1, c->ws_f1_bytes, (size_t)nmax * F * 4, "workspace up"))) return rc;
+    }
+    if ((rc = ensure(c, c->ws_yr, c->ws_yr_bytes, (size_t)R * D * 4, "workspace expert outputs"))) return rc;
+    int off = 0;
+    for (int e = 0; e < E; ++e) {
+      const int ne = c->moe_counts_host[e];
+      if (ne == 0) continue;
+      const int BN = gemm_pick_bn(ne), Bpad = (ne + BN - 1) / BN * BN;
+      const WeightView &gv = w_gate[e]->v, &uv = w_up[e]->v;
+      if ((rc = moe_operand(c, w_gate[e], x, slot_token + off, ne, D, BN, Bpad))) return rc;
+      if ((rc = moe_gemm(c, w_gate[e], ne, BN, Bpad, c->ws_f0))) return rc;
+      if (uv.fmt != gv.fmt || uv.gemm_shift != gv.gemm_shift || uv.Kpad != gv.Kpad)
+        if ((rc = moe_operand(c, w_up[e], x, slot_token + off, ne, D, BN, Bpad))) return rc;
+      if ((rc = moe_gemm(c, w_up[e], ne, BN, Bpad, c->ws_f1))) return rc;
+      // silu(gate) * up -> the down projection's operand
+      QuantArgs qa{};
+      qa.x = c->ws_f0;
+      qa.up = c->ws_f1;
+      qa.B = ne;
+      qa.K = F;
+      qa.opnd = reinterpret_cast<__nv_bfloat16*>(c->ws_op);
+      qa.Bpad = Bpad;
+      qa.Kpad = w_down[e]->v.Kpad;
+      qa.BN = BN;
+      qa.int4_order = w_down[e]->v.fmt == 4;
+      qa.shift = w_down[e]->v.gemm_shift;
+      if ((rc = after_launch(c, launch_quantize(qa, 2, c->stream, true), "moe swiglu"))) return rc;
+      if ((rc = moe_gemm(c, w_down[e], ne, BN, Bpad, c->ws_yr + (size_t)off * D))) return rc;
+      off += ne;
+    }
+    return after_launch(c, launch_moe_combine(c->ws_yr, gate, route_pos, T, D, K, y, c->stream), "moe combine");
   })
 }
 

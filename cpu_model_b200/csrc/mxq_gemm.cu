@@ -226,9 +226,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tc_kernel(GemmArgs a) {
   const int rt = blockIdx.x;       // 128-row weight tile
   const int nt = blockIdx.y;       // token tile
   const int S = gridDim.z;         // K splits (= cluster size)
-  const int KT = a.w.Kpad / kTileK;
-  const int kb = (int)blockIdx.z * KT / S;
-  const int nk = ((int)blockIdx.z + 1) * KT / S - kb;      // k-tiles of this CTA
+  const int KT = a.w.Kpad / kTileK;                         // k-tiles of the operand
+  // this row tile's stored k-tiles: all KT (dense) or its block-sparse list
+  const bool sparse = a.w.kt_ptr != nullptr;
+  const int tbase = sparse ? a.w.kt_ptr[rt] : rt * KT;
+  const int ntot = sparse ? a.w.kt_ptr[rt + 1] - tbase : KT;
+  const int kb = (int)blockIdx.z * ntot / S;
+  const int nk = ((int)blockIdx.z + 1) * ntot / S - kb;    // k-tiles of this CTA (may be 0)
   const int nch = (nk + KPS - 1) / KPS;                      // chunks (the last may be short)
   const int ngrp = nk < C::NG ? nk : C::NG;                   // groups that own k-tiles
   uint32_t* status = a.status;
@@ -258,7 +262,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tc_kernel(GemmArgs a) {
   // elected lane issues the copies).  Warp 1 owns the TMEM allocation.
   if (warp == 0) {
     // ------------------------------------------------ raw weight producer
-    const uint8_t* wsrc = a.w.data + ((size_t)rt * KT + kb) * C::RAW_W;
+    const uint8_t* wsrc = a.w.data + ((size_t)tbase + kb) * C::RAW_W;
     bool ok = true;
     for (int c = 0; c < nch && ok; ++c) {
       const int st = c % RSC;
@@ -291,8 +295,18 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tc_kernel(GemmArgs a) {
       if (elect_one()) {
         const int nt_c = nk - c * C::XK < C::XK ? nk - c * C::XK : C::XK;
         mbar_arrive_expect_tx(&x_full[st], (uint32_t)(nt_c * C::X_TILE));
-        bulk_g2s(x_ring + st * C::X_CHUNK, xsrc + (size_t)c * C::X_CHUNK, (uint32_t)(nt_c * C::X_TILE),
-                 &x_full[st]);
+        if (!sparse) {
+          bulk_g2s(x_ring + st * C::X_CHUNK, xsrc + (size_t)c * C::X_CHUNK, (uint32_t)(nt_c * C::X_TILE),
+                   &x_full[st]);
+        } else {
+          // the stored k-tiles are not contiguous in K: one copy per tile
+          const uint8_t* xrow = reinterpret_cast<const uint8_t*>(a.opnd) + (size_t)nt * KT * C::X_TILE;
+          for (int j = 0; j < nt_c; ++j) {
+            const int kx = a.w.kt_idx[tbase + kb + c * C::XK + j];
+            bulk_g2s(x_ring + st * C::X_CHUNK + j * C::X_TILE, xrow + (size_t)kx * C::X_TILE, C::X_TILE,
+                     &x_full[st]);
+          }
+        }
       }
       __syncwarp();
     }
@@ -325,7 +339,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tc_kernel(GemmArgs a) {
     // this thread's row's two E8M0 bytes per k-tile, straight from global
     // memory (2 bytes per row per tile; a bulk copy of them would cost as
     // much as a weight chunk), one chunk ahead
-    const uint16_t* srow = reinterpret_cast<const uint16_t*>(a.w.scales) + ((size_t)rt * KT + kb) * 128 + row;
+    const uint16_t* srow = reinterpret_cast<const uint16_t*>(a.w.scales) + ((size_t)tbase + kb) * 128 + row;
     uint32_t sc_next = grp < nk ? ldg_u16(srow + (size_t)grp * 128) : 0u;
     const uint32_t acc = tmem + (uint32_t)(grp * BN);
     bool ok = true;
@@ -380,8 +394,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tc_kernel(GemmArgs a) {
       if (elect_one()) mma_commit(acc_full);
       __syncwarp();
     }
-    // epilogue: sum the group accumulators in group order
-    ok = mbar_wait(acc_full, 0, status);
+    // epilogue: sum the group accumulators in group order (a CTA with no
+    // stored k-tiles -- an all-zero row tile of a block-sparse weight, or an
+    // empty split -- writes zeros)
+    if (ngrp > 0) ok = mbar_wait(acc_full, 0, status);
     ok = __all_sync(0xffffffffu, ok);     // tcgen05.ld is warp-collective
     tc_fence_after();
     if (ok) {
@@ -396,8 +412,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tc_kernel(GemmArgs a) {
       if (h * CPG < BN) {
 #pragma unroll 1
         for (int cc = h * CPG; cc < (h + 1) * CPG; cc += 8) {
-          float f[8];
-          {
+          float f[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+          if (ngrp > 0) {
             uint32_t v[8];
             tmem_ld8(lane_base + (uint32_t)cc, v);
             tmem_ld_wait();
@@ -530,8 +546,11 @@ cudaError_t launch_t(const GemmArgs& a, cudaStream_t st, bool pdl) {
     if (e != cudaSuccess) return e;
     configured = true;
   }
-  const int T = a.w.Npad / 128, NT = a.Bpad / BN, KT = a.w.Kpad / kTileK;
-  const int S = a.splits > 0 ? (a.splits < KT ? a.splits : KT) : pick_splits<WFMT, BN>(T * NT, KT);
+  const int T = a.w.Npad / 128, NT = a.Bpad / BN;
+  // k-tiles per row tile: all of K, or the block-sparse average
+  const int KT = a.w.kt_ptr ? (a.w.nnz_tiles + T - 1) / T : a.w.Kpad / kTileK;
+  const int S = a.splits > 0 ? (a.splits < KT ? a.splits : (KT > 0 ? KT : 1))
+                             : pick_splits<WFMT, BN>(T * NT, KT > 0 ? KT : 1);
   if (S > kMaxSplits) return cudaErrorInvalidValue;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)T, (unsigned)NT, (unsigned)S);

@@ -26,10 +26,17 @@ struct WeightView {
   // times the scale) finite: every finite scale byte minus gemm_shift
   // <= 246 (int4) / 231 (int8).  A NaN scale byte gives NaN on either form.
   int gemm_fused;
+  // Block-sparse weights (mxq_weight_create_bsr): row tile rt keeps only the
+  // k-tiles kt_idx[kt_ptr[rt] .. kt_ptr[rt+1]), stored compactly in that
+  // order (data [tile][128][TB], scales [tile][128][2]).  Null when dense.
+  const int32_t* kt_ptr;
+  const int32_t* kt_idx;
+  int nnz_tiles;
 };
 
 struct QuantArgs {
   const float* x;        // fp32 input [B][K] (modes 0-2; gate for mode 2)
+  const int32_t* gather; // optional (mode 0): source row of x per output row (MoE dispatch)
   const float* up;       // up projection (mode 2)
   const uint8_t* in_q;   // MX input (mode 3)
   const uint8_t* in_s;
@@ -84,6 +91,15 @@ constexpr int kGemvAutoBatch = 4;
 constexpr int kRgemvMaxBatch = 4;
 bool rgemv_supported(const WeightView& w, int B);
 cudaError_t launch_rgemv(const GemvArgs& a, cudaStream_t st, bool pdl);
+
+// MoE bookkeeping (mxq_moe.cu): per-expert route counts, slot offsets, the
+// token row gathered into each slot, the slot of each route; the weighted
+// combine of the k expert outputs per token.
+cudaError_t launch_moe_assign(const int32_t* idx, int T, int k, int E, int32_t* counts,
+                              int32_t* offsets, int32_t* slot_token, int32_t* route_pos,
+                              cudaStream_t st);
+cudaError_t launch_moe_combine(const float* yr, const float* gate, const int32_t* route_pos, int T,
+                               int D, int k, float* y, cudaStream_t st);
 
 cudaError_t launch_scale_range(const uint8_t* scales, size_t count, uint32_t* out2,
                                cudaStream_t st);

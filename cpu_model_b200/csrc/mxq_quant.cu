@@ -54,7 +54,7 @@ __global__ void __launch_bounds__(256) quantize_kernel(QuantArgs a) {
         sb = a.in_s[(long)t * kb + b];
       } else {
         float v;
-        if (MODE == 0) v = a.x[idx];
+        if (MODE == 0) v = a.x[a.gather ? (long)a.gather[t] * a.K + (long)b * kBlock + lane : idx];
         else if (MODE == 1) v = det_silu(a.x[idx]);
         else v = det_swiglu(a.x[idx], a.up[idx]);
         const float av = fabsf(v);

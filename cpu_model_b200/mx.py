@@ -113,9 +113,13 @@ class MXWeight:
     """MXINT8Tensor (int8 [N][K] or int4 packed [N][K/2]) + E8M0 scales
     [N][K/32], uploaded once into the library's tiled device layout."""
 
-    def __init__(self, data, scales, fmt, n, k, ctx=None):
+    def __init__(self, data, scales, fmt, n, k, ctx=None, block_mask=None):
+        """block_mask (optional): host uint8 [ceil(n/64)][k/64], nonzero =
+        64x64 block present; the weight is then stored block-sparse
+        (mxq_weight_create_bsr) and masked-out blocks read as zero."""
         self.ctx = ctx or context()
         self.fmt, self.n, self.k = fmt, n, k
+        self.block_sparse = block_mask is not None
         data = torch.as_tensor(data)
         scales = torch.as_tensor(scales)
         exp_bytes = n * k // (2 if fmt == FMT_INT4 else 1)
@@ -130,8 +134,15 @@ class MXWeight:
             raise ValueError("data and scales must both be host or both be device tensors")
         h = ctypes.c_void_p()
         self.ctx._bind()
-        check(self.ctx.lib.mxq_weight_create(self.ctx.h, fmt, n, k, _ptr(data), _ptr(scales), on_dev,
-                                             ctypes.byref(h)), self.ctx.h)
+        if block_mask is None:
+            check(self.ctx.lib.mxq_weight_create(self.ctx.h, fmt, n, k, _ptr(data), _ptr(scales), on_dev,
+                                                 ctypes.byref(h)), self.ctx.h)
+        else:
+            mask = torch.as_tensor(block_mask).to(torch.uint8).contiguous().cpu()
+            if mask.numel() != ((n + 63) // 64) * (k // 64):
+                raise ValueError("block mask has %d entries, expected %d" % (mask.numel(), ((n + 63) // 64) * (k // 64)))
+            check(self.ctx.lib.mxq_weight_create_bsr(self.ctx.h, fmt, n, k, _ptr(data), _ptr(scales), _ptr(mask),
+                                                     on_dev, ctypes.byref(h)), self.ctx.h)
         self.h = h
 
     def close(self):
@@ -338,3 +349,25 @@ def fused_compute_gae(rewards, values, dones, next_values, gamma=0.99, lam=0.95,
     check(ctx.lib.mxq_gae(ctx.h, _ptr(rewards), _ptr(values), _ptr(dones), _ptr(next_values), t, e,
                           float(gamma), float(lam), _ptr(adv), _ptr(ret)), ctx.h)
     return adv, ret
+
+
+def moe_swiglu(x, logits, gate_w, up_w, down_w, k, ctx=None):
+    """Top-k SwiGLU mixture-of-experts layer (mxq_moe_swiglu): x fp32 [T][D]
+    and router logits [T][E] on the device; gate_w/up_w/down_w lists of E
+    MXWeight ([F][D], [F][D], [D][F], dense or block-sparse).  Returns y
+    [T][D].  k > E raises ValueError (the HashedRouter contract)."""
+    ctx = ctx or context()
+    _need_cuda(x, torch.float32, "x")
+    _need_cuda(logits, torch.float32, "logits")
+    t, d = x.shape
+    e = len(gate_w)
+    if logits.shape != (t, e) or len(up_w) != e or len(down_w) != e:
+        raise ValueError("moe: logits must be [T][E] with E gate/up/down weights")
+    arr = lambda ws: (ctypes.c_void_p * e)(*[w.h.value for w in ws])
+    g, u, dn = arr(gate_w), arr(up_w), arr(down_w)
+    y = torch.empty((t, d), dtype=torch.float32, device=x.device)
+    ctx._bind()
+    check(ctx.lib.mxq_moe_swiglu(ctx.h, ctypes.cast(g, ctypes.c_void_p), ctypes.cast(u, ctypes.c_void_p),
+                                 ctypes.cast(dn, ctypes.c_void_p), e, _ptr(x), _ptr(logits), t, k, _ptr(y)),
+          ctx.h)
+    return y

@@ -43,3 +43,23 @@ def weights(fmt, n, k, emin, emax, seed):
 
 def normal(shape, seed):
     return rng(seed).standard_normal(size=shape, dtype=np.float32)
+
+
+def block_mask(n, k, density, seed, block=64):
+    """uint8 [ceil(n/64)][k/64]: each 64x64 block present with probability
+    `density` (uniform-random mask, as the block-sparse MoE layer uses)."""
+    g = rng(seed)
+    return (g.random(((n + block - 1) // block, k // block)) < density).astype(np.uint8)
+
+
+def apply_block_mask(fmt, data, mask, block=64):
+    """Copy of `data` ([n][k] int8, or [n][k/2] packed int4) with every
+    masked-out 64x64 block set to zero weights."""
+    out = data.copy()
+    nb, kb = mask.shape
+    per = block // 2 if fmt == 4 else block   # bytes of one block row
+    for br in range(nb):
+        for bc in range(kb):
+            if not mask[br, bc]:
+                out[br * block:(br + 1) * block, bc * per:(bc + 1) * per] = 0
+    return out

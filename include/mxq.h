@@ -95,6 +95,17 @@ MXQ_API int mxq_launch_count(mxq_ctx ctx, uint64_t* out);
 MXQ_API int mxq_weight_create(mxq_ctx ctx, int fmt, size_t n, size_t k,
                               const void* data, const uint8_t* scales,
                               int on_device, mxq_weight* out);
+/* Block-sparse MX weight for the MoE expert matrices (the gathered-row
+ * expert pool of nn/tests/autotest.hpp:126-136 as 64x64-block sparse
+ * matrices): the same dense data/scales as mxq_weight_create plus a host
+ * byte mask [ceil(n/64)][k/64] (nonzero = block present).  Only tiles with a
+ * present block are stored; masked-out blocks read as zero.  K must be a
+ * multiple of 64.  Linears on such a weight always take the tensor-core
+ * path; mxq_gather_dot and mxq_block_dots return MXQ_ERR_UNSUPPORTED. */
+MXQ_API int mxq_weight_create_bsr(mxq_ctx ctx, int fmt, size_t n, size_t k,
+                                  const void* data, const uint8_t* scales,
+                                  const uint8_t* block_mask, int on_device,
+                                  mxq_weight* out);
 MXQ_API int mxq_weight_destroy(mxq_weight w);
 MXQ_API int mxq_weight_shape(mxq_weight w, int* fmt, size_t* n, size_t* k);
 
@@ -172,6 +183,22 @@ MXQ_API int mxq_linear_noalloc(mxq_ctx ctx, mxq_weight w, const float* x,
 MXQ_API int mxq_route_topk(mxq_ctx ctx, const float* logits, size_t t,
                            size_t n_experts, size_t k, int32_t* idx,
                            float* gate);
+
+/* Top-k SwiGLU mixture-of-experts layer (the expert execution behind
+ * mx_rank16_dot_ptrs, nn/tests/test_auto_generated.cpp:55, with the 1024 x
+ * 16-row micro-experts of nn/config/model_config.hpp:23-25 generalised to
+ * block-sparse expert matrices): routes with mxq_route_topk's contract over
+ * logits [T][E], then per expert e: y_e = down_e(quant(silu(gate_e(x)) *
+ * up_e(x))) on the tokens routed to it, and y[t] = sum_j gate_j * y_{e_j}[t]
+ * in routing order.  w_gate/w_up: E weights [F][D]; w_down: E weights
+ * [D][F] (dense or block-sparse).  x [T][D], logits [T][E], y [T][D], all
+ * device pointers.  Reads back the per-expert token counts once (a stream
+ * synchronisation) to size the expert launches. */
+MXQ_API int mxq_moe_swiglu(mxq_ctx ctx, const mxq_weight* w_gate,
+                           const mxq_weight* w_up, const mxq_weight* w_down,
+                           size_t n_experts, const float* x,
+                           const float* logits, size_t t, size_t k,
+                           float* y);
 
 /* ---------------------------------------------------------------- GAE --- */
 /* nca::env::ReplayMemory::fused_compute_gae

@@ -245,3 +245,52 @@ def test_gae_matches_reference_build_live():
     a0, r0 = oracle.gae(r, v, dn, nv, 0.97, 0.9)
     a1, r1 = oracle.ref_gae(r, v, dn, nv, 0.97, 0.9)
     assert np.array_equal(a0, a1) and np.array_equal(r0, r1)
+
+
+# ------------------------------------------------- block-sparse MoE ---
+def test_block_mask_helpers():
+    m = synth.block_mask(200, 256, 0.25, 3)
+    assert m.shape == (4, 4) and set(np.unique(m)) <= {0, 1}
+    big = synth.block_mask(4096, 4096, 0.25, 4)
+    assert abs(big.mean() - 0.25) < 0.02
+    for fmt in (8, 4):
+        w, _ = synth.weights(fmt, 128, 128, -8, -3, 5)
+        mask = np.array([[1, 0], [0, 1]], np.uint8)
+        wm = synth.apply_block_mask(fmt, w, mask)
+        vals = synth.unpack_int4(wm) if fmt == 4 else wm
+        full = synth.unpack_int4(w) if fmt == 4 else w
+        assert np.all(vals[:64, 64:] == 0) and np.all(vals[64:, :64] == 0)
+        assert np.array_equal(vals[:64, :64], full[:64, :64]) and np.array_equal(vals[64:, 64:], full[64:, 64:])
+
+
+@pytest.mark.parametrize("fmt", [4, 8])
+def test_moe_oracle_composes_its_primitives(fmt):
+    """mxo_moe equals the oracle's own quantise / GEMV / SwiGLU-quantise /
+    top-k primitives composed in Python with an fp64 combine."""
+    t, d, f, e, k = 6, 64, 128, 3, 2
+    x = synth.normal((t, d), 1)
+    logits = synth.normal((t, e), 2)
+    experts = []
+    for j in range(e):
+        wg, sg = synth.weights(fmt, f, d, -6, -3, 10 + j)
+        wu, su = synth.weights(fmt, f, d, -6, -3, 20 + j)
+        wd, sd = synth.weights(fmt, d, f, -6, -3, 30 + j)
+        mg = synth.block_mask(f, d, 0.5, 40 + j)
+        md = synth.block_mask(d, f, 0.5, 50 + j)
+        experts.append((synth.apply_block_mask(fmt, wg, mg), sg, synth.apply_block_mask(fmt, wu, mg), su,
+                        synth.apply_block_mask(fmt, wd, md), sd))
+    y = oracle.moe(fmt, x, logits, d, f, k, experts)
+    idx, gate = oracle.route_topk(logits, k)
+    xq, xs = oracle.quantize_x(x)
+    ref = np.zeros((t, d), np.float64)
+    for ti in range(t):
+        for j in range(k):
+            wg, sg, wu, su, wd, sd = experts[idx[ti, j]]
+            g = oracle.gemv(fmt, xq[ti:ti + 1], xs[ti:ti + 1], wg, sg, f, d)
+            u = oracle.gemv(fmt, xq[ti:ti + 1], xs[ti:ti + 1], wu, su, f, d)
+            hq, hs = oracle.swiglu_quantize(g, u)
+            out = oracle.gemv(fmt, hq, hs, wd, sd, d, f)
+            ref[ti] += np.float64(gate[ti, j]) * out[0].astype(np.float64)
+    assert np.array_equal(y, ref.astype(np.float32))
+    with pytest.raises(ValueError):
+        oracle.moe(fmt, x, logits, d, f, e + 1, experts)
