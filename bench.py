@@ -36,6 +36,9 @@ DOWN = (4096, 11008)
 EMIN, EMAX = -8, -3
 COPIES = 8
 SWEEP = [8, 64, 512]
+# block-sparse MoE layer: 4096 tokens, d 4096, 8 experts, top-2, SwiGLU FFN
+# 14336, MX-int4 expert matrices with 25 % of their 64x64 blocks present
+MOE = {"tokens": 4096, "d": 4096, "ffn": 14336, "experts": 8, "top_k": 2, "density": 0.25}
 
 
 def pair_bytes(b):
@@ -154,6 +157,64 @@ def cpu_pair_sample(seconds=10.0, batch=1, threads=0):
                 steps, batch, el, "AVX-512 VNNI dpbusd" if used else "portable int loop")}
 
 
+def moe_weights(ctx, dev, seed=7):
+    """Per expert (gate [F][D], up [F][D], down [D][F]) block-sparse MX-int4
+    weights generated on the device (uniform int4 nibbles, exponents
+    [EMIN, EMAX]) with uniform-random 64x64 block masks; returns the weight
+    handles, the masks and the raw device data (for the CPU sample)."""
+    import torch
+    from cpu_model_b200 import mx, synth
+    g = torch.Generator(device=dev)
+    g.manual_seed(seed)
+    d, f = MOE["d"], MOE["ffn"]
+    experts = []
+    for e in range(MOE["experts"]):
+        mats = []
+        for j, (n, k) in enumerate(((f, d), (f, d), (d, f))):
+            data = torch.randint(0, 256, (n, k // 2), dtype=torch.uint8, device=dev, generator=g)
+            sc = torch.randint(127 + EMIN, 127 + EMAX + 1, (n, k // 32), dtype=torch.uint8, device=dev, generator=g)
+            mask = synth.block_mask(n, k, MOE["density"], seed * 1000 + e * 10 + j)
+            mats.append((mx.MXWeight(data, sc, 4, n, k, ctx, block_mask=mask), mask, data, sc))
+        experts.append(mats)
+    return experts
+
+
+def cpu_moe_sample(experts, x, logits, tokens=16, threads=0):
+    """The same layer on the host for a few tokens: routing and requantisation
+    from the oracle, each expert linear by the multi-threaded dpbusd
+    restatement (oracle/mx_cpu_baseline.c) on the masked dense weights."""
+    from oracle import oracle
+    from cpu_model_b200 import synth
+    d, f, k = MOE["d"], MOE["ffn"], MOE["top_k"]
+    host = []
+    for mats in experts:
+        hm = []
+        for (W, mask, data, sc) in mats:
+            w = synth.apply_block_mask(4, data.cpu().numpy(), mask)
+            s_ = sc.cpu().numpy()
+            hm.append((w, s_, oracle.weight_sums(4, w, W.n, W.k)))
+        host.append(hm)
+    xs_h = x[:tokens].cpu().numpy()
+    idx, gate = oracle.route_topk(logits[:tokens].cpu().numpy(), k)
+    used = False
+    t0 = time.perf_counter()
+    for t in range(tokens):
+        xq, xs = oracle.quantize_x(xs_h[t:t + 1])
+        acc = np.zeros(d, np.float64)
+        for j in range(k):
+            (wg, sg, zg), (wu, su, zu), (wd, sd, zd) = host[idx[t, j]]
+            gv, used = oracle.baseline_gemv(4, xq, xs, wg, sg, zg, f, d, threads)
+            uv, _ = oracle.baseline_gemv(4, xq, xs, wu, su, zu, f, d, threads)
+            hq, hs = oracle.swiglu_quantize(gv, uv)
+            out, _ = oracle.baseline_gemv(4, hq, hs, wd, sd, zd, d, f, threads)
+            acc += np.float64(gate[t, j]) * out[0]
+    el = time.perf_counter() - t0
+    cores = threads if threads > 0 else oracle.max_threads()
+    return {"value": tokens / el, "unit": "tokens/s", "cores": cores, "kind": "port",
+            "sample": "%d tokens x top-%d experts, dense masked weights (%.1f s), %s" % (
+                tokens, k, el, "AVX-512 VNNI dpbusd" if used else "portable int loop")}
+
+
 def run_reference(args):
     rank, world, _ = dist_env()
     if rank != 0:
@@ -180,6 +241,55 @@ def run_reference(args):
         "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
+
+
+def time_moe(ctx, dev, args, world, max_over_ranks, barrier, peaks, rank):
+    """The block-sparse MoE layer (mxq_moe_swiglu) at its full size: whole
+    layer calls timed with CUDA events (each call reads the per-expert token
+    counts back once to size its launches, so the loop is not captured)."""
+    import torch
+    from cpu_model_b200 import mx, synth
+    experts = moe_weights(ctx, dev)
+    gate_w = [m[0][0] for m in experts]
+    up_w = [m[1][0] for m in experts]
+    down_w = [m[2][0] for m in experts]
+    t, d, e, k = MOE["tokens"], MOE["d"], MOE["experts"], MOE["top_k"]
+    x = torch.from_numpy(synth.normal((t, d), 201)).to(dev)
+    logits = torch.from_numpy(synth.normal((t, e), 202)).to(dev)
+    for _ in range(2):
+        mx.moe_swiglu(x, logits, gate_w, up_w, down_w, k, ctx)
+    ctx.synchronize()
+    steps = max(3, args.steps // 20)
+    barrier()
+    torch.cuda.synchronize()
+    stream = torch.cuda.current_stream()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(steps):
+        mx.moe_swiglu(x, logits, gate_w, up_w, down_w, k, ctx)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ctx.synchronize()
+    ms = max_over_ranks(e0.elapsed_time(e1) / steps)
+    # algorithmic (nonzero-block) work: 2 flops per stored nonzero weight per
+    # route, over the experts the routing actually chose
+    idx, _ = mx.route_topk(logits, k, ctx)
+    counts = np.bincount(idx.cpu().numpy().ravel(), minlength=e)
+    nnz = [sum(int(m[1].sum()) * 64 * 64 for m in mats) for mats in experts]
+    flops = 2.0 * float(sum(int(counts[j]) * nnz[j] for j in range(e)))
+    out = {"tokens_per_s": world * t / (ms / 1e3), "ms_per_step": ms, "steps": steps,
+           "nonzero_tflops": flops / (ms / 1e3) / 1e12,
+           "frac_of_bf16_peak": flops / (ms / 1e3) / 1e12 / peaks["bf16_tflops"],
+           "nonzero_gop_per_step": flops / 1e9,
+           "config": dict(MOE, weights="mx-int4 block-sparse 64x64", routing="softmax top-2 over N(0,1) logits"),
+           "api": "mxq_moe_swiglu"}
+    if rank == 0 and world == 1 and not args.no_cpu:
+        out["cpu_baseline"] = cpu_moe_sample(experts, x, logits)
+    for mats in experts:
+        for m in mats:
+            m[0].close()
+    return out
 
 
 def workload_config(batch, copies=COPIES):
@@ -349,6 +459,10 @@ def run_ours(args):
         entry["path"] = "gemv-dp4a" if sb <= 4 else "tcgen05-bf16"
         sweep[str(sb)] = entry
 
+    moe = None
+    if not args.no_moe:
+        moe = time_moe(ctx, dev, args, world, max_over_ranks, barrier, peaks, rank)
+
     if rank == 0:
         line = {
             "metric": "MX-int4 qlinear tokens/s (7B MLP up+down pair)",
@@ -368,6 +482,8 @@ def run_ours(args):
             "clocks": clocks,
             "sweep": sweep,
         }
+        if moe is not None:
+            line["moe"] = moe
         if world == 1 and not args.no_cpu:
             line["cpu_baseline"] = cpu_pair_sample(seconds=args.cpu_seconds, batch=b)
         print(json.dumps(line), flush=True)
@@ -390,6 +506,7 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-sweep", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--no-moe", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--copies", type=int, default=COPIES,
                     help="distinct weight-pair copies rotated per step (default 8 = 383 MB)")
