@@ -10,8 +10,8 @@
 // 7B MLP 18-19 groups of the up projection, 6-7 of the down projection per
 // CTA).  Inside a CTA the 16 warps split K; a warp streams its K-slice of
 // every group it owns, straight from HBM into registers (128-bit
-// ld.global.nc, no L1 allocation), with two batches of loads in flight
-// (64 KB per SM).  In the tiled weight layout a group's k-tile is 128 (int4)
+// ld.global.nc, no L1 allocation), with two batches of 8 loads in flight
+// (128 KB per SM).  In the tiled weight layout a group's k-tile is 128 (int4)
 // or 256 (int8) contiguous bytes, so one warp load covers 4 (2) k-tiles of the
 // group in full 128-byte lines.  Partial sums stay inside the CTA: each warp
 // folds its lanes with shuffles, writes one value per row to shared memory,
@@ -32,7 +32,7 @@ namespace {
 
 constexpr int kWarps = 16;
 constexpr int kThreads = kWarps * 32;
-constexpr int kD = 4;   // loads per batch (two batches in flight)
+constexpr int kD = 8;   // loads per batch (two batches in flight)
 
 template <int WFMT>
 struct RCfg {
