@@ -13,6 +13,7 @@
 #include <stdexcept>
 #include <string>
 #include <utility>
+#include <vector>
 
 #include "mxq.h"
 
@@ -81,6 +82,15 @@ class MXINT8Tensor {
       k_ = o.k_;
     }
     return *this;
+  }
+  // Block-sparse form (64x64 blocks; block_mask host bytes [ceil(rows/64)][k/64]).
+  MXINT8Tensor(const Context& ctx, int fmt, size_t rows, size_t k, const void* data,
+               const uint8_t* scales, const uint8_t* block_mask, bool on_device) {
+    mxq_check(mxq_weight_create_bsr(ctx.get(), fmt, rows, k, data, scales, block_mask, on_device ? 1 : 0,
+                                    &w_),
+              ctx.get());
+    rows_ = rows;
+    k_ = k;
   }
   MXINT8Tensor(const MXINT8Tensor&) = delete;
   MXINT8Tensor& operator=(const MXINT8Tensor&) = delete;
@@ -165,6 +175,26 @@ inline void gated_mlp_step(const nca::linalg::Context& c, const float* x, size_t
                            const nca::linalg::MXINT8Tensor& up,
                            const nca::linalg::MXINT8Tensor& down, float* y) {
   nca::linalg::mxq_check(mxq_mlp_swiglu(c.get(), gate.handle(), up.handle(), down.handle(), x, batch, y),
+                         c.get());
+}
+
+// Top-k SwiGLU mixture-of-experts layer over E experts (gate/up [F][D],
+// down [D][F]); x [T][D], logits [T][E], y [T][D] on the device.  k > E
+// throws std::invalid_argument like HashedRouter.
+inline void moe_swiglu(const nca::linalg::Context& c, const std::vector<const nca::linalg::MXINT8Tensor*>& gate,
+                       const std::vector<const nca::linalg::MXINT8Tensor*>& up,
+                       const std::vector<const nca::linalg::MXINT8Tensor*>& down, const float* x,
+                       const float* logits, size_t tokens, size_t k, float* y) {
+  nca::linalg::require(gate.size() == up.size() && gate.size() == down.size() && !gate.empty(),
+                       "moe_swiglu: gate/up/down expert lists differ in length");
+  std::vector<mxq_weight> g, u, d;
+  for (size_t e = 0; e < gate.size(); ++e) {
+    g.push_back(gate[e]->handle());
+    u.push_back(up[e]->handle());
+    d.push_back(down[e]->handle());
+  }
+  nca::linalg::mxq_check(mxq_moe_swiglu(c.get(), g.data(), u.data(), d.data(), gate.size(), x, logits,
+                                        tokens, k, y),
                          c.get());
 }
 
