@@ -1,0 +1,74 @@
+"""Rank bodies for the multi-process (gloo, CPU) tests of
+cpu_model_b200.shard: the exchange logic runs for real over
+torch.distributed, the per-rank compute is the CPU oracle."""
+import os
+
+import numpy as np
+import torch
+import torch.distributed as dist
+
+from oracle import oracle
+from cpu_model_b200 import shard, synth
+
+
+def _init(rank, world, port):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+
+
+def oracle_linear(fmt, k):
+    def linear(x, w):
+        data, scales, n = w
+        xq, xs = oracle.quantize_x(x.numpy())
+        return torch.from_numpy(oracle.gemv(fmt, xq, xs, data, scales, n, k))
+    return linear
+
+
+def row_slice(fmt, data, scales):
+    def fn(lo, hi):
+        return (np.ascontiguousarray(data[lo:hi]), np.ascontiguousarray(scales[lo:hi]), hi - lo)
+    return fn
+
+
+def pair_worker(rank, world, port, fmt, b, d, f, outdir):
+    _init(rank, world, port)
+    wu, su = synth.weights(fmt, f, d, -7, -3, 1)
+    wd, sd = synth.weights(fmt, d, f, -7, -3, 2)
+    up = shard.ColumnShardedLinear(f, row_slice(fmt, wu, su), oracle_linear(fmt, d))
+    down = shard.ColumnShardedLinear(d, row_slice(fmt, wd, sd), oracle_linear(fmt, f))
+    x = torch.from_numpy(synth.normal((b, d), 3))
+    y = shard.sharded_pair(x, up, down)
+    np.save(os.path.join(outdir, "pair_%d.npy" % rank), y.numpy())
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+def moe_experts(fmt, e, d, f):
+    out = []
+    for j in range(e):
+        wg, sg = synth.weights(fmt, f, d, -7, -3, 10 + j)
+        wu, su = synth.weights(fmt, f, d, -7, -3, 20 + j)
+        wd, sd = synth.weights(fmt, d, f, -7, -3, 30 + j)
+        mg, md = synth.block_mask(f, d, 0.5, 40 + j), synth.block_mask(d, f, 0.5, 50 + j)
+        out.append((synth.apply_block_mask(fmt, wg, mg), sg, synth.apply_block_mask(fmt, wu, mg), su,
+                    synth.apply_block_mask(fmt, wd, md), sd))
+    return out
+
+
+def moe_worker(rank, world, port, fmt, t, d, f, e, k, outdir):
+    _init(rank, world, port)
+    experts = moe_experts(fmt, e, d, f)
+    x = synth.normal((t, d), 100 + rank)
+    logits = synth.normal((t, e), 200 + rank)
+    idx, gate = oracle.route_topk(logits, k)
+
+    def expert_mlp(j, rows):
+        wg, sg, wu, su, wd, sd = experts[j]
+        return torch.from_numpy(oracle.mlp_swiglu(fmt, rows.numpy(), d, f, wg, sg, wu, su, wd, sd)[0])
+
+    y = shard.moe_expert_parallel(torch.from_numpy(x), torch.from_numpy(idx), torch.from_numpy(gate), e,
+                                  expert_mlp)
+    np.save(os.path.join(outdir, "moe_%d.npy" % rank), y.numpy())
+    dist.barrier()
+    dist.destroy_process_group()

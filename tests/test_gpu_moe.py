@@ -121,6 +121,7 @@ def test_moe_matches_oracle(ctx, fmt, t, d, f, e, k, density):
     x = synth.normal((t, d), 7)
     logits = synth.normal((t, e), 8)
     ref = oracle.moe(fmt, x, logits, d, f, k, host_w)
+    assert np.linalg.norm(ref) > 0
     xd, ld = cuda(x), cuda(logits)
     g, u, dn = ([w[i] for w in dev_w] for i in range(3))
     y = host(mx.moe_swiglu(xd, ld, g, u, dn, k, ctx))
@@ -137,13 +138,14 @@ def test_moe_matches_oracle(ctx, fmt, t, d, f, e, k, density):
 def test_moe_idle_experts_and_errors(ctx):
     """Experts that receive no token are skipped; k > E is rejected with the
     router's invalid-argument contract."""
-    t, d, f, e, k = 16, 128, 128, 4, 1
+    t, d, f, e, k = 16, 128, 256, 4, 1
     host_w, dev_w = make_experts(ctx, 4, e, d, f, 0.5, 300)
     x = synth.normal((t, d), 9)
     logits = synth.normal((t, e), 10)
     logits[:, 1] -= 100.0       # experts 1 and 3 never win
     logits[:, 3] -= 100.0
     ref = oracle.moe(4, x, logits, d, f, k, host_w)
+    assert np.linalg.norm(ref) > 0
     g, u, dn = ([w[i] for w in dev_w] for i in range(3))
     y = host(mx.moe_swiglu(cuda(x), cuda(logits), g, u, dn, k, ctx))
     ctx.synchronize()

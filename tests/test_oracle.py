@@ -267,7 +267,7 @@ def test_block_mask_helpers():
 def test_moe_oracle_composes_its_primitives(fmt):
     """mxo_moe equals the oracle's own quantise / GEMV / SwiGLU-quantise /
     top-k primitives composed in Python with an fp64 combine."""
-    t, d, f, e, k = 6, 64, 128, 3, 2
+    t, d, f, e, k = 6, 128, 256, 3, 2
     x = synth.normal((t, d), 1)
     logits = synth.normal((t, e), 2)
     experts = []
@@ -291,6 +291,7 @@ def test_moe_oracle_composes_its_primitives(fmt):
             hq, hs = oracle.swiglu_quantize(g, u)
             out = oracle.gemv(fmt, hq, hs, wd, sd, d, f)
             ref[ti] += np.float64(gate[ti, j]) * out[0].astype(np.float64)
+    assert np.linalg.norm(ref) > 0
     assert np.array_equal(y, ref.astype(np.float32))
     with pytest.raises(ValueError):
         oracle.moe(fmt, x, logits, d, f, e + 1, experts)
