@@ -157,18 +157,21 @@ def cpu_pair_sample(seconds=10.0, batch=1, threads=0):
                 steps, batch, el, "AVX-512 VNNI dpbusd" if used else "portable int loop")}
 
 
-def moe_weights(ctx, dev, seed=7):
+def moe_weights(ctx, dev, seed=7, experts_range=None):
     """Per expert (gate [F][D], up [F][D], down [D][F]) block-sparse MX-int4
     weights generated on the device (uniform int4 nibbles, exponents
     [EMIN, EMAX]) with uniform-random 64x64 block masks; returns the weight
-    handles, the masks and the raw device data (for the CPU sample)."""
+    handles, the masks and the raw device data (for the CPU sample).  Each
+    expert has its own seed, so any subset (expert parallelism) holds the
+    same bytes as the full set."""
     import torch
     from cpu_model_b200 import mx, synth
     g = torch.Generator(device=dev)
-    g.manual_seed(seed)
     d, f = MOE["d"], MOE["ffn"]
     experts = []
-    for e in range(MOE["experts"]):
+    lo, hi = experts_range or (0, MOE["experts"])
+    for e in range(lo, hi):
+        g.manual_seed(seed * 1000 + e)
         mats = []
         for j, (n, k) in enumerate(((f, d), (f, d), (d, f))):
             data = torch.randint(0, 256, (n, k // 2), dtype=torch.uint8, device=dev, generator=g)
@@ -286,6 +289,88 @@ def time_moe(ctx, dev, args, world, max_over_ranks, barrier, peaks, rank):
            "api": "mxq_moe_swiglu"}
     if rank == 0 and world == 1 and not args.no_cpu:
         out["cpu_baseline"] = cpu_moe_sample(experts, x, logits)
+    for mats in experts:
+        for m in mats:
+            m[0].close()
+    return out
+
+
+def time_sharded(ctx, dev, args, world, rank, max_over_ranks, barrier):
+    """N > 1 only: the multi-GPU forms of the path, over NCCL.
+    pair -- the MLP pair column-sharded (each rank owns F/N rows of up and
+    D/N rows of down, full K), one all-gather after each linear; one token
+    stream of `batch`, so tokens/s does not multiply with N (strong scaling).
+    moe -- the MoE layer with the 8 experts partitioned over the ranks and
+    the 4096 tokens split over them, routes dispatched and returned with
+    all_to_all_single."""
+    import torch
+    from cpu_model_b200 import mx, shard, synth
+    out = {}
+    up_full = synth.weights(4, UP[0], UP[1], EMIN, EMAX, 301)
+    dn_full = synth.weights(4, DOWN[0], DOWN[1], EMIN, EMAX, 302)
+
+    def slice_weight(full, n, k):
+        def fn(lo, hi):
+            w, s_ = full
+            return mx.MXWeight(torch.from_numpy(np.ascontiguousarray(w[lo:hi])),
+                               torch.from_numpy(np.ascontiguousarray(s_[lo:hi])), 4, hi - lo, k, ctx)
+        return fn
+
+    lin = lambda x, w: mx.mx_linear(x, w, ctx)
+    up = shard.ColumnShardedLinear(UP[0], slice_weight(up_full, *UP), lin)
+    down = shard.ColumnShardedLinear(DOWN[0], slice_weight(dn_full, *DOWN), lin)
+    pair = {}
+    for b in (1, 64):
+        x = torch.from_numpy(synth.normal((b, UP[1]), 303)).to(dev)
+        for _ in range(args.warmup):
+            shard.sharded_pair(x, up, down)
+        steps = max(10, args.steps // 4)
+        barrier()
+        torch.cuda.synchronize()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(steps):
+            shard.sharded_pair(x, up, down)
+        e1.record()
+        torch.cuda.synchronize()
+        ms = max_over_ranks(e0.elapsed_time(e1) / steps)
+        pair[str(b)] = {"ms_per_step": ms, "tokens_per_s": b / (ms / 1e3)}
+    up.w.close()
+    down.w.close()
+    out["pair_column_sharded"] = dict(pair, scaling="strong", collective="all_gather (NCCL) after each linear")
+
+    e_lo, e_hi = shard.row_shards(MOE["experts"], world)[rank]
+    experts = moe_weights(ctx, dev, experts_range=(e_lo, e_hi))
+    local = {e_lo + i: (m[0][0], m[1][0], m[2][0]) for i, m in enumerate(experts)}
+    t_local = MOE["tokens"] // world
+    x = torch.from_numpy(synth.normal((MOE["tokens"], MOE["d"]), 201)).to(dev)[rank * t_local:(rank + 1) * t_local]
+    logits = torch.from_numpy(synth.normal((MOE["tokens"], MOE["experts"]), 202)).to(dev)[rank * t_local:(rank + 1) * t_local]
+
+    def expert_mlp(e, rows):
+        g, u, d_ = local[e]
+        return mx.gated_mlp_step(rows, g, u, d_, ctx)
+
+    def layer():
+        idx, gate = mx.route_topk(logits.contiguous(), MOE["top_k"], ctx)
+        return shard.moe_expert_parallel(x.contiguous(), idx, gate, MOE["experts"], expert_mlp)
+
+    for _ in range(2):
+        layer()
+    steps = max(3, args.steps // 20)
+    barrier()
+    torch.cuda.synchronize()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        layer()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = max_over_ranks(e0.elapsed_time(e1) / steps)
+    out["moe_expert_parallel"] = {"ms_per_step": ms, "tokens_per_s": MOE["tokens"] / (ms / 1e3),
+                                  "experts_per_rank": e_hi - e_lo, "tokens_per_rank": t_local,
+                                  "collective": "all_to_all_single (NCCL) dispatch + return"}
     for mats in experts:
         for m in mats:
             m[0].close()
@@ -462,6 +547,9 @@ def run_ours(args):
     moe = None
     if not args.no_moe:
         moe = time_moe(ctx, dev, args, world, max_over_ranks, barrier, peaks, rank)
+    sharded = None
+    if world > 1 and not args.no_shard:
+        sharded = time_sharded(ctx, dev, args, world, rank, max_over_ranks, barrier)
 
     if rank == 0:
         line = {
@@ -484,6 +572,8 @@ def run_ours(args):
         }
         if moe is not None:
             line["moe"] = moe
+        if sharded is not None:
+            line["sharded"] = sharded
         if world == 1 and not args.no_cpu:
             line["cpu_baseline"] = cpu_pair_sample(seconds=args.cpu_seconds, batch=b)
         print(json.dumps(line), flush=True)
@@ -507,6 +597,7 @@ def main():
     ap.add_argument("--no-sweep", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-moe", action="store_true")
+    ap.add_argument("--no-shard", action="store_true", help="N > 1: skip the column-sharded / expert-parallel forms")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--copies", type=int, default=COPIES,
                     help="distinct weight-pair copies rotated per step (default 8 = 383 MB)")
