@@ -295,6 +295,86 @@ def time_moe(ctx, dev, args, world, max_over_ranks, barrier, peaks, rank):
     return out
 
 
+# the reference's PPO rollout forward (training/ppo_trainer.cpp:57-66, :77):
+# states 1616 -> latent 2048 -> 80 logits + value, MX-int8 weights; 256
+# rollouts x 512 steps per batch, then GAE (gamma 0.99, lambda 0.95)
+PPO = {"rollouts": 256, "steps": 512, "state": 1616, "state_padded": 1632, "latent": 2048, "actions": 80}
+
+
+def time_ppo(ctx, dev, args, world, max_over_ranks, barrier, peaks, rank):
+    """One rollout batch through the MX policy forward and GAE (data
+    parallel: every rank its own batch)."""
+    import torch
+    from cpu_model_b200 import mx, synth
+    p = PPO
+    rows = p["rollouts"] * p["steps"]
+    wp, sp = synth.weights(8, p["latent"], p["state_padded"], -9, -5, 401)
+    wpi, spi = synth.weights(8, p["actions"], p["latent"], -9, -5, 402)
+    wv, sv = synth.weights(8, 1, p["latent"], -9, -5, 403)
+    Wp = mx.MXWeight(torch.from_numpy(wp), torch.from_numpy(sp), 8, p["latent"], p["state_padded"], ctx)
+    Wpi = mx.MXWeight(torch.from_numpy(wpi), torch.from_numpy(spi), 8, p["actions"], p["latent"], ctx)
+    Wv = mx.MXWeight(torch.from_numpy(wv), torch.from_numpy(sv), 8, 1, p["latent"], ctx)
+    g = torch.Generator(device=dev)
+    g.manual_seed(404)
+    states = torch.randn((rows, p["state_padded"]), generator=g, device=dev)
+    states[:, p["state"]:] = 0.0
+    actions = torch.nn.functional.one_hot(torch.randint(0, p["actions"], (rows,), generator=g, device=dev),
+                                          p["actions"]).float()
+    rewards = torch.randn((p["steps"], p["rollouts"]), generator=g, device=dev)
+    dones = torch.zeros((p["steps"], p["rollouts"]), dtype=torch.uint8, device=dev)
+    dones[-1] = 1
+    nv = torch.zeros(p["rollouts"], device=dev)
+
+    def step():
+        lp, alp, ent, val = mx.ppo_rollout_forward(states, actions, Wp, Wpi, Wv, ctx)
+        return mx.fused_compute_gae(rewards, val.reshape(p["steps"], p["rollouts"]), dones, nv, 0.99, 0.95, ctx)
+
+    for _ in range(2):
+        step()
+    ctx.synchronize()
+    n = max(3, args.steps // 40)
+    barrier()
+    torch.cuda.synchronize()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(n):
+        step()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = max_over_ranks(e0.elapsed_time(e1) / n)
+    flops = 2.0 * rows * p["latent"] * (p["state_padded"] + p["actions"] + 1)
+    out = {"rows_per_s": world * rows / (ms / 1e3), "ms_per_batch": ms, "batches": n,
+           "tflops": flops / (ms / 1e3) / 1e12, "frac_of_bf16_peak": flops / (ms / 1e3) / 1e12 / peaks["bf16_tflops"],
+           "config": dict(p, weights="mx-int8", gae="gamma 0.99, lambda 0.95"),
+           "api": "mx.ppo_rollout_forward (3 x mxq_linear + mxq_policy_head) + mxq_gae"}
+    if rank == 0 and world == 1 and not args.no_cpu:
+        from oracle import oracle
+        sample = 64
+        st = states[:sample].cpu().numpy()
+        zp, zpi, zv = (oracle.weight_sums(8, w, n_, k_) for w, n_, k_ in
+                       ((wp, p["latent"], p["state_padded"]), (wpi, p["actions"], p["latent"]), (wv, 1, p["latent"])))
+        t0 = time.perf_counter()
+        reps = 0
+        while True:
+            q, s_ = oracle.quantize_x(st)
+            lat, used = oracle.baseline_gemv(8, q, s_, wp, sp, zp, p["latent"], p["state_padded"])
+            lq, ls = oracle.quantize_x(lat)
+            lg, _ = oracle.baseline_gemv(8, lq, ls, wpi, spi, zpi, p["actions"], p["latent"])
+            oracle.baseline_gemv(8, lq, ls, wv, sv, zv, 1, p["latent"])
+            oracle.policy_head(lg, np.zeros_like(lg))
+            reps += 1
+            el = time.perf_counter() - t0
+            if el >= 3.0:
+                break
+        out["cpu_baseline"] = {"value": reps * sample / el, "unit": "rows/s", "cores": oracle.max_threads(),
+                               "kind": "port", "sample": "%d x %d rows through the three MX linears + head (%.1f s), %s"
+                               % (reps, sample, el, "AVX-512 VNNI dpbusd" if used else "portable int loop")}
+    for w in (Wp, Wpi, Wv):
+        w.close()
+    return out
+
+
 def time_sharded(ctx, dev, args, world, rank, max_over_ranks, barrier):
     """N > 1 only: the multi-GPU forms of the path, over NCCL.
     pair -- the MLP pair column-sharded (each rank owns F/N rows of up and
@@ -547,6 +627,9 @@ def run_ours(args):
     moe = None
     if not args.no_moe:
         moe = time_moe(ctx, dev, args, world, max_over_ranks, barrier, peaks, rank)
+    ppo = None
+    if not args.no_ppo:
+        ppo = time_ppo(ctx, dev, args, world, max_over_ranks, barrier, peaks, rank)
     sharded = None
     if world > 1 and not args.no_shard:
         sharded = time_sharded(ctx, dev, args, world, rank, max_over_ranks, barrier)
@@ -572,6 +655,8 @@ def run_ours(args):
         }
         if moe is not None:
             line["moe"] = moe
+        if ppo is not None:
+            line["ppo_rollout"] = ppo
         if sharded is not None:
             line["sharded"] = sharded
         if world == 1 and not args.no_cpu:
@@ -597,6 +682,7 @@ def main():
     ap.add_argument("--no-sweep", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-moe", action="store_true")
+    ap.add_argument("--no-ppo", action="store_true")
     ap.add_argument("--no-shard", action="store_true", help="N > 1: skip the column-sharded / expert-parallel forms")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--copies", type=int, default=COPIES,

@@ -58,6 +58,7 @@ SIGNATURES = {
     "mxq_linear_noalloc": [_vp, _vp, _vp, _sz, _vp],
     "mxq_route_topk": [_vp, _vp, _sz, _sz, _sz, _vp, _vp],
     "mxq_moe_swiglu": [_vp, _vp, _vp, _vp, _sz, _vp, _vp, _sz, _sz, _vp],
+    "mxq_policy_head": [_vp, _vp, _vp, _sz, _sz, _vp, _vp, _vp],
     "mxq_gae": [_vp, _vp, _vp, _vp, _vp, _sz, _sz, _f, _f, _vp, _vp],
 }
 

@@ -214,6 +214,45 @@ __global__ void gae_kernel(const float* __restrict__ r, const float* __restrict_
   }
 }
 
+// ------------------------------------------------------- policy head ---
+// training/ppo_trainer.cpp:64-66 and :77: one warp per row; max by shuffles,
+// sums by a fixed shuffle tree (deterministic), exp by det_expf.
+__device__ __forceinline__ float warp_sum_fixed(float v) {
+  for (int o = 16; o > 0; o >>= 1) v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+__global__ void policy_head_kernel(const float* __restrict__ x, const float* __restrict__ a, int rows,
+                                   int cols, float* __restrict__ lp, float* __restrict__ alp,
+                                   float* __restrict__ ent) {
+  const int row = (int)(((long)blockIdx.x * blockDim.x + threadIdx.x) >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= rows) return;                       // whole warps leave together
+  const float* xr = x + (long)row * cols;
+  const float* ar = a + (long)row * cols;
+  float* lr = lp + (long)row * cols;
+  float m = -3.402823466e38f;
+  for (int j = lane; j < cols; j += 32) m = fmaxf(m, xr[j]);
+  m = warp_max(m, 32);
+  float s = 0.0f;
+  for (int j = lane; j < cols; j += 32) s = __fadd_rn(s, det_expf(__fsub_rn(xr[j], m)));
+  s = warp_sum_fixed(s);
+  const float lse = __fadd_rn(m, logf(s));
+  float sa = 0.0f, se = 0.0f;
+  for (int j = lane; j < cols; j += 32) {
+    const float l = __fsub_rn(xr[j], lse);
+    lr[j] = l;
+    sa = __fadd_rn(sa, __fmul_rn(l, ar[j]));
+    se = __fsub_rn(se, __fmul_rn(det_expf(l), l));
+  }
+  sa = warp_sum_fixed(sa);
+  se = warp_sum_fixed(se);
+  if (lane == 0) {
+    alp[row] = sa;
+    ent[row] = se;
+  }
+}
+
 int check_ctx(mxq_context* c) {
   return c ? MXQ_OK : fail(nullptr, MXQ_ERR_INVALID_ARGUMENT, "null context");
 }
@@ -885,6 +924,21 @@ int mxq_mlp_swiglu(mxq_ctx c, mxq_weight wg, mxq_weight wu, mxq_weight wd,
     if ((rc = after_launch(c, launch_quantize(qa, 2, c->stream, true), "swiglu quantize"))) return rc;
     return gemv_dev(c, wd, hq, hs, b, y);
   })
+}
+
+int mxq_policy_head(mxq_ctx c, const float* logits, const float* actions, size_t rows,
+                    size_t cols, float* log_probs, float* action_logp, float* entropy) {
+  if (int rc = check_ctx(c)) return rc;
+  if (!logits || !actions || !log_probs || !action_logp || !entropy)
+    return fail(c, MXQ_ERR_INVALID_ARGUMENT, "null pointer");
+  if (cols == 0 || cols > (1u << 24) || rows > (1u << 28))
+    return fail(c, MXQ_ERR_INVALID_ARGUMENT, "policy head: bad shape %zux%zu", rows, cols);
+  if (rows == 0) return MXQ_OK;
+  DeviceGuard g(c->device);
+  const long threads = (long)rows * 32;
+  policy_head_kernel<<<(unsigned)((threads + 255) / 256), 256, 0, c->stream>>>(
+      logits, actions, (int)rows, (int)cols, log_probs, action_logp, entropy);
+  return after_launch(c, cudaGetLastError(), "policy_head");
 }
 
 // Expert layer operand: rows gathered from x (slot -> token row), quantised

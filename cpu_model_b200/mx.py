@@ -371,3 +371,41 @@ def moe_swiglu(x, logits, gate_w, up_w, down_w, k, ctx=None):
                                  ctypes.cast(dn, ctypes.c_void_p), e, _ptr(x), _ptr(logits), t, k, _ptr(y)),
           ctx.h)
     return y
+
+
+def policy_head(logits, actions, ctx=None):
+    """PPO rollout head (mxq_policy_head): (log_probs [R][C], action_logp [R],
+    entropy [R]) from logits and action weights [R][C]."""
+    ctx = ctx or context()
+    _need_cuda(logits, torch.float32, "logits")
+    _need_cuda(actions, torch.float32, "actions")
+    if logits.shape != actions.shape or logits.dim() != 2:
+        raise ValueError("policy_head: logits and actions must both be [R][C]")
+    r, c = logits.shape
+    lp = torch.empty_like(logits)
+    alp = torch.empty(r, dtype=torch.float32, device=logits.device)
+    ent = torch.empty(r, dtype=torch.float32, device=logits.device)
+    ctx._bind()
+    check(ctx.lib.mxq_policy_head(ctx.h, _ptr(logits), _ptr(actions), r, c, _ptr(lp), _ptr(alp), _ptr(ent)),
+          ctx.h)
+    return lp, alp, ent
+
+
+def ppo_rollout_forward(states, actions, w_proj, w_policy, w_value, ctx=None):
+    """The rollout forward of PPOTrainer::update_step
+    (training/ppo_trainer.cpp:57-66, :77) with its three products as MX
+    linears: latent = states . proj, logits = latent . policy^T, values =
+    latent . value^T, then the policy head.  states [R][S] is zero-padded to
+    the projection's K (S = 1616 -> 1632, the next multiple of 32).
+    Returns (log_probs, action_logp, entropy, values [R])."""
+    ctx = ctx or w_proj.ctx
+    _need_cuda(states, torch.float32, "states")
+    if states.shape[1] != w_proj.k:
+        if states.shape[1] > w_proj.k:
+            raise ValueError("states have %d features, projection K is %d" % (states.shape[1], w_proj.k))
+        states = torch.nn.functional.pad(states, (0, w_proj.k - states.shape[1]))
+    latent = mx_linear(states.contiguous(), w_proj, ctx)
+    logits = mx_linear(latent, w_policy, ctx)
+    values = mx_linear(latent, w_value, ctx)[:, 0]
+    lp, alp, ent = policy_head(logits, actions, ctx)
+    return lp, alp, ent, values

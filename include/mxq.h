@@ -200,6 +200,17 @@ MXQ_API int mxq_moe_swiglu(mxq_ctx ctx, const mxq_weight* w_gate,
                            const float* logits, size_t t, size_t k,
                            float* y);
 
+/* --------------------------------------------------------- PPO head --- */
+/* The rollout head of PPOTrainer::update_step (training/ppo_trainer.cpp:64-66
+ * and :77) after its three MX linears (states -> latent -> logits, latent ->
+ * value): per row log_probs = log_softmax(logits), action_logp = sum_j
+ * log_probs * actions, entropy = -sum_j exp(log_probs) * log_probs.
+ * logits/actions/log_probs [rows][cols], action_logp/entropy [rows]. */
+MXQ_API int mxq_policy_head(mxq_ctx ctx, const float* logits,
+                            const float* actions, size_t rows, size_t cols,
+                            float* log_probs, float* action_logp,
+                            float* entropy);
+
 /* ---------------------------------------------------------------- GAE --- */
 /* nca::env::ReplayMemory::fused_compute_gae
  * (agentic_env/replay_memory.cpp:204-253) over an interleaved [T][E]

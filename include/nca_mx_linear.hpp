@@ -198,4 +198,12 @@ inline void moe_swiglu(const nca::linalg::Context& c, const std::vector<const nc
                          c.get());
 }
 
+// PPOTrainer::update_step's rollout head (training/ppo_trainer.cpp:64-66,
+// :77) after its MX linears: log_softmax, action log-probability, entropy.
+inline void policy_head(const nca::linalg::Context& c, const float* logits, const float* actions,
+                        size_t rows, size_t cols, float* log_probs, float* action_logp, float* entropy) {
+  nca::linalg::mxq_check(
+      mxq_policy_head(c.get(), logits, actions, rows, cols, log_probs, action_logp, entropy), c.get());
+}
+
 }  // namespace nca::layers

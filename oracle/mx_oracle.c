@@ -365,6 +365,34 @@ int mxo_moe(int fmt, const float* x, const float* logits, size_t T, size_t D,
     return 0;
 }
 
+/* ------------------------------------------------------- policy head --- */
+
+/* training/ppo_trainer.cpp:64-66 (log_softmax, action log-probability) and
+ * :77 (entropy), one row at a time. */
+void mxo_policy_head(const float* logits, const float* actions, size_t rows,
+                     size_t cols, float* log_probs, float* action_logp,
+                     float* entropy)
+{
+    for (size_t r = 0; r < rows; ++r) {
+        const float* x = logits + r * cols;
+        const float* a = actions + r * cols;
+        float* lp = log_probs + r * cols;
+        float m = x[0];
+        for (size_t j = 1; j < cols; ++j) m = x[j] > m ? x[j] : m;
+        float s = 0.0f;
+        for (size_t j = 0; j < cols; ++j) s = s + mxo_expf(x[j] - m);
+        const float lse = m + logf(s);
+        float alp = 0.0f, ent = 0.0f;
+        for (size_t j = 0; j < cols; ++j) {
+            lp[j] = x[j] - lse;
+            alp = alp + lp[j] * a[j];
+            ent = ent - mxo_expf(lp[j]) * lp[j];
+        }
+        action_logp[r] = alp;
+        entropy[r] = ent;
+    }
+}
+
 /* ---------------------------------------------------------------- GAE --- */
 
 /* agentic_env/replay_memory.cpp:204-253, same operation order per element. */

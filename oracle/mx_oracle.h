@@ -109,6 +109,14 @@ void mxo_gae(const float* rewards, const float* values, const uint8_t* dones,
              const float* next_values, size_t T, size_t E, float gamma,
              float lambda, float* adv, float* ret);
 
+/* PPO rollout head of PPOTrainer::update_step (training/ppo_trainer.cpp:64-66
+ * and :77): per row, log_probs = log_softmax(logits) (max, then the sum of
+ * exp(x - max) in column order, lse = max + log(sum)), action_logp =
+ * sum_j log_probs * actions, entropy = -sum_j exp(log_probs) * log_probs. */
+void mxo_policy_head(const float* logits, const float* actions, size_t rows,
+                     size_t cols, float* log_probs, float* action_logp,
+                     float* entropy);
+
 /* Block-sparse MoE layer on dense-with-zero-blocks expert matrices:
  * route top-k over logits [T][E]; per token, x is quantised once; each chosen
  * expert e runs gated_mlp on it; y[t] = sum_j gate_j * expert_j(x_t)

@@ -188,6 +188,18 @@ def ref_gae(rewards, values, dones, next_values, gamma, lam):
     return adv, ret
 
 
+def policy_head(logits, actions):
+    """(log_probs [R][C], action_logp [R], entropy [R]) of the PPO rollout head."""
+    logits = np.ascontiguousarray(logits, np.float32)
+    actions = np.ascontiguousarray(actions, np.float32)
+    r, c = logits.shape
+    lp = np.empty((r, c), np.float32)
+    alp = np.empty(r, np.float32)
+    ent = np.empty(r, np.float32)
+    lib().mxo_policy_head(_p(logits), _p(actions), *_sz(r, c), _p(lp), _p(alp), _p(ent))
+    return lp, alp, ent
+
+
 def moe(fmt, x, logits, d, f, k, experts):
     """experts: list of (wg, sg, wu, su, wd, sd) dense-with-zero-blocks."""
     x = np.ascontiguousarray(x, np.float32)

@@ -295,3 +295,19 @@ def test_moe_oracle_composes_its_primitives(fmt):
     assert np.array_equal(y, ref.astype(np.float32))
     with pytest.raises(ValueError):
         oracle.moe(fmt, x, logits, d, f, e + 1, experts)
+
+
+# ------------------------------------------------------ PPO rollout head ---
+def test_policy_head_matches_numpy():
+    """training/ppo_trainer.cpp:64-66, :77 restated; fp64 numpy reference."""
+    g = synth.rng(5)
+    logits = (g.standard_normal((37, 80)) * 3).astype(np.float32)
+    actions = np.eye(80, dtype=np.float32)[g.integers(0, 80, 37)]
+    lp, alp, ent = oracle.policy_head(logits, actions)
+    x = logits.astype(np.float64)
+    ref_lp = x - x.max(1, keepdims=True) - np.log(np.exp(x - x.max(1, keepdims=True)).sum(1, keepdims=True))
+    assert np.abs(lp - ref_lp).max() < 1e-5
+    assert np.allclose(np.exp(lp.astype(np.float64)).sum(1), 1.0, atol=1e-5)
+    assert np.abs(alp - (ref_lp * actions).sum(1)).max() < 1e-5
+    ref_ent = -(np.exp(ref_lp) * ref_lp).sum(1)
+    assert np.abs(ent - ref_ent).max() < 1e-4 and np.all(ent > 0)
