@@ -55,24 +55,32 @@ constexpr int kMaxSplits = 8;   // portable cluster size
 // hand-off chain is latency-bound).  RS and WS are multiples of NG: every
 // ring stage is then always refilled by the same group, in order, which keeps
 // the mbarrier parity waits unambiguous.
-template <int WFMT, int BN>
+// MT = 1 or 2 weight row tiles (128 rows each) per CTA: with MT = 2 every
+// activation tile feeds twice the weight rows, halving the operand traffic
+// per MMA (the per-SM copy engine, not HBM or the tensor pipe, bounds the
+// kernel).  The NG converter groups split as MT row tiles x GPR k-phases;
+// each group keeps its own accumulator.
+template <int WFMT, int BN, int MT>
 struct Cfg {
   static constexpr int NG = BN <= 64 ? 4 : 2;
   static constexpr int GW = kConvWarps / NG;             // warps per group
   static constexpr int GT = GW * 32;
-  static constexpr int KPS = NG;                         // k-tiles per chunk (one per group)
+  static constexpr int GPR = NG / MT;                    // groups per row tile
+  static constexpr int KPS = MT == 1 ? NG : (WFMT == 8 ? 2 : 4);   // k-tiles per chunk and row tile
+  static constexpr int TPG = KPS / GPR;                  // k-tiles per group per chunk
+  static constexpr int WSG = (MT == 2 && NG == 2) ? 2 : 1;         // weight stages per group
   static constexpr int TB = WFMT == 4 ? 32 : 64;
   static constexpr int RAW_W = 128 * TB;                 // packed weights of one k-tile
-  static constexpr int RAW_CHUNK = KPS * RAW_W;          // scales are read per thread
-  static constexpr int RAW_TARGET = WFMT == 8 ? (BN <= 64 ? 68 * 1024 : 34 * 1024)
-                                              : (BN <= 64 ? 48 * 1024 : (BN <= 128 ? 40 * 1024 : 26 * 1024));
+  static constexpr int RAW_CHUNK = MT * KPS * RAW_W;     // [MT][KPS][RAW_W]; scales read per thread
+  static constexpr int RAW_TARGET = MT == 2 ? 64 * 1024
+                                  : (WFMT == 8 ? (BN <= 64 ? 68 * 1024 : 34 * 1024)
+                                               : (BN <= 64 ? 48 * 1024 : (BN <= 128 ? 40 * 1024 : 26 * 1024)));
   static constexpr int RSC = RAW_TARGET / RAW_CHUNK < 2 ? 2 : RAW_TARGET / RAW_CHUNK;
   static constexpr int W_TILE = 128 * 128;
-  static constexpr int WS = NG;                          // one weight stage per group
+  static constexpr int WS = NG * WSG;
   static constexpr int X_TILE = BN * 128;
-  // activation chunks of XK k-tiles, about 32 KB per copy (a multiple of KPS)
-  static constexpr int XM = KPS * X_TILE >= 32768 ? 1 : 32768 / (KPS * X_TILE);
-  static constexpr int XK = XM * KPS;
+  // activation chunks of XK k-tiles, about 32 KB per copy
+  static constexpr int XK = X_TILE >= 32768 ? 1 : 32768 / X_TILE;
   static constexpr int X_CHUNK = XK * X_TILE;
   static constexpr int BUDGET = 222 * 1024;
   static constexpr int XS_FIT = (BUDGET - 2048 - RSC * RAW_CHUNK - WS * W_TILE) / X_CHUNK;
@@ -86,11 +94,14 @@ struct Cfg {
   // and the 16-byte bf16 chunks they become
   static constexpr int WORDS = 128 * TB / 4 / GT;
   static constexpr int NCH = WFMT == 4 ? WORDS : WORDS / 2;
-  static_assert(XSC >= 2, "activation ring");
+  static_assert(MT == 1 || MT == 2, "row tiles per CTA");
+  static_assert(NG % MT == 0 && KPS % GPR == 0, "group split");
+  // parity safety: any XSC consecutive activation chunks hold a tile of every group
+  static_assert(XSC >= 2 && XSC * XK >= GPR, "activation ring");
   static_assert(ACC_COLS <= 512, "tensor memory");
   static_assert(SMEM <= 227 * 1024, "shared memory");
   static_assert(WORDS == 4 || WORDS == 8 || WORDS == 16, "converter split");
-  // the split-K partial tile [BN][128] fp32 reuses the w and x rings
+  // the split-K partial tile [BN][128] fp32 (one row tile at a time) reuses the w and x rings
   static_assert((size_t)BN * 128 * 4 <= OP_BYTES, "partial tile");
 };
 
@@ -198,13 +209,14 @@ __device__ __forceinline__ void named_bar_sync(int id, int nthreads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
 }
 
-template <int WFMT, int BN>
+template <int WFMT, int BN, int MT>
 __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tc_kernel(GemmArgs a) {
-  using C = Cfg<WFMT, BN>;
+  using C = Cfg<WFMT, BN, MT>;
   constexpr int WS = C::WS;
   constexpr int XSC = C::XSC;
   constexpr int RSC = C::RSC;
   constexpr int KPS = C::KPS;
+  constexpr int XK = C::XK;
   extern __shared__ uint8_t smem_raw[];
   // 1024-byte alignment for the 128B-swizzled operand tiles
   const uint32_t base_u32 = smem_u32(smem_raw);
@@ -223,18 +235,20 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tc_kernel(GemmArgs a) {
   float* part = reinterpret_cast<float*>(w_ring);            // split-K partial [BN][128]
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int rt = blockIdx.x;       // 128-row weight tile
+  const int rt0 = blockIdx.x * MT;  // first 128-row weight tile
   const int nt = blockIdx.y;       // token tile
   const int S = gridDim.z;         // K splits (= cluster size)
   const int KT = a.w.Kpad / kTileK;                         // k-tiles of the operand
-  // this row tile's stored k-tiles: all KT (dense) or its block-sparse list
-  const bool sparse = a.w.kt_ptr != nullptr;
-  const int tbase = sparse ? a.w.kt_ptr[rt] : rt * KT;
-  const int ntot = sparse ? a.w.kt_ptr[rt + 1] - tbase : KT;
+  // stored k-tiles of the row tile(s): all KT (dense) or the block-sparse
+  // list (block-sparse weights run with MT = 1)
+  const bool sparse = MT == 1 && a.w.kt_ptr != nullptr;
+  const int tbase = sparse ? a.w.kt_ptr[rt0] : rt0 * KT;
+  const int ntot = sparse ? a.w.kt_ptr[rt0 + 1] - tbase : KT;
   const int kb = (int)blockIdx.z * ntot / S;
   const int nk = ((int)blockIdx.z + 1) * ntot / S - kb;    // k-tiles of this CTA (may be 0)
   const int nch = (nk + KPS - 1) / KPS;                      // chunks (the last may be short)
-  const int ngrp = nk < C::NG ? nk : C::NG;                   // groups that own k-tiles
+  const int gpr_active = nk < C::GPR ? nk : C::GPR;          // groups per row tile with k-tiles
+  const int ngrp = MT * gpr_active;
   uint32_t* status = a.status;
 
   if (threadIdx.x == 0) {
@@ -244,7 +258,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tc_kernel(GemmArgs a) {
     }
     for (int i = 0; i < XSC; ++i) {
       mbar_init(&x_full[i], 1);
-      mbar_init(&x_empty[i], C::XK);
+      mbar_init(&x_empty[i], XK * MT);
     }
     for (int i = 0; i < WS; ++i) mbar_init(&w_empty[i], 1);
     mbar_init(acc_full, ngrp > 0 ? ngrp : 1);
@@ -256,13 +270,14 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tc_kernel(GemmArgs a) {
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  // Chunks of KPS consecutive k-tiles move as one bulk copy each (weights,
-  // scales, activations): large copies stream far better than per-tile ones.
-  // The producer warps run their loops warp-uniformly (every lane waits, the
-  // elected lane issues the copies).  Warp 1 owns the TMEM allocation.
+  bool eok = false;                // converter warps: every wait before the epilogue succeeded
+  // Chunks of KPS consecutive k-tiles (per row tile) and XK activation tiles
+  // move as one bulk copy each: large copies stream far better than per-tile
+  // ones.  The producer warps run their loops warp-uniformly (every lane
+  // waits, the elected lane issues the copies).  Warp 1 owns the TMEM
+  // allocation.
   if (warp == 0) {
     // ------------------------------------------------ raw weight producer
-    const uint8_t* wsrc = a.w.data + ((size_t)tbase + kb) * C::RAW_W;
     bool ok = true;
     for (int c = 0; c < nch && ok; ++c) {
       const int st = c % RSC;
@@ -272,8 +287,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tc_kernel(GemmArgs a) {
       if (elect_one()) {
         const int nt_c = nk - c * KPS < KPS ? nk - c * KPS : KPS;
         uint8_t* dst = raw_ring + st * C::RAW_CHUNK;
-        mbar_arrive_expect_tx(&raw_full[st], (uint32_t)(nt_c * C::RAW_W));
-        bulk_g2s(dst, wsrc + (size_t)c * KPS * C::RAW_W, (uint32_t)(nt_c * C::RAW_W), &raw_full[st]);
+        mbar_arrive_expect_tx(&raw_full[st], (uint32_t)(MT * nt_c * C::RAW_W));
+#pragma unroll
+        for (int r = 0; r < MT; ++r) {
+          const int tb = sparse ? tbase : (rt0 + r) * KT;
+          bulk_g2s(dst + r * KPS * C::RAW_W, a.w.data + ((size_t)tb + kb + (size_t)c * KPS) * C::RAW_W,
+                   (uint32_t)(nt_c * C::RAW_W), &raw_full[st]);
+        }
       }
       __syncwarp();
     }
@@ -285,7 +305,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tc_kernel(GemmArgs a) {
     asm volatile("griddepcontrol.wait;" ::: "memory");
     const uint8_t* xsrc =
         reinterpret_cast<const uint8_t*>(a.opnd) + ((size_t)nt * KT + kb) * C::X_TILE;
-    const int nxc = (nk + C::XK - 1) / C::XK;
+    const int nxc = (nk + XK - 1) / XK;
     bool ok = true;
     for (int c = 0; c < nxc && ok; ++c) {
       const int st = c % XSC;
@@ -293,7 +313,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tc_kernel(GemmArgs a) {
       ok = __all_sync(0xffffffffu, ok);
       if (!ok) break;
       if (elect_one()) {
-        const int nt_c = nk - c * C::XK < C::XK ? nk - c * C::XK : C::XK;
+        const int nt_c = nk - c * XK < XK ? nk - c * XK : XK;
         mbar_arrive_expect_tx(&x_full[st], (uint32_t)(nt_c * C::X_TILE));
         if (!sparse) {
           bulk_g2s(x_ring + st * C::X_CHUNK, xsrc + (size_t)c * C::X_CHUNK, (uint32_t)(nt_c * C::X_TILE),
@@ -302,7 +322,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tc_kernel(GemmArgs a) {
           // the stored k-tiles are not contiguous in K: one copy per tile
           const uint8_t* xrow = reinterpret_cast<const uint8_t*>(a.opnd) + (size_t)nt * KT * C::X_TILE;
           for (int j = 0; j < nt_c; ++j) {
-            const int kx = a.w.kt_idx[tbase + kb + c * C::XK + j];
+            const int kx = a.w.kt_idx[tbase + kb + c * XK + j];
             bulk_g2s(x_ring + st * C::X_CHUNK + j * C::X_TILE, xrow + (size_t)kx * C::X_TILE, C::X_TILE,
                      &x_full[st]);
           }
@@ -313,18 +333,20 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tc_kernel(GemmArgs a) {
     for (int c = nxc - (nxc < XSC ? nxc : XSC); c < nxc && ok; ++c)
       ok = mbar_wait(&x_full[c % XSC], (c / XSC) & 1, status);
   } else if (warp >= kRoleWarps) {
-    // --------------------- converter groups: convert, issue MMAs, epilogue
-    // Group g takes k-tile g of every chunk and issues its MMAs into its own
+    // ----------------------------- converter groups: convert, issue MMAs
+    // Group g serves row tile r = g / GPR and takes the k-tiles j = p, p+GPR,
+    // ... (p = g % GPR) of every chunk, issuing their MMAs into its own
     // accumulator (TMEM columns g*BN ..), so each accumulator sums its tiles
-    // in a fixed order.  Per chunk: wait for the raw chunk, convert the
-    // group's tile into registers, release the raw chunk (every converter
-    // warp arrives once per chunk, tile or not), wait for the group's weight
-    // stage, store, fence to the async proxy, group barrier, then one elected
-    // lane of the group's issuing warp waits for the activation chunk and
-    // issues 4 MMAs.  Every warp of a group passes the group barrier once per
-    // chunk whatever happened, so a timed-out wait cannot strand the others.
+    // in a fixed order.  Per tile: convert into registers, wait for the
+    // group's weight stage, store, fence to the async proxy, group barrier,
+    // then one elected lane of the group's issuing warp waits for the
+    // activation chunk and issues 4 MMAs.  The raw chunk is released once
+    // per chunk by every converter warp.  Every warp of a group passes the
+    // group barrier once per tile whatever happened, so a timed-out wait
+    // cannot strand the others.
     const int cw = warp - kRoleWarps;
     const int grp = cw / C::GW;
+    const int r = grp / C::GPR, ph = grp % C::GPR;
     const int gt = (cw % C::GW) * 32 + lane;           // thread within the group
     const bool issuer = (cw % C::GW) == (grp & 3);     // spread over the SM's 4 schedulers
     constexpr int WPR = C::TB / 4;                     // words per row
@@ -333,147 +355,156 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tc_kernel(GemmArgs a) {
     const int shift = a.w.gemm_shift;
     const bool fused = a.w.gemm_fused != 0;
     const uint32_t idesc = idesc_bf16(128, BN);
-    uint8_t* wt = w_ring + grp * C::W_TILE;
-    const uint64_t wd = sw128_kmajor_desc(smem_u32(wt));
     const uint64_t xdesc = sw128_kmajor_desc(smem_u32(x_ring));
     // this thread's row's two E8M0 bytes per k-tile, straight from global
     // memory (2 bytes per row per tile; a bulk copy of them would cost as
-    // much as a weight chunk), one chunk ahead
-    const uint16_t* srow = reinterpret_cast<const uint16_t*>(a.w.scales) + ((size_t)tbase + kb) * 128 + row;
-    uint32_t sc_next = grp < nk ? ldg_u16(srow + (size_t)grp * 128) : 0u;
+    // much as a weight chunk), one tile ahead
+    const int tb_r = sparse ? tbase : (rt0 + r) * KT;
+    const uint16_t* srow = reinterpret_cast<const uint16_t*>(a.w.scales) + ((size_t)tb_r + kb) * 128 + row;
+    uint32_t sc_next = ph < nk ? ldg_u16(srow + (size_t)ph * 128) : 0u;
     const uint32_t acc = tmem + (uint32_t)(grp * BN);
+    int ntile = 0;                                     // tiles this group has issued
     bool ok = true;
     for (int c = 0; c < nch; ++c) {
       const int rs = c % RSC;
-      const int i = c * KPS + grp;                     // this group's k-tile
-      const bool has = i < nk;                         // group-uniform
-      const uint32_t sc2 = sc_next;
-      if (i + KPS < nk) sc_next = ldg_u16(srow + (size_t)(i + KPS) * 128);
       if (ok) ok = mbar_wait(&raw_full[rs], (c / RSC) & 1, status);
       ok = __all_sync(0xffffffffu, ok);
-      uint4 out[C::NCH];
-      if (ok && has) {
-        const uint8_t* raw = raw_ring + rs * C::RAW_CHUNK;
-        const uint8_t* tile = raw + grp * C::RAW_W;
-        if (fused)
-          convert_share<WFMT, C::WORDS, C::NCH, true>(tile, sc2, row, w0, shift, out);
-        else
-          convert_share<WFMT, C::WORDS, C::NCH, false>(tile, sc2, row, w0, shift, out);
-      }
-      __syncwarp();
-      if (ok && lane == 0) mbar_arrive(&raw_empty[rs]);
-      if (ok && has && c > 0) ok = mbar_wait(&w_empty[grp], (c - 1) & 1, status);
-      ok = __all_sync(0xffffffffu, ok);
-      if (ok && has) {
-#pragma unroll
-        for (int j = 0; j < C::NCH; ++j)
-          *reinterpret_cast<uint4*>(wt + sw128_offset(row, c0 + j)) = out[j];
-        // each writer makes its stores visible to the tensor core's async proxy
-        fence_proxy_async_smem();
-      }
-      named_bar_sync(1 + grp, C::GT);
-      if (issuer && has) {
-        const int cx = i / C::XK, xs = cx % XSC;
-        if (ok) ok = mbar_wait(&x_full[xs], (cx / XSC) & 1, status);
-        ok = __all_sync(0xffffffffu, ok);
-        if (ok) {
-          tc_fence_after();
-          const uint64_t xd = xdesc + (uint64_t)((xs * C::X_CHUNK + (i % C::XK) * C::X_TILE) >> 4);
-          if (elect_one()) {
-#pragma unroll
-            for (int kk = 0; kk < 4; ++kk)
-              mma_bf16_ss(acc, wd + 2 * kk, xd + 2 * kk, idesc, (c != 0 || kk != 0) ? 1u : 0u);
-            mma_commit(&w_empty[grp]);
-            mma_commit(&x_empty[xs]);
-          }
-          __syncwarp();
+      const uint8_t* raw = raw_ring + rs * C::RAW_CHUNK + r * KPS * C::RAW_W;
+#pragma unroll 1
+      for (int t = 0; t < C::TPG; ++t) {
+        const int j = ph + t * C::GPR;
+        const int i = c * KPS + j;                     // this group's k-tile
+        const bool has = i < nk;                       // group-uniform
+        const uint32_t sc2 = sc_next;
+        if (i + C::GPR < nk) sc_next = ldg_u16(srow + (size_t)(i + C::GPR) * 128);
+        uint4 out[C::NCH];
+        if (ok && has) {
+          if (fused)
+            convert_share<WFMT, C::WORDS, C::NCH, true>(raw + j * C::RAW_W, sc2, row, w0, shift, out);
+          else
+            convert_share<WFMT, C::WORDS, C::NCH, false>(raw + j * C::RAW_W, sc2, row, w0, shift, out);
         }
+        if (t == C::TPG - 1) {
+          __syncwarp();
+          if (ok && lane == 0) mbar_arrive(&raw_empty[rs]);
+        }
+        const int ws = grp * C::WSG + (ntile % C::WSG);
+        if (ok && has && ntile >= C::WSG) ok = mbar_wait(&w_empty[ws], ((ntile / C::WSG) - 1) & 1, status);
+        ok = __all_sync(0xffffffffu, ok);
+        uint8_t* wt = w_ring + ws * C::W_TILE;
+        if (ok && has) {
+#pragma unroll
+          for (int q = 0; q < C::NCH; ++q)
+            *reinterpret_cast<uint4*>(wt + sw128_offset(row, c0 + q)) = out[q];
+          // each writer makes its stores visible to the tensor core's async proxy
+          fence_proxy_async_smem();
+        }
+        named_bar_sync(1 + grp, C::GT);
+        if (issuer && has) {
+          const int cx = i / XK, xs = cx % XSC;
+          if (ok) ok = mbar_wait(&x_full[xs], (cx / XSC) & 1, status);
+          ok = __all_sync(0xffffffffu, ok);
+          if (ok) {
+            tc_fence_after();
+            const uint64_t wd = sw128_kmajor_desc(smem_u32(wt));
+            const uint64_t xd = xdesc + (uint64_t)((xs * C::X_CHUNK + (i % XK) * C::X_TILE) >> 4);
+            if (elect_one()) {
+#pragma unroll
+              for (int kk = 0; kk < 4; ++kk)
+                mma_bf16_ss(acc, wd + 2 * kk, xd + 2 * kk, idesc, (ntile != 0 || kk != 0) ? 1u : 0u);
+              mma_commit(&w_empty[ws]);
+              mma_commit(&x_empty[xs]);
+            }
+            __syncwarp();
+          }
+        }
+        if (has) ++ntile;
       }
     }
-    if (issuer && ok && grp < ngrp) {
+    if (issuer && ok && ph < gpr_active) {
       if (elect_one()) mma_commit(acc_full);
       __syncwarp();
     }
-    // epilogue: sum the group accumulators in group order (a CTA with no
-    // stored k-tiles -- an all-zero row tile of a block-sparse weight, or an
-    // empty split -- writes zeros)
     if (ngrp > 0) ok = mbar_wait(acc_full, 0, status);
-    ok = __all_sync(0xffffffffu, ok);     // tcgen05.ld is warp-collective
-    tc_fence_after();
-    if (ok) {
-      // warp w reads TMEM lanes 32*(w%4)..; the column range is split over
-      // the kConvWarps/4 warps that share a lane quarter
-      constexpr int NH = kConvWarps / 4;
+    eok = __all_sync(0xffffffffu, ok);
+  }
+
+  // ---------------------------------------------------------- epilogue
+  // Row tile r's result is the sum of its GPR group accumulators in group
+  // order (a CTA with no stored k-tiles -- an all-zero row tile of a
+  // block-sparse weight, or an empty split -- writes zeros).  Warp w reads
+  // TMEM lanes 32*(w%4)..; with MT = 2 half of the converter warps take each
+  // row tile.  With a K split, each row tile's partial goes through shared
+  // memory and is reduced over the cluster before the next row tile.
+  const bool epi = warp >= kRoleWarps;
+#pragma unroll 1
+  for (int rr = 0; rr < MT; ++rr) {
+    if (epi) {
+      constexpr int NH = kConvWarps / 4 / MT;          // warps per lane quarter per row tile
       constexpr int CPG = BN / NH >= 8 ? BN / NH : 8;
-      const int q = warp & 3, h = (warp - kRoleWarps) >> 2;
+      const int q = warp & 3, hh = (warp - kRoleWarps) >> 2;
+      const int wr = hh / NH, h = hh % NH;             // row tile and column group of this warp
       const int trow = q * 32 + lane;
-      const int row_g = rt * 128 + trow;
+      const int row_g = (rt0 + rr) * 128 + trow;
       const uint32_t lane_base = tmem + ((uint32_t)(q * 32) << 16);
-      if (h * CPG < BN) {
+      tc_fence_after();
+      if (wr == rr && h * CPG < BN && eok) {
 #pragma unroll 1
         for (int cc = h * CPG; cc < (h + 1) * CPG; cc += 8) {
           float f[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-          if (ngrp > 0) {
+          for (int g = 0; g < gpr_active; ++g) {
             uint32_t v[8];
-            tmem_ld8(lane_base + (uint32_t)cc, v);
+            tmem_ld8(lane_base + (uint32_t)((rr * C::GPR + g) * BN + cc), v);
             tmem_ld_wait();
 #pragma unroll
-            for (int j = 0; j < 8; ++j) f[j] = __uint_as_float(v[j]);
-          }
-          for (int g = 1; g < ngrp; ++g) {
-            uint32_t v[8];
-            tmem_ld8(lane_base + (uint32_t)(g * BN + cc), v);
-            tmem_ld_wait();
-#pragma unroll
-            for (int j = 0; j < 8; ++j) f[j] += __uint_as_float(v[j]);
+            for (int jj = 0; jj < 8; ++jj) f[jj] = g == 0 ? __uint_as_float(v[jj]) : f[jj] + __uint_as_float(v[jj]);
           }
           if (S > 1) {
 #pragma unroll
-            for (int j = 0; j < 8; ++j) part[(cc + j) * 128 + trow] = f[j];
+            for (int jj = 0; jj < 8; ++jj) part[(cc + jj) * 128 + trow] = f[jj];
           } else {
 #pragma unroll
-            for (int j = 0; j < 8; ++j) {
-              const int tok = nt * BN + cc + j;
-              if (tok < a.B && row_g < a.w.N) a.y[(size_t)tok * a.w.N + row_g] = f[j];
+            for (int jj = 0; jj < 8; ++jj) {
+              const int tok = nt * BN + cc + jj;
+              if (tok < a.B && row_g < a.w.N) a.y[(size_t)tok * a.w.N + row_g] = f[jj];
             }
           }
         }
       }
     }
-  }
-
-  if (S > 1) {
-    // ---------------------------------------- split-K reduction over DSMEM
-    __syncwarp();
-    cluster_sync_all();                         // all partial tiles written
-    const uint32_t rank = cluster_ctarank();
-    const int tb = (int)rank * BN / S, te = ((int)rank + 1) * BN / S;
-    const uint32_t pbase = smem_u32(part);
-    uint32_t src[kMaxSplits];
+    if (S > 1) {
+      // ------------------------------------- split-K reduction over DSMEM
+      __syncwarp();
+      cluster_sync_all();                       // all partial tiles written
+      const uint32_t rank = cluster_ctarank();
+      const int tb = (int)rank * BN / S, te = ((int)rank + 1) * BN / S;
+      const uint32_t pbase = smem_u32(part);
+      uint32_t src[kMaxSplits];
 #pragma unroll
-    for (int s = 0; s < kMaxSplits; ++s) src[s] = s < S ? mapa_shared(pbase, (uint32_t)s) : 0u;
-    const int n4 = (te - tb) * 32;              // float4 per token row of 128
-    for (int i = threadIdx.x; i < n4; i += kGemmThreads) {
-      const int tok = tb + (i >> 5), r4 = (i & 31) * 4;
-      const uint32_t off = (uint32_t)(tok * 128 + r4) * 4u;
-      float4 acc = ld_dsmem_f4(src[0] + off);
+      for (int s2 = 0; s2 < kMaxSplits; ++s2) src[s2] = s2 < S ? mapa_shared(pbase, (uint32_t)s2) : 0u;
+      const int n4 = (te - tb) * 32;            // float4 per token row of 128
+      for (int i = threadIdx.x; i < n4; i += kGemmThreads) {
+        const int tok = tb + (i >> 5), r4 = (i & 31) * 4;
+        const uint32_t off = (uint32_t)(tok * 128 + r4) * 4u;
+        float4 sum = ld_dsmem_f4(src[0] + off);
 #pragma unroll
-      for (int s = 1; s < kMaxSplits; ++s) {
-        if (s < S) {
-          const float4 v = ld_dsmem_f4(src[s] + off);
-          acc.x += v.x; acc.y += v.y; acc.z += v.z; acc.w += v.w;
+        for (int s2 = 1; s2 < kMaxSplits; ++s2) {
+          if (s2 < S) {
+            const float4 v = ld_dsmem_f4(src[s2] + off);
+            sum.x += v.x; sum.y += v.y; sum.z += v.z; sum.w += v.w;
+          }
+        }
+        const int gtok = nt * BN + tok, grow = (rt0 + rr) * 128 + r4;
+        if (gtok < a.B) {
+          float* yr = a.y + (size_t)gtok * a.w.N;
+          if (grow + 0 < a.w.N) yr[grow + 0] = sum.x;
+          if (grow + 1 < a.w.N) yr[grow + 1] = sum.y;
+          if (grow + 2 < a.w.N) yr[grow + 2] = sum.z;
+          if (grow + 3 < a.w.N) yr[grow + 3] = sum.w;
         }
       }
-      const int gtok = nt * BN + tok, grow = rt * 128 + r4;
-      if (gtok < a.B) {
-        float* yr = a.y + (size_t)gtok * a.w.N;
-        if (grow + 0 < a.w.N) yr[grow + 0] = acc.x;
-        if (grow + 1 < a.w.N) yr[grow + 1] = acc.y;
-        if (grow + 2 < a.w.N) yr[grow + 2] = acc.z;
-        if (grow + 3 < a.w.N) yr[grow + 3] = acc.w;
-      }
+      cluster_sync_all();                       // peers are done reading this CTA
     }
-    cluster_sync_all();                         // peers are done reading this CTA
   }
 
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
@@ -487,9 +518,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tc_kernel(GemmArgs a) {
 
 // How many CTAs of one K-split cluster size can be resident at once (cached
 // per kernel instance; 0 if the query fails).
-template <int WFMT, int BN>
+template <int WFMT, int BN, int MT>
 int max_clusters(int S) {
-  using C = Cfg<WFMT, BN>;
+  using C = Cfg<WFMT, BN, MT>;
   static int cache[kMaxSplits + 1] = {};
   if (cache[S] != 0) return cache[S] < 0 ? 0 : cache[S];
   cudaLaunchConfig_t cfg = {};
@@ -504,7 +535,7 @@ int max_clusters(int S) {
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   int n = 0;
-  if (cudaOccupancyMaxActiveClusters(&n, gemm_tc_kernel<WFMT, BN>, &cfg) != cudaSuccess || n <= 0) {
+  if (cudaOccupancyMaxActiveClusters(&n, gemm_tc_kernel<WFMT, BN, MT>, &cfg) != cudaSuccess || n <= 0) {
     (void)cudaGetLastError();
     cache[S] = -1;
     return 0;
@@ -516,17 +547,17 @@ int max_clusters(int S) {
 // Pick the K split: minimise waves x (k-tiles per CTA + fixed per-CTA cost),
 // the fixed cost (prologue, pipeline fill, epilogue) counted as 4 k-tiles,
 // plus the shared-memory reduction when split (grows with the tile width).
-template <int WFMT, int BN>
+template <int WFMT, int BN, int MT>
 int pick_splits(int units, int KT) {
   int best = 1;
   long best_cost = -1;
   for (int S = 1; S <= kMaxSplits; ++S) {
     if (S > 1 && KT / S < 4) break;
-    const int mc = max_clusters<WFMT, BN>(S);
+    const int mc = max_clusters<WFMT, BN, MT>(S);
     if (mc <= 0) continue;
     const long waves = (units + mc - 1) / mc;
-    const long overhead = 4 + (S > 1 ? 1 + BN / 128 : 0);
-    const long cost = waves * ((KT + S - 1) / S + overhead);
+    const long overhead = 4 + (S > 1 ? MT * (1 + BN / 128) : 0);
+    const long cost = waves * (MT * ((KT + S - 1) / S) + overhead);
     if (best_cost < 0 || cost < best_cost) {
       best_cost = cost;
       best = S;
@@ -535,22 +566,22 @@ int pick_splits(int units, int KT) {
   return best;
 }
 
-template <int WFMT, int BN>
+template <int WFMT, int BN, int MT>
 cudaError_t launch_t(const GemmArgs& a, cudaStream_t st, bool pdl) {
-  using C = Cfg<WFMT, BN>;
+  using C = Cfg<WFMT, BN, MT>;
   static bool configured = false;
   if (!configured) {
-    cudaError_t e = cudaFuncSetAttribute(gemm_tc_kernel<WFMT, BN>,
+    cudaError_t e = cudaFuncSetAttribute(gemm_tc_kernel<WFMT, BN, MT>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          (int)C::SMEM);
     if (e != cudaSuccess) return e;
     configured = true;
   }
-  const int T = a.w.Npad / 128, NT = a.Bpad / BN;
+  const int T = a.w.Npad / (128 * MT), NT = a.Bpad / BN;
   // k-tiles per row tile: all of K, or the block-sparse average
   const int KT = a.w.kt_ptr ? (a.w.nnz_tiles + T - 1) / T : a.w.Kpad / kTileK;
   const int S = a.splits > 0 ? (a.splits < KT ? a.splits : (KT > 0 ? KT : 1))
-                             : pick_splits<WFMT, BN>(T * NT, KT > 0 ? KT : 1);
+                             : pick_splits<WFMT, BN, MT>(T * NT, KT > 0 ? KT : 1);
   if (S > kMaxSplits) return cudaErrorInvalidValue;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)T, (unsigned)NT, (unsigned)S);
@@ -573,17 +604,26 @@ cudaError_t launch_t(const GemmArgs& a, cudaStream_t st, bool pdl) {
   }
   cfg.attrs = attr;
   cfg.numAttrs = na;
-  return cudaLaunchKernelEx(&cfg, gemm_tc_kernel<WFMT, BN>, a);
+  return cudaLaunchKernelEx(&cfg, gemm_tc_kernel<WFMT, BN, MT>, a);
+}
+
+// Two row tiles per CTA for dense weights once the token tile is wide
+// enough that the activation operand dominates the per-CTA traffic;
+// block-sparse weights keep one (their row tiles store different k-tiles).
+template <int WFMT, int BN>
+cudaError_t launch_mt(const GemmArgs& a, cudaStream_t st, bool pdl) {
+  if (BN >= 64 && a.w.kt_ptr == nullptr) return launch_t<WFMT, BN, 2>(a, st, pdl);
+  return launch_t<WFMT, BN, 1>(a, st, pdl);
 }
 
 template <int WFMT>
 cudaError_t launch_fmt(const GemmArgs& a, cudaStream_t st, bool pdl) {
   switch (a.BN) {
-    case 16: return launch_t<WFMT, 16>(a, st, pdl);
-    case 32: return launch_t<WFMT, 32>(a, st, pdl);
-    case 64: return launch_t<WFMT, 64>(a, st, pdl);
-    case 128: return launch_t<WFMT, 128>(a, st, pdl);
-    case 256: return launch_t<WFMT, 256>(a, st, pdl);
+    case 16: return launch_t<WFMT, 16, 1>(a, st, pdl);
+    case 32: return launch_t<WFMT, 32, 1>(a, st, pdl);
+    case 64: return launch_mt<WFMT, 64>(a, st, pdl);
+    case 128: return launch_mt<WFMT, 128>(a, st, pdl);
+    case 256: return launch_mt<WFMT, 256>(a, st, pdl);
   }
   return cudaErrorInvalidValue;
 }
