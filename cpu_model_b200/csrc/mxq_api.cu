@@ -2,6 +2,8 @@
 // workspace, regime selection and the small kernels (weight repack, top-k
 // routing, GAE).  No exception crosses the boundary; every entry returns an
 // MXQ_* status.
+#include <atomic>
+#include <chrono>
 #include <cstdio>
 #include <cstring>
 #include <cstdarg>
@@ -34,10 +36,33 @@ struct mxq_context {
   int32_t* ws_moe = nullptr; size_t ws_moe_bytes = 0;
   float* ws_yr = nullptr;    size_t ws_yr_bytes = 0;
   int32_t* moe_counts_host = nullptr; size_t moe_counts_cap = 0;
+  // host-buffer entry points: pinned staging and one CUDA graph per
+  // (call, weights, batch); ws_gen changes whenever a workspace moves, which
+  // retires every captured graph
+  uint64_t ws_gen = 1;
+  cudaStream_t hstream = nullptr;   // private stream of the host-buffer calls (capturable)
+  cudaEvent_t hevent = nullptr;
+  // small host calls: mapped pinned buffers read and written by kernels, a
+  // device sequence counter and the host's mirror of it
+  uint32_t* seq_dev = nullptr;
+  uint32_t host_seq = 0;
+  float* pin_in = nullptr;  size_t pin_in_bytes = 0;
+  float* pin_out = nullptr; size_t pin_out_bytes = 0;
+  struct HostGraph {
+    int kind;
+    uint64_t w1, w2;
+    size_t b;
+    uint64_t gen;
+    cudaStream_t stream;
+    cudaGraphExec_t exec;   // null: capture failed, run uncaptured
+    bool mapped;            // copies by kernels through mapped memory, completion by a flag
+  };
+  std::vector<HostGraph> graphs;
 };
 
 struct mxq_weight_s {
   mxq_context* ctx = nullptr;
+  uint64_t serial = 0;        // unique per created weight (graph cache keys)
   WeightView v{};
   uint8_t* data = nullptr;
   uint8_t* scales = nullptr;
@@ -78,6 +103,7 @@ struct DeviceGuard {
 template <typename T>
 int ensure(mxq_context* c, T*& p, size_t& cap, size_t bytes, const char* what) {
   if (bytes <= cap) return MXQ_OK;
+  ++c->ws_gen;
   if (p) cudaFree(p);
   p = nullptr;
   cap = 0;
@@ -90,6 +116,26 @@ int ensure(mxq_context* c, T*& p, size_t& cap, size_t bytes, const char* what) {
 }
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+uint64_t next_weight_serial() {
+  static std::atomic<uint64_t> n{0};
+  return ++n;
+}
+
+// Pinned host staging for the host-buffer entry points (moves bump ws_gen).
+int ensure_pinned(mxq_context* c, float*& p, size_t& cap, size_t bytes, const char* what) {
+  if (bytes <= cap) return MXQ_OK;
+  ++c->ws_gen;
+  if (p) cudaFreeHost(p);
+  p = nullptr;
+  cap = 0;
+  void* q = nullptr;
+  cudaError_t e = cudaHostAlloc(&q, bytes, cudaHostAllocMapped);
+  if (e != cudaSuccess) return cuda_fail(c, e, what);
+  p = static_cast<float*>(q);
+  cap = bytes;
+  return MXQ_OK;
+}
 
 // ------------------------------------------------------------ repack ---
 __global__ void repack_kernel(const uint8_t* __restrict__ data,
@@ -250,6 +296,33 @@ __global__ void policy_head_kernel(const float* __restrict__ x, const float* __r
   if (lane == 0) {
     alp[row] = sa;
     ent[row] = se;
+  }
+}
+
+// ------------------------------------------------- host-call transfers ---
+// Small host calls move their data through mapped pinned memory with
+// kernels: the input is read from host memory by one CTA, and the output,
+// the status word and a fresh sequence number are written back by one CTA,
+// the sequence number last, after a system-scope fence, so the host can
+// poll for it instead of a stream synchronisation.
+__global__ void host_in_kernel(float* __restrict__ dst, const float* __restrict__ src, size_t n) {
+  for (size_t i = threadIdx.x; i < n / 4; i += blockDim.x)
+    reinterpret_cast<float4*>(dst)[i] = reinterpret_cast<const float4*>(src)[i];
+  for (size_t i = n / 4 * 4 + threadIdx.x; i < n; i += blockDim.x) dst[i] = src[i];
+}
+
+__global__ void host_out_kernel(const float* __restrict__ src, float* dst, size_t n, const uint32_t* status,
+                                uint32_t* status_host, uint32_t* seq_dev, volatile uint32_t* flag_host) {
+  for (size_t i = threadIdx.x; i < n / 4; i += blockDim.x)
+    reinterpret_cast<float4*>(dst)[i] = reinterpret_cast<const float4*>(src)[i];
+  for (size_t i = n / 4 * 4 + threadIdx.x; i < n; i += blockDim.x) dst[i] = src[i];
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    *status_host = *status;
+    const uint32_t v = *seq_dev + 1;
+    *seq_dev = v;
+    __threadfence_system();
+    *flag_host = v;
   }
 }
 
@@ -454,6 +527,13 @@ int mxq_destroy(mxq_ctx c) {
     cudaFree(c->ws_out);
     cudaFree(c->ws_moe);
     cudaFree(c->ws_yr);
+    for (auto& g : c->graphs)
+      if (g.exec) cudaGraphExecDestroy(g.exec);
+    if (c->pin_in) cudaFreeHost(c->pin_in);
+    if (c->pin_out) cudaFreeHost(c->pin_out);
+    if (c->hstream) cudaStreamSynchronize(c->hstream), cudaStreamDestroy(c->hstream);
+    if (c->hevent) cudaEventDestroy(c->hevent);
+    if (c->seq_dev) cudaFree(c->seq_dev);
     if (c->moe_counts_host) cudaFreeHost(c->moe_counts_host);
     delete c;
     return MXQ_OK;
@@ -539,6 +619,7 @@ int mxq_weight_create(mxq_ctx c, int fmt, size_t n, size_t k, const void* data,
     const size_t dsc_bytes = (size_t)Npad * Kpad / kBlock;
     auto* w = new mxq_weight_s();
     w->ctx = c;
+    w->serial = next_weight_serial();
     cudaError_t e = cudaMalloc(&w->data, dst_bytes);
     if (e == cudaSuccess) e = cudaMalloc(&w->scales, dsc_bytes);
     const uint8_t* src_d = static_cast<const uint8_t*>(data);
@@ -628,6 +709,7 @@ int mxq_weight_create_bsr(mxq_ctx c, int fmt, size_t n, size_t k, const void* da
     const size_t mask_bytes = (size_t)NB * KB;
     auto* w = new mxq_weight_s();
     w->ctx = c;
+    w->serial = next_weight_serial();
     const size_t nt_alloc = ntiles > 0 ? (size_t)ntiles : 1;
     cudaError_t e = cudaMalloc(&w->data, nt_alloc * 128 * TB);
     if (e == cudaSuccess) e = cudaMalloc(&w->scales, nt_alloc * 256);
@@ -840,18 +922,149 @@ int mxq_linear_pair(mxq_ctx c, mxq_weight w1, mxq_weight w2, const float* x,
   })
 }
 
-static int host_call(mxq_context* c, size_t in_elems, size_t out_elems,
-                     const float* x_host, float* y_host,
+// Host-buffer calls: x_host -> pinned staging -> device, fn, device ->
+// pinned staging -> y_host.  The first call of a (kind, weights, batch) runs
+// as plain launches (sizing every workspace); the next one records the
+// copies and launches into a CUDA graph, which later calls replay with one
+// launch.  Any workspace move (ws_gen) or stream change retires the graph.
+// The calls are synchronous, so they run on the context's private stream
+// (capturable even when the caller's stream is the legacy default stream),
+// after whatever the caller had queued on its own stream.
+struct StreamSwap {
+  mxq_context* c;
+  cudaStream_t user;
+  StreamSwap(mxq_context* cc, cudaStream_t s) : c(cc), user(cc->stream) { c->stream = s; }
+  ~StreamSwap() { c->stream = user; }
+};
+
+static int host_call(mxq_context* c, int kind, uint64_t w1, uint64_t w2, size_t b, size_t in_elems,
+                     size_t out_elems, const float* x_host, float* y_host,
                      int (*fn)(mxq_context*, void*, const float*, float*), void* arg) {
+  if (!c->hstream) {
+    cudaError_t e = cudaStreamCreateWithFlags(&c->hstream, cudaStreamNonBlocking);
+    if (e == cudaSuccess) e = cudaEventCreateWithFlags(&c->hevent, cudaEventDisableTiming);
+    if (e == cudaSuccess) e = cudaMalloc(&c->seq_dev, sizeof(uint32_t));
+    if (e == cudaSuccess) e = cudaMemset(c->seq_dev, 0, sizeof(uint32_t));
+    if (e != cudaSuccess) return cuda_fail(c, e, "host-call stream");
+    c->host_seq = 0;
+  }
+  // order after the caller's queued work (nothing to order after when idle)
+  cudaError_t ev = cudaStreamQuery(c->stream);
+  if (ev == cudaErrorNotReady) {
+    ev = cudaEventRecord(c->hevent, c->stream);
+    if (ev == cudaSuccess) ev = cudaStreamWaitEvent(c->hstream, c->hevent, 0);
+  }
+  if (ev != cudaSuccess) return cuda_fail(c, ev, "host-call ordering");
+  StreamSwap swap(c, c->hstream);
   int rc;
-  if ((rc = ensure(c, c->ws_in, c->ws_in_bytes, in_elems * 4, "workspace in"))) return rc;
-  if ((rc = ensure(c, c->ws_out, c->ws_out_bytes, out_elems * 4, "workspace out"))) return rc;
-  cudaError_t e = cudaMemcpyAsync(c->ws_in, x_host, in_elems * 4, cudaMemcpyHostToDevice, c->stream);
+  const size_t in_bytes = in_elems * 4, out_bytes = out_elems * 4;
+  const size_t out_pad = (out_bytes + 15) / 16 * 16;
+  if ((rc = ensure(c, c->ws_in, c->ws_in_bytes, in_bytes, "workspace in"))) return rc;
+  if ((rc = ensure(c, c->ws_out, c->ws_out_bytes, out_bytes, "workspace out"))) return rc;
+  if ((rc = ensure_pinned(c, c->pin_in, c->pin_in_bytes, in_bytes, "pinned in"))) return rc;
+  if ((rc = ensure_pinned(c, c->pin_out, c->pin_out_bytes, out_pad + 16, "pinned out"))) return rc;
+  // pin_out: [y][status word][sequence flag]
+  uint32_t* st_host = reinterpret_cast<uint32_t*>(reinterpret_cast<uint8_t*>(c->pin_out) + out_pad);
+  uint32_t* flag_host = st_host + 1;
+  const bool small = in_bytes + out_bytes <= ((size_t)1 << 20);
+  mxq_context::HostGraph* hg = nullptr;
+  for (auto& g : c->graphs)
+    if (g.kind == kind && g.w1 == w1 && g.w2 == w2 && g.b == b) hg = &g;
+  if (hg && (hg->gen != c->ws_gen || hg->stream != c->stream)) {
+    if (hg->exec) cudaGraphExecDestroy(hg->exec);
+    *hg = mxq_context::HostGraph{kind, w1, w2, b, 0, nullptr, nullptr, false};
+  }
+  std::memcpy(c->pin_in, x_host, in_bytes);
+  if (hg && hg->gen == c->ws_gen && hg->exec) {
+    cudaError_t e = cudaSuccess;
+    if (hg->mapped) {
+      // one launch; completion seen through the mapped sequence flag
+      const uint32_t expect = c->host_seq + 1;
+      e = cudaGraphLaunch(hg->exec, c->stream);
+      if (e != cudaSuccess) return cuda_fail(c, e, "graph launch");
+      const auto t0 = std::chrono::steady_clock::now();
+      for (uint32_t it = 0;; ++it) {
+        if (__atomic_load_n(flag_host, __ATOMIC_ACQUIRE) == expect) break;
+        if ((it & 1023u) == 1023u &&
+            std::chrono::steady_clock::now() - t0 > std::chrono::seconds(2)) {
+          e = cudaStreamSynchronize(c->stream);           // bounded: fall back to the stream
+          c->host_seq = __atomic_load_n(flag_host, __ATOMIC_ACQUIRE);
+          if (e != cudaSuccess) return cuda_fail(c, e, "host call");
+          if (c->host_seq != expect) return fail(c, MXQ_ERR_CUDA, "host call: completion flag not seen");
+          break;
+        }
+      }
+      c->host_seq = expect;
+    } else {
+      // the graph ends with the status word's copy: one synchronisation
+      e = cudaGraphLaunch(hg->exec, c->stream);
+      if (e == cudaSuccess) e = cudaStreamSynchronize(c->stream);
+      if (e != cudaSuccess) return cuda_fail(c, e, "graph launch");
+    }
+    c->launches += 2;
+    const uint32_t st = hg->mapped ? *st_host : *c->status_host;
+    if (st) {
+      cudaMemset(c->status, 0, sizeof(uint32_t));
+      return fail(c, MXQ_ERR_TIMEOUT, "a device-side bounded wait gave up (status 0x%x)", st);
+    }
+    std::memcpy(y_host, c->pin_out, out_bytes);
+    return MXQ_OK;
+  }
+  // plain launches (the first call of a key sizes every buffer it touches)
+  const uint64_t gen0 = c->ws_gen;
+  cudaError_t e = cudaMemcpyAsync(c->ws_in, c->pin_in, in_bytes, cudaMemcpyHostToDevice, c->stream);
   if (e != cudaSuccess) return cuda_fail(c, e, "copy in");
   if ((rc = fn(c, arg, c->ws_in, c->ws_out))) return rc;
-  e = cudaMemcpyAsync(y_host, c->ws_out, out_elems * 4, cudaMemcpyDeviceToHost, c->stream);
+  e = cudaMemcpyAsync(c->pin_out, c->ws_out, out_bytes, cudaMemcpyDeviceToHost, c->stream);
   if (e != cudaSuccess) return cuda_fail(c, e, "copy out");
-  return mxq_synchronize(c);
+  if ((rc = mxq_synchronize(c))) return rc;
+  std::memcpy(y_host, c->pin_out, out_bytes);
+  if (!hg) {
+    c->graphs.push_back(mxq_context::HostGraph{kind, w1, w2, b, 0, c->stream, nullptr, false});
+    hg = &c->graphs.back();
+  }
+  if (c->ws_gen == gen0 && hg->gen == 0) {
+    // record the call for the next time
+    cudaGraph_t graph = nullptr;
+    cudaGraphExec_t exec = nullptr;
+    float* din = nullptr;
+    float* dout = nullptr;
+    uint32_t* dst_ = nullptr;
+    bool good = !small || (cudaHostGetDevicePointer(reinterpret_cast<void**>(&din), c->pin_in, 0) == cudaSuccess &&
+                           cudaHostGetDevicePointer(reinterpret_cast<void**>(&dout), c->pin_out, 0) == cudaSuccess);
+    if (good && small) dst_ = reinterpret_cast<uint32_t*>(reinterpret_cast<uint8_t*>(dout) + out_pad);
+    good = good && cudaStreamBeginCapture(c->stream, cudaStreamCaptureModeThreadLocal) == cudaSuccess;
+    if (good) {
+      const uint64_t launches = c->launches;
+      bool inner;
+      if (small) {
+        host_in_kernel<<<1, 1024, 0, c->stream>>>(c->ws_in, din, in_elems);
+        inner = cudaGetLastError() == cudaSuccess;
+        inner = inner && fn(c, arg, c->ws_in, c->ws_out) == MXQ_OK;
+        host_out_kernel<<<1, 1024, 0, c->stream>>>(c->ws_out, dout, out_elems, c->status, dst_, c->seq_dev,
+                                                   dst_ + 1);
+        inner = inner && cudaGetLastError() == cudaSuccess;
+      } else {
+        inner = cudaMemcpyAsync(c->ws_in, c->pin_in, in_bytes, cudaMemcpyHostToDevice, c->stream) == cudaSuccess;
+        inner = inner && fn(c, arg, c->ws_in, c->ws_out) == MXQ_OK;
+        inner = inner && cudaMemcpyAsync(c->pin_out, c->ws_out, out_bytes, cudaMemcpyDeviceToHost,
+                                         c->stream) == cudaSuccess;
+        inner = inner && cudaMemcpyAsync(c->status_host, c->status, sizeof(uint32_t), cudaMemcpyDeviceToHost,
+                                         c->stream) == cudaSuccess;
+      }
+      c->launches = launches;
+      good = cudaStreamEndCapture(c->stream, &graph) == cudaSuccess && inner && graph && c->ws_gen == gen0;
+    }
+    if (good) good = cudaGraphInstantiate(&exec, graph, 0) == cudaSuccess;
+    if (graph) cudaGraphDestroy(graph);
+    (void)cudaGetLastError();
+    hg->gen = c->ws_gen;
+    hg->stream = c->stream;
+    hg->exec = good ? exec : nullptr;
+    hg->mapped = small;
+    if (!good && exec) cudaGraphExecDestroy(exec);
+  }
+  return MXQ_OK;
 }
 
 struct LinArg { mxq_weight w; size_t b; };
@@ -864,7 +1077,7 @@ int mxq_linear_host(mxq_ctx c, mxq_weight w, const float* x_host, size_t b, floa
     if (!x_host || !y_host || b == 0) return fail(c, MXQ_ERR_INVALID_ARGUMENT, "null pointer or empty batch");
     DeviceGuard g(c->device);
     LinArg la{w, b};
-    return host_call(c, b * w->v.K, b * w->v.N, x_host, y_host,
+    return host_call(c, 1, w->serial, 0, b, b * w->v.K, b * w->v.N, x_host, y_host,
                      [](mxq_context* cc, void* p, const float* xi, float* yo) {
                        auto* a = static_cast<LinArg*>(p);
                        return linear_dev(cc, a->w, xi, a->b, yo, MXQ_ACT_NONE);
@@ -883,7 +1096,7 @@ int mxq_linear_pair_host(mxq_ctx c, mxq_weight w1, mxq_weight w2, const float* x
       return fail(c, MXQ_ERR_INVALID_ARGUMENT, "pair shape mismatch: w1 N=%d, w2 K=%d", w1->v.N, w2->v.K);
     DeviceGuard g(c->device);
     PairArg pa{w1, w2, b};
-    return host_call(c, b * w1->v.K, b * w2->v.N, x_host, y_host,
+    return host_call(c, 2, w1->serial, w2->serial, b, b * w1->v.K, b * w2->v.N, x_host, y_host,
                      [](mxq_context* cc, void* p, const float* xi, float* yo) {
                        auto* a = static_cast<PairArg*>(p);
                        return mxq_linear_pair(cc, a->w1, a->w2, xi, a->b, yo);
