@@ -9,14 +9,15 @@
 // contiguous, balanced range of groups (ranges differ by one group: for a
 // 7B MLP 18-19 groups of the up projection, 6-7 of the down projection per
 // CTA).  Inside a CTA the 16 warps split K; a warp streams its K-slice of
-// every group it owns, straight from HBM into registers (128-bit
-// ld.global.nc, no L1 allocation), with two batches of 8 loads in flight
-// (128 KB per SM).  In the tiled weight layout a group's k-tile is 128 (int4)
-// or 256 (int8) contiguous bytes, so one warp load covers 4 (2) k-tiles of the
-// group in full 128-byte lines.  Partial sums stay inside the CTA: each warp
-// folds its lanes with shuffles, writes one value per row to shared memory,
-// and after the last group the CTA adds the 16 warps' values in warp order
-// -- no cross-CTA reduction, deterministic results.
+// every group it owns from HBM into a ring of shared-memory slots private to
+// each thread (cp.async, up to 16 rounds in flight, issued before the kernel
+// waits for its predecessor), and reads back only what it loaded.  In the
+// tiled weight layout a group's k-tile is 128 (int4) or 256 (int8)
+// contiguous bytes, so one warp round covers 4 (2) k-tiles of the group in
+// full 128-byte lines.  Partial sums stay inside the CTA: each warp folds its
+// lanes with shuffles, writes one value per row to shared memory, and after
+// the last group the CTA adds the 16 warps' values in warp order -- no
+// cross-CTA reduction, deterministic results.
 //
 // Activations (an MX activation, or fp32 rows quantised here with
 // quantize_kernel's arithmetic -- identical bytes) are staged once per warp
@@ -32,7 +33,36 @@ namespace {
 
 constexpr int kWarps = 16;
 constexpr int kThreads = kWarps * 32;
-constexpr int kD = 8;   // loads per batch (two batches in flight)
+// Weight loads land in a per-thread ring of kRing 16-byte slots in shared
+// memory (cp.async, slot-major so a warp's accesses are contiguous), with
+// the 4-byte words holding their scale bytes beside them: 16 rounds (128 KB
+// per SM; 8 rounds for batches 3-4) are in flight from the first
+// instruction.
+template <int NB>
+struct RRing {
+  static constexpr int R = 8;
+  static constexpr int BYTES = R * kThreads * (16 + 4);
+};
+
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async4(uint32_t dst, const void* src) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(dst), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+__device__ __forceinline__ uint4 lds128(uint32_t a) {
+  uint4 v;
+  asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(a));
+  return v;
+}
+__device__ __forceinline__ uint32_t lds32(uint32_t a) {
+  uint32_t v;
+  asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(a));
+  return v;
+}
 
 template <int WFMT>
 struct RCfg {
@@ -72,7 +102,7 @@ __host__ __device__ __forceinline__ RGeom rgeom(const WeightView& w) {
 }
 
 template <int WFMT, int NB, bool FAST, bool INF32>
-__global__ void __launch_bounds__(kThreads, 1) rgemv_kernel(GemvArgs a) {
+__global__ void __launch_bounds__(kThreads, 2) rgemv_kernel(GemvArgs a) {
   using C = RCfg<WFMT>;
   extern __shared__ __align__(16) uint8_t smem[];
   const RGeom g = rgeom<WFMT>(a.w);
@@ -92,9 +122,11 @@ __global__ void __launch_bounds__(kThreads, 1) rgemv_kernel(GemvArgs a) {
   // shared memory: per warp its activation slice, then the partial sums
   const int slice = g.kts * kTileK;                      // activation bytes per token
   const int per_warp = (NB * slice + NB * g.kts * 2 * 4 + 15) / 16 * 16;
-  int8_t* act = reinterpret_cast<int8_t*>(smem + warp * per_warp);
+  constexpr int kRing = RRing<NB>::R;
+  constexpr int kRingBytes = RRing<NB>::BYTES;
+  int8_t* act = reinterpret_cast<int8_t*>(smem + kRingBytes + warp * per_warp);
   float* fa = reinterpret_cast<float*>(act + NB * slice);
-  float* part = reinterpret_cast<float*>(smem + kWarps * per_warp);   // [warp][group][4 rows][NB]
+  float* part = reinterpret_cast<float*>(smem + kRingBytes + kWarps * per_warp);   // [warp][group][4 rows][NB]
   const int max_ng = (g.G4 + G - 1) / G;
 
   // The lane streams the sequence (group gi, load li) with li fastest; two
@@ -131,25 +163,34 @@ __global__ void __launch_bounds__(kThreads, 1) rgemv_kernel(GemvArgs a) {
   row_base(ic);
   int issued = 0;
 
-  uint4 wa[kD], wb[kD];
-  uint32_t sa[kD], sb[kD];
-  auto issue = [&](uint4 (&w)[kD], uint32_t (&s)[kD]) {
-#pragma unroll
-    for (int d = 0; d < kD; ++d) {
-      if (issued < Q) {
-        if ((kmask >> ic.li) & 1u) {
-          w[d] = ldg_stream(ic.wp);
-          s[d] = __ldg(ic.sp);
-        } else {
-          w[d] = make_uint4(0, 0, 0, 0);
-          s[d] = 127;
-        }
-        step(ic);
-        ++issued;
+  const uint32_t ring_w = smem_u32(smem);
+  const uint32_t ring_s = ring_w + kRing * kThreads * 16;
+  const int tid = threadIdx.x;
+  // the scale byte's position in its aligned 4-byte word (rows of a lane
+  // keep one parity; the scale array starts 4-byte aligned)
+  const int ssub = (2 * (rr & 1) + bh) & 3;
+  // one round: this thread's next load (if any) into ring slot `slot`; a
+  // group is committed every round, so the wait depth below stays constant
+  auto issue_one = [&](int slot) {
+    if (issued < Q) {
+      if ((kmask >> ic.li) & 1u) {
+        cp_async16(ring_w + (uint32_t)(slot * kThreads + tid) * 16u, ic.wp);
+        cp_async4(ring_s + (uint32_t)(slot * kThreads + tid) * 4u,
+                  reinterpret_cast<const void*>(reinterpret_cast<uintptr_t>(ic.sp) & ~(uintptr_t)3));
       }
+      step(ic);
+      ++issued;
     }
+    cp_async_commit();
   };
-  issue(wa, sa);
+  // the weights do not depend on the previous kernel: the whole ring is in
+  // flight before the wait for it
+#pragma unroll 1
+  for (int r = 0; r < kRing; ++r) issue_one(r);
+  // Two CTAs fit on an SM: let the next kernel on the stream launch now, so
+  // its CTAs start their own weight stream while this one finishes (its
+  // griddepcontrol.wait still waits for this whole grid to complete).
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   if (a.pf_bytes && threadIdx.x == 0) {
     prefetch_l2_share(a.pf_ptr, a.pf_bytes, blockIdx.x, gridDim.x);
     prefetch_l2_share(a.pf_ptr2, a.pf_bytes2, blockIdx.x, gridDim.x);
@@ -299,18 +340,21 @@ __global__ void __launch_bounds__(kThreads, 1) rgemv_kernel(GemvArgs a) {
 
   // every lane runs the same number of steps (Q is CTA-uniform), so the
   // shuffles above are never divergent
-  for (int q0 = 0; q0 < Q; q0 += 2 * kD) {
-    issue(wb, sb);
-#pragma unroll
-    for (int d = 0; d < kD; ++d)
-      if (q0 + d < Q) compute(wa[d], sa[d]);
-    issue(wa, sa);
-#pragma unroll
-    for (int d = 0; d < kD; ++d)
-      if (q0 + kD + d < Q) compute(wb[d], sb[d]);
+#pragma unroll 1
+  for (int q = 0; q < Q; ++q) {
+    cp_async_wait<kRing - 1>();                     // round q has landed
+    const int slot = q % kRing;
+    uint4 w = make_uint4(0, 0, 0, 0);
+    uint32_t sc = 127;
+    if ((kmask >> cli) & 1u) {
+      w = lds128(ring_w + (uint32_t)(slot * kThreads + tid) * 16u);
+      sc = (lds32(ring_s + (uint32_t)(slot * kThreads + tid) * 4u) >> (8 * ssub)) & 0xFFu;
+    }
+    compute(w, sc);
+    issue_one(slot);                                // refill the slot just read
   }
+  cp_async_wait<0>();
 
-  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   __syncthreads();
   // y = sum over the 16 warps, in warp order
   for (int e = threadIdx.x; e < ng * 4 * NB; e += kThreads) {
@@ -342,7 +386,8 @@ size_t smem_bytes(const WeightView& w, int nb) {
   const int per_warp = (nb * g.kts * kTileK + nb * g.kts * 2 * 4 + 15) / 16 * 16;
   const int G = sms();
   const int max_ng = (g.G4 + G - 1) / G;
-  return (size_t)kWarps * per_warp + (size_t)kWarps * max_ng * 4 * nb * 4;
+  const size_t ring = nb <= 2 ? RRing<1>::BYTES : RRing<4>::BYTES;
+  return ring + (size_t)kWarps * per_warp + (size_t)kWarps * max_ng * 4 * nb * 4;
 }
 
 template <int WFMT, int NB, bool FAST, bool INF32>
