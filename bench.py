@@ -314,6 +314,9 @@ def time_ppo(ctx, dev, args, world, max_over_ranks, barrier, peaks, rank):
     Wp = mx.MXWeight(torch.from_numpy(wp), torch.from_numpy(sp), 8, p["latent"], p["state_padded"], ctx)
     Wpi = mx.MXWeight(torch.from_numpy(wpi), torch.from_numpy(spi), 8, p["actions"], p["latent"], ctx)
     Wv = mx.MXWeight(torch.from_numpy(wv), torch.from_numpy(sv), 8, 1, p["latent"], ctx)
+    # policy and value rows as one head weight: the latent is quantised once
+    Wh = mx.MXWeight(torch.from_numpy(np.concatenate([wpi, wv])), torch.from_numpy(np.concatenate([spi, sv])), 8,
+                     p["actions"] + 1, p["latent"], ctx)
     g = torch.Generator(device=dev)
     g.manual_seed(404)
     states = torch.randn((rows, p["state_padded"]), generator=g, device=dev)
@@ -326,7 +329,7 @@ def time_ppo(ctx, dev, args, world, max_over_ranks, barrier, peaks, rank):
     nv = torch.zeros(p["rollouts"], device=dev)
 
     def step():
-        lp, alp, ent, val = mx.ppo_rollout_forward(states, actions, Wp, Wpi, Wv, ctx)
+        lp, alp, ent, val = mx.ppo_rollout_forward(states, actions, Wp, Wh, None, ctx)
         return mx.fused_compute_gae(rewards, val.reshape(p["steps"], p["rollouts"]), dones, nv, 0.99, 0.95, ctx)
 
     for _ in range(2):
@@ -344,10 +347,12 @@ def time_ppo(ctx, dev, args, world, max_over_ranks, barrier, peaks, rank):
     torch.cuda.synchronize()
     ms = max_over_ranks(e0.elapsed_time(e1) / n)
     flops = 2.0 * rows * p["latent"] * (p["state_padded"] + p["actions"] + 1)
+    Wpi.close()
+    Wv.close()
     out = {"rows_per_s": world * rows / (ms / 1e3), "ms_per_batch": ms, "batches": n,
            "tflops": flops / (ms / 1e3) / 1e12, "frac_of_bf16_peak": flops / (ms / 1e3) / 1e12 / peaks["bf16_tflops"],
            "config": dict(p, weights="mx-int8", gae="gamma 0.99, lambda 0.95"),
-           "api": "mx.ppo_rollout_forward (3 x mxq_linear + mxq_policy_head) + mxq_gae"}
+           "api": "mx.ppo_rollout_forward (mxq_linear projection + one combined policy/value head linear + mxq_policy_head) + mxq_gae"}
     if rank == 0 and world == 1 and not args.no_cpu:
         from oracle import oracle
         sample = 64
@@ -370,7 +375,7 @@ def time_ppo(ctx, dev, args, world, max_over_ranks, barrier, peaks, rank):
         out["cpu_baseline"] = {"value": reps * sample / el, "unit": "rows/s", "cores": oracle.max_threads(),
                                "kind": "port", "sample": "%d x %d rows through the three MX linears + head (%.1f s), %s"
                                % (reps, sample, el, "AVX-512 VNNI dpbusd" if used else "portable int loop")}
-    for w in (Wp, Wpi, Wv):
+    for w in (Wp, Wh):
         w.close()
     return out
 

@@ -391,12 +391,14 @@ def policy_head(logits, actions, ctx=None):
     return lp, alp, ent
 
 
-def ppo_rollout_forward(states, actions, w_proj, w_policy, w_value, ctx=None):
+def ppo_rollout_forward(states, actions, w_proj, w_policy, w_value=None, ctx=None):
     """The rollout forward of PPOTrainer::update_step
-    (training/ppo_trainer.cpp:57-66, :77) with its three products as MX
-    linears: latent = states . proj, logits = latent . policy^T, values =
-    latent . value^T, then the policy head.  states [R][S] is zero-padded to
-    the projection's K (S = 1616 -> 1632, the next multiple of 32).
+    (training/ppo_trainer.cpp:57-66, :77) with its products as MX linears:
+    latent = states . proj, logits = latent . policy^T, values = latent .
+    value^T, then the policy head.  states [R][S] is zero-padded to the
+    projection's K (S = 1616 -> 1632, the next multiple of 32).  With
+    w_value None, w_policy holds A + 1 rows, the last being the value head,
+    so the latent is quantised once for both.
     Returns (log_probs, action_logp, entropy, values [R])."""
     ctx = ctx or w_proj.ctx
     _need_cuda(states, torch.float32, "states")
@@ -405,7 +407,12 @@ def ppo_rollout_forward(states, actions, w_proj, w_policy, w_value, ctx=None):
             raise ValueError("states have %d features, projection K is %d" % (states.shape[1], w_proj.k))
         states = torch.nn.functional.pad(states, (0, w_proj.k - states.shape[1]))
     latent = mx_linear(states.contiguous(), w_proj, ctx)
-    logits = mx_linear(latent, w_policy, ctx)
-    values = mx_linear(latent, w_value, ctx)[:, 0]
+    if w_value is None:
+        head = mx_linear(latent, w_policy, ctx)
+        a = head.shape[1] - 1
+        logits, values = head[:, :a].contiguous(), head[:, a].contiguous()
+    else:
+        logits = mx_linear(latent, w_policy, ctx)
+        values = mx_linear(latent, w_value, ctx)[:, 0]
     lp, alp, ent = policy_head(logits, actions, ctx)
     return lp, alp, ent, values

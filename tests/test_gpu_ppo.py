@@ -70,5 +70,11 @@ def test_ppo_rollout_forward_reference_shapes(ctx):
     assert rel_l2(host(lp), lp0) <= REL_TOL
     assert rel_l2(host(alp), alp0) <= REL_TOL
     assert rel_l2(host(ent), ent0) <= REL_TOL
-    for w in (Wp, Wpi, Wv):
+    # one combined [81][2048] head: the latent quantised once, same results
+    Wh = mx.MXWeight(torch.from_numpy(np.concatenate([wpi, wv])), torch.from_numpy(np.concatenate([spi, sv])),
+                     8, a + 1, d, ctx)
+    lp2, alp2, ent2, val2 = mx.ppo_rollout_forward(cuda(states), cuda(actions), Wp, Wh, None, ctx)
+    assert rel_l2(host(lp2), host(lp)) <= 1e-6 and rel_l2(host(val2), host(val)) <= 1e-6
+    assert rel_l2(host(alp2), host(alp)) <= 1e-6 and rel_l2(host(ent2), host(ent)) <= 1e-6
+    for w in (Wp, Wpi, Wv, Wh):
         w.close()
