@@ -368,6 +368,301 @@ __global__ void __launch_bounds__(kThreads, 2) rgemv_kernel(GemvArgs a) {
   }
 }
 
+// ---------------------------------------------------------------------------
+// Weight-resident decode GEMV (batch 1).  The ring kernel above keeps only 8
+// of a CTA's ~20 rounds in flight before it must wait for its predecessor;
+// the rest stream after the wait with their HBM latency exposed (timestamped
+// traces of the 7B up projection: ~6.5 us of an ~8.5 us launch period were
+// spent in the loop after the wait).  Here one CTA per SM holds its whole
+// share in registers: every weight load (up to kResRounds 16-byte loads a
+// thread, 96 registers) and the 256-byte scale blocks of the row tiles it
+// touches (16-byte cp.async into shared memory) are issued before
+// griddepcontrol.wait.  The activation row is then copied into shared memory
+// with one round of cp.async and quantised there, and the dot products run
+// from registers.  For int4 weights each 8-element group of the activation
+// is stored even elements first, so a weight word's low nibbles (shifted up)
+// and high nibbles (masked) are 16*w bytes that meet their activations
+// without byte permutes; 4 groups share each activation load and their lanes
+// are folded together by a transpose reduction.  The K range is dealt to the
+// 16 warps in contiguous runs of whole loads whose lengths differ by at most
+// one (the down projection's 43 loads go 3,3,...,2).
+constexpr int kResRounds = 24;
+
+struct ResGeom {
+  int KT, NL, kts, G4;   // k-tiles, loads per group, k-tiles of the largest warp slice, 4-row groups
+};
+
+template <int WFMT>
+__host__ __device__ __forceinline__ ResGeom res_geom(const WeightView& w) {
+  using C = RCfg<WFMT>;
+  ResGeom g;
+  g.KT = w.Kpad / kTileK;
+  g.NL = (g.KT + C::KPL - 1) / C::KPL;
+  g.kts = (g.NL + kWarps - 1) / kWarps * C::KPL;
+  g.G4 = (w.N + 3) / 4;
+  return g;
+}
+
+template <int WFMT>
+int res_rounds(const WeightView& w, int ctas) {
+  const ResGeom g = res_geom<WFMT>(w);
+  const int max_ng = (g.G4 + ctas - 1) / ctas;
+  return (max_ng + 3) / 4 * 4 * ((g.NL + kWarps - 1) / kWarps);
+}
+
+template <int WFMT>
+size_t res_smem_bytes(const WeightView& w, bool inf32, int ctas) {
+  const ResGeom g = res_geom<WFMT>(w);
+  const int per_warp = (g.kts * kTileK + g.kts * 2 * 4 + 15) / 16 * 16;
+  const int max_ng = (g.G4 + ctas - 1) / ctas;
+  const size_t xin = ((size_t)w.K * (inf32 ? 4 : 1) + 15) / 16 * 16;
+  return (size_t)2 * g.KT * 256 + xin + (size_t)kWarps * per_warp + (size_t)kWarps * max_ng * 4 * 4;
+}
+
+template <int WFMT, bool FAST, bool INF32>
+__global__ void __launch_bounds__(kThreads, 1) rgemv_res_kernel(GemvArgs a) {
+  using C = RCfg<WFMT>;
+  constexpr int GB = 4, RMAX = kResRounds;
+  extern __shared__ __align__(16) uint8_t smem[];
+  const ResGeom g = res_geom<WFMT>(a.w);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, tid = threadIdx.x;
+  const int G = gridDim.x;
+  const int g_lo = (int)((long)blockIdx.x * g.G4 / G);
+  const int ng = (int)((long)(blockIdx.x + 1) * g.G4 / G) - g_lo;
+  const int nbk = (ng + GB - 1) / GB;
+  const int l_lo = warp * g.NL / kWarps;
+  const int nload = (warp + 1) * g.NL / kWarps - l_lo;
+  const int kt0 = l_lo * C::KPL;
+  const int nr = nbk * nload * GB;                       // <= RMAX (checked by the host)
+  const int kto = lane / C::LPK;
+  const int rr = (lane % C::LPK) / C::TPL;
+  const int sub = lane % C::TPL;
+  const int bh = WFMT == 4 ? sub : (sub >> 1);
+  uint32_t kmask = 0;
+  for (int li = 0; li < nload && li < 32; ++li)
+    if (kt0 + li * C::KPL + kto < g.KT) kmask |= 1u << li;
+
+  // shared memory: the 256-byte scale blocks [2 row tiles][KT] of the (at
+  // most two) row tiles this CTA's rows touch, the activation input, then per
+  // warp its quantised K-slice, then the partial sums
+  const int K = a.w.K;
+  const int slice = g.kts * kTileK;
+  const int nblk = g.kts * 2;
+  const int per_warp = (slice + nblk * 4 + 15) / 16 * 16;
+  const int max_ng = (g.G4 + G - 1) / G;
+  const uint32_t sc_base = smem_u32(smem);
+  const int rt0 = (g_lo * 4) >> 7;                          // first row tile of this CTA
+  const int nrt = (((g_lo + ng) * 4 - 1) >> 7) - rt0 + 1;   // 1 or 2 (ng * 4 <= 96 rows)
+  uint8_t* xin = smem + 2 * g.KT * 256;
+  const int xin_bytes = (K * (INF32 ? 4 : 1) + 15) / 16 * 16;
+  int8_t* act = reinterpret_cast<int8_t*>(xin + xin_bytes + warp * per_warp);
+  float* fa = reinterpret_cast<float*>(act + slice);
+  float* part = reinterpret_cast<float*>(xin + xin_bytes + kWarps * per_warp);
+
+  // ---- every weight load of this thread, before the wait
+  uint4 wv[RMAX];
+  uint32_t vmask = 0;                                    // rounds that were loaded
+  {
+    int ibi = 0, ili = 0;
+#pragma unroll
+    for (int r = 0; r < RMAX; ++r) {
+      const int gg = r % GB;
+      const int gi = ibi * GB + gg;
+      wv[r] = make_uint4(0, 0, 0, 0);
+      if (r < nr && gi < ng && ((kmask >> ili) & 1u)) {
+        const int n = (g_lo + gi) * 4 + rr;
+        const size_t rowoff = ((size_t)(n >> 7) * g.KT + kt0 + ili * C::KPL + kto) * 128 + (n & 127);
+        wv[r] = ldg_stream(a.w.data + rowoff * C::TB + sub * 16);
+        vmask |= 1u << r;
+      }
+      if (gg == GB - 1 && ++ili == nload) { ili = 0; ++ibi; }
+    }
+    // the scale blocks: contiguous [KT][256 B] per row tile, 16-byte copies
+    const int per_rt = g.KT * 16;
+    for (int c = tid; c < nrt * per_rt; c += kThreads) {
+      const int part_ = c / per_rt, cc = c % per_rt;
+      cp_async16(sc_base + (uint32_t)(part_ * per_rt + cc) * 16u,
+                 a.w.scales + ((size_t)(rt0 + part_) * g.KT * 256 + (size_t)cc * 16));
+    }
+    cp_async_commit();
+  }
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  if (a.pf_bytes && threadIdx.x == 0) {
+    prefetch_l2_share(a.pf_ptr, a.pf_bytes, blockIdx.x, gridDim.x);
+    prefetch_l2_share(a.pf_ptr2, a.pf_bytes2, blockIdx.x, gridDim.x);
+  }
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+
+  // ---- the activation row into shared memory (one round of copies), and
+  // this lane's MX block scales into registers meanwhile
+  const int kb = K / kBlock;
+  if (INF32) {
+    for (int c = tid; c < K / 4; c += kThreads) cp_async16(smem_u32(xin) + c * 16, a.xf + c * 4);
+  } else {
+    for (int c = tid; c < K / 16; c += kThreads) cp_async16(smem_u32(xin) + c * 16, a.xq + c * 16);
+  }
+  cp_async_commit();
+  float fxs[2] = {0.0f, 0.0f};
+  if (!INF32) {
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      const int bb = lane + 32 * i, b = kt0 * 2 + bb;
+      if (bb < nblk && b < kb) fxs[i] = e8m0_to_float(a.xs[b]);
+    }
+  }
+  cp_async_wait<0>();
+  __syncthreads();
+
+  // ---- quantise this warp's K-slice (quantize_kernel's arithmetic)
+  if (INF32) {
+    const float* xf = reinterpret_cast<const float*>(xin);
+    for (int c = lane; c < nblk * 8; c += 32) {            // 8-lane groups share a block
+      const int bl = c / 8, p4 = c % 8;
+      const int b = kt0 * 2 + bl;
+      const bool live = b < kb;
+      float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (live) v = *reinterpret_cast<const float4*>(xf + b * kBlock + p4 * 4);
+      const float e4[4] = {v.x, v.y, v.z, v.w};
+      float m = 0.0f;
+      bool nf = false;
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float av = fabsf(e4[e]);
+        nf |= !(av <= 3.402823466e38f);
+        m = fmaxf(m, nf ? 0.0f : av);
+      }
+#pragma unroll
+      for (int o = 4; o > 0; o >>= 1) {
+        m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+        nf |= __shfl_xor_sync(0xffffffffu, (int)nf, o) != 0;
+      }
+      uint32_t s8 = 0;
+      int e = 0;
+      if (live) {
+        if (nf) s8 = 255;
+        else if (m != 0.0f) { e = e8m0_exponent<127>(m); s8 = (uint32_t)(e + 127); }
+      }
+      uint32_t packed = 0;
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const int q = (s8 != 0 && s8 != 255) ? quant_value(e4[k], e) : 0;
+        packed |= ((uint32_t)q & 0xFFu) << (8 * k);
+      }
+      if (WFMT == 4) {   // lanes p4 = 2j, 2j+1 hold the two halves of an 8-group
+        const uint32_t other = __shfl_xor_sync(0xffffffffu, packed, 1);
+        packed = (p4 & 1) ? __byte_perm(other, packed, 0x7531) : __byte_perm(packed, other, 0x6420);
+      }
+      *reinterpret_cast<uint32_t*>(act + bl * kBlock + p4 * 4) = packed;
+      if (p4 == 0) fa[bl] = live ? e8m0_to_float(s8) : 0.0f;
+    }
+  } else {
+    for (int c = lane; c < g.kts * 4; c += 32) {
+      const int k = kt0 * kTileK + c * 16;
+      uint4 v = make_uint4(0, 0, 0, 0);
+      if (k < K) {
+        v = *reinterpret_cast<const uint4*>(xin + k);
+        v.x ^= 0x80808080u; v.y ^= 0x80808080u; v.z ^= 0x80808080u; v.w ^= 0x80808080u;
+        if (WFMT == 4)
+          v = make_uint4(__byte_perm(v.x, v.y, 0x6420), __byte_perm(v.x, v.y, 0x7531),
+                         __byte_perm(v.z, v.w, 0x6420), __byte_perm(v.z, v.w, 0x7531));
+      }
+      *reinterpret_cast<uint4*>(act + c * 16) = v;
+    }
+#pragma unroll
+    for (int i = 0; i < 2; ++i)
+      if (lane + 32 * i < nblk) fa[lane + 32 * i] = fxs[i];
+  }
+  __syncwarp();
+
+  // ---- dot products from registers
+  const int8_t* xrow = act + kto * kTileK + (WFMT == 4 ? sub * 32 : sub * 16);
+  const float* frow = fa + kto * 2 + bh;
+  // lane bits that separate the lanes of one row: sub-slice bits, then the
+  // k-tile bits (int4: 1, 8, 16; int8: 1, 2, 16)
+  constexpr int LA = 1, LB = WFMT == 4 ? 8 : 2, LC = 16;
+  const bool bA = (lane & LA) != 0, bB = (lane & LB) != 0;
+  // this lane's scale byte for group gi at load li (row tile, k-tile, row, block)
+  auto scale_at = [&](int gi, int li_) -> uint32_t {
+    const int n = (g_lo + gi) * 4 + rr;
+    const int off = (((n >> 7) - rt0) * g.KT + kt0 + li_ * C::KPL + kto) * 256 + (n & 127) * 2 + bh;
+    uint32_t v;
+    asm volatile("ld.shared.u8 %0, [%1];" : "=r"(v) : "r"(sc_base + (uint32_t)off));
+    return v;
+  };
+  float acc[GB] = {0.0f, 0.0f, 0.0f, 0.0f};
+  int li = 0, bi = 0;
+#pragma unroll
+  for (int r0 = 0; r0 < RMAX; r0 += GB) {
+    if (r0 < nr) {                                       // warp-uniform
+      const int j = li * C::KPL;
+      const float fx = frow[j * 2];
+      uint4 x0, x1 = make_uint4(0, 0, 0, 0);
+      x0 = *reinterpret_cast<const uint4*>(xrow + j * kTileK);
+      if (WFMT == 4) x1 = *reinterpret_cast<const uint4*>(xrow + j * kTileK + 16);
+#pragma unroll
+      for (int gg = 0; gg < GB; ++gg) {
+        const int r = r0 + gg;
+        const uint32_t s = (vmask >> r) & 1u ? scale_at(bi * GB + gg, li) : 127u;
+        const uint4 w = wv[r];
+        int d0, d1;
+        float fw;
+        if (WFMT == 4) {
+          fw = FAST ? __int_as_float((int)((s - C::SHIFT) << 23))
+                    : (s == 255u ? __int_as_float(0x7fc00000) : pow2_exact((int)s - 127 - C::SHIFT));
+          const uint32_t m = 0xF0F0F0F0u;
+          d0 = __dp4a((int)((w.x << 4) & m), (int)x0.x, 0);
+          d1 = __dp4a((int)(w.x & m), (int)x0.y, 0);
+          d0 = __dp4a((int)((w.y << 4) & m), (int)x0.z, d0);
+          d1 = __dp4a((int)(w.y & m), (int)x0.w, d1);
+          d0 = __dp4a((int)((w.z << 4) & m), (int)x1.x, d0);
+          d1 = __dp4a((int)(w.z & m), (int)x1.y, d1);
+          d0 = __dp4a((int)((w.w << 4) & m), (int)x1.z, d0);
+          d1 = __dp4a((int)(w.w & m), (int)x1.w, d1);
+        } else {
+          fw = FAST ? __int_as_float((int)(s << 23)) : (s == 255u ? __int_as_float(0x7fc00000) : pow2_exact((int)s - 127));
+          d0 = __dp4a((int)x0.x, (int)w.x, 0);
+          d1 = __dp4a((int)x0.y, (int)w.y, 0);
+          d0 = __dp4a((int)x0.z, (int)w.z, d0);
+          d1 = __dp4a((int)x0.w, (int)w.w, d1);
+        }
+        acc[gg] = __fmaf_rn((float)(d0 + d1), __fmul_rn(fx, fw), acc[gg]);
+      }
+      if (++li == nload) {
+        // fold the lanes of each row for the 4 groups at once: after the LA
+        // and LB halving steps each lane holds one group
+        const float s0 = bA ? acc[0] : acc[2], s1 = bA ? acc[1] : acc[3];
+        float k0 = bA ? acc[2] : acc[0], k1 = bA ? acc[3] : acc[1];
+        k0 += __shfl_xor_sync(0xffffffffu, s0, LA);
+        k1 += __shfl_xor_sync(0xffffffffu, s1, LA);
+        const float sx = bB ? k0 : k1;
+        float k = bB ? k1 : k0;
+        k += __shfl_xor_sync(0xffffffffu, sx, LB);
+        k += __shfl_xor_sync(0xffffffffu, k, LC);
+        const int gi = bi * GB + (bA ? 2 : 0) + (bB ? 1 : 0);
+        if (!(lane & LC) && gi < ng) part[(warp * max_ng + gi) * 4 + rr] = k;
+#pragma unroll
+        for (int gg = 0; gg < GB; ++gg) acc[gg] = 0.0f;
+        li = 0;
+        ++bi;
+      }
+    }
+  }
+  // warps without loads (K shorter than 16 loads) still own zero partials
+  if (nload == 0)
+    for (int e = lane; e < ng * 4; e += 32) part[(warp * max_ng + e / 4) * 4 + e % 4] = 0.0f;
+
+  __syncthreads();
+  // y = sum over the 16 warps, in warp order
+  for (int e = threadIdx.x; e < ng * 4; e += kThreads) {
+    const int gi = e / 4, r4 = e % 4;
+    const int n = (g_lo + gi) * 4 + r4;
+    float s = 0.0f;
+#pragma unroll
+    for (int w = 0; w < kWarps; ++w) s += part[(w * max_ng + gi) * 4 + r4];
+    if (n < a.w.N) a.y[n] = s;
+  }
+}
+
 int g_sms = 0;
 
 int sms() {
@@ -434,6 +729,50 @@ cudaError_t launch_fast(const GemvArgs& a, cudaStream_t st, bool pdl) {
                                                                       : launch_nb<WFMT, false, INF32>(a, st, pdl);
 }
 
+
+template <int WFMT, bool FAST, bool INF32>
+cudaError_t launch_res_t(const GemvArgs& a, cudaStream_t st, bool pdl) {
+  const int G4 = (a.w.N + 3) / 4;
+  const int grid = G4 < sms() ? G4 : sms();
+  const size_t smem = res_smem_bytes<WFMT>(a.w, INF32, grid);
+  static size_t configured = 0;
+  if (smem > 48 * 1024 && smem > configured) {
+    cudaError_t e = cudaFuncSetAttribute(rgemv_res_kernel<WFMT, FAST, INF32>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    configured = smem;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)grid);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, rgemv_res_kernel<WFMT, FAST, INF32>, a);
+}
+
+template <int WFMT, bool INF32>
+cudaError_t launch_res(const GemvArgs& a, cudaStream_t st, bool pdl) {
+  return a.w.scale_lo >= (WFMT == 4 ? 5 : 1) && a.w.scale_hi <= 254 ? launch_res_t<WFMT, true, INF32>(a, st, pdl)
+                                                                      : launch_res_t<WFMT, false, INF32>(a, st, pdl);
+}
+
+// The weight-resident kernel takes batch 1 when a thread's share fits its
+// registers, the warp slices hold at most 64 MX blocks and everything it
+// stages fits shared memory.
+template <int WFMT>
+bool res_ok(const WeightView& w, int B, bool inf32) {
+  if (B != 1 || w.kt_ptr) return false;
+  const int G4 = (w.N + 3) / 4;
+  const int ctas = G4 < sms() ? G4 : sms();
+  const ResGeom g = res_geom<WFMT>(w);
+  return res_rounds<WFMT>(w, ctas) <= kResRounds && g.kts <= 32 &&
+         res_smem_bytes<WFMT>(w, inf32, ctas) <= 200 * 1024;
+}
 }  // namespace
 
 bool rgemv_supported(const WeightView& w, int B) {
@@ -445,6 +784,8 @@ bool rgemv_supported(const WeightView& w, int B) {
 cudaError_t launch_rgemv(const GemvArgs& a, cudaStream_t st, bool pdl) {
   if (!rgemv_supported(a.w, a.B) || a.rows || a.block_dots) return cudaErrorInvalidValue;
   const bool f32 = a.xf != nullptr;
+  if (a.w.fmt == 4 && res_ok<4>(a.w, a.B, f32)) return f32 ? launch_res<4, true>(a, st, pdl) : launch_res<4, false>(a, st, pdl);
+  if (a.w.fmt == 8 && res_ok<8>(a.w, a.B, f32)) return f32 ? launch_res<8, true>(a, st, pdl) : launch_res<8, false>(a, st, pdl);
   if (a.w.fmt == 4) return f32 ? launch_fast<4, true>(a, st, pdl) : launch_fast<4, false>(a, st, pdl);
   return f32 ? launch_fast<8, true>(a, st, pdl) : launch_fast<8, false>(a, st, pdl);
 }
