@@ -650,7 +650,8 @@ def run_ours(args):
             "data": "synthetic", "config": workload_config(b, args.copies),
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
                          "frac": achieved / peaks["hbm_gbs"], "traffic": None,
-                         "kernel": "rgemv_kernel<int4> (up 4096->11008)" if b <= 4 else "gemm_tc_kernel<int4> (up 4096->11008)",
+                         "kernel": ("rgemv_res_kernel<int4> (up 4096->11008, weight-resident)" if b == 1 else
+                                    "rgemv_kernel<int4> (up 4096->11008)" if b <= 4 else "gemm_tc_kernel<int4> (up 4096->11008)"),
                          "algorithmic_bytes_per_launch": gbytes, "launch_ms": gemv_ms,
                          "peak_src": peaks["src"] + " hbm_gbs (burst copy)"},
             "pair_hbm_gbs": pair_bytes(b) / (ms / 1e3) / 1e9,
