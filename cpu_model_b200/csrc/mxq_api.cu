@@ -339,7 +339,12 @@ int use_gemv(mxq_context* c, size_t b, const mxq_weight_s* w) {
   if (w->v.kt_ptr) return 0;   // block-sparse: the GEMM walks the tile list
   if (c->path == MXQ_PATH_GEMV) return 1;
   if (c->path == MXQ_PATH_GEMM) return 0;
-  return b <= (size_t)kGemvAutoBatch;
+  return b <= (size_t)kGemvAutoBatch || bgemv_supported(w->v, (int)b);
+}
+
+// Batches the GEMV kernels take for this weight.
+int gemv_batch_ok(const mxq_weight_s* w, size_t b) {
+  return b <= (size_t)gemv_max_batch() || bgemv_supported(w->v, (int)b);
 }
 
 int after_launch(mxq_context* c, cudaError_t e, const char* what) {
@@ -352,6 +357,27 @@ int after_launch(mxq_context* c, cudaError_t e, const char* what) {
 // (optional) is the weight the following call will read: its bytes are
 // prefetched into L2 while this GEMV streams, so the next layer starts warm.
 int gemv_f32(mxq_context* c, mxq_weight w, const float* x, size_t b, float* y, mxq_weight next) {
+  if (b >= 2 && bgemv_supported(w->v, (int)b)) {
+    // small batch: MX-quantise the rows, then the MMA GEMV
+    const int K = w->v.K;
+    int rc;
+    if ((rc = ensure(c, c->ws_q, c->ws_q_bytes, b * K, "workspace q"))) return rc;
+    if ((rc = ensure(c, c->ws_s, c->ws_s_bytes, b * K / kBlock, "workspace s"))) return rc;
+    QuantArgs qa{};
+    qa.x = x;
+    qa.B = (int)b;
+    qa.K = K;
+    qa.out_q = c->ws_q;
+    qa.out_s = c->ws_s;
+    if ((rc = after_launch(c, launch_quantize(qa, MXQ_ACT_NONE, c->stream, true), "quantize"))) return rc;
+    GemvArgs ga{};
+    ga.w = w->v;
+    ga.xq = c->ws_q;
+    ga.xs = c->ws_s;
+    ga.y = y;
+    ga.B = (int)b;
+    return after_launch(c, launch_bgemv(ga, c->stream, true), "gemv");
+  }
   GemvArgs ga{};
   ga.w = w->v;
   ga.xf = x;
@@ -373,8 +399,8 @@ int linear_dev(mxq_context* c, mxq_weight w, const float* x, size_t b, float* y,
   const int K = w->v.K;
   int rc;
   if (use_gemv(c, b, w)) {
-    if (b > (size_t)gemv_max_batch())
-      return fail(c, MXQ_ERR_INVALID_ARGUMENT, "GEMV path supports batch <= %d", gemv_max_batch());
+    if (!gemv_batch_ok(w, b))
+      return fail(c, MXQ_ERR_INVALID_ARGUMENT, "GEMV path supports batch <= %d for this weight", gemv_max_batch());
     if (act == MXQ_ACT_NONE) return gemv_f32(c, w, x, b, y, nullptr);
     if ((rc = ensure(c, c->ws_q, c->ws_q_bytes, b * K, "workspace q"))) return rc;
     if ((rc = ensure(c, c->ws_s, c->ws_s_bytes, b * K / kBlock, "workspace s"))) return rc;
@@ -391,6 +417,7 @@ int linear_dev(mxq_context* c, mxq_weight w, const float* x, size_t b, float* y,
     ga.xs = c->ws_s;
     ga.y = y;
     ga.B = (int)b;
+    if (b >= 2 && bgemv_supported(w->v, (int)b)) return after_launch(c, launch_bgemv(ga, c->stream, true), "gemv");
     return after_launch(c, launch_gemv(ga, c->stream, true), "gemv");
   }
   const int BN = gemm_pick_bn((int)b);
@@ -424,14 +451,15 @@ int gemv_dev(mxq_context* c, mxq_weight w, const uint8_t* xq, const uint8_t* xs,
              size_t b, float* y) {
   int rc;
   if (use_gemv(c, b, w)) {
-    if (b > (size_t)gemv_max_batch())
-      return fail(c, MXQ_ERR_INVALID_ARGUMENT, "GEMV path supports batch <= %d", gemv_max_batch());
+    if (!gemv_batch_ok(w, b))
+      return fail(c, MXQ_ERR_INVALID_ARGUMENT, "GEMV path supports batch <= %d for this weight", gemv_max_batch());
     GemvArgs ga{};
     ga.w = w->v;
     ga.xq = xq;
     ga.xs = xs;
     ga.y = y;
     ga.B = (int)b;
+    if (b >= 2 && bgemv_supported(w->v, (int)b)) return after_launch(c, launch_bgemv(ga, c->stream, true), "gemv");
     if (rgemv_supported(w->v, (int)b)) return after_launch(c, launch_rgemv(ga, c->stream, true), "gemv");
     return after_launch(c, launch_gemv(ga, c->stream, true), "gemv");
   }

@@ -83,8 +83,15 @@ struct GemmArgs {
 cudaError_t launch_gemm(const GemmArgs& a, cudaStream_t st, bool pdl);
 int gemm_pick_bn(int B);
 
-// Batches up to this size take the GEMV in MXQ_PATH_AUTO.
+// Batches up to this size take the GEMV in MXQ_PATH_AUTO (larger ones up to
+// kBgemvMaxBatch too, where the small-batch MMA GEMV supports the shape).
 constexpr int kGemvAutoBatch = 4;
+
+// Small-batch decode GEMV on the int8 MMA (mxq_bgemv.cu), 2 <= batch <=
+// kBgemvMaxBatch, MX input only (GemvArgs.xq/xs); no gather/dots/prefetch.
+constexpr int kBgemvMaxBatch = 16;
+bool bgemv_supported(const WeightView& w, int B);
+cudaError_t launch_bgemv(const GemvArgs& a, cudaStream_t st, bool pdl);
 
 // Persistent decode GEMV (mxq_rgemv.cu), batch <= kRgemvMaxBatch: MX or fp32
 // input (GemvArgs.xq/xs or .xf), optional L2 prefetch; no gather/dots.

@@ -124,6 +124,40 @@ def test_gemv_parity(ctx, fmt, b, n, k):
     assert rel_l2(y, ref) <= REL_TOL
 
 
+@pytest.mark.parametrize("fmt", [8, 4])
+@pytest.mark.parametrize("b", [6, 12, 16])
+@pytest.mark.parametrize("n,k", [(33, 96), (1000, 4096)])
+def test_small_batch_mma_gemv_parity(ctx, fmt, b, n, k):
+    """Batches 9-16 on the int8-MMA GEMV (batches 2-8 are covered above)."""
+    w, ws, W = weight(ctx, fmt, n, k, 50 + n + k)
+    x = edge_inputs(b, k, 51 + b)
+    xq, xs = oracle.quantize_x(x)
+    ref = oracle.gemv(fmt, xq, xs, w, ws, n, k)
+    ctx.set_path(mx.PATH_GEMV)
+    try:
+        y = host(mx.mx_gemv(mx.MXActivation(cuda(xq), cuda(xs)), W, ctx))
+        ctx.synchronize()
+    finally:
+        ctx.set_path(mx.PATH_AUTO)
+    assert rel_l2(y, ref) <= REL_TOL
+
+
+@pytest.mark.parametrize("b", [5, 12, 16])
+def test_auto_path_small_batch_fp32(ctx, b):
+    """fp32 rows through mx_linear in the automatic path: the MMA GEMV where
+    the shape fits (up 4096 -> 11008), the tensor-core GEMM otherwise
+    (down 11008 -> 4096 at batch > 8); both against the oracle."""
+    for (n, k, seed) in [(11008, 4096, 61), (4096, 11008, 62)]:
+        w, ws, W = weight(ctx, 4, n, k, seed, -8, -3)
+        x = synth.normal((b, k), seed + b)
+        xq, xs = oracle.quantize_x(x)
+        y = host(mx.mx_linear(cuda(x), W, ctx))
+        ctx.synchronize()
+        rows = np.random.default_rng(seed).choice(n, 128, replace=False).astype(np.int32)
+        ref = oracle.gather_dot(4, xq, xs, w, ws, k, rows)
+        assert rel_l2(y[:, rows], ref) <= REL_TOL
+
+
 # ---------------------------------------------------- tensor-core GEMM ---
 @pytest.mark.parametrize("fmt", [8, 4])
 @pytest.mark.parametrize("b", [1, 9, 16, 40, 64, 100, 256, 300])
