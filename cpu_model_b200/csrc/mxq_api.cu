@@ -357,7 +357,7 @@ int after_launch(mxq_context* c, cudaError_t e, const char* what) {
 // (optional) is the weight the following call will read: its bytes are
 // prefetched into L2 while this GEMV streams, so the next layer starts warm.
 int gemv_f32(mxq_context* c, mxq_weight w, const float* x, size_t b, float* y, mxq_weight next) {
-  if (b >= 2 && bgemv_supported(w->v, (int)b)) {
+  if (bgemv_supported(w->v, (int)b)) {
     // small batch: MX-quantise the rows, then the MMA GEMV
     const int K = w->v.K;
     int rc;
@@ -417,7 +417,7 @@ int linear_dev(mxq_context* c, mxq_weight w, const float* x, size_t b, float* y,
     ga.xs = c->ws_s;
     ga.y = y;
     ga.B = (int)b;
-    if (b >= 2 && bgemv_supported(w->v, (int)b)) return after_launch(c, launch_bgemv(ga, c->stream, true), "gemv");
+    if (bgemv_supported(w->v, (int)b)) return after_launch(c, launch_bgemv(ga, c->stream, true), "gemv");
     return after_launch(c, launch_gemv(ga, c->stream, true), "gemv");
   }
   const int BN = gemm_pick_bn((int)b);
@@ -459,7 +459,7 @@ int gemv_dev(mxq_context* c, mxq_weight w, const uint8_t* xq, const uint8_t* xs,
     ga.xs = xs;
     ga.y = y;
     ga.B = (int)b;
-    if (b >= 2 && bgemv_supported(w->v, (int)b)) return after_launch(c, launch_bgemv(ga, c->stream, true), "gemv");
+    if (bgemv_supported(w->v, (int)b)) return after_launch(c, launch_bgemv(ga, c->stream, true), "gemv");
     if (rgemv_supported(w->v, (int)b)) return after_launch(c, launch_rgemv(ga, c->stream, true), "gemv");
     return after_launch(c, launch_gemv(ga, c->stream, true), "gemv");
   }

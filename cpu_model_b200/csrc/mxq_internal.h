@@ -87,8 +87,11 @@ int gemm_pick_bn(int B);
 // kBgemvMaxBatch too, where the small-batch MMA GEMV supports the shape).
 constexpr int kGemvAutoBatch = 4;
 
-// Small-batch decode GEMV on the int8 MMA (mxq_bgemv.cu), 2 <= batch <=
-// kBgemvMaxBatch, MX input only (GemvArgs.xq/xs); no gather/dots/prefetch.
+// Small-batch decode GEMV on the int8 MMA (mxq_bgemv.cu), kBgemvMinBatch <=
+// batch <= kBgemvMaxBatch, MX input only (GemvArgs.xq/xs); no
+// gather/dots/prefetch.  Batch 2 stays on the cp.async-ring kernel, which
+// measured faster there (10.2 vs 11.6 us for the 7B up projection).
+constexpr int kBgemvMinBatch = 3;
 constexpr int kBgemvMaxBatch = 16;
 bool bgemv_supported(const WeightView& w, int B);
 cudaError_t launch_bgemv(const GemvArgs& a, cudaStream_t st, bool pdl);

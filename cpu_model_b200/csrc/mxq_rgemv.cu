@@ -27,6 +27,7 @@
 // 2^(e_x + e_w - 4) scales it into the fp32 sum.
 #include "mxq_internal.h"
 
+
 namespace mxq {
 
 namespace {
