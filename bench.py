@@ -35,6 +35,10 @@ UP = (11008, 4096)     # (N, K)
 DOWN = (4096, 11008)
 EMIN, EMAX = -8, -3
 COPIES = 8
+# DRAM bytes of one batch-1 up-projection launch on MX input, measured with
+# ncu (dram__bytes_read.sum 24,021,760 + dram__bytes_write.sum 0) against the
+# 24,001,664 algorithmic bytes: every weight byte crosses DRAM once
+ROOFLINE_TRAFFIC_B1 = 24021760
 SWEEP = [8, 64, 512]
 # block-sparse MoE layer: 4096 tokens, d 4096, 8 experts, top-2, SwiGLU FFN
 # 14336, MX-int4 expert matrices with 25 % of their 64x64 blocks present
@@ -649,7 +653,11 @@ def run_ours(args):
             "vs_baseline": None, "dtype": "mx-int4 (int4 w, int8 a, int32 dot, fp32 sum)",
             "data": "synthetic", "config": workload_config(b, args.copies),
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
-                         "frac": achieved / peaks["hbm_gbs"], "traffic": None,
+                         "frac": achieved / peaks["hbm_gbs"],
+                         "traffic": ROOFLINE_TRAFFIC_B1 if b == 1 else None,
+                         "traffic_src": ("ncu dram__bytes_read.sum + dram__bytes_write.sum of one "
+                                         "rgemv_res_kernel<int4, MX in> launch (up 4096->11008), "
+                                         "profiles/rgemv_res_int4_b1_mlp_pair.md") if b == 1 else None,
                          "kernel": ("rgemv_res_kernel<int4> (up 4096->11008, weight-resident)" if b == 1 else
                                     "rgemv_kernel<int4> (up 4096->11008)" if b <= 4 else "gemm_tc_kernel<int4> (up 4096->11008)"),
                          "algorithmic_bytes_per_launch": gbytes, "launch_ms": gemv_ms,
