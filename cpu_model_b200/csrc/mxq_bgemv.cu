@@ -25,10 +25,10 @@
 // warp streams its (unit, k-tile) stages -- 16 rows x 32 (64) bytes plus the
 // 32 scale bytes -- through a private shared-memory ring of 6 stages with
 // cp.async, the first ring's worth issued before the kernel waits for its
-// predecessor.  Accumulators stay in registers per
-// unit; after the last stage each warp parks its partial sums in its own
-// shared-memory region and the CTA adds the 16 warps'
-// values in warp order: deterministic, no cross-CTA reduction.
+// predecessor.  Accumulators stay in registers per unit; after the last
+// stage each warp parks its partial sums in its own shared-memory region and
+// the CTA adds the 16 warps' values in warp order: deterministic, no
+// cross-CTA reduction.
 //
 // Input: an MX activation (u8 q+128 bytes and E8M0 scales).  fp32 callers
 // quantise first (quantize_kernel), which gives the same bytes.
@@ -118,24 +118,28 @@ __global__ void __launch_bounds__(kBT, 1) bgemv_kernel(GemvArgs a) {
   uint8_t* act = ring + kBR * C::SB;
   float* fa = reinterpret_cast<float*>(act + g.kts * 2 * NT * 32);
 
-  // stage q = (unit q / nkt, k-tile kt0 + q % nkt): lane L copies 16 B
-  // (int4) / 32 B (int8) of row L/2, lanes 0-1 the 32 scale bytes
-  auto issue = [&](int q, int slot) {
-    if (q < Q) {
-      const int u = u_lo + q / nkt, kt = kt0 + q % nkt;
-      const int row0 = u * 16;
-      const size_t tile = (size_t)(row0 >> 7) * g.KT + kt;
-      const int r = lane >> 1, h = lane & 1;
-      const uint8_t* src = a.w.data + (tile * 128 + (row0 & 127) + r) * C::TB + h * (C::TB / 2);
-      const uint32_t dst = ring_s + slot * C::SB + r * C::S + h * (C::TB / 2);
+  // stages in order (unit, k-tile), k-tile fastest; the issue cursor walks
+  // them incrementally.  Lane L copies 16 B (int4) / 32 B (int8) of row L/2,
+  // lanes 0-1 the 32 scale bytes.
+  const int r_ld = lane >> 1, h_ld = lane & 1;
+  int iq = 0, iu = u_lo, ikt = kt0;
+  auto issue = [&](int slot) {
+    if (iq < Q) {
+      const int row0 = iu * 16;
+      const size_t tile = (size_t)(row0 >> 7) * g.KT + ikt;
+      const uint8_t* src = a.w.data + (tile * 128 + (row0 & 127) + r_ld) * C::TB + h_ld * (C::TB / 2);
+      const uint32_t dst = ring_s + slot * C::SB + r_ld * C::S + h_ld * (C::TB / 2);
       bcp16(dst, src);
       if (WFMT == 8) bcp16(dst + 16, src + 16);
-      if (lane < 2) bcp16(ring_s + slot * C::SB + 16 * C::S + lane * 16, a.w.scales + (tile * 128 + (row0 & 127)) * 2 + lane * 16);
+      if (lane < 2)
+        bcp16(ring_s + slot * C::SB + 16 * C::S + lane * 16, a.w.scales + (tile * 128 + (row0 & 127)) * 2 + lane * 16);
+      ++iq;
+      if (++ikt == kt0 + nkt) { ikt = kt0; ++iu; }
     }
     bcommit();
   };
 #pragma unroll 1
-  for (int s = 0; s < kBR; ++s) issue(s, s);
+  for (int s = 0; s < kBR; ++s) issue(s);
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   asm volatile("griddepcontrol.wait;" ::: "memory");
 
@@ -186,15 +190,14 @@ __global__ void __launch_bounds__(kBT, 1) bgemv_kernel(GemvArgs a) {
 #pragma unroll
       for (int i = 0; i < 4; ++i) acc[u][m][i] = 0.0f;
 
-  int q = 0;
+  int slot = 0;                                           // ring slot of the next stage
 #pragma unroll
   for (int u = 0; u < kMaxUnits; ++u) {
     if (u < nu) {
 #pragma unroll 1
-      for (int j = 0; j < nkt; ++j, ++q) {
+      for (int j = 0; j < nkt; ++j) {
         bwait<kBR - 1>();
         __syncwarp();
-        const int slot = q % kBR;
         const uint8_t* st = ring + slot * C::SB;
         // weight scales of rows gq, gq+8 (both blocks of the k-tile)
         const uint32_t sr0 = *reinterpret_cast<const uint16_t*>(st + 16 * C::S + gq * 2);
@@ -241,7 +244,8 @@ __global__ void __launch_bounds__(kBT, 1) bgemv_kernel(GemvArgs a) {
           }
         }
         __syncwarp();                                     // every lane is done with the slot
-        issue(q + kBR, slot);
+        issue(slot);                                      // the stage kBR ahead
+        slot = slot + 1 == kBR ? 0 : slot + 1;
       }
     }
   }
