@@ -36,6 +36,15 @@ struct mxq_context {
   int32_t* ws_moe = nullptr; size_t ws_moe_bytes = 0;
   float* ws_yr = nullptr;    size_t ws_yr_bytes = 0;
   int32_t* moe_counts_host = nullptr; size_t moe_counts_cap = 0;
+  // MoE expert lanes: experts run round-robin on kMoeLanes streams, each with
+  // its own operand and gate/up workspaces, forked from and joined to the
+  // caller's stream (consecutive experts' GEMMs overlap their tails)
+  static constexpr int kMoeLanes = 3;
+  cudaStream_t moe_st[kMoeLanes] = {};
+  cudaEvent_t moe_ev[kMoeLanes + 1] = {};
+  uint8_t* ml_op[kMoeLanes] = {}; size_t ml_op_bytes[kMoeLanes] = {};
+  float* ml_f0[kMoeLanes] = {};   size_t ml_f0_bytes[kMoeLanes] = {};
+  float* ml_f1[kMoeLanes] = {};   size_t ml_f1_bytes[kMoeLanes] = {};
   // host-buffer entry points: pinned staging and one CUDA graph per
   // (call, weights, batch); ws_gen changes whenever a workspace moves, which
   // retires every captured graph
@@ -563,6 +572,14 @@ int mxq_destroy(mxq_ctx c) {
     if (c->hevent) cudaEventDestroy(c->hevent);
     if (c->seq_dev) cudaFree(c->seq_dev);
     if (c->moe_counts_host) cudaFreeHost(c->moe_counts_host);
+    for (int l = 0; l < mxq_context::kMoeLanes; ++l) {
+      if (c->moe_st[l]) cudaStreamSynchronize(c->moe_st[l]), cudaStreamDestroy(c->moe_st[l]);
+      cudaFree(c->ml_op[l]);
+      cudaFree(c->ml_f0[l]);
+      cudaFree(c->ml_f1[l]);
+    }
+    for (auto& ev : c->moe_ev)
+      if (ev) cudaEventDestroy(ev);
     delete c;
     return MXQ_OK;
   })
@@ -1278,15 +1295,57 @@ int mxq_moe_swiglu(mxq_ctx c, const mxq_weight* w_gate, const mxq_weight* w_up,
         kmax = w_up[e]->v.Kpad > kmax ? w_up[e]->v.Kpad : kmax;
         kmax = w_down[e]->v.Kpad > kmax ? w_down[e]->v.Kpad : kmax;
       }
-      if ((rc = ensure(c, c->ws_op, c->ws_op_bytes, Bpm * kmax * 2, "workspace operand"))) return rc;
-      if ((rc = ensure(c, c->ws_f0, c->ws_f0_bytes, (size_t)nmax * F * 4, "workspace gate"))) return rc;
-      if ((rc = ensure(c, c->ws_f1, c->ws_f1_bytes, (size_t)nmax * F * 4, "workspace up"))) return rc;
+      for (int l = 0; l < mxq_context::kMoeLanes; ++l) {
+        if ((rc = ensure(c, c->ml_op[l], c->ml_op_bytes[l], Bpm * kmax * 2, "workspace operand"))) return rc;
+        if ((rc = ensure(c, c->ml_f0[l], c->ml_f0_bytes[l], (size_t)nmax * F * 4, "workspace gate"))) return rc;
+        if ((rc = ensure(c, c->ml_f1[l], c->ml_f1_bytes[l], (size_t)nmax * F * 4, "workspace up"))) return rc;
+      }
+      for (int l = 0; l < mxq_context::kMoeLanes; ++l)
+        if (!c->moe_st[l]) {
+          cudaError_t e = cudaStreamCreateWithFlags(&c->moe_st[l], cudaStreamNonBlocking);
+          if (e != cudaSuccess) return cuda_fail(c, e, "moe lane stream");
+        }
+      for (auto& ev : c->moe_ev)
+        if (!ev) {
+          cudaError_t e = cudaEventCreateWithFlags(&ev, cudaEventDisableTiming);
+          if (e != cudaSuccess) return cuda_fail(c, e, "moe lane event");
+        }
     }
     if ((rc = ensure(c, c->ws_yr, c->ws_yr_bytes, (size_t)R * D * 4, "workspace expert outputs"))) return rc;
-    int off = 0;
+    // fork the expert lanes off the caller's stream
+    if (nmax > 0) {
+      cudaError_t e = cudaEventRecord(c->moe_ev[mxq_context::kMoeLanes], c->stream);
+      for (int l = 0; l < mxq_context::kMoeLanes && e == cudaSuccess; ++l)
+        e = cudaStreamWaitEvent(c->moe_st[l], c->moe_ev[mxq_context::kMoeLanes], 0);
+      if (e != cudaSuccess) return cuda_fail(c, e, "moe fork");
+    }
+    // expert j (in id order, non-empty ones) runs on lane j % kMoeLanes with
+    // that lane's workspaces; the swap below is undone on every exit
+    struct LaneSwap {
+      mxq_context* c;
+      cudaStream_t st;
+      uint8_t* op;
+      float *f0, *f1;
+      explicit LaneSwap(mxq_context* cc) : c(cc), st(cc->stream), op(cc->ws_op), f0(cc->ws_f0), f1(cc->ws_f1) {}
+      void use(int l) {
+        c->stream = c->moe_st[l];
+        c->ws_op = c->ml_op[l];
+        c->ws_f0 = c->ml_f0[l];
+        c->ws_f1 = c->ml_f1[l];
+      }
+      ~LaneSwap() {
+        c->stream = st;
+        c->ws_op = op;
+        c->ws_f0 = f0;
+        c->ws_f1 = f1;
+      }
+    };
+    int off = 0, lane_j = 0;
     for (int e = 0; e < E; ++e) {
       const int ne = c->moe_counts_host[e];
       if (ne == 0) continue;
+      LaneSwap lane(c);
+      lane.use(lane_j++ % mxq_context::kMoeLanes);
       const int BN = gemm_pick_bn(ne), Bpad = (ne + BN - 1) / BN * BN;
       const WeightView &gv = w_gate[e]->v, &uv = w_up[e]->v;
       if ((rc = moe_operand(c, w_gate[e], x, slot_token + off, ne, D, BN, Bpad))) return rc;
@@ -1309,6 +1368,15 @@ int mxq_moe_swiglu(mxq_ctx c, const mxq_weight* w_gate, const mxq_weight* w_up,
       if ((rc = after_launch(c, launch_quantize(qa, 2, c->stream, true), "moe swiglu"))) return rc;
       if ((rc = moe_gemm(c, w_down[e], ne, BN, Bpad, c->ws_yr + (size_t)off * D))) return rc;
       off += ne;
+    }
+    // join: the combine on the caller's stream waits for every lane
+    if (nmax > 0) {
+      cudaError_t e = cudaSuccess;
+      for (int l = 0; l < mxq_context::kMoeLanes && e == cudaSuccess; ++l) {
+        e = cudaEventRecord(c->moe_ev[l], c->moe_st[l]);
+        if (e == cudaSuccess) e = cudaStreamWaitEvent(c->stream, c->moe_ev[l], 0);
+      }
+      if (e != cudaSuccess) return cuda_fail(c, e, "moe join");
     }
     return after_launch(c, launch_moe_combine(c->ws_yr, gate, route_pos, T, D, K, y, c->stream), "moe combine");
   })
