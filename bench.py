@@ -632,7 +632,8 @@ def run_ours(args):
                  "up_kernel_ms": kms,
                  "up_kernel_hbm_gbs": gemv_bytes(UP[0], UP[1], sb) / (kms / 1e3) / 1e9,
                  "up_kernel_tflops": fl / (kms / 1e3) / 1e12}
-        entry["path"] = "gemv-dp4a" if sb <= 4 else "tcgen05-bf16"
+        entry["path"] = ("gemv-resident-dp4a" if sb == 1 else "gemv-ring-dp4a" if sb == 2 else
+                         "gemv-mma-s8" if sb <= 16 else "tcgen05-bf16")
         sweep[str(sb)] = entry
 
     moe = None
