@@ -199,6 +199,35 @@ def test_gemm_extreme_weight_scales(ctx, fmt):
     assert rel_l2(y, ref) <= REL_TOL
 
 
+@pytest.mark.parametrize("fmt", [8, 4])
+def test_decode_gemv_exact_scale_path(ctx, fmt):
+    """Weight scale bytes 0..7 (exponents -127..-120, below the fast path's
+    range) and one row whose first block scale is 0xFF (NaN): the decode
+    GEMVs take their exact-scale path -- batch 1 (weight-resident), 2 (ring),
+    5 (int8 MMA), on MX input and on fp32 rows.  Activations scaled by 2^40
+    keep the products normal; NaN rows must match the oracle's."""
+    n, k = 1000, 4096
+    w, ws = synth.weights(fmt, n, k, -127, -120, 63)
+    ws[3, 0] = 255
+    W = mx.MXWeight(torch.from_numpy(w), torch.from_numpy(ws), fmt, n, k, ctx)
+    for b in (1, 2, 5):
+        x = synth.normal((b, k), 64 + b) * np.float32(2.0 ** 40)
+        xq, xs = oracle.quantize_x(x)
+        ref = oracle.gemv(fmt, xq, xs, w, ws, n, k)
+        ctx.set_path(mx.PATH_GEMV)
+        try:
+            y_mx = host(mx.mx_gemv(mx.MXActivation(cuda(xq), cuda(xs)), W, ctx))
+            y_f32 = host(mx.mx_linear(cuda(x), W, ctx))
+            ctx.synchronize()
+        finally:
+            ctx.set_path(mx.PATH_AUTO)
+        nan = np.isnan(ref)
+        assert nan[:, 3].all() and nan.sum() == b
+        for y in (y_mx, y_f32):
+            assert np.array_equal(np.isnan(y), nan), b
+            assert rel_l2(y[~nan], ref[~nan]) <= REL_TOL, b
+
+
 def test_golden_fixture_on_gpu(ctx):
     import os
     d = np.load(os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden", "mx_oracle.npz"))
