@@ -1,6 +1,8 @@
-// mxq_rgemv.cu -- persistent decode GEMV (batch <= 4): the HBM-bound mx_gemv
+// mxq_rgemv.cu -- persistent decode GEMVs (batch <= 4): the HBM-bound mx_gemv
 // of the reference (nn/tests/test_auto_generated.cpp:56; dpbusd design
-// nn/user.md:17).
+// nn/user.md:17).  Two kernels: the cp.async-ring kernel below (batches 2-4,
+// and batch 1 when the weight-resident kernel further down does not fit the
+// shape) and the weight-resident batch-1 kernel.
 //
 // One CTA per SM, 16 warps, one wave: fixed per-CTA costs (activation
 // staging, pipeline ramp) are paid once per launch, not once per wave.
@@ -10,8 +12,8 @@
 // 7B MLP 18-19 groups of the up projection, 6-7 of the down projection per
 // CTA).  Inside a CTA the 16 warps split K; a warp streams its K-slice of
 // every group it owns from HBM into a ring of shared-memory slots private to
-// each thread (cp.async, up to 16 rounds in flight, issued before the kernel
-// waits for its predecessor), and reads back only what it loaded.  In the
+// each thread (cp.async, 8 rounds in flight, issued before the kernel waits
+// for its predecessor), and reads back only what it loaded.  In the
 // tiled weight layout a group's k-tile is 128 (int4) or 256 (int8)
 // contiguous bytes, so one warp round covers 4 (2) k-tiles of the group in
 // full 128-byte lines.  Partial sums stay inside the CTA: each warp folds its
@@ -36,9 +38,9 @@ constexpr int kWarps = 16;
 constexpr int kThreads = kWarps * 32;
 // Weight loads land in a per-thread ring of kRing 16-byte slots in shared
 // memory (cp.async, slot-major so a warp's accesses are contiguous), with
-// the 4-byte words holding their scale bytes beside them: 16 rounds (128 KB
-// per SM; 8 rounds for batches 3-4) are in flight from the first
-// instruction.
+// the 4-byte words holding their scale bytes beside them: 8 rounds (80 KB per
+// CTA, so two consecutive kernels' CTAs share an SM) are in flight from the
+// first instruction.
 template <int NB>
 struct RRing {
   static constexpr int R = 8;
@@ -596,6 +598,12 @@ __global__ void __launch_bounds__(kThreads, 1) rgemv_res_kernel(GemvArgs a) {
   for (int r0 = 0; r0 < RMAX; r0 += GB) {
     if (r0 < nr) {                                       // warp-uniform
       const int j = li * C::KPL;
+      // the block's 4 groups are 16 consecutive rows: when they lie in one
+      // row tile their scale bytes sit 8 bytes apart from one base
+      const int nb = (g_lo + bi * GB) * 4;               // first row of the block
+      const bool one_tile = (nb >> 7) == ((nb + 4 * GB - 1) >> 7);
+      const uint32_t sbase = sc_base + (uint32_t)((((nb >> 7) - rt0) * g.KT + kt0 + j + kto) * 256 +
+                                                  ((nb & 127) + rr) * 2 + bh);
       const float fx = frow[j * 2];
       uint4 x0, x1 = make_uint4(0, 0, 0, 0);
       x0 = *reinterpret_cast<const uint4*>(xrow + j * kTileK);
@@ -603,7 +611,11 @@ __global__ void __launch_bounds__(kThreads, 1) rgemv_res_kernel(GemvArgs a) {
 #pragma unroll
       for (int gg = 0; gg < GB; ++gg) {
         const int r = r0 + gg;
-        const uint32_t s = (vmask >> r) & 1u ? scale_at(bi * GB + gg, li) : 127u;
+        uint32_t s = 127u;
+        if ((vmask >> r) & 1u) {
+          if (one_tile) asm volatile("ld.shared.u8 %0, [%1];" : "=r"(s) : "r"(sbase + 8u * gg));
+          else s = scale_at(bi * GB + gg, li);
+        }
         const uint4 w = wv[r];
         int d0, d1;
         float fw;
