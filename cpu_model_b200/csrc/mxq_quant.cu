@@ -36,6 +36,11 @@ __device__ __forceinline__ int nf_zero(int q, uint32_t sb) { return sb == 255u ?
 template <int MODE>
 __global__ void __launch_bounds__(256) quantize_kernel(QuantArgs a) {
   asm volatile("griddepcontrol.wait;" ::: "memory");
+  // Dependents may launch now: the kernels that follow (GEMVs, the GEMM)
+  // stream their weights before their own griddepcontrol.wait and read this
+  // kernel's output only after it, which waits for this grid to complete.
+  // Everything before this kernel is complete once its own wait returns.
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   const int lane = threadIdx.x & 31;
   const long warp = ((long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const long nwarps = ((long)gridDim.x * blockDim.x) >> 5;
@@ -91,7 +96,6 @@ __global__ void __launch_bounds__(256) quantize_kernel(QuantArgs a) {
           __float2bfloat16_rn(f);
     }
   }
-  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
 
 // Operand-only form (no MX bytes requested): one thread per 16-byte output
@@ -102,6 +106,11 @@ __global__ void __launch_bounds__(256) quantize_kernel(QuantArgs a) {
 template <int MODE>
 __global__ void __launch_bounds__(256) operand_kernel(QuantArgs a) {
   asm volatile("griddepcontrol.wait;" ::: "memory");
+  // Dependents may launch now: the kernels that follow (GEMVs, the GEMM)
+  // stream their weights before their own griddepcontrol.wait and read this
+  // kernel's output only after it, which waits for this grid to complete.
+  // Everything before this kernel is complete once its own wait returns.
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   const int kb = a.K / kBlock;
   const long cpr = a.Kpad / 8;                          // chunks per token row
   const long total = (long)a.Bpad * cpr;                // multiple of 4 (Kpad % 64 == 0)
@@ -186,7 +195,6 @@ __global__ void __launch_bounds__(256) operand_kernel(QuantArgs a) {
       *reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(a.opnd) + off) = *reinterpret_cast<const uint4*>(o);
     }
   }
-  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
 
 cudaError_t launch_quantize(const QuantArgs& a, int mode, cudaStream_t st,
