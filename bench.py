@@ -657,8 +657,8 @@ def run_ours(args):
                          "frac": achieved / peaks["hbm_gbs"],
                          "traffic": ROOFLINE_TRAFFIC_B1 if b == 1 else None,
                          "traffic_src": ("ncu dram__bytes_read.sum + dram__bytes_write.sum of one "
-                                         "rgemv_res_kernel<int4, MX in> launch (up 4096->11008), "
-                                         "profiles/rgemv_res_int4_b1_mlp_pair.md") if b == 1 else None,
+                                         "rgemv_res_kernel<int4, MX in> launch (up 4096->11008)")
+                                        if b == 1 else None,
                          "kernel": ("rgemv_res_kernel<int4> (up 4096->11008, weight-resident)" if b == 1 else
                                     "rgemv_kernel<int4> (up 4096->11008)" if b <= 4 else "gemm_tc_kernel<int4> (up 4096->11008)"),
                          "algorithmic_bytes_per_launch": gbytes, "launch_ms": gemv_ms,

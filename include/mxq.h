@@ -65,7 +65,8 @@ extern "C" {
 #define MXQ_ACT_NONE 0
 #define MXQ_ACT_SILU 1
 
-#define MXQ_PATH_AUTO 0 /* streaming GEMV for batch <= 4, tensor-core GEMM above */
+#define MXQ_PATH_AUTO 0 /* GEMV kernels for batch <= 4, and up to 16 where the int8-MMA GEMV fits the
+                          shape; tensor-core GEMM above */
 #define MXQ_PATH_GEMV 1
 #define MXQ_PATH_GEMM 2
 
@@ -80,7 +81,9 @@ MXQ_API int mxq_destroy(mxq_ctx ctx);
 MXQ_API int mxq_set_stream(mxq_ctx ctx, void* cuda_stream);
 /* Regime override, the counterpart of nca::simd::set_override_backend
  * (nn/core/simd/dispatch.cpp:83-87): MXQ_PATH_*.  MXQ_PATH_GEMV accepts
- * batch <= 8 (streaming split-K kernel up to 4, register-blocked above). */
+ * batch <= 8 on every shape (batch 1 weight-resident kernel, 2 cp.async-ring
+ * kernel, 3-8 int8-MMA kernel where it fits, register-blocked otherwise) and
+ * batch <= 16 where the int8-MMA kernel fits the shape. */
 MXQ_API int mxq_set_path(mxq_ctx ctx, int path);
 MXQ_API int mxq_reserve(mxq_ctx ctx, size_t max_batch, size_t max_k);
 MXQ_API int mxq_synchronize(mxq_ctx ctx);
