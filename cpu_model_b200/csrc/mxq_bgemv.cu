@@ -305,13 +305,8 @@ template <int WFMT, int NT, int R, bool FAST>
 cudaError_t blaunch_t(const GemvArgs& a, cudaStream_t st, bool pdl) {
   const BGeom g = bgeom<WFMT>(a.w);
   const size_t smem = (size_t)kBW * bwarp_bytes<WFMT, NT>(g, R);
-  static size_t configured = 0;
-  if (smem > 48 * 1024 && smem > configured) {
-    cudaError_t e = cudaFuncSetAttribute(bgemv_kernel<WFMT, NT, R, FAST>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         (int)smem);
-    if (e != cudaSuccess) return e;
-    configured = smem;
-  }
+  static SmemAttr smem_attr;
+  if (cudaError_t e = smem_attr.ensure(bgemv_kernel<WFMT, NT, R, FAST>, smem)) return e;
   const int grid = g.U < bsms() ? g.U : bsms();
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)grid);

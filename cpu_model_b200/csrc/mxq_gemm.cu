@@ -569,14 +569,8 @@ int pick_splits(int units, int KT) {
 template <int WFMT, int BN, int MT>
 cudaError_t launch_t(const GemmArgs& a, cudaStream_t st, bool pdl) {
   using C = Cfg<WFMT, BN, MT>;
-  static bool configured = false;
-  if (!configured) {
-    cudaError_t e = cudaFuncSetAttribute(gemm_tc_kernel<WFMT, BN, MT>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         (int)C::SMEM);
-    if (e != cudaSuccess) return e;
-    configured = true;
-  }
+  static SmemAttr smem_attr;
+  if (cudaError_t e = smem_attr.ensure(gemm_tc_kernel<WFMT, BN, MT>, (size_t)C::SMEM)) return e;
   const int T = a.w.Npad / (128 * MT), NT = a.Bpad / BN;
   // k-tiles per row tile: all of K, or the block-sparse average
   const int KT = a.w.kt_ptr ? (a.w.nnz_tiles + T - 1) / T : a.w.Kpad / kTileK;

@@ -362,14 +362,8 @@ cudaError_t launch_t(const GemvArgs& a, cudaStream_t st, bool pdl) {
   const size_t smem = (size_t)kGemvWarps * gemv_warp_bytes(NB, S) +
                       (size_t)kGemvWarps * ROWS * NB * 4;
   if (smem > 227 * 1024) return cudaErrorInvalidValue;
-  static size_t configured = 0;
-  if (smem > 48 * 1024 && smem > configured) {
-    cudaError_t e = cudaFuncSetAttribute(gemv_kernel<WFMT, NB, GATHER, INF32>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         (int)smem);
-    if (e != cudaSuccess) return e;
-    configured = smem;
-  }
+  static SmemAttr smem_attr;
+  if (cudaError_t e = smem_attr.ensure(gemv_kernel<WFMT, NB, GATHER, INF32>, smem)) return e;
   const int ncols = GATHER ? a.nrows : a.w.Npad;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)((ncols + ROWS - 1) / ROWS));

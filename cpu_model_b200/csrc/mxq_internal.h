@@ -34,6 +34,24 @@ struct WeightView {
   int nnz_tiles;
 };
 
+// The largest dynamic shared memory already allowed for one kernel, per
+// device: cudaFuncSetAttribute applies to the current device only, so a
+// process with contexts on several devices sets it once on each.
+struct SmemAttr {
+  static constexpr int kMaxDevices = 64;
+  size_t bytes[kMaxDevices] = {};
+  template <typename F>
+  cudaError_t ensure(F* fn, size_t smem) {
+    if (smem <= 48 * 1024) return cudaSuccess;
+    int dev = -1;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) dev = -1;
+    if (dev >= 0 && bytes[dev] >= smem) return cudaSuccess;
+    const cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e == cudaSuccess && dev >= 0) bytes[dev] = smem;
+    return e;
+  }
+};
+
 struct QuantArgs {
   const float* x;        // fp32 input [B][K] (modes 0-2; gate for mode 2)
   const int32_t* gather; // optional (mode 0): source row of x per output row (MoE dispatch)

@@ -702,13 +702,8 @@ template <int WFMT, int NB, bool FAST, bool INF32>
 cudaError_t launch_t(const GemvArgs& a, cudaStream_t st, bool pdl) {
   const size_t smem = smem_bytes<WFMT>(a.w, NB);
   if (smem > 220 * 1024) return cudaErrorInvalidValue;
-  static size_t configured = 0;
-  if (smem > 48 * 1024 && smem > configured) {
-    cudaError_t e = cudaFuncSetAttribute(rgemv_kernel<WFMT, NB, FAST, INF32>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (e != cudaSuccess) return e;
-    configured = smem;
-  }
+  static SmemAttr smem_attr;
+  if (cudaError_t e = smem_attr.ensure(rgemv_kernel<WFMT, NB, FAST, INF32>, smem)) return e;
   const int G4 = (a.w.N + 3) / 4;
   const int grid = G4 < sms() ? G4 : sms();
   cudaLaunchConfig_t cfg = {};
@@ -748,13 +743,8 @@ cudaError_t launch_res_t(const GemvArgs& a, cudaStream_t st, bool pdl) {
   const int G4 = (a.w.N + 3) / 4;
   const int grid = G4 < sms() ? G4 : sms();
   const size_t smem = res_smem_bytes<WFMT>(a.w, INF32, grid);
-  static size_t configured = 0;
-  if (smem > 48 * 1024 && smem > configured) {
-    cudaError_t e = cudaFuncSetAttribute(rgemv_res_kernel<WFMT, FAST, INF32>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (e != cudaSuccess) return e;
-    configured = smem;
-  }
+  static SmemAttr smem_attr;
+  if (cudaError_t e = smem_attr.ensure(rgemv_res_kernel<WFMT, FAST, INF32>, smem)) return e;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)grid);
   cfg.blockDim = dim3(kThreads);
