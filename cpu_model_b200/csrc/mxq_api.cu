@@ -1319,6 +1319,18 @@ int mxq_moe_swiglu(mxq_ctx c, const mxq_weight* w_gate, const mxq_weight* w_up,
         e = cudaStreamWaitEvent(c->moe_st[l], c->moe_ev[mxq_context::kMoeLanes], 0);
       if (e != cudaSuccess) return cuda_fail(c, e, "moe fork");
     }
+    // an error return between the fork and the join still makes the
+    // caller's stream wait for whatever the lanes have queued
+    struct LaneJoinOnError {
+      mxq_context* c;
+      bool armed;
+      ~LaneJoinOnError() {
+        if (!armed) return;
+        for (int l = 0; l < mxq_context::kMoeLanes; ++l)
+          if (cudaEventRecord(c->moe_ev[l], c->moe_st[l]) == cudaSuccess)
+            cudaStreamWaitEvent(c->stream, c->moe_ev[l], 0);
+      }
+    } join_guard{c, nmax > 0};
     // expert j (in id order, non-empty ones) runs on lane j % kMoeLanes with
     // that lane's workspaces; the swap below is undone on every exit
     struct LaneSwap {
@@ -1370,6 +1382,7 @@ int mxq_moe_swiglu(mxq_ctx c, const mxq_weight* w_gate, const mxq_weight* w_up,
       off += ne;
     }
     // join: the combine on the caller's stream waits for every lane
+    join_guard.armed = false;
     if (nmax > 0) {
       cudaError_t e = cudaSuccess;
       for (int l = 0; l < mxq_context::kMoeLanes && e == cudaSuccess; ++l) {
