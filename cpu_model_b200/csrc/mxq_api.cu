@@ -850,6 +850,7 @@ int mxq_quantize_x(mxq_ctx c, const float* x, size_t b, size_t k, int act,
                    uint8_t* q, uint8_t* s) {
   if (int rc = check_ctx(c)) return rc;
   if (!x || !q || !s) return fail(c, MXQ_ERR_INVALID_ARGUMENT, "null pointer");
+  if (!aligned16(x)) return fail(c, MXQ_ERR_INVALID_ARGUMENT, "fp32 input must be 16-byte aligned (it is read in 16-byte vectors)");
   if (b == 0 || k == 0 || k % kBlock)
     return fail(c, MXQ_ERR_INVALID_ARGUMENT, "quantize: K must be a positive multiple of 32");
   if (act != MXQ_ACT_NONE && act != MXQ_ACT_SILU)
@@ -868,6 +869,7 @@ int mxq_swiglu_quantize(mxq_ctx c, const float* gate, const float* up, size_t b,
                         size_t k, uint8_t* q, uint8_t* s) {
   if (int rc = check_ctx(c)) return rc;
   if (!gate || !up || !q || !s) return fail(c, MXQ_ERR_INVALID_ARGUMENT, "null pointer");
+  if (!aligned16(gate) || !aligned16(up)) return fail(c, MXQ_ERR_INVALID_ARGUMENT, "fp32 input must be 16-byte aligned (it is read in 16-byte vectors)");
   if (b == 0 || k == 0 || k % kBlock)
     return fail(c, MXQ_ERR_INVALID_ARGUMENT, "quantize: K must be a positive multiple of 32");
   DeviceGuard g(c->device);
@@ -939,6 +941,7 @@ int mxq_linear(mxq_ctx c, mxq_weight w, const float* x, size_t b, float* y) {
     if (int rc = check_ctx(c)) return rc;
     if (int rc = check_weight(c, w)) return rc;
     if (!x || !y || b == 0) return fail(c, MXQ_ERR_INVALID_ARGUMENT, "null pointer or empty batch");
+    if (!aligned16(x)) return fail(c, MXQ_ERR_INVALID_ARGUMENT, "fp32 input must be 16-byte aligned (it is read in 16-byte vectors)");
     DeviceGuard g(c->device);
     return linear_dev(c, w, x, b, y, MXQ_ACT_NONE);
   })
@@ -951,6 +954,7 @@ int mxq_linear_pair(mxq_ctx c, mxq_weight w1, mxq_weight w2, const float* x,
     if (int rc = check_weight(c, w1)) return rc;
     if (int rc = check_weight(c, w2)) return rc;
     if (!x || !y || b == 0) return fail(c, MXQ_ERR_INVALID_ARGUMENT, "null pointer or empty batch");
+    if (!aligned16(x)) return fail(c, MXQ_ERR_INVALID_ARGUMENT, "fp32 input must be 16-byte aligned (it is read in 16-byte vectors)");
     if (w2->v.K != w1->v.N)
       return fail(c, MXQ_ERR_INVALID_ARGUMENT, "pair shape mismatch: w1 N=%d, w2 K=%d", w1->v.N, w2->v.K);
     DeviceGuard g(c->device);
@@ -1157,6 +1161,7 @@ int mxq_mlp_swiglu(mxq_ctx c, mxq_weight wg, mxq_weight wu, mxq_weight wd,
     if (int rc = check_weight(c, wu)) return rc;
     if (int rc = check_weight(c, wd)) return rc;
     if (!x || !y || b == 0) return fail(c, MXQ_ERR_INVALID_ARGUMENT, "null pointer or empty batch");
+    if (!aligned16(x)) return fail(c, MXQ_ERR_INVALID_ARGUMENT, "fp32 input must be 16-byte aligned (it is read in 16-byte vectors)");
     if (wg->v.N != wu->v.N || wg->v.K != wu->v.K || wd->v.K != wg->v.N || wd->v.N != wg->v.K)
       return fail(c, MXQ_ERR_INVALID_ARGUMENT, "gated MLP shape mismatch");
     DeviceGuard g(c->device);
@@ -1236,6 +1241,7 @@ int mxq_moe_swiglu(mxq_ctx c, const mxq_weight* w_gate, const mxq_weight* w_up,
     if (int rc = check_ctx(c)) return rc;
     if (!w_gate || !w_up || !w_down || !x || !logits || !y || n_experts == 0)
       return fail(c, MXQ_ERR_INVALID_ARGUMENT, "null pointer or no experts");
+    if (!aligned16(x)) return fail(c, MXQ_ERR_INVALID_ARGUMENT, "fp32 input must be 16-byte aligned (it is read in 16-byte vectors)");
     if (k == 0 || k > n_experts)
       return fail(c, MXQ_ERR_INVALID_ARGUMENT, "top-k: k=%zu must be in [1, n_experts=%zu]", k, n_experts);
     if (k > 64 || n_experts > 4096) return fail(c, MXQ_ERR_UNSUPPORTED, "top-k: k <= 64 and n_experts <= 4096");
@@ -1485,6 +1491,7 @@ extern "C" int mxq_linear_noalloc(mxq_ctx c, mxq_weight w, const float* x, size_
     if (int rc = check_ctx(c)) return rc;
     if (int rc = check_weight(c, w)) return rc;
     if (!x || !y || b == 0) return fail(c, MXQ_ERR_INVALID_ARGUMENT, "null pointer or empty batch");
+    if (!aligned16(x)) return fail(c, MXQ_ERR_INVALID_ARGUMENT, "fp32 input must be 16-byte aligned (it is read in 16-byte vectors)");
     if (b > (size_t)(1 << 20)) return fail(c, MXQ_ERR_INVALID_ARGUMENT, "mxq_linear_noalloc: batch %zu too large", b);
     DeviceGuard g(c->device);   // the scratch address is per device: look it up with the device current
     const int BN = gemm_pick_bn((int)b);

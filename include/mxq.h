@@ -16,7 +16,9 @@
  *     handle, a null handle or pointer is MXQ_ERR_INVALID_ARGUMENT.
  *     mxq_last_error() describes the last failure on a context.
  *   - Data pointers are DEVICE pointers owned by the caller (16-byte
- *     aligned), except in the *_host entry points, which take host memory.
+ *     aligned; MX activations and fp32 inputs off a 16-byte boundary are
+ *     refused with MXQ_ERR_INVALID_ARGUMENT before any launch), except in
+ *     the *_host entry points, which take host memory.
  *     Weight handles own their device copy of the weights.
  *   - Work is enqueued on the context's stream (mxq_set_stream; default the
  *     legacy stream) and is asynchronous; mxq_synchronize() waits and

@@ -327,6 +327,25 @@ def test_fixed_size_checks(ctx):
 
 
 # ------------------------------------------------------ routing / GAE ---
+def test_misaligned_fp32_input_rejected(ctx):
+    """fp32 inputs are read in 16-byte vectors: a device pointer off a
+    16-byte boundary is refused on the host, before any launch, and the
+    context stays usable."""
+    n, k = 64, 256
+    w, ws, W = weight(ctx, 8, n, k, 71)
+    buf = torch.from_numpy(synth.normal((1, k + 4), 72)).reshape(-1).cuda()
+    x_bad = buf[1:1 + k].view(1, k)
+    assert x_bad.data_ptr() % 16 == 4
+    with pytest.raises(ValueError):
+        mx.mx_linear(x_bad, W, ctx)
+    x_ok = buf[4:4 + k].view(1, k)
+    assert x_ok.data_ptr() % 16 == 0
+    y = host(mx.mx_linear(x_ok, W, ctx))
+    ctx.synchronize()
+    xq, xs = oracle.quantize_x(host(x_ok))
+    assert rel_l2(y, oracle.gemv(8, xq, xs, w, ws, n, k)) <= REL_TOL
+
+
 def test_route_topk_bit_exact(ctx):
     logits = synth.normal((4096, 8), 90)
     logits[7, 3] = logits[7, 5] = 9.0        # tie
