@@ -40,6 +40,16 @@ COPIES = 8
 # 24,001,664 algorithmic bytes: every weight byte crosses DRAM once
 ROOFLINE_TRAFFIC_B1 = 24021760
 SWEEP = [8, 64, 512]
+# the roofline leg times this many launches of the dominant kernel whatever
+# --steps is, so its per-launch figure does not depend on the run length
+ROOFLINE_LAUNCHES = 200
+# int8 dense tensor peak of the B200 (spec; MEASURED_PEAKS.json holds no int8
+# figure): north_star's denominator for the tensor-core GEMM
+INT8_SPEC_TOPS = 4500.0
+# single MX-int8 linear GEMV: 4096 x 4096, exponents [-10, -4], batch 1,
+# seed 0; distinct weight copies rotated so the timed launches stream from
+# HBM (32 x 17.3 MB = 554 MB > 4 x the 126 MB L2)
+CFG1 = {"n": 4096, "k": 4096, "emin": -10, "emax": -4, "copies": 32}
 # block-sparse MoE layer: 4096 tokens, d 4096, 8 experts, top-2, SwiGLU FFN
 # 14336, MX-int4 expert matrices with 25 % of their 64x64 blocks present
 MOE = {"tokens": 4096, "d": 4096, "ffn": 14336, "experts": 8, "top_k": 2, "density": 0.25}
@@ -58,6 +68,12 @@ def gemv_bytes(n, k, b):
     return n * k // 2 + n * k // 32 + b * (k + k // 32) + b * n * 4
 
 
+def int8_gemv_bytes(n, k, b):
+    """Algorithmic bytes of one MX-int8 linear: int8 weights + E8M0 scales +
+    MX activations + fp32 outputs (17,322,112 at 4096 x 4096, batch 1)."""
+    return n * k + n * k // 32 + b * (k + k // 32) + b * n * 4
+
+
 def pair_flops(b):
     return 2 * b * (UP[0] * UP[1] + DOWN[0] * DOWN[1])
 
@@ -66,8 +82,9 @@ def load_peaks():
     p = os.path.join(ROOT, "MEASURED_PEAKS.json")
     if os.path.exists(p):
         d = json.load(open(p))
-        return {"hbm_gbs": d["hbm_gbs"], "bf16_tflops": d["bf16_tflops"], "src": "measured"}
-    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "src": "fallback"}
+        return {"hbm_gbs": d["hbm_gbs"], "bf16_tflops": d["bf16_tflops"],
+                "bf16_tflops_sustained": d.get("bf16_tflops_sustained", d["bf16_tflops"]), "src": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "src": "fallback"}
 
 
 class Clocks:
@@ -157,8 +174,34 @@ def cpu_pair_sample(seconds=10.0, batch=1, threads=0):
             break
     cores = threads if threads > 0 else oracle.max_threads()
     return {"value": batch * steps / el, "unit": "tokens/s", "cores": cores, "kind": "port",
+            "bytes_per_s": steps * pair_bytes(batch) / el,
             "sample": "%d pair steps at batch %d (%.1f s), %s" % (
-                steps, batch, el, "AVX-512 VNNI dpbusd" if used else "portable int loop")}
+                steps, batch, el, "AVX-512 VNNI _mm512_dpbusd_epi32" if used else "portable int loop")}
+
+
+def cpu_int8_sample(seconds=5.0, threads=0):
+    """The single MX-int8 4096 x 4096 linear at batch 1 on the host cores
+    (the dpbusd restatement), quantisation included."""
+    from oracle import oracle
+    from cpu_model_b200 import synth
+    n, k = CFG1["n"], CFG1["k"]
+    w, ws = synth.weights(8, n, k, CFG1["emin"], CFG1["emax"], 0)
+    sums = oracle.weight_sums(8, w, n, k)
+    x = synth.normal((1, k), 0)
+    steps = 0
+    t0 = time.perf_counter()
+    while True:
+        xq, xs = oracle.quantize_x(x)
+        _, used = oracle.baseline_gemv(8, xq, xs, w, ws, sums, n, k, threads)
+        steps += 1
+        el = time.perf_counter() - t0
+        if el >= seconds:
+            break
+    cores = threads if threads > 0 else oracle.max_threads()
+    return {"value": steps / el, "unit": "tokens/s", "cores": cores, "kind": "port",
+            "bytes_per_s": steps * int8_gemv_bytes(n, k, 1) / el,
+            "sample": "%d linears at batch 1 (%.1f s), %s" % (
+                steps, el, "AVX-512 VNNI _mm512_dpbusd_epi32" if used else "portable int loop")}
 
 
 def moe_weights(ctx, dev, seed=7, experts_range=None):
@@ -250,6 +293,65 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
+def time_cfg1(ctx, dev, args, world, max_over_ranks, barrier, peaks, rank, capture):
+    """The single MX-int8 4096 x 4096 linear (fp32 x quantised inside the
+    GEMV, fp32 y) at batch 1: ROOFLINE_LAUNCHES mxq_linear calls rotating
+    CFG1["copies"] weight copies (copy 0 is the seed-0 matrix), replayed as
+    one CUDA graph and timed with CUDA events on the launching stream."""
+    import torch
+    from cpu_model_b200 import mx, synth
+    n, k = CFG1["n"], CFG1["k"]
+    ws_ = []
+    for c in range(CFG1["copies"]):
+        w, s_ = synth.weights(8, n, k, CFG1["emin"], CFG1["emax"], c)
+        ws_.append(mx.MXWeight(torch.from_numpy(w), torch.from_numpy(s_), 8, n, k, ctx))
+    x = torch.from_numpy(synth.normal((1, k), 0)).to(dev)
+    y = torch.empty((1, n), dtype=torch.float32, device=dev)
+    lib = ctx.lib
+    ctx._bind()
+
+    def one(i):
+        mx.check(lib.mxq_linear(ctx.h, ws_[i % len(ws_)].h, mx._ptr(x), 1, mx._ptr(y)), ctx.h)
+
+    for i in range(max(3, len(ws_))):
+        one(i)
+    ctx.synchronize()
+    l0 = ctx.launch_count()
+    g = capture(lambda: [one(i) for i in range(ROOFLINE_LAUNCHES)])
+    launches = ctx.launch_count() - l0
+    g.replay()
+    torch.cuda.synchronize()
+    barrier()
+    torch.cuda.synchronize()
+    stream = torch.cuda.current_stream(dev)
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    g.replay()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms = max_over_ranks(e0.elapsed_time(e1) / ROOFLINE_LAUNCHES)
+    ctx.synchronize()
+    del g
+    nbytes = int8_gemv_bytes(n, k, 1)
+    gbs = nbytes / (ms / 1e3) / 1e9
+    out = {"metric": "MX-int8 qlinear tokens/s (4096x4096, batch 1)", "tokens_per_s": world / (ms / 1e3),
+           "ms_per_token": ms, "launches": ROOFLINE_LAUNCHES, "kernel_launches_per_call": launches // ROOFLINE_LAUNCHES,
+           "config": {"workload": "mx_int8_linear_4096", "weights": "int8 [-127,127], E8M0 exp [-10,-4], seed 0",
+                      "activations": "fp32 N(0,1) -> MX-int8 per 32-block, seed 0",
+                      "l2": "rotating %d weight copies (%.0f MB) vs 126 MB L2" % (CFG1["copies"], CFG1["copies"] * nbytes / 1e6)},
+           "roofline": {"bound": "hbm", "achieved": gbs, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                        "frac": gbs / peaks["hbm_gbs"], "algorithmic_bytes_per_launch": nbytes,
+                        "peak_src": peaks["src"] + " hbm_gbs (burst copy)",
+                        "kernel": "rgemv_res_kernel<int8, fp32 in> (weight-resident decode GEMV)"},
+           "api": "mxq_linear"}
+    if rank == 0 and world == 1 and not args.no_cpu:
+        out["cpu_baseline"] = cpu_int8_sample(seconds=min(5.0, args.cpu_seconds))
+    for w in ws_:
+        w.close()
+    return out
+
+
 def time_moe(ctx, dev, args, world, max_over_ranks, barrier, peaks, rank):
     """The block-sparse MoE layer (mxq_moe_swiglu) at its full size: whole
     layer calls timed with CUDA events (each call reads the per-expert token
@@ -285,9 +387,18 @@ def time_moe(ctx, dev, args, world, max_over_ranks, barrier, peaks, rank):
     counts = np.bincount(idx.cpu().numpy().ravel(), minlength=e)
     nnz = [sum(int(m[1].sum()) * 64 * 64 for m in mats) for mats in experts]
     flops = 2.0 * float(sum(int(counts[j]) * nnz[j] for j in range(e)))
+    tf = flops / (ms / 1e3) / 1e12
     out = {"tokens_per_s": world * t / (ms / 1e3), "ms_per_step": ms, "steps": steps,
-           "nonzero_tflops": flops / (ms / 1e3) / 1e12,
-           "frac_of_bf16_peak": flops / (ms / 1e3) / 1e12 / peaks["bf16_tflops"],
+           "nonzero_tflops": tf,
+           "frac_of_bf16_peak": tf / peaks["bf16_tflops"],
+           "roofline": {"bound": "tensor", "achieved": tf, "unit": "TFLOP/s",
+                        "peak": peaks["bf16_tflops_sustained"], "frac": tf / peaks["bf16_tflops_sustained"],
+                        "peak_src": peaks["src"] + " bf16_tflops_sustained (a ms-long layer call)",
+                        "frac_of_int8_spec": tf / INT8_SPEC_TOPS,
+                        "int8_spec_tops": INT8_SPEC_TOPS,
+                        "ops": "2 per stored nonzero weight per route (nonzero 64x64 blocks only)",
+                        "kernel": "whole layer: gemm_tc_kernel<int4> on block-sparse tiles (kind::f16, "
+                                  "bf16 operands) + router/quantiser/combine kernels"},
            "nonzero_gop_per_step": flops / 1e9,
            "config": dict(MOE, weights="mx-int4 block-sparse 64x64", routing="softmax top-2 over N(0,1) logits"),
            "api": "mxq_moe_swiglu"}
@@ -618,7 +729,7 @@ def run_ours(args):
         ms, launches = time_pairs(b, args.steps, args.warmup)
     clocks = clk.summary()
     value = world * b / (ms / 1e3)
-    gemv_ms = time_gemv(b, max(args.steps, 20))
+    gemv_ms = time_gemv(b, ROOFLINE_LAUNCHES)
     gbytes = gemv_bytes(UP[0], UP[1], b)
     achieved = gbytes / (gemv_ms / 1e3) / 1e9
     e2e_ms, h2d, d2h = time_e2e(b, max(10, args.steps // 4))
@@ -626,16 +737,24 @@ def run_ours(args):
     sweep = {}
     for sb in ([] if args.no_sweep else SWEEP):
         sms, _ = time_pairs(sb, max(10, args.steps // 4), 3)
-        kms = time_gemv(sb, 20)
+        kms = time_gemv(sb, ROOFLINE_LAUNCHES if sb <= 64 else 40)
         fl = 2 * sb * UP[0] * UP[1]
         entry = {"tokens_per_s": world * sb / (sms / 1e3), "ms_per_step": sms,
                  "up_kernel_ms": kms,
                  "up_kernel_hbm_gbs": gemv_bytes(UP[0], UP[1], sb) / (kms / 1e3) / 1e9,
                  "up_kernel_tflops": fl / (kms / 1e3) / 1e12}
+        if sb > 16:
+            # the tensor-core GEMM against north_star's int8 denominator and
+            # against the bf16 rate its kind::f16 MMAs run at (their ceiling)
+            entry["up_kernel_frac_of_int8_spec"] = fl / (kms / 1e3) / 1e12 / INT8_SPEC_TOPS
+            entry["up_kernel_frac_of_bf16_burst"] = fl / (kms / 1e3) / 1e12 / peaks["bf16_tflops"]
         entry["path"] = ("gemv-resident-dp4a" if sb == 1 else "gemv-ring-dp4a" if sb == 2 else
                          "gemv-mma-s8" if sb <= 16 else "tcgen05-bf16")
         sweep[str(sb)] = entry
 
+    cfg1 = None
+    if not args.no_cfg1:
+        cfg1 = time_cfg1(ctx, dev, args, world, max_over_ranks, barrier, peaks, rank, capture)
     moe = None
     if not args.no_moe:
         moe = time_moe(ctx, dev, args, world, max_over_ranks, barrier, peaks, rank)
@@ -670,6 +789,8 @@ def run_ours(args):
             "clocks": clocks,
             "sweep": sweep,
         }
+        if cfg1 is not None:
+            line["int8_linear_4096"] = cfg1
         if moe is not None:
             line["moe"] = moe
         if ppo is not None:
@@ -699,6 +820,7 @@ def main():
     ap.add_argument("--no-sweep", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-moe", action="store_true")
+    ap.add_argument("--no-cfg1", action="store_true", help="skip the single MX-int8 4096x4096 linear line")
     ap.add_argument("--no-ppo", action="store_true")
     ap.add_argument("--no-shard", action="store_true", help="N > 1: skip the column-sharded / expert-parallel forms")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)

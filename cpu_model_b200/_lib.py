@@ -56,10 +56,17 @@ SIGNATURES = {
     "mxq_linear_pair_host": [_vp, _vp, _vp, _vp, _sz, _vp],
     "mxq_mlp_swiglu": [_vp, _vp, _vp, _vp, _vp, _sz, _vp],
     "mxq_linear_noalloc": [_vp, _vp, _vp, _sz, _vp],
+    "mxq_debug_gemm_stall": [_vp, _vp, _vp, _sz, _vp, ctypes.c_uint32],
     "mxq_route_topk": [_vp, _vp, _sz, _sz, _sz, _vp, _vp],
+    "mxq_quantize_w": [_vp, _i, _vp, _sz, _sz, _vp, _vp, _vp],
+    "mxq_rank16_dot_ptrs": [_vp, _vp, _sz, _vp, _vp, _sz, _vp],
+    "mxq_halting_step": [_vp, _vp, _vp, _vp, _sz, _f, _vp, _vp, _vp],
+    "mxq_hashed_route": [_vp, _vp, _sz, _sz, _sz, _sz, _sz, ctypes.c_uint64, _vp, _vp],
+    "mxq_hashed_route_host": [_vp, _vp, _sz, _sz, _sz, _sz, _sz, ctypes.c_uint64, _vp, _vp],
     "mxq_moe_swiglu": [_vp, _vp, _vp, _vp, _sz, _vp, _vp, _sz, _sz, _vp],
     "mxq_policy_head": [_vp, _vp, _vp, _sz, _sz, _vp, _vp, _vp],
     "mxq_gae": [_vp, _vp, _vp, _vp, _vp, _sz, _sz, _f, _f, _vp, _vp],
+    "mxq_gae_ring": [_vp, _vp, _vp, _vp, _vp, _sz, _sz, _sz, _sz, _sz, _f, _f, _vp, _vp],
 }
 
 _lib = None

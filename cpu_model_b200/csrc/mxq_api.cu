@@ -269,6 +269,29 @@ __global__ void gae_kernel(const float* __restrict__ r, const float* __restrict_
   }
 }
 
+// The same sweep on the ReplayMemory ring (agentic_env/replay_memory.cpp:
+// 210-251): items start at `start`, indices wrap once at `cap`, one thread
+// per environment of the first `active`.
+__global__ void gae_ring_kernel(const float* __restrict__ r, const float* __restrict__ v,
+                                const uint8_t* __restrict__ d, const float* __restrict__ nv,
+                                long cap, long start, int T, int E, int active, float gamma, float gl,
+                                float* __restrict__ adv, float* __restrict__ ret) {
+  const int k = blockIdx.x * blockDim.x + threadIdx.x;
+  if (k >= active) return;
+  float acc = 0.0f, vn = nv[k];
+  for (int t = T - 1; t >= 0; --t) {
+    long i = start + (long)t * E + k;
+    if (i >= cap) i -= cap;
+    const float df = d[i] ? 0.0f : 1.0f;
+    const float vt = v[i];
+    const float delta = __fsub_rn(__fadd_rn(r[i], __fmul_rn(__fmul_rn(gamma, vn), df)), vt);
+    acc = __fadd_rn(delta, __fmul_rn(__fmul_rn(gl, acc), df));
+    adv[i] = acc;
+    ret[i] = __fadd_rn(acc, vt);
+    vn = vt;
+  }
+}
+
 // ------------------------------------------------------- policy head ---
 // training/ppo_trainer.cpp:64-66 and :77: one warp per row; max by shuffles,
 // sums by a fixed shuffle tree (deterministic), exp by det_expf.
@@ -1401,6 +1424,46 @@ int mxq_moe_swiglu(mxq_ctx c, const mxq_weight* w_gate, const mxq_weight* w_up,
   })
 }
 
+int mxq_debug_gemm_stall(mxq_ctx c, mxq_weight w, const float* x, size_t b, float* y, uint32_t wait_us) {
+  MXQ_TRY({
+    if (int rc = check_ctx(c)) return rc;
+    if (int rc = check_weight(c, w)) return rc;
+    if (!x || !y || b == 0) return fail(c, MXQ_ERR_INVALID_ARGUMENT, "null pointer or empty batch");
+    if (!aligned16(x)) return fail(c, MXQ_ERR_INVALID_ARGUMENT, "fp32 input must be 16-byte aligned (it is read in 16-byte vectors)");
+    if (wait_us == 0 || wait_us > 1000000u)
+      return fail(c, MXQ_ERR_INVALID_ARGUMENT, "debug stall: wait limit must be in [1, 1e6] microseconds");
+    DeviceGuard g(c->device);
+    const int BN = gemm_pick_bn((int)b);
+    const int Bpad = (int)((b + BN - 1) / BN * BN);
+    int rc;
+    if ((rc = ensure(c, c->ws_op, c->ws_op_bytes, (size_t)Bpad * w->v.Kpad * 2, "workspace operand"))) return rc;
+    QuantArgs qa{};
+    qa.x = x;
+    qa.B = (int)b;
+    qa.K = w->v.K;
+    qa.opnd = reinterpret_cast<__nv_bfloat16*>(c->ws_op);
+    qa.Bpad = Bpad;
+    qa.Kpad = w->v.Kpad;
+    qa.BN = BN;
+    qa.int4_order = w->v.fmt == 4;
+    qa.shift = w->v.gemm_shift;
+    if ((rc = after_launch(c, launch_quantize(qa, MXQ_ACT_NONE, c->stream, false), "quantize"))) return rc;
+    GemmArgs ga{};
+    ga.w = w->v;
+    ga.opnd = qa.opnd;
+    ga.y = y;
+    ga.B = (int)b;
+    ga.Bpad = Bpad;
+    ga.BN = BN;
+    ga.status = c->status;
+    ga.splits = 1;
+    ga.wait_ns = (uint64_t)wait_us * 1000ull;
+    ga.withhold_x0 = 1;
+    if ((rc = after_launch(c, launch_gemm(ga, c->stream, false), "gemm"))) return rc;
+    return mxq_synchronize(c);
+  })
+}
+
 int mxq_route_topk(mxq_ctx c, const float* logits, size_t t, size_t n_experts,
                    size_t k, int32_t* idx, float* gate) {
   if (int rc = check_ctx(c)) return rc;
@@ -1427,6 +1490,132 @@ int mxq_gae(mxq_ctx c, const float* rewards, const float* values, const uint8_t*
   gae_kernel<<<(unsigned)((e + 127) / 128), 128, 0, c->stream>>>(rewards, values, dones, next_values,
                                                                 (int)t, (int)e, gamma, gl, adv, ret);
   return after_launch(c, cudaGetLastError(), "gae");
+}
+
+int mxq_quantize_w(mxq_ctx c, int fmt, const float* w, size_t n, size_t k, void* data, uint8_t* scales,
+                   int32_t* w_sums) {
+  if (int rc = check_ctx(c)) return rc;
+  if (!w || !data || !scales) return fail(c, MXQ_ERR_INVALID_ARGUMENT, "null pointer");
+  if (fmt != MXQ_FMT_INT4 && fmt != MXQ_FMT_INT8)
+    return fail(c, MXQ_ERR_INVALID_ARGUMENT, "unknown weight format %d", fmt);
+  if (n == 0 || k == 0 || k % kBlock)
+    return fail(c, MXQ_ERR_INVALID_ARGUMENT, "quantize_w: K must be a positive multiple of 32");
+  if (n > (1u << 24) || k > (1u << 24)) return fail(c, MXQ_ERR_INVALID_ARGUMENT, "quantize_w: shape too large");
+  DeviceGuard g(c->device);
+  return after_launch(c, launch_quantize_w(fmt, w, (int)n, (int)k, static_cast<uint8_t*>(data), scales, w_sums,
+                                           c->stream), "quantize_w");
+}
+
+int mxq_rank16_dot_ptrs(mxq_ctx c, const mxq_weight* rows, size_t nrows, const uint8_t* xq, const uint8_t* xs,
+                        size_t b, float* y) {
+  if (int rc = check_ctx(c)) return rc;
+  if (!rows || !xq || !xs || !y || b == 0 || nrows == 0)
+    return fail(c, MXQ_ERR_INVALID_ARGUMENT, "null pointer or empty input");
+  if (nrows > (size_t)kRowPtrsMax)
+    return fail(c, MXQ_ERR_INVALID_ARGUMENT, "rank16_dot_ptrs: at most %d weights per call", kRowPtrsMax);
+  if (b > (1u << 20)) return fail(c, MXQ_ERR_INVALID_ARGUMENT, "rank16_dot_ptrs: batch too large");
+  if (!aligned16(xq)) return fail(c, MXQ_ERR_INVALID_ARGUMENT, "activation must be 16-byte aligned");
+  const WeightView* v[kRowPtrsMax];
+  for (size_t j = 0; j < nrows; ++j) {
+    if (int rc = check_weight(c, rows[j])) return rc;
+    if (int rc = reject_sparse(c, rows[j], "rank16_dot_ptrs")) return rc;
+    v[j] = &rows[j]->v;
+    if (v[j]->fmt != v[0]->fmt || v[j]->K != v[0]->K)
+      return fail(c, MXQ_ERR_INVALID_ARGUMENT, "rank16_dot_ptrs: weight %zu differs in format or K", j);
+  }
+  DeviceGuard g(c->device);
+  return after_launch(c, launch_row_ptrs(v, (int)nrows, xq, xs, (int)b, y, c->stream), "rank16_dot_ptrs");
+}
+
+int mxq_halting_step(mxq_ctx c, mxq_weight w, const uint8_t* xq, const uint8_t* xs, size_t b, float bias,
+                     mxq_halting_state* state, float* p, uint8_t* should_halt) {
+  if (int rc = check_ctx(c)) return rc;
+  if (int rc = check_weight(c, w)) return rc;
+  if (!xq || !xs || !state || !p || !should_halt || b == 0)
+    return fail(c, MXQ_ERR_INVALID_ARGUMENT, "null pointer or empty batch");
+  if (int rc = reject_sparse(c, w, "halting_step")) return rc;
+  if (w->v.N != 1) return fail(c, MXQ_ERR_INVALID_ARGUMENT, "halting_step: w_halt must have 1 row, has %d", w->v.N);
+  if (b > (1u << 24)) return fail(c, MXQ_ERR_INVALID_ARGUMENT, "halting_step: batch too large");
+  if (!aligned16(xq)) return fail(c, MXQ_ERR_INVALID_ARGUMENT, "activation must be 16-byte aligned");
+  DeviceGuard g(c->device);
+  return after_launch(c, launch_halting(w->v, xq, xs, (int)b, bias, MXQ_HALT_EPS, state, p, should_halt, c->stream),
+                      "halting_step");
+}
+
+static int hashed_route_check(mxq_context* c, size_t t, size_t d, size_t n_experts, size_t top_k, size_t n_hashes) {
+  if (top_k == 0 || top_k > n_experts)
+    return fail(c, MXQ_ERR_INVALID_ARGUMENT, "HashedRouter: top_k (%zu) must be in [1, n_experts=%zu]", top_k,
+                n_experts);
+  if (top_k > 64 || n_experts > 65536) return fail(c, MXQ_ERR_UNSUPPORTED, "HashedRouter: top_k <= 64, n_experts <= 65536");
+  if (n_hashes == 0 || n_hashes > 32) return fail(c, MXQ_ERR_INVALID_ARGUMENT, "HashedRouter: n_hashes must be in [1, 32]");
+  if (d == 0 || d % kBlock || d > (1u << 24)) return fail(c, MXQ_ERR_INVALID_ARGUMENT, "HashedRouter: d must be a positive multiple of 32");
+  if (t > (1u << 24)) return fail(c, MXQ_ERR_INVALID_ARGUMENT, "HashedRouter: too many tokens");
+  return MXQ_OK;
+}
+
+int mxq_hashed_route(mxq_ctx c, const float* x, size_t t, size_t d, size_t n_experts, size_t top_k,
+                     size_t n_hashes, uint64_t seed, int32_t* idx, int32_t* score) {
+  if (int rc = check_ctx(c)) return rc;
+  if (!x || !idx || !score) return fail(c, MXQ_ERR_INVALID_ARGUMENT, "null pointer");
+  if (int rc = hashed_route_check(c, t, d, n_experts, top_k, n_hashes)) return rc;
+  if (t == 0) return MXQ_OK;
+  DeviceGuard g(c->device);
+  return after_launch(c, launch_hashed_route(x, (int)t, (int)d, (int)n_experts, (int)top_k, (int)n_hashes, seed,
+                                             idx, score, c->stream), "hashed_route");
+}
+
+int mxq_hashed_route_host(mxq_ctx c, const float* x, size_t t, size_t d, size_t n_experts, size_t top_k,
+                          size_t n_hashes, uint64_t seed, int32_t* idx, int32_t* score) {
+  MXQ_TRY({
+    if (int rc = check_ctx(c)) return rc;
+    if (!x || !idx || !score) return fail(c, MXQ_ERR_INVALID_ARGUMENT, "null pointer");
+    if (int rc = hashed_route_check(c, t, d, n_experts, top_k, n_hashes)) return rc;
+    if (t == 0) return MXQ_OK;
+    DeviceGuard g(c->device);
+    int rc;
+    const size_t in_bytes = t * d * 4, out_bytes = 2 * t * top_k * 4;
+    if ((rc = ensure(c, c->ws_in, c->ws_in_bytes, in_bytes, "workspace in"))) return rc;
+    if ((rc = ensure(c, c->ws_out, c->ws_out_bytes, out_bytes, "workspace out"))) return rc;
+    int32_t* didx = reinterpret_cast<int32_t*>(c->ws_out);
+    int32_t* dsc = didx + t * top_k;
+    cudaError_t e = cudaMemcpyAsync(c->ws_in, x, in_bytes, cudaMemcpyHostToDevice, c->stream);
+    if (e != cudaSuccess) return cuda_fail(c, e, "copy in");
+    if ((rc = after_launch(c, launch_hashed_route(c->ws_in, (int)t, (int)d, (int)n_experts, (int)top_k,
+                                                  (int)n_hashes, seed, didx, dsc, c->stream), "hashed_route")))
+      return rc;
+    e = cudaMemcpyAsync(idx, didx, t * top_k * 4, cudaMemcpyDeviceToHost, c->stream);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(score, dsc, t * top_k * 4, cudaMemcpyDeviceToHost, c->stream);
+    if (e != cudaSuccess) return cuda_fail(c, e, "copy out");
+    return mxq_synchronize(c);
+  })
+}
+
+int mxq_gae_ring(mxq_ctx c, const float* rewards, const float* values, const uint8_t* dones,
+                 const float* next_values, size_t capacity, size_t size, size_t cursor, size_t t,
+                 size_t e, float gamma, float lambda, float* adv, float* ret) {
+  if (int rc = check_ctx(c)) return rc;
+  if (!rewards || !values || !dones || !next_values || !adv || !ret)
+    return fail(c, MXQ_ERR_INVALID_ARGUMENT, "null pointer");
+  if (capacity == 0 || size > capacity || cursor >= capacity || capacity > ((size_t)1 << 40))
+    return fail(c, MXQ_ERR_INVALID_ARGUMENT, "gae ring: need size <= capacity, cursor < capacity");
+  if (size < capacity && cursor != size % capacity)
+    return fail(c, MXQ_ERR_INVALID_ARGUMENT, "gae ring: a ring that is not full has cursor == size");
+  // agentic_env/replay_memory.cpp:205-213: empty sweep, truncation to what is stored
+  size_t total = t * e;
+  if (t == 0 || e == 0 || size == 0) return MXQ_OK;
+  if (total > size) {
+    t = size / e;
+    total = t * e;
+  }
+  if (t == 0) return MXQ_OK;
+  if (t > (size_t)INT32_MAX || e > (size_t)INT32_MAX) return fail(c, MXQ_ERR_INVALID_ARGUMENT, "gae ring: too large");
+  const size_t start = (capacity + cursor - total) % capacity;
+  const int active = (int)(e > 1024 ? 1024 : e);   // the reference's MAX_ENVS
+  DeviceGuard g(c->device);
+  const float gl = gamma * lambda;
+  gae_ring_kernel<<<(unsigned)((active + 127) / 128), 128, 0, c->stream>>>(
+      rewards, values, dones, next_values, (long)capacity, (long)start, (int)t, (int)e, active, gamma, gl, adv, ret);
+  return after_launch(c, cudaGetLastError(), "gae ring");
 }
 
 }  // extern "C"

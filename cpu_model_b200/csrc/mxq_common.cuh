@@ -21,6 +21,8 @@ constexpr int kTileK = 64;           // K elements per tile in the tiled layout
 
 // Device status word bits (written by bounded waits that gave up).
 constexpr uint32_t kStatusTimeout = 1u;
+// Default limit of a bounded device wait (wall time, %globaltimer).
+constexpr uint64_t kWaitLimitNs = 2000000000ull;
 
 // ------------------------------------------------------------ powers of 2 --
 
@@ -186,7 +188,7 @@ __device__ __forceinline__ uint64_t globaltimer_ns() {
 // returns false.  Every wait in the pipelines below goes through this, so a
 // broken invariant ends the kernel instead of hanging the GPU.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint32_t* status,
-                                          uint64_t limit_ns = 2000000000ull) {
+                                          uint64_t limit_ns = kWaitLimitNs) {
   if (mbar_try_wait_sleep(bar, parity, 20000u)) return true;
   const uint64_t t0 = globaltimer_ns();
   for (uint32_t it = 0; it < (1u << 26); ++it) {   // also capped in polls

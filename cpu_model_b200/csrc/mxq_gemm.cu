@@ -100,6 +100,8 @@ struct Cfg {
   static_assert(XSC >= 2 && XSC * XK >= GPR, "activation ring");
   static_assert(ACC_COLS <= 512, "tensor memory");
   static_assert(SMEM <= 227 * 1024, "shared memory");
+  // mbarriers (raw, activation, weight stages, accumulator, MMA drains) + TMEM slot
+  static_assert((2 * RSC + 2 * XSC + WS + 1 + NG) * 8 + 4 <= 1024, "barrier area");
   static_assert(WORDS == 4 || WORDS == 8 || WORDS == 16, "converter split");
   // the split-K partial tile [BN][128] fp32 (one row tile at a time) reuses the w and x rings
   static_assert((size_t)BN * 128 * 4 <= OP_BYTES, "partial tile");
@@ -231,7 +233,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tc_kernel(GemmArgs a) {
   uint64_t* x_empty = x_full + XSC;
   uint64_t* w_empty = x_empty + XSC;
   uint64_t* acc_full = w_empty + WS;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_full + 1);
+  uint64_t* mma_done = acc_full + 1;                         // [NG] error-path MMA drains
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + C::NG);
   float* part = reinterpret_cast<float*>(w_ring);            // split-K partial [BN][128]
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -250,6 +253,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tc_kernel(GemmArgs a) {
   const int gpr_active = nk < C::GPR ? nk : C::GPR;          // groups per row tile with k-tiles
   const int ngrp = MT * gpr_active;
   uint32_t* status = a.status;
+  const uint64_t lim = a.wait_ns ? a.wait_ns : kWaitLimitNs;
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < RSC; ++i) {
@@ -262,6 +266,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tc_kernel(GemmArgs a) {
     }
     for (int i = 0; i < WS; ++i) mbar_init(&w_empty[i], 1);
     mbar_init(acc_full, ngrp > 0 ? ngrp : 1);
+    for (int i = 0; i < C::NG; ++i) mbar_init(&mma_done[i], 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   if (warp == 1) tmem_alloc(tmem_slot, C::TMEM_COLS);
@@ -279,11 +284,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tc_kernel(GemmArgs a) {
   if (warp == 0) {
     // ------------------------------------------------ raw weight producer
     bool ok = true;
+    int issued = 0;                       // chunks whose copies were issued
     for (int c = 0; c < nch && ok; ++c) {
       const int st = c % RSC;
-      if (c >= RSC) ok = mbar_wait(&raw_empty[st], ((c / RSC) - 1) & 1, status);
+      if (c >= RSC) ok = mbar_wait(&raw_empty[st], ((c / RSC) - 1) & 1, status, lim);
       ok = __all_sync(0xffffffffu, ok);
       if (!ok) break;
+      issued = c + 1;
       if (elect_one()) {
         const int nt_c = nk - c * KPS < KPS ? nk - c * KPS : KPS;
         uint8_t* dst = raw_ring + st * C::RAW_CHUNK;
@@ -297,9 +304,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tc_kernel(GemmArgs a) {
       }
       __syncwarp();
     }
-    // drain: the last issued copies have landed before shared memory is released
-    for (int c = nch - (nch < RSC ? nch : RSC); c < nch && ok; ++c)
-      ok = mbar_wait(&raw_full[c % RSC], (c / RSC) & 1, status);
+    // drain: the last issued copies have landed before shared memory is
+    // released -- on the error path too (each wait is bounded; the phase
+    // waited on is the latest one of its stage)
+    for (int c = issued - (issued < RSC ? issued : RSC); c < issued; ++c)
+      (void)mbar_wait(&raw_full[c % RSC], (c / RSC) & 1, status, lim);
   } else if (warp == 2) {
     // ------------------------------------------- activation tile producer
     asm volatile("griddepcontrol.wait;" ::: "memory");
@@ -307,11 +316,14 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tc_kernel(GemmArgs a) {
         reinterpret_cast<const uint8_t*>(a.opnd) + ((size_t)nt * KT + kb) * C::X_TILE;
     const int nxc = (nk + XK - 1) / XK;
     bool ok = true;
+    int issued = 0;
     for (int c = 0; c < nxc && ok; ++c) {
       const int st = c % XSC;
-      if (c >= XSC) ok = mbar_wait(&x_empty[st], ((c / XSC) - 1) & 1, status);
+      if (c >= XSC) ok = mbar_wait(&x_empty[st], ((c / XSC) - 1) & 1, status, lim);
       ok = __all_sync(0xffffffffu, ok);
       if (!ok) break;
+      issued = c + 1;
+      if (c == 0 && a.withhold_x0) continue;   // test hook: this chunk never arrives
       if (elect_one()) {
         const int nt_c = nk - c * XK < XK ? nk - c * XK : XK;
         mbar_arrive_expect_tx(&x_full[st], (uint32_t)(nt_c * C::X_TILE));
@@ -330,8 +342,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tc_kernel(GemmArgs a) {
       }
       __syncwarp();
     }
-    for (int c = nxc - (nxc < XSC ? nxc : XSC); c < nxc && ok; ++c)
-      ok = mbar_wait(&x_full[c % XSC], (c / XSC) & 1, status);
+    for (int c = issued - (issued < XSC ? issued : XSC); c < issued; ++c)
+      if (c != 0 || !a.withhold_x0) (void)mbar_wait(&x_full[c % XSC], (c / XSC) & 1, status, lim);
   } else if (warp >= kRoleWarps) {
     // ----------------------------- converter groups: convert, issue MMAs
     // Group g serves row tile r = g / GPR and takes the k-tiles j = p, p+GPR,
@@ -364,10 +376,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tc_kernel(GemmArgs a) {
     uint32_t sc_next = ph < nk ? ldg_u16(srow + (size_t)ph * 128) : 0u;
     const uint32_t acc = tmem + (uint32_t)(grp * BN);
     int ntile = 0;                                     // tiles this group has issued
+    bool mma_issued = false;                           // this (issuer) warp issued an MMA
     bool ok = true;
     for (int c = 0; c < nch; ++c) {
       const int rs = c % RSC;
-      if (ok) ok = mbar_wait(&raw_full[rs], (c / RSC) & 1, status);
+      if (ok) ok = mbar_wait(&raw_full[rs], (c / RSC) & 1, status, lim);
       ok = __all_sync(0xffffffffu, ok);
       const uint8_t* raw = raw_ring + rs * C::RAW_CHUNK + r * KPS * C::RAW_W;
 #pragma unroll 1
@@ -389,7 +402,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tc_kernel(GemmArgs a) {
           if (ok && lane == 0) mbar_arrive(&raw_empty[rs]);
         }
         const int ws = grp * C::WSG + (ntile % C::WSG);
-        if (ok && has && ntile >= C::WSG) ok = mbar_wait(&w_empty[ws], ((ntile / C::WSG) - 1) & 1, status);
+        if (ok && has && ntile >= C::WSG) ok = mbar_wait(&w_empty[ws], ((ntile / C::WSG) - 1) & 1, status, lim);
         ok = __all_sync(0xffffffffu, ok);
         uint8_t* wt = w_ring + ws * C::W_TILE;
         if (ok && has) {
@@ -402,7 +415,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tc_kernel(GemmArgs a) {
         named_bar_sync(1 + grp, C::GT);
         if (issuer && has) {
           const int cx = i / XK, xs = cx % XSC;
-          if (ok) ok = mbar_wait(&x_full[xs], (cx / XSC) & 1, status);
+          if (ok) ok = mbar_wait(&x_full[xs], (cx / XSC) & 1, status, lim);
           ok = __all_sync(0xffffffffu, ok);
           if (ok) {
             tc_fence_after();
@@ -416,6 +429,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tc_kernel(GemmArgs a) {
               mma_commit(&x_empty[xs]);
             }
             __syncwarp();
+            mma_issued = true;
           }
         }
         if (has) ++ntile;
@@ -425,7 +439,14 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tc_kernel(GemmArgs a) {
       if (elect_one()) mma_commit(acc_full);
       __syncwarp();
     }
-    if (ngrp > 0) ok = mbar_wait(acc_full, 0, status);
+    // error path: MMAs this warp issued finish before the CTA frees shared
+    // and tensor memory (the commit tracks the issuing lane's MMAs)
+    if (issuer && mma_issued && !ok) {
+      if (elect_one()) mma_commit(&mma_done[grp]);
+      __syncwarp();
+      (void)mbar_wait(&mma_done[grp], 0, status, lim);
+    }
+    if (ngrp > 0) ok = ok && mbar_wait(acc_full, 0, status, lim);
     eok = __all_sync(0xffffffffu, ok);
   }
 

@@ -3,6 +3,7 @@
 #pragma once
 #include <cstdint>
 #include <cuda_runtime.h>
+#include "../../include/mxq.h"
 #include "mxq_common.cuh"
 
 namespace mxq {
@@ -96,6 +97,10 @@ struct GemmArgs {
   int B, Bpad, BN;
   uint32_t* status;          // device status word (bounded waits)
   int splits;                // K splits over a cluster; 0 = chosen by occupancy
+  uint64_t wait_ns;          // limit of every bounded wait; 0 = kWaitLimitNs
+  // Test hook (mxq_debug_gemm_stall): the activation producer withholds its
+  // first copy, so the waits on it run out and the error path is exercised.
+  int withhold_x0;
 };
 
 cudaError_t launch_gemm(const GemmArgs& a, cudaStream_t st, bool pdl);
@@ -131,6 +136,23 @@ cudaError_t launch_moe_combine(const float* yr, const float* gate, const int32_t
 
 cudaError_t launch_scale_range(const uint8_t* scales, size_t count, uint32_t* out2,
                                cudaStream_t st);
+
+// Small operators around the linear layer (mxq_ops.cu).
+// mx_quantize_w: fp32 [N][K] -> int8 [N][K] / packed int4 [N][K/2] + E8M0
+// [N][K/32] + optional w_sums int32 [N][K/32].
+cudaError_t launch_quantize_w(int fmt, const float* w, int N, int K, uint8_t* data, uint8_t* scales,
+                              int32_t* wsums, cudaStream_t st);
+// ACT halting step on a 1-row weight, one state per token.
+constexpr float kHaltEps = 0.01f;
+cudaError_t launch_halting(const WeightView& w, const uint8_t* xq, const uint8_t* xs, int B, float bias,
+                           float eps, mxq_halting_state* st, float* p, uint8_t* halt, cudaStream_t s);
+// Dots against row 0 of up to kRowPtrsMax separate weights (same fmt and K).
+constexpr int kRowPtrsMax = 64;
+cudaError_t launch_row_ptrs(const WeightView* const* ws, int nrows, const uint8_t* xq, const uint8_t* xs, int B,
+                            float* y, cudaStream_t s);
+// LSH top-K router over fp32 rows [T][D] with H <= 32 hyperplanes.
+cudaError_t launch_hashed_route(const float* x, int T, int D, int E, int K, int H, uint64_t seed, int32_t* idx,
+                                int32_t* score, cudaStream_t s);
 
 cudaError_t launch_repack(const uint8_t* data, const uint8_t* scales, int fmt,
                           int N, int K, int Npad, int Kpad, uint8_t* out_data,

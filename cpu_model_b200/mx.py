@@ -23,7 +23,8 @@ __all__ = [
     "mx_quantize_x", "mx_fused_silu_quantize_x", "fused_gated_silu_quantize",
     "mx_gemv", "mx_dot", "mx_dual_dot", "mx_quad_dot", "mx_rank16_dot",
     "mx_rank16_dot_ptrs", "mx_block_dots", "mx_linear", "mx_linear_pair",
-    "gated_mlp_step", "route_topk", "HashedRouter", "fused_compute_gae",
+    "gated_mlp_step", "route_topk", "HashedRouter", "HaltingState", "halting_step", "mx_quantize_w",
+    "fused_compute_gae", "fused_compute_gae_ring",
     "FMT_INT4", "FMT_INT8", "PATH_AUTO", "PATH_GEMV", "PATH_GEMM",
 ]
 
@@ -240,10 +241,27 @@ def mx_rank16_dot(x, w, ctx=None):
     return mx_gemv(x, w, ctx)
 
 
-def mx_rank16_dot_ptrs(x, w, rows, ctx=None):
-    """nca::linalg::mx_rank16_dot_ptrs: rows gathered by id (the reference
-    passed 16 MXINT8Tensor pointers; here an int32 row-id tensor into one
-    expert-pool weight)."""
+def mx_rank16_dot_ptrs(x, w, rows=None, ctx=None):
+    """nca::linalg::mx_rank16_dot_ptrs.  Two forms:
+    - the reference's pointer-array form (nn/tests/autotest.hpp:126-136):
+      `w` a list of one-row MXWeight (16 in the reference, up to 64 here),
+      rows None -> y [B][len(w)] (mxq_rank16_dot_ptrs);
+    - rows gathered by id from one expert-pool weight: `w` an MXWeight and
+      `rows` an int32 device tensor of row ids (mxq_gather_dot)."""
+    if isinstance(w, (list, tuple)):
+        ctx = ctx or w[0].ctx
+        if rows is not None:
+            raise ValueError("mx_rank16_dot_ptrs: the pointer form takes no row ids")
+        for wj in w:
+            _check_act(x, wj)
+            if wj.n != 1:
+                raise ValueError("mx_rank16_dot_ptrs: each weight must have one row, got %d" % wj.n)
+        arr = (ctypes.c_void_p * len(w))(*[wj.h.value for wj in w])
+        y = torch.empty((x.batch, len(w)), dtype=torch.float32, device=x.q.device)
+        ctx._bind()
+        check(ctx.lib.mxq_rank16_dot_ptrs(ctx.h, ctypes.cast(arr, ctypes.c_void_p), len(w), _ptr(x.q), _ptr(x.s),
+                                          x.batch, _ptr(y)), ctx.h)
+        return y
     ctx = ctx or w.ctx
     _check_act(x, w)
     _need_cuda(rows, torch.int32, "rows")
@@ -316,20 +334,101 @@ def route_topk(logits, k, ctx=None):
 
 
 class HashedRouter:
-    """Router with the reference's HashedRouter::Config{d, n_experts, top_k,
-    ...} construction contract (nn/tests/test_robustness.cpp:13-35): top_k >
-    n_experts raises ValueError at construction.  Routing scores are the
-    caller's logits (softmax top-k)."""
+    """linalg::HashedRouter{Config{d, n_experts, top_k, n_hashes}}
+    (nn/tests/test_robustness.cpp:13-35): top_k > n_experts raises ValueError
+    at construction (the reference's invalid_argument).
 
-    def __init__(self, d, n_experts, top_k, n_hashes=8):
+    route(x): the LSH router (mxq_hashed_route) -- sign-of-projection codes of
+    the MX-quantised input over n_hashes seeded +-1 hyperplanes, experts
+    ranked by Hamming similarity of seeded expert codes, ties to the lower id;
+    returns (idx int32 [T][top_k], score int32 [T][top_k]).
+    route_logits(logits): softmax top-k over caller-supplied logits
+    (mxq_route_topk), the MoE layer's router."""
+
+    def __init__(self, d, n_experts, top_k, n_hashes=8, seed=0):
         if top_k > n_experts or top_k == 0:
             raise ValueError("HashedRouter: top_k (%d) exceeds n_experts (%d)" % (top_k, n_experts))
-        self.d, self.n_experts, self.top_k, self.n_hashes = d, n_experts, top_k, n_hashes
+        if not 1 <= n_hashes <= 32 or d % 32:
+            raise ValueError("HashedRouter: n_hashes in [1, 32] and d a multiple of 32")
+        self.d, self.n_experts, self.top_k, self.n_hashes, self.seed = d, n_experts, top_k, n_hashes, seed
 
-    def route(self, logits, ctx=None):
+    def route(self, x, ctx=None):
+        ctx = ctx or context()
+        _need_cuda(x, torch.float32, "x")
+        x2 = x.reshape(-1, x.shape[-1])
+        if x2.shape[1] != self.d:
+            raise ValueError("x has %d features, router d is %d" % (x2.shape[1], self.d))
+        t = x2.shape[0]
+        idx = torch.empty((t, self.top_k), dtype=torch.int32, device=x.device)
+        score = torch.empty((t, self.top_k), dtype=torch.int32, device=x.device)
+        ctx._bind()
+        check(ctx.lib.mxq_hashed_route(ctx.h, _ptr(x2), t, self.d, self.n_experts, self.top_k, self.n_hashes,
+                                       self.seed, _ptr(idx), _ptr(score)), ctx.h)
+        return idx, score
+
+    def route_logits(self, logits, ctx=None):
         if logits.shape[-1] != self.n_experts:
             raise ValueError("logits last dim %d != n_experts %d" % (logits.shape[-1], self.n_experts))
         return route_topk(logits.reshape(-1, self.n_experts), self.top_k, ctx)
+
+
+class HaltingState:
+    """nca::layers::HaltingState (nn/core/layers/halting.hpp:16-20) for B
+    tokens on the device: 16 bytes per token {float p_sum, float remainder,
+    uint64 steps} (mxq_halting_state)."""
+
+    def __init__(self, batch, device=None):
+        self.raw = torch.zeros((batch, 4), dtype=torch.float32,
+                               device=device if device is not None else torch.cuda.current_device())
+
+    @property
+    def p_sum(self):
+        return self.raw[:, 0]
+
+    @property
+    def remainder(self):
+        return self.raw[:, 1]
+
+    @property
+    def steps(self):
+        return self.raw[:, 2:4].contiguous().view(torch.int64).reshape(-1)
+
+
+def halting_step(x, w_halt, bias, state, ctx=None):
+    """nca::layers::halting_step (nn/core/layers/halting.hpp:24-30), batched
+    over the tokens of an MXActivation: p = sigmoid(w_halt . x + bias), ACT
+    update of `state` (HaltingState) in place.  Returns (p [B], should_halt
+    uint8 [B])."""
+    ctx = ctx or w_halt.ctx
+    _check_act(x, w_halt)
+    if w_halt.n != 1:
+        raise ValueError("halting_step: w_halt must have one row, got %d" % w_halt.n)
+    if state.raw.shape[0] != x.batch:
+        raise ValueError("halting_step: state holds %d tokens, activation %d" % (state.raw.shape[0], x.batch))
+    p = torch.empty(x.batch, dtype=torch.float32, device=x.q.device)
+    h = torch.empty(x.batch, dtype=torch.uint8, device=x.q.device)
+    ctx._bind()
+    check(ctx.lib.mxq_halting_step(ctx.h, w_halt.h, _ptr(x.q), _ptr(x.s), x.batch, float(bias), _ptr(state.raw),
+                                   _ptr(p), _ptr(h)), ctx.h)
+    return p, h
+
+
+def mx_quantize_w(w, fmt, ctx=None, with_sums=True):
+    """nca::linalg::mx_quantize_w on the device: fp32 [N][K] -> (data int8
+    [N][K] or packed int4 uint8 [N][K/2], E8M0 scales [N][K/32], w_sums int32
+    [N][K/32] or None)."""
+    ctx = ctx or context()
+    _need_cuda(w, torch.float32, "w")
+    n, k = w.shape
+    if fmt not in (FMT_INT4, FMT_INT8):
+        raise ValueError("unknown weight format %d" % fmt)
+    data = torch.empty((n, k // 2), dtype=torch.uint8, device=w.device) if fmt == FMT_INT4 else \
+        torch.empty((n, k), dtype=torch.int8, device=w.device)
+    scales = torch.empty((n, k // 32), dtype=torch.uint8, device=w.device)
+    sums = torch.empty((n, k // 32), dtype=torch.int32, device=w.device) if with_sums else None
+    ctx._bind()
+    check(ctx.lib.mxq_quantize_w(ctx.h, fmt, _ptr(w), n, k, _ptr(data), _ptr(scales), _ptr(sums)), ctx.h)
+    return data, scales, sums
 
 
 def fused_compute_gae(rewards, values, dones, next_values, gamma=0.99, lam=0.95, ctx=None):
@@ -348,6 +447,29 @@ def fused_compute_gae(rewards, values, dones, next_values, gamma=0.99, lam=0.95,
     ctx._bind()
     check(ctx.lib.mxq_gae(ctx.h, _ptr(rewards), _ptr(values), _ptr(dones), _ptr(next_values), t, e,
                           float(gamma), float(lam), _ptr(adv), _ptr(ret)), ctx.h)
+    return adv, ret
+
+
+def fused_compute_gae_ring(rewards, values, dones, next_values, size, cursor, t, e, adv, ret, gamma=0.99,
+                           lam=0.95, ctx=None):
+    """ReplayMemory::fused_compute_gae on the ring buffer itself
+    (mxq_gae_ring): 1-D device ring arrays of the capacity, `size` items
+    stored, next write at `cursor`; the latest t*e items are swept and only
+    the first 1024 environments written, as in the reference.  adv/ret are
+    updated in place and returned."""
+    ctx = ctx or context()
+    for name, tns, dt in (("rewards", rewards, torch.float32), ("values", values, torch.float32),
+                          ("dones", dones, torch.uint8), ("next_values", next_values, torch.float32),
+                          ("adv", adv, torch.float32), ("ret", ret, torch.float32)):
+        _need_cuda(tns, dt, name)
+    cap = rewards.numel()
+    if values.numel() != cap or dones.numel() != cap or adv.numel() != cap or ret.numel() != cap:
+        raise ValueError("GAE ring arrays must all hold the capacity")
+    if next_values.numel() < min(e, 1024):
+        raise ValueError("next_values needs one value per environment")
+    ctx._bind()
+    check(ctx.lib.mxq_gae_ring(ctx.h, _ptr(rewards), _ptr(values), _ptr(dones), _ptr(next_values), cap, size,
+                               cursor, t, e, float(gamma), float(lam), _ptr(adv), _ptr(ret)), ctx.h)
     return adv, ret
 
 

@@ -75,6 +75,17 @@ extern "C" {
 typedef struct mxq_context* mxq_ctx;
 typedef struct mxq_weight_s* mxq_weight;
 
+/* nca::layers::HaltingState (nn/core/layers/halting.hpp:16-20): the same
+ * members and, with size_t of 8 bytes, the same layout. */
+typedef struct mxq_halting_state {
+  float p_sum;
+  float remainder;
+  uint64_t steps;
+} mxq_halting_state;
+
+/* Halting threshold: a token halts once p_sum + p >= 1 - MXQ_HALT_EPS. */
+#define MXQ_HALT_EPS 0.01f
+
 /* ---------------------------------------------------------- lifecycle --- */
 /* deployment/nca_deploy.h:28-30 (create/destroy) pattern. */
 MXQ_API int mxq_abi_version(void);
@@ -114,6 +125,17 @@ MXQ_API int mxq_weight_create_bsr(mxq_ctx ctx, int fmt, size_t n, size_t k,
 MXQ_API int mxq_weight_destroy(mxq_weight w);
 MXQ_API int mxq_weight_shape(mxq_weight w, int* fmt, size_t* n, size_t* k);
 
+/* nca::linalg::mx_quantize_w (nn/tests/test_auto_generated.cpp:46;
+ * training/fidelity_test.cpp:60-61) on the device: fp32 rows w [N][K] ->
+ * data int8 [N][K] (fmt 8) or packed int4 [N][K/2] (fmt 4), E8M0 scales
+ * [N][K/32] (block exponent: the smallest e with max|w| <= QMAX * 2^e, QMAX
+ * 127 / 7), and, when w_sums is not null, the per-block sums of the
+ * quantised values [N][K/32] (the reference's dpbusd correction term).  A
+ * block holding a NaN or inf gets scale 0xFF and zero values. */
+MXQ_API int mxq_quantize_w(mxq_ctx ctx, int fmt, const float* w, size_t n,
+                           size_t k, void* data, uint8_t* scales,
+                           int32_t* w_sums);
+
 /* --------------------------------------------------------- quantisers --- */
 /* nca::linalg::mx_quantize_x / mx_fused_silu_quantize_x
  * (nn/tests/test_auto_generated.cpp:47-48; semantics
@@ -139,6 +161,15 @@ MXQ_API int mxq_gemv(mxq_ctx ctx, mxq_weight w, const uint8_t* xq,
 MXQ_API int mxq_gather_dot(mxq_ctx ctx, mxq_weight w, const uint8_t* xq,
                            const uint8_t* xs, size_t b, const int32_t* rows,
                            size_t nrows, float* y);
+/* nca::linalg::mx_rank16_dot_ptrs in the reference's pointer-array form
+ * (const MXINT8Tensor** of 16 one-row tensors, nn/tests/autotest.hpp:126-136):
+ * y[b][j] = row 0 of weight rows[j] dotted with activation b, for nrows <= 64
+ * weights of one format and K (host array of handles; device activations and
+ * y [B][nrows]).  The fp32 sum runs in a fixed order (lane l of a warp takes
+ * blocks l, l+32, ...; a xor-butterfly combines the lanes). */
+MXQ_API int mxq_rank16_dot_ptrs(mxq_ctx ctx, const mxq_weight* rows, size_t nrows,
+                                const uint8_t* xq, const uint8_t* xs, size_t b,
+                                float* y);
 /* Per-block int32 dots sum_{i<32} q_x * q_w, out [B][N][K/32]; the
  * dpbusd - 128 * w_sum quantity of the reference's VNNI kernel. */
 MXQ_API int mxq_block_dots(mxq_ctx ctx, mxq_weight w, const uint8_t* xq,
@@ -180,6 +211,30 @@ MXQ_API int mxq_mlp_swiglu(mxq_ctx ctx, mxq_weight gate, mxq_weight up,
 MXQ_API int mxq_linear_noalloc(mxq_ctx ctx, mxq_weight w, const float* x,
                                size_t b, float* y);
 
+/* Test hook for the failure path; no counterpart in the reference.  Runs
+ * the tensor-core linear (one K split) with the first activation copy
+ * withheld and every device-side wait limited to wait_us microseconds
+ * (1 .. 1e6), so the kernel's bounded waits run out: the kernel drains the
+ * copies and tensor-core work it started, frees its tensor memory, records
+ * the timeout in the status word and returns.  The call then synchronises and
+ * returns mxq_synchronize's status, MXQ_ERR_TIMEOUT; y is left undefined and
+ * the context stays usable. */
+MXQ_API int mxq_debug_gemm_stall(mxq_ctx ctx, mxq_weight w, const float* x,
+                                 size_t b, float* y, uint32_t wait_us);
+
+/* ------------------------------------------------------------ halting --- */
+/* nca::layers::halting_step (nn/core/layers/halting.hpp:24-30), batched: per
+ * token b, p = sigmoid(w_halt . x_b + bias) with the 1-row MX dot of
+ * mxq_rank16_dot_ptrs's fixed order and the library's deterministic exp;
+ * state[b].steps += 1; if state[b].p_sum + p >= 1 - MXQ_HALT_EPS the token
+ * halts (should_halt[b] = 1, remainder = 1 - p_sum, p_sum = 1), else p_sum
+ * += p (should_halt[b] = 0).  p[b] = the halting probability.  Device
+ * pointers: xq [B][K], xs [B][K/32], state [B], p [B], should_halt [B]. */
+MXQ_API int mxq_halting_step(mxq_ctx ctx, mxq_weight w_halt, const uint8_t* xq,
+                             const uint8_t* xs, size_t b, float bias,
+                             mxq_halting_state* state, float* p,
+                             uint8_t* should_halt);
+
 /* ------------------------------------------------------------ routing --- */
 /* Top-k expert selection with the HashedRouter contract
  * (nn/tests/test_robustness.cpp:13-35: k > n_experts is an invalid
@@ -188,6 +243,28 @@ MXQ_API int mxq_linear_noalloc(mxq_ctx ctx, mxq_weight w, const float* x,
 MXQ_API int mxq_route_topk(mxq_ctx ctx, const float* logits, size_t t,
                            size_t n_experts, size_t k, int32_t* idx,
                            float* gate);
+
+/* linalg::HashedRouter{Config{d, n_experts, top_k, n_hashes}}::route(x, idx)
+ * (nn/tests/test_robustness.cpp:13-35; "rank-16 VNNI LSH router",
+ * nn/docs/job.md:11).  The reference's algorithm is absent from its
+ * snapshot; this one is a sign-of-projection LSH over the MX-quantised input:
+ * x fp32 [T][d] is quantised per 32-block as mxq_quantize_x does; hyperplane
+ * h < n_hashes (<= 32) has +-1 entries generated from `seed` (no stored
+ * weights); bit h of the token's code is 1 when its projection (per-block
+ * exact int dot, scaled by 2^e_x, summed in block order in fp32) is > 0;
+ * expert e has a seeded n_hashes-bit code, its score is n_hashes minus the
+ * Hamming distance of the two codes; idx [T][top_k] = the top_k scores,
+ * descending, ties to the lower expert id; score [T][top_k] those scores.
+ * top_k > n_experts (or 0) is MXQ_ERR_INVALID_ARGUMENT, the reference's
+ * invalid_argument.  d must be a multiple of 32.  Device pointers. */
+MXQ_API int mxq_hashed_route(mxq_ctx ctx, const float* x, size_t t, size_t d,
+                             size_t n_experts, size_t top_k, size_t n_hashes,
+                             uint64_t seed, int32_t* idx, int32_t* score);
+/* Same with host buffers (the reference's call passes host memory). */
+MXQ_API int mxq_hashed_route_host(mxq_ctx ctx, const float* x_host, size_t t,
+                                  size_t d, size_t n_experts, size_t top_k,
+                                  size_t n_hashes, uint64_t seed,
+                                  int32_t* idx_host, int32_t* score_host);
 
 /* Top-k SwiGLU mixture-of-experts layer (the expert execution behind
  * mx_rank16_dot_ptrs, nn/tests/test_auto_generated.cpp:55, with the 1024 x
@@ -219,11 +296,28 @@ MXQ_API int mxq_policy_head(mxq_ctx ctx, const float* logits,
 /* ---------------------------------------------------------------- GAE --- */
 /* nca::env::ReplayMemory::fused_compute_gae
  * (agentic_env/replay_memory.cpp:204-253) over an interleaved [T][E]
- * trajectory (dones as bytes); writes advantages and returns. */
+ * trajectory (dones as bytes); writes advantages and returns.  Every
+ * environment is computed; the reference stops at its MAX_ENVS = 1024 and
+ * leaves the others untouched (mxq_gae_ring keeps that cap). */
 MXQ_API int mxq_gae(mxq_ctx ctx, const float* rewards, const float* values,
                     const uint8_t* dones, const float* next_values, size_t t,
                     size_t e, float gamma, float lambda, float* adv,
                     float* ret);
+
+/* The same sweep on ReplayMemory's own ring buffer
+ * (agentic_env/replay_memory.cpp:204-253, fused_compute_gae(rollout_steps,
+ * num_envs, gamma, lambda, final_next_values)): rewards/values/dones/adv/ret
+ * are device ring arrays of `capacity` items, `size` of them stored, the
+ * next write at `cursor` (a ring that is not full has cursor == size).  The
+ * latest t*e items ending at the cursor are swept, t cut to size/e when
+ * fewer are stored; indices wrap at the capacity; like the reference, only
+ * the first 1024 environments (its MAX_ENVS) are computed and the rest of the
+ * ring is left as it was. */
+MXQ_API int mxq_gae_ring(mxq_ctx ctx, const float* rewards, const float* values,
+                         const uint8_t* dones, const float* next_values,
+                         size_t capacity, size_t size, size_t cursor, size_t t,
+                         size_t e, float gamma, float lambda, float* adv,
+                         float* ret);
 
 #ifdef __cplusplus
 }

@@ -173,9 +173,19 @@ void mxo_quantize_w(int fmt, const float* w, size_t N, size_t K,
         for (size_t b = 0; b < nb; ++b) {
             const float* v = w + n * K + b * MXO_BLOCK;
             float max_abs = 0.0f;
+            int finite = 1;
             for (int i = 0; i < MXO_BLOCK; ++i) {
                 float a = fabsf(v[i]);
-                if (a > max_abs) max_abs = a;
+                if (!(a == a) || isinf(a)) finite = 0;
+                else if (a > max_abs) max_abs = a;
+            }
+            if (!finite) {
+                /* a block holding a NaN/inf: scale 0xFF, zero values (the
+                 * activation quantiser's convention) */
+                scales[n * nb + b] = 0xFF;
+                if (fmt == MXO_FMT_INT8) memset((int8_t*)data + n * K + b * MXO_BLOCK, 0, MXO_BLOCK);
+                if (w_sums) w_sums[n * nb + b] = 0;
+                continue;
             }
             uint8_t sb = mxo_e8m0_from_absmax(max_abs, qmax);
             scales[n * nb + b] = sb;
@@ -207,9 +217,18 @@ static int32_t block_dot(int fmt, const uint8_t* xq, const void* w, size_t K,
                          size_t n, size_t b)
 {
     int32_t acc = 0;
-    for (int i = 0; i < MXO_BLOCK; ++i) {
-        size_t k = b * MXO_BLOCK + i;
-        acc += ((int32_t)xq[k] - 128) * mxo_weight_at(fmt, w, K, n, k);
+    const uint8_t* x = xq + b * MXO_BLOCK;
+    if (fmt == MXO_FMT_INT8) {
+        const int8_t* wr = (const int8_t*)w + n * K + b * MXO_BLOCK;
+        for (int i = 0; i < MXO_BLOCK; ++i) acc += ((int32_t)x[i] - 128) * (int32_t)wr[i];
+    } else {
+        const uint8_t* wr = (const uint8_t*)w + n * (K / 2) + b * (MXO_BLOCK / 2);
+        for (int i = 0; i < MXO_BLOCK / 2; ++i) {
+            int lo = wr[i] & 0xF, hi = wr[i] >> 4;
+            lo = lo >= 8 ? lo - 16 : lo;
+            hi = hi >= 8 ? hi - 16 : hi;
+            acc += ((int32_t)x[2 * i] - 128) * lo + ((int32_t)x[2 * i + 1] - 128) * hi;
+        }
     }
     return acc;
 }
@@ -242,6 +261,8 @@ void mxo_gemv(int fmt, const uint8_t* xq, const uint8_t* xs, const void* w,
               const uint8_t* ws, size_t B, size_t N, size_t K, float* y)
 {
     size_t nb = K / MXO_BLOCK;
+    /* rows are independent: the threads change no result */
+    #pragma omp parallel for schedule(static) collapse(2)
     for (size_t r = 0; r < B; ++r)
         for (size_t n = 0; n < N; ++n)
             y[r * N + n] = row_dot(fmt, xq + r * K, xs + r * nb, w, ws, K, n);
@@ -252,10 +273,130 @@ void mxo_gather_dot(int fmt, const uint8_t* xq, const uint8_t* xs,
                     const int32_t* rows, size_t nrows, size_t B, float* y)
 {
     size_t nb = K / MXO_BLOCK;
+    #pragma omp parallel for schedule(static) collapse(2)
     for (size_t r = 0; r < B; ++r)
         for (size_t j = 0; j < nrows; ++j)
             y[r * nrows + j] = row_dot(fmt, xq + r * K, xs + r * nb, w, ws, K,
                                        (size_t)rows[j]);
+}
+
+/* ------------------------------------ fixed-order fp32 row dots ------- */
+
+/* 2^n for n in [-149, 127], exact (denormals included). */
+static float pow2x(int n) { return ldexpf(1.0f, n); }
+
+static float e8m0_f32(uint8_t s) { return s == 0xFF ? NAN : pow2x((int)s - 127); }
+
+/* The GPU's one-warp row dot: lane l sums, in fp32 and block order, the
+ * terms (d_b * 2^e_x,b) * 2^e_w,b of blocks b = l, l+32, ...; the 32 lane sums
+ * are combined by the xor-butterfly v_l += v_(l^o), o = 16, 8, 4, 2, 1. */
+static float lane_tree_dot(int fmt, const uint8_t* xq, const uint8_t* xs, const void* w,
+                           const uint8_t* ws, size_t K, size_t n)
+{
+    size_t nb = K / MXO_BLOCK;
+    float v[32];
+    for (int l = 0; l < 32; ++l) v[l] = 0.0f;
+    for (size_t b = 0; b < nb; ++b) {
+        int32_t d = block_dot(fmt, xq, w, K, n, b);
+        float t = ((float)d * e8m0_f32(xs[b])) * e8m0_f32(ws[n * nb + b]);
+        v[b % 32] = v[b % 32] + t;
+    }
+    for (int o = 16; o > 0; o >>= 1) {
+        float u[32];
+        for (int l = 0; l < 32; ++l) u[l] = v[l] + v[l ^ o];
+        for (int l = 0; l < 32; ++l) v[l] = u[l];
+    }
+    return v[0];
+}
+
+void mxo_rank16_dot_ptrs(int fmt, const uint8_t* xq, const uint8_t* xs,
+                         const void* const* rows, const uint8_t* const* row_scales,
+                         size_t nrows, size_t B, size_t K, float* y)
+{
+    size_t nb = K / MXO_BLOCK;
+    for (size_t r = 0; r < B; ++r)
+        for (size_t j = 0; j < nrows; ++j)
+            y[r * nrows + j] = lane_tree_dot(fmt, xq + r * K, xs + r * nb, rows[j], row_scales[j], K, 0);
+}
+
+/* ACT halting (Graves 2016) over B tokens with the GPU's operation order. */
+void mxo_halting_step(int fmt, const uint8_t* xq, const uint8_t* xs, const void* w,
+                      const uint8_t* ws, size_t B, size_t K, float bias, float eps,
+                      float* p_sum, float* remainder, uint64_t* steps, float* p, uint8_t* halt)
+{
+    size_t nb = K / MXO_BLOCK;
+    for (size_t r = 0; r < B; ++r) {
+        float z = lane_tree_dot(fmt, xq + r * K, xs + r * nb, w, ws, K, 0) + bias;
+        float pr = 1.0f / (1.0f + mxo_expf(-z));
+        steps[r] += 1;
+        int h = p_sum[r] + pr >= 1.0f - eps;
+        if (h) {
+            remainder[r] = 1.0f - p_sum[r];
+            p_sum[r] = 1.0f;
+        } else {
+            p_sum[r] = p_sum[r] + pr;
+        }
+        p[r] = pr;
+        halt[r] = (uint8_t)h;
+    }
+}
+
+/* splitmix64 finaliser (the router's hyperplane and code generator) */
+static uint64_t mix64(uint64_t z)
+{
+    z += 0x9E3779B97F4A7C15ull;
+    z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+    z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+    return z ^ (z >> 31);
+}
+
+int mxo_hashed_route(const float* x, size_t T, size_t D, size_t E, size_t K, size_t H,
+                     uint64_t seed, int32_t* idx, int32_t* score)
+{
+    if (K == 0 || K > E || H == 0 || H > 32 || D % MXO_BLOCK) return -1;
+    size_t nb = D / MXO_BLOCK;
+    uint8_t q[MXO_BLOCK], sb;
+    uint32_t mask = H == 32 ? 0xFFFFFFFFu : ((1u << H) - 1u);
+    for (size_t t = 0; t < T; ++t) {
+        float proj[32] = {0};
+        for (size_t b = 0; b < nb; ++b) {
+            const float* xb = x + t * D + b * MXO_BLOCK;
+            int any = 0;
+            for (int i = 0; i < MXO_BLOCK; ++i) any |= xb[i] != 0.0f;
+            quantize_block(xb, q, &sb);
+            if (!any || sb == 0xFF) continue;   /* a zero block adds nothing; a non-finite one is skipped */
+            float sx = pow2x((int)sb - 127);
+            for (size_t h = 0; h < H; ++h) {
+                int32_t d = 0;
+                for (int i = 0; i < MXO_BLOCK; ++i) {
+                    size_t k = b * MXO_BLOCK + i;
+                    uint64_t rr = mix64(seed ^ ((uint64_t)(h + 1) << 40) ^ (uint64_t)(k >> 6));
+                    int sg = ((rr >> (k & 63)) & 1ull) ? 1 : -1;
+                    d += ((int32_t)q[i] - 128) * sg;
+                }
+                proj[h] = proj[h] + (float)d * sx;
+            }
+        }
+        uint32_t code = 0;
+        for (size_t h = 0; h < H; ++h)
+            if (proj[h] > 0.0f) code |= 1u << h;
+        int32_t chosen[64];
+        for (size_t j = 0; j < K; ++j) {
+            int best = -1, bs = -1;
+            for (size_t e = 0; e < E; ++e) {
+                int used = 0;
+                for (size_t p2 = 0; p2 < j; ++p2) used |= chosen[p2] == (int32_t)e;
+                if (used) continue;
+                uint32_t ce = (uint32_t)mix64(seed ^ 0xC0DEC0DEull ^ ((uint64_t)e << 20)) & mask;
+                int sc = (int)H - __builtin_popcount((code ^ ce) & mask);
+                if (sc > bs) { bs = sc; best = (int)e; }
+            }
+            chosen[j] = best;
+            idx[t * K + j] = best;
+            score[t * K + j] = bs;
+        }
+    }
+    return 0;
 }
 
 /* ---------------------------------------------------------------- MLP --- */
@@ -396,6 +537,43 @@ void mxo_policy_head(const float* logits, const float* actions, size_t rows,
 /* ---------------------------------------------------------------- GAE --- */
 
 /* agentic_env/replay_memory.cpp:204-253, same operation order per element. */
+/* ReplayMemory::fused_compute_gae on the ring buffer itself
+ * (agentic_env/replay_memory.cpp:204-253): the latest T*E items ending at
+ * the write cursor (T cut to size/E when fewer are stored), at most the
+ * first 1024 environments (the reference's MAX_ENVS), indices wrapping at
+ * the capacity.  Entries outside that window are not written. */
+void mxo_gae_ring(const float* rewards, const float* values, const uint8_t* dones,
+                  const float* next_values, size_t cap, size_t size, size_t cursor,
+                  size_t T, size_t E, float gamma, float lambda, float* adv, float* ret)
+{
+    size_t total = T * E;
+    if (total == 0 || size == 0) return;
+    if (total > size) {
+        T = size / E;
+        total = T * E;
+    }
+    size_t start = (cap + cursor - total) % cap;
+    size_t active = E > 1024 ? 1024 : E;
+    float gl = gamma * lambda;
+    float* acc = (float*)calloc(active ? active : 1, sizeof(float));
+    float* vn = (float*)malloc((active ? active : 1) * sizeof(float));
+    memcpy(vn, next_values, active * sizeof(float));
+    for (size_t tt = T; tt-- > 0;) {
+        for (size_t k = 0; k < active; ++k) {
+            size_t i = start + tt * E + k;
+            if (i >= cap) i -= cap;
+            float done_f = dones[i] ? 0.0f : 1.0f;
+            float delta = rewards[i] + gamma * vn[k] * done_f - values[i];
+            acc[k] = delta + gl * acc[k] * done_f;
+            adv[i] = acc[k];
+            ret[i] = acc[k] + values[i];
+            vn[k] = values[i];
+        }
+    }
+    free(acc);
+    free(vn);
+}
+
 void mxo_gae(const float* rewards, const float* values, const uint8_t* dones,
              const float* next_values, size_t T, size_t E, float gamma,
              float lambda, float* adv, float* ret)

@@ -89,6 +89,31 @@ void mxo_gather_dot(int fmt, const uint8_t* xq, const uint8_t* xs,
                     const void* w, const uint8_t* ws, size_t K,
                     const int32_t* rows, size_t nrows, size_t B, float* y);
 
+/* mx_rank16_dot_ptrs in the pointer-array form (nn/tests/autotest.hpp:126-136):
+ * y[b][j] = row 0 of rows[j] (scales row_scales[j]) dotted with activation b,
+ * summed in the GPU's fixed order: lane l of a warp adds the fp32 terms
+ * (d * 2^e_x) * 2^e_w of blocks l, l+32, ... in order, then a xor-butterfly
+ * over the 32 lanes (so the result is bit-identical to the GPU's). */
+void mxo_rank16_dot_ptrs(int fmt, const uint8_t* xq, const uint8_t* xs,
+                         const void* const* rows, const uint8_t* const* row_scales,
+                         size_t nrows, size_t B, size_t K, float* y);
+
+/* layers::halting_step (nn/core/layers/halting.hpp:24-30), ACT: p = sigmoid(
+ * w . x + bias) (the dot in the order above, exp by mxo_expf), steps += 1;
+ * halt when p_sum + p >= 1 - eps: remainder = 1 - p_sum, p_sum = 1; else
+ * p_sum += p.  State arrays [B] are updated in place. */
+void mxo_halting_step(int fmt, const uint8_t* xq, const uint8_t* xs, const void* w,
+                      const uint8_t* ws, size_t B, size_t K, float bias, float eps,
+                      float* p_sum, float* remainder, uint64_t* steps, float* p, uint8_t* halt);
+
+/* linalg::HashedRouter::route (nn/tests/test_robustness.cpp:13-35) as the
+ * library defines it (the reference's algorithm is absent): sign-of-
+ * projection LSH over the MX-quantised input with H seeded +-1 hyperplanes,
+ * Hamming similarity to seeded expert codes, top-K (ties to the lower id).
+ * Returns -1 when K > E, K == 0, H not in [1, 32] or D % 32 != 0. */
+int mxo_hashed_route(const float* x, size_t T, size_t D, size_t E, size_t K, size_t H,
+                     uint64_t seed, int32_t* idx, int32_t* score);
+
 /* gated_mlp_step (nn/tests/test_auto_generated.cpp:42).  x fp32 [B][D] -> quantise -> gate,up [F] ->
  * swiglu-quantise -> down [D].  If mid_q/mid_s are non-NULL the intermediate
  * MX activation is written there ([B][F], [B][F/32]). */
@@ -108,6 +133,14 @@ int mxo_route_topk(const float* logits, size_t T, size_t E, size_t k,
 void mxo_gae(const float* rewards, const float* values, const uint8_t* dones,
              const float* next_values, size_t T, size_t E, float gamma,
              float lambda, float* adv, float* ret);
+
+/* The same on the ReplayMemory ring (agentic_env/replay_memory.cpp:204-253):
+ * rewards/values/dones/adv/ret hold `cap` items, `size` of them valid, the
+ * next write at `cursor`; the latest T*E items are swept (T cut to size/E),
+ * environments beyond the reference's MAX_ENVS = 1024 are left untouched. */
+void mxo_gae_ring(const float* rewards, const float* values, const uint8_t* dones,
+                  const float* next_values, size_t cap, size_t size, size_t cursor,
+                  size_t T, size_t E, float gamma, float lambda, float* adv, float* ret);
 
 /* PPO rollout head of PPOTrainer::update_step (training/ppo_trainer.cpp:64-66
  * and :77): per row, log_probs = log_softmax(logits) (max, then the sum of

@@ -42,6 +42,7 @@ def lib():
         _c.mxo_silu.argtypes = [ctypes.c_float]
         _c.mxo_weight_at.restype = ctypes.c_int
         _c.mxo_route_topk.restype = ctypes.c_int
+        _c.mxo_hashed_route.restype = ctypes.c_int
         _c.mxo_moe.restype = ctypes.c_int
         _c.mxb_gemv.restype = ctypes.c_int
         _c.mxb_max_threads.restype = ctypes.c_int
@@ -99,6 +100,48 @@ def quantize_w(fmt, w):
     sums = np.empty((n, k // 32), np.int32)
     lib().mxo_quantize_w(ctypes.c_int(fmt), _p(w), *_sz(n, k), _p(data), _p(scales), _p(sums))
     return data, scales, sums
+
+
+def rank16_dot_ptrs(fmt, xq, xs, rows, row_scales, k):
+    """rows: list of one-row weights (int8 [1][K] or int4 [1][K/2]) with
+    their scales [1][K/32]; y [B][len(rows)] in the GPU's summation order."""
+    xq = np.ascontiguousarray(xq, np.uint8)
+    xs = np.ascontiguousarray(xs, np.uint8)
+    b = xq.shape[0]
+    rs = [np.ascontiguousarray(r) for r in rows]
+    ss = [np.ascontiguousarray(x, np.uint8) for x in row_scales]
+    rp = (ctypes.c_void_p * len(rs))(*[r.ctypes.data for r in rs])
+    sp = (ctypes.c_void_p * len(ss))(*[x.ctypes.data for x in ss])
+    y = np.empty((b, len(rs)), np.float32)
+    lib().mxo_rank16_dot_ptrs(ctypes.c_int(fmt), _p(xq), _p(xs), rp, sp, *_sz(len(rs), b, k), _p(y))
+    return y
+
+
+def halting_step(fmt, xq, xs, w, ws, k, bias, p_sum, remainder, steps, eps=0.01):
+    """ACT halting over B tokens; the state arrays (float32, float32, uint64)
+    are updated in place.  Returns (p, halt)."""
+    xq = np.ascontiguousarray(xq, np.uint8)
+    b = xq.shape[0]
+    p = np.empty(b, np.float32)
+    h = np.empty(b, np.uint8)
+    lib().mxo_halting_step(ctypes.c_int(fmt), _p(xq), _p(np.ascontiguousarray(xs, np.uint8)), _p(np.ascontiguousarray(w)),
+                           _p(np.ascontiguousarray(ws, np.uint8)), *_sz(b, k), ctypes.c_float(bias), ctypes.c_float(eps),
+                           _p(p_sum), _p(remainder), _p(steps), _p(p), _p(h))
+    return p, h
+
+
+def hashed_route(x, n_experts, top_k, n_hashes, seed):
+    """(idx [T][top_k], score [T][top_k]) of the LSH router; ValueError for
+    top_k > n_experts (the reference's invalid_argument)."""
+    x = np.ascontiguousarray(x, np.float32)
+    t, d = x.shape
+    idx = np.empty((t, max(top_k, 1)), np.int32)
+    sc = np.empty((t, max(top_k, 1)), np.int32)
+    rc = lib().mxo_hashed_route(_p(x), *_sz(t, d, n_experts, top_k, n_hashes), ctypes.c_uint64(seed), _p(idx),
+                                _p(sc))
+    if rc != 0:
+        raise ValueError("HashedRouter: top_k=%d must be in [1, n_experts=%d]" % (top_k, n_experts))
+    return idx, sc
 
 
 def block_dots(fmt, xq, w, n, k):
@@ -166,6 +209,39 @@ def gae(rewards, values, dones, next_values, gamma, lam):
     lib().mxo_gae(_p(r), _p(v), _p(d), _p(nv), *_sz(t, e), ctypes.c_float(gamma), ctypes.c_float(lam),
                   _p(adv), _p(ret))
     return adv, ret
+
+
+def gae_ring(rewards, values, dones, next_values, size, cursor, t, e, gamma, lam, adv, ret):
+    """Ring-buffer GAE (mxo_gae_ring) over 1-D ring arrays of the capacity;
+    adv/ret (float32, capacity) are updated in place and returned."""
+    r = np.ascontiguousarray(rewards, np.float32)
+    v = np.ascontiguousarray(values, np.float32)
+    d = np.ascontiguousarray(dones, np.uint8)
+    nv = np.ascontiguousarray(next_values, np.float32)
+    assert adv.dtype == np.float32 and ret.dtype == np.float32 and adv.flags.c_contiguous and ret.flags.c_contiguous
+    lib().mxo_gae_ring(_p(r), _p(v), _p(d), _p(nv), *_sz(r.size, size, cursor, t, e), ctypes.c_float(gamma),
+                       ctypes.c_float(lam), _p(adv), _p(ret))
+    return adv, ret
+
+
+def ref_gae_ring(rewards_pushed, dones_pushed, values_latest, cap, t, e, next_values, gamma, lam):
+    """The reference's own ReplayMemory (oracle/_ref/libref_gae.so): push the
+    given items one by one into a ring of `cap` items (wrapping when more are
+    pushed), write_values(len(values_latest)), fused_compute_gae(t, e).
+    Returns the ring's (rewards, values, dones, advantages, returns, size,
+    cursor)."""
+    rp = np.ascontiguousarray(rewards_pushed, np.float32)
+    dp = np.ascontiguousarray(dones_pushed, np.uint8)
+    vl = np.ascontiguousarray(values_latest, np.float32)
+    nv = np.ascontiguousarray(next_values, np.float32)
+    out = {k: np.zeros(cap, np.float32) for k in ("r", "v", "adv", "ret")}
+    d_out = np.zeros(cap, np.uint8)
+    meta = np.zeros(2, np.uint64)
+    L = ctypes.CDLL(REF_GAE)
+    L.ref_gae_ring(_p(rp), _p(dp), *_sz(rp.size), _p(vl), *_sz(vl.size, cap, t, e), _p(nv), ctypes.c_float(gamma),
+                   ctypes.c_float(lam), _p(out["r"]), _p(out["v"]), _p(d_out), _p(out["adv"]), _p(out["ret"]),
+                   _p(meta))
+    return out["r"], out["v"], d_out, out["adv"], out["ret"], int(meta[0]), int(meta[1])
 
 
 def ref_gae_available():

@@ -33,3 +33,48 @@ extern "C" int ref_gae(const float* rewards, const float* values,
     std::memcpy(ret, rm.get_returns(), n * sizeof(float));
     return 0;
 }
+
+// The ring form: push n_push items one by one into a ReplayMemory of `cap`
+// items (it wraps when n_push > cap), write the latest n_val values, run
+// fused_compute_gae(T, E), and copy out the whole ring plus (size, cursor).
+extern "C" int ref_gae_ring(const float* rewards, const unsigned char* dones, size_t n_push,
+                            const float* values, size_t n_val, size_t cap, size_t T, size_t E,
+                            const float* next_values, float gamma, float lambda,
+                            float* r_out, float* v_out, unsigned char* d_out, float* adv_out,
+                            float* ret_out, unsigned long long* meta) {
+    nca::env::ReplayMemory rm(cap, 1, 1);
+    float s = 0.f, a = 0.f;
+    for (size_t i = 0; i < n_push; ++i) rm.push(&s, &a, rewards[i], dones[i] != 0);
+    rm.write_values(n_val, values);
+    rm.fused_compute_gae(T, E, gamma, lambda, next_values);
+    // the ring's own arrays: the latest span views expose rewards/dones, the
+    // accessors values/advantages/returns (all `cap` long)
+    nca::env::BatchSpan spans[2];
+    size_t ns = rm.get_latest_spans(rm.size(), spans);
+    std::memset(r_out, 0, cap * sizeof(float));
+    std::memset(d_out, 0, cap);
+    const float* base_r = nullptr;
+    const bool* base_d = nullptr;
+    for (size_t j = 0; j < ns; ++j) {
+        // the span starting lowest in memory starts at ring index 0 when the
+        // ring has wrapped; otherwise the single span starts at index 0 too
+        if (!base_r || spans[j].rewards < base_r) {
+            base_r = spans[j].rewards;
+            base_d = spans[j].dones;
+        }
+    }
+    for (size_t j = 0; j < ns; ++j) {
+        size_t off = (size_t)(spans[j].rewards - base_r);
+        for (size_t i = 0; i < spans[j].count; ++i) {
+            r_out[off + i] = spans[j].rewards[i];
+            d_out[off + i] = spans[j].dones[i] ? 1 : 0;
+        }
+    }
+    (void)base_d;
+    std::memcpy(v_out, rm.get_values(), cap * sizeof(float));
+    std::memcpy(adv_out, rm.get_advantages(), cap * sizeof(float));
+    std::memcpy(ret_out, rm.get_returns(), cap * sizeof(float));
+    meta[0] = rm.size();
+    meta[1] = n_push % cap;
+    return 0;
+}

@@ -2,6 +2,11 @@
 
     python tests/golden/make_golden.py
 
+gae_ring_reference.npz -- the same function on the reference's own ring
+    buffer (ReplayMemory with capacity < items pushed, a sweep cut to what is
+    stored, more than its MAX_ENVS = 1024 environments), through
+    oracle/_ref's ref_gae_ring; the advantages/returns of the whole ring.
+
 gae_reference.npz -- outputs of the REFERENCE's own
     nca::env::ReplayMemory::fused_compute_gae, compiled from its sources
     (agentic_env/replay_memory.cpp) into oracle/_ref/libref_gae.so by
@@ -57,6 +62,31 @@ def make_gae():
     np.savez_compressed(os.path.join(HERE, "gae_reference.npz"), **out)
 
 
+# (capacity, items pushed, rollout_steps T, envs E): a wrapped ring, a full
+# ring with the cursor back at 0, a sweep cut to what is stored, more than the
+# reference's MAX_ENVS = 1024 environments (the rest of the ring untouched),
+# and a wrapped ring of wide rows
+GAE_RING_CASES = [(100, 250, 10, 7), (64, 64, 8, 8), (50, 30, 10, 4), (3000, 3000, 2, 1500),
+                  (1000, 1700, 5, 150)]
+
+
+def make_gae_ring():
+    """Outputs of the reference's own ReplayMemory ring: items pushed one by
+    one (wrapping), the latest values written, fused_compute_gae(T, E)."""
+    out = {}
+    g = synth.rng(11)
+    for i, (cap, npush, t, e) in enumerate(GAE_RING_CASES):
+        rp = g.standard_normal(npush, dtype=np.float32)
+        dp = (g.random(npush) < 0.1).astype(np.uint8)
+        vl = g.standard_normal(min(t * e, min(npush, cap)), dtype=np.float32)
+        nv = g.standard_normal(e, dtype=np.float32)
+        r, v, d, adv, ret, size, cur = oracle.ref_gae_ring(rp, dp, vl, cap, t, e, nv, 0.99, 0.95)
+        p = "c%d_" % i
+        out.update({p + "r": r, p + "v": v, p + "d": d, p + "nv": nv, p + "adv": adv, p + "ret": ret,
+                    p + "meta": np.array([cap, size, cur, t, e], np.int64)})
+    np.savez_compressed(os.path.join(HERE, "gae_ring_reference.npz"), **out)
+
+
 def make_mx():
     out = {}
     cases = [
@@ -86,5 +116,6 @@ def make_mx():
 
 if __name__ == "__main__":
     make_gae()
+    make_gae_ring()
     make_mx()
     print("wrote", os.listdir(HERE))

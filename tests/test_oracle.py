@@ -234,6 +234,44 @@ def test_gae_matches_reference_fixture(case):
     assert np.array_equal(ret, d[case + "_ret"])
 
 
+def gae_ring_cases():
+    d = np.load(os.path.join(GOLD, "gae_ring_reference.npz"))
+    n = len({f.split("_")[0] for f in d.files})
+    for i in range(n):
+        p = "c%d_" % i
+        yield {k[len(p):]: d[k] for k in d.files if k.startswith(p)}
+
+
+def test_gae_ring_matches_reference_fixture():
+    """The ring form (agentic_env/replay_memory.cpp:204-253) against the
+    reference's own ReplayMemory: wrapped rings, a sweep cut to what is
+    stored, more than MAX_ENVS = 1024 environments (the rest untouched)."""
+    for c in gae_ring_cases():
+        cap, size, cur, t, e = (int(v) for v in c["meta"])
+        adv = np.zeros(cap, np.float32)
+        ret = np.zeros(cap, np.float32)
+        oracle.gae_ring(c["r"], c["v"], c["d"], c["nv"], size, cur, t, e, 0.99, 0.95, adv, ret)
+        assert np.array_equal(adv, c["adv"]) and np.array_equal(ret, c["ret"]), (cap, size, cur, t, e)
+        if e > 1024:        # the reference leaves environments >= 1024 untouched
+            cols = np.arange(cap) % e
+            assert np.all(c["adv"][cols >= 1024] == 0) and np.any(c["adv"][cols < 1024] != 0)
+
+
+@pytest.mark.skipif(not oracle.ref_gae_available(), reason="reference GAE not built here")
+def test_gae_ring_matches_reference_build_live():
+    g = synth.rng(123)
+    for cap, npush, t, e in [(37, 100, 6, 5), (500, 777, 3, 1100), (10, 4, 3, 2)]:
+        rp = g.standard_normal(npush, dtype=np.float32)
+        dp = (g.random(npush) < 0.2).astype(np.uint8)
+        vl = g.standard_normal(min(t * e, min(npush, cap)), dtype=np.float32)
+        nv = g.standard_normal(e, dtype=np.float32)
+        r, v, d, adv, ret, size, cur = oracle.ref_gae_ring(rp, dp, vl, cap, t, e, nv, 0.98, 0.9)
+        a2 = np.zeros(cap, np.float32)
+        r2 = np.zeros(cap, np.float32)
+        oracle.gae_ring(r, v, d, nv, size, cur, t, e, 0.98, 0.9, a2, r2)
+        assert np.array_equal(a2, adv) and np.array_equal(r2, ret)
+
+
 @pytest.mark.skipif(not oracle.ref_gae_available(), reason="reference GAE not built here")
 def test_gae_matches_reference_build_live():
     g = synth.rng(99)
