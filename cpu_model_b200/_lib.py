@@ -59,6 +59,8 @@ SIGNATURES = {
     "mxq_debug_gemm_stall": [_vp, _vp, _vp, _sz, _vp, ctypes.c_uint32],
     "mxq_route_topk": [_vp, _vp, _sz, _sz, _sz, _vp, _vp],
     "mxq_quantize_w": [_vp, _i, _vp, _sz, _sz, _vp, _vp, _vp],
+    "mxq_weight_quantize": [_vp, _i, _sz, _sz, _vp, _i, ctypes.POINTER(_vp)],
+    "mxq_halting_step_host": [_vp, _vp, _vp, _vp, _f, _vp, _vp, _vp],
     "mxq_rank16_dot_ptrs": [_vp, _vp, _sz, _vp, _vp, _sz, _vp],
     "mxq_halting_step": [_vp, _vp, _vp, _vp, _sz, _f, _vp, _vp, _vp],
     "mxq_hashed_route": [_vp, _vp, _sz, _sz, _sz, _sz, _sz, ctypes.c_uint64, _vp, _vp],

@@ -1506,6 +1506,69 @@ int mxq_quantize_w(mxq_ctx c, int fmt, const float* w, size_t n, size_t k, void*
                                            c->stream), "quantize_w");
 }
 
+int mxq_weight_quantize(mxq_ctx c, int fmt, size_t n, size_t k, const float* w, int on_device, mxq_weight* out) {
+  MXQ_TRY({
+    if (int rc = check_ctx(c)) return rc;
+    if (!w || !out) return fail(c, MXQ_ERR_INVALID_ARGUMENT, "null pointer");
+    *out = nullptr;
+    if (fmt != MXQ_FMT_INT4 && fmt != MXQ_FMT_INT8)
+      return fail(c, MXQ_ERR_INVALID_ARGUMENT, "unknown weight format %d", fmt);
+    if (n == 0 || k == 0 || k % kBlock)
+      return fail(c, MXQ_ERR_INVALID_ARGUMENT, "weight_quantize: K must be a positive multiple of 32");
+    if (n > (1u << 24) || k > (1u << 24)) return fail(c, MXQ_ERR_INVALID_ARGUMENT, "weight_quantize: shape too large");
+    DeviceGuard g(c->device);
+    // scratch: quantised bytes, scales, then (host input) the fp32 rows at a
+    // 16-byte boundary
+    const size_t data_bytes = fmt == 4 ? n * k / 2 : n * k, sc_bytes = n * k / kBlock;
+    const size_t off = (data_bytes + sc_bytes + 15) / 16 * 16;
+    const size_t in_bytes = on_device ? 0 : n * k * 4;
+    uint8_t* tmp = nullptr;
+    cudaError_t e = cudaMalloc(&tmp, off + in_bytes);
+    if (e != cudaSuccess) return cuda_fail(c, e, "weight_quantize scratch");
+    const float* src = w;
+    if (!on_device) {
+      float* staged = reinterpret_cast<float*>(tmp + off);
+      e = cudaMemcpyAsync(staged, w, in_bytes, cudaMemcpyHostToDevice, c->stream);
+      src = staged;
+    }
+    if (e == cudaSuccess) e = launch_quantize_w(fmt, src, (int)n, (int)k, tmp, tmp + data_bytes, nullptr, c->stream);
+    if (e != cudaSuccess) {
+      cudaStreamSynchronize(c->stream);
+      cudaFree(tmp);
+      return cuda_fail(c, e, "weight_quantize");
+    }
+    c->launches++;
+    const int rc = mxq_weight_create(c, fmt, n, k, tmp, tmp + data_bytes, 1, out);
+    cudaStreamSynchronize(c->stream);
+    cudaFree(tmp);
+    return rc;
+  })
+}
+
+int mxq_halting_step_host(mxq_ctx c, mxq_weight w, const uint8_t* xq, const uint8_t* xs, float bias,
+                          mxq_halting_state* state, float* p, uint8_t* should_halt) {
+  MXQ_TRY({
+    if (int rc = check_ctx(c)) return rc;
+    if (!state || !p || !should_halt) return fail(c, MXQ_ERR_INVALID_ARGUMENT, "null pointer");
+    DeviceGuard g(c->device);
+    int rc;
+    // device staging: [state 16 B][p 4 B][halt 1 B]
+    if ((rc = ensure(c, c->ws_out, c->ws_out_bytes, 32, "workspace out"))) return rc;
+    uint8_t* base = reinterpret_cast<uint8_t*>(c->ws_out);
+    auto* dst = reinterpret_cast<mxq_halting_state*>(base);
+    float* dp = reinterpret_cast<float*>(base + 16);
+    uint8_t* dh = base + 20;
+    cudaError_t e = cudaMemcpyAsync(dst, state, sizeof(mxq_halting_state), cudaMemcpyHostToDevice, c->stream);
+    if (e != cudaSuccess) return cuda_fail(c, e, "copy in");
+    if ((rc = mxq_halting_step(c, w, xq, xs, 1, bias, dst, dp, dh))) return rc;
+    e = cudaMemcpyAsync(state, dst, sizeof(mxq_halting_state), cudaMemcpyDeviceToHost, c->stream);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(p, dp, 4, cudaMemcpyDeviceToHost, c->stream);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(should_halt, dh, 1, cudaMemcpyDeviceToHost, c->stream);
+    if (e != cudaSuccess) return cuda_fail(c, e, "copy out");
+    return mxq_synchronize(c);
+  })
+}
+
 int mxq_rank16_dot_ptrs(mxq_ctx c, const mxq_weight* rows, size_t nrows, const uint8_t* xq, const uint8_t* xs,
                         size_t b, float* y) {
   if (int rc = check_ctx(c)) return rc;

@@ -136,6 +136,12 @@ MXQ_API int mxq_quantize_w(mxq_ctx ctx, int fmt, const float* w, size_t n,
                            size_t k, void* data, uint8_t* scales,
                            int32_t* w_sums);
 
+/* mx_quantize_w and upload in one call: fp32 rows w [N][K] (host when
+ * on_device = 0, device when 1) are quantised on the device
+ * (mxq_quantize_w's rules) into a new weight handle. */
+MXQ_API int mxq_weight_quantize(mxq_ctx ctx, int fmt, size_t n, size_t k,
+                                const float* w, int on_device, mxq_weight* out);
+
 /* --------------------------------------------------------- quantisers --- */
 /* nca::linalg::mx_quantize_x / mx_fused_silu_quantize_x
  * (nn/tests/test_auto_generated.cpp:47-48; semantics
@@ -234,6 +240,14 @@ MXQ_API int mxq_halting_step(mxq_ctx ctx, mxq_weight w_halt, const uint8_t* xq,
                              const uint8_t* xs, size_t b, float bias,
                              mxq_halting_state* state, float* p,
                              uint8_t* should_halt);
+
+/* One token with the state and outputs in HOST memory, the reference's
+ * halting_step(x_q, w_halt, b_halt, state, should_halt) call shape
+ * (device activation xq [K], xs [K/32]); synchronous. */
+MXQ_API int mxq_halting_step_host(mxq_ctx ctx, mxq_weight w_halt,
+                                  const uint8_t* xq, const uint8_t* xs,
+                                  float bias, mxq_halting_state* state_host,
+                                  float* p_host, uint8_t* should_halt_host);
 
 /* ------------------------------------------------------------ routing --- */
 /* Top-k expert selection with the HashedRouter contract
