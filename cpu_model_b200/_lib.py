@@ -57,6 +57,7 @@ SIGNATURES = {
     "mxq_mlp_swiglu": [_vp, _vp, _vp, _vp, _vp, _sz, _vp],
     "mxq_linear_noalloc": [_vp, _vp, _vp, _sz, _vp],
     "mxq_debug_gemm_stall": [_vp, _vp, _vp, _sz, _vp, ctypes.c_uint32],
+    "mxq_debug_pair_stall": [_vp, _vp, _vp, _vp, _vp, ctypes.c_uint32],
     "mxq_route_topk": [_vp, _vp, _sz, _sz, _sz, _vp, _vp],
     "mxq_quantize_w": [_vp, _i, _vp, _sz, _sz, _vp, _vp, _vp],
     "mxq_weight_quantize": [_vp, _i, _sz, _sz, _vp, _i, ctypes.POINTER(_vp)],

@@ -20,7 +20,7 @@ struct mxq_context {
   int device = 0;
   cudaStream_t stream = nullptr;
   int path = MXQ_PATH_AUTO;
-  uint32_t* status = nullptr;  // device status word
+  uint32_t* status = nullptr;  // device status word; status[1..2]: the pair kernel's grid barrier
   uint32_t* status_host = nullptr;  // pinned mirror, read after one stream sync
   uint64_t launches = 0;
   std::string err;
@@ -559,8 +559,8 @@ int mxq_create(int device, mxq_ctx* out) {
                   device, prop.major, prop.minor);
     auto* c = new mxq_context();
     c->device = device;
-    e = cudaMalloc(&c->status, sizeof(uint32_t));
-    if (e == cudaSuccess) e = cudaMemset(c->status, 0, sizeof(uint32_t));
+    e = cudaMalloc(&c->status, 4 * sizeof(uint32_t));
+    if (e == cudaSuccess) e = cudaMemset(c->status, 0, 4 * sizeof(uint32_t));
     if (e == cudaSuccess) e = cudaHostAlloc(&c->status_host, sizeof(uint32_t), cudaHostAllocDefault);
     if (e != cudaSuccess) {
       delete c;
@@ -659,7 +659,8 @@ int mxq_synchronize(mxq_ctx c) {
   if (e != cudaSuccess) return cuda_fail(c, e, "synchronize");
   const uint32_t st = *c->status_host;
   if (st) {
-    cudaMemset(c->status, 0, sizeof(uint32_t));
+    // the status word and the grid barrier a timed-out kernel may have left mid-way
+    cudaMemset(c->status, 0, 4 * sizeof(uint32_t));
     return fail(c, MXQ_ERR_TIMEOUT, "a device-side bounded wait gave up (status 0x%x)", st);
   }
   return MXQ_OK;
@@ -984,6 +985,19 @@ int mxq_linear_pair(mxq_ctx c, mxq_weight w1, mxq_weight w2, const float* x,
     int rc;
     if ((rc = ensure(c, c->ws_f0, c->ws_f0_bytes, b * w1->v.N * 4, "workspace mid"))) return rc;
     if (use_gemv(c, b, w1) && use_gemv(c, b, w2)) {
+      if (b == 1 && pair_supported(w1->v, w2->v)) {
+        // batch 1: both projections in one kernel, every weight byte of the
+        // pair in flight from its start
+        PairArgs pa{};
+        pa.w1 = w1->v;
+        pa.w2 = w2->v;
+        pa.x = x;
+        pa.y1 = c->ws_f0;
+        pa.y = y;
+        pa.bar = c->status + 1;
+        pa.status = c->status;
+        return after_launch(c, launch_pair(pa, c->stream, true), "pair");
+      }
       // decode: two launches; each GEMV quantises its fp32 input itself and
       // the first warms L2 with the second's weights while it streams
       if ((rc = gemv_f32(c, w1, x, b, c->ws_f0, w2))) return rc;
@@ -1076,7 +1090,7 @@ static int host_call(mxq_context* c, int kind, uint64_t w1, uint64_t w2, size_t 
     c->launches += 2;
     const uint32_t st = hg->mapped ? *st_host : *c->status_host;
     if (st) {
-      cudaMemset(c->status, 0, sizeof(uint32_t));
+      cudaMemset(c->status, 0, 4 * sizeof(uint32_t));
       return fail(c, MXQ_ERR_TIMEOUT, "a device-side bounded wait gave up (status 0x%x)", st);
     }
     std::memcpy(y_host, c->pin_out, out_bytes);
@@ -1460,6 +1474,35 @@ int mxq_debug_gemm_stall(mxq_ctx c, mxq_weight w, const float* x, size_t b, floa
     ga.wait_ns = (uint64_t)wait_us * 1000ull;
     ga.withhold_x0 = 1;
     if ((rc = after_launch(c, launch_gemm(ga, c->stream, false), "gemm"))) return rc;
+    return mxq_synchronize(c);
+  })
+}
+
+int mxq_debug_pair_stall(mxq_ctx c, mxq_weight w1, mxq_weight w2, const float* x, float* y, uint32_t wait_us) {
+  MXQ_TRY({
+    if (int rc = check_ctx(c)) return rc;
+    if (int rc = check_weight(c, w1)) return rc;
+    if (int rc = check_weight(c, w2)) return rc;
+    if (!x || !y) return fail(c, MXQ_ERR_INVALID_ARGUMENT, "null pointer");
+    if (!aligned16(x)) return fail(c, MXQ_ERR_INVALID_ARGUMENT, "fp32 input must be 16-byte aligned (it is read in 16-byte vectors)");
+    if (wait_us == 0 || wait_us > 1000000u)
+      return fail(c, MXQ_ERR_INVALID_ARGUMENT, "debug stall: wait limit must be in [1, 1e6] microseconds");
+    if (!pair_supported(w1->v, w2->v))
+      return fail(c, MXQ_ERR_UNSUPPORTED, "debug pair stall: the one-kernel pair does not support these weights");
+    DeviceGuard g(c->device);
+    int rc;
+    if ((rc = ensure(c, c->ws_f0, c->ws_f0_bytes, (size_t)w1->v.N * 4, "workspace mid"))) return rc;
+    PairArgs pa{};
+    pa.w1 = w1->v;
+    pa.w2 = w2->v;
+    pa.x = x;
+    pa.y1 = c->ws_f0;
+    pa.y = y;
+    pa.bar = c->status + 1;
+    pa.status = c->status;
+    pa.wait_ns = (uint64_t)wait_us * 1000ull;
+    pa.withhold_arrive = 1;
+    if ((rc = after_launch(c, launch_pair(pa, c->stream, false), "pair"))) return rc;
     return mxq_synchronize(c);
   })
 }

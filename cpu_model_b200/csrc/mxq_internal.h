@@ -125,6 +125,25 @@ constexpr int kRgemvMaxBatch = 4;
 bool rgemv_supported(const WeightView& w, int B);
 cudaError_t launch_rgemv(const GemvArgs& a, cudaStream_t st, bool pdl);
 
+// Decode linear pair in one kernel (mxq_pair.cu): batch 1, fp32 x [w1.K] ->
+// y1 [w1.N] (also written out, fp32) -> y [w2.N]; bit-identical to two
+// weight-resident GEMV launches.  `bar` = two zeroed words of device memory
+// (grid barrier count and generation) owned by the caller's context.
+struct PairArgs {
+  WeightView w1, w2;
+  const float* x;
+  float* y1;
+  float* y;
+  uint32_t* bar;
+  uint32_t* status;
+  uint64_t wait_ns;   // barrier limit; 0 = kWaitLimitNs
+  // Test hook (mxq_debug_pair_stall): CTA 0 does not arrive at the grid
+  // barrier, so every CTA's wait runs out and the error path is exercised.
+  int withhold_arrive;
+};
+bool pair_supported(const WeightView& w1, const WeightView& w2);
+cudaError_t launch_pair(const PairArgs& a, cudaStream_t st, bool pdl);
+
 // MoE bookkeeping (mxq_moe.cu): per-expert route counts, slot offsets, the
 // token row gathered into each slot, the slot of each route; the weighted
 // combine of the k expert outputs per token.

@@ -249,6 +249,16 @@ MXQ_API int mxq_halting_step_host(mxq_ctx ctx, mxq_weight w_halt,
                                   float bias, mxq_halting_state* state_host,
                                   float* p_host, uint8_t* should_halt_host);
 
+/* Test hook, no counterpart in the reference: the one-kernel batch-1 pair of
+ * mxq_linear_pair with one CTA kept from arriving at its grid barrier and the
+ * barrier's wait limited to wait_us microseconds (1 .. 1e6): every CTA's wait
+ * runs out, the down projection is skipped, the timeout lands in the status
+ * word, and the call returns mxq_synchronize's status, MXQ_ERR_TIMEOUT, with
+ * the barrier reset so the context stays usable.  MXQ_ERR_UNSUPPORTED when
+ * the pair does not take the one-kernel path. */
+MXQ_API int mxq_debug_pair_stall(mxq_ctx ctx, mxq_weight w1, mxq_weight w2,
+                                 const float* x, float* y, uint32_t wait_us);
+
 /* ------------------------------------------------------------ routing --- */
 /* Top-k expert selection with the HashedRouter contract
  * (nn/tests/test_robustness.cpp:13-35: k > n_experts is an invalid
