@@ -59,6 +59,18 @@ SIGNATURES = {
     "mxq_debug_gemm_stall": [_vp, _vp, _vp, _sz, _vp, ctypes.c_uint32],
     "mxq_debug_pair_stall": [_vp, _vp, _vp, _vp, _vp, ctypes.c_uint32],
     "mxq_route_topk": [_vp, _vp, _sz, _sz, _sz, _vp, _vp],
+    "mxq_decoder_create": [_vp, _vp, ctypes.c_uint64, ctypes.POINTER(_vp)],
+    "mxq_decoder_destroy": [_vp],
+    "mxq_decoder_reset": [_vp],
+    "mxq_decoder_length": [_vp, ctypes.POINTER(_i)],
+    "mxq_decoder_prefill": [_vp, _vp, _sz, _sz, _vp],
+    "mxq_decoder_decode": [_vp, _vp, _sz, _vp],
+    "mxq_decoder_score": [_vp, _vp, _sz, _sz, _vp, _vp],
+    "mxq_decoder_weight": [_vp, _i, _i, ctypes.POINTER(_vp)],
+    "mxq_decoder_embedding": [_vp, _sz, _sz, _vp],
+    "mxq_decoder_set_trace": [_vp, _i],
+    "mxq_decoder_get_trace": [_vp, _i, _vp, _sz],
+    "mxq_weight_download": [_vp, _vp, _vp],
     "mxq_quantize_w": [_vp, _i, _vp, _sz, _sz, _vp, _vp, _vp],
     "mxq_weight_quantize": [_vp, _i, _sz, _sz, _vp, _i, ctypes.POINTER(_vp)],
     "mxq_halting_step_host": [_vp, _vp, _vp, _vp, _f, _vp, _vp, _vp],

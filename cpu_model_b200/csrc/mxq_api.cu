@@ -862,6 +862,37 @@ int mxq_weight_destroy(mxq_weight w) {
   return MXQ_OK;
 }
 
+int mxq_weight_download(mxq_weight w, void* data_host, uint8_t* scales_host) {
+  MXQ_TRY({
+    if (!w || !data_host || !scales_host) return fail(nullptr, MXQ_ERR_INVALID_ARGUMENT, "null pointer");
+    if (w->v.kt_ptr) return fail(w->ctx, MXQ_ERR_UNSUPPORTED, "weight_download: block-sparse weights are not supported");
+    DeviceGuard g(w->ctx->device);
+    const WeightView& v = w->v;
+    const int TB = v.fmt == 4 ? 32 : 64, KT = v.Kpad / kTileK;
+    const size_t tb = (size_t)v.Npad * v.Kpad / (v.fmt == 4 ? 2 : 1), sb = (size_t)v.Npad * v.Kpad / kBlock;
+    std::vector<uint8_t> td(tb), ts(sb);
+    cudaError_t e = cudaStreamSynchronize(w->ctx->stream);
+    if (e == cudaSuccess) e = cudaMemcpy(td.data(), v.data, tb, cudaMemcpyDeviceToHost);
+    if (e == cudaSuccess) e = cudaMemcpy(ts.data(), v.scales, sb, cudaMemcpyDeviceToHost);
+    if (e != cudaSuccess) return cuda_fail(w->ctx, e, "weight_download");
+    const size_t row_bytes = v.fmt == 4 ? (size_t)v.K / 2 : (size_t)v.K, nb = (size_t)v.K / kBlock;
+    uint8_t* dd = static_cast<uint8_t*>(data_host);
+    for (int n = 0; n < v.N; ++n)
+      for (int kt = 0; kt < KT; ++kt) {
+        const size_t src = (((size_t)(n / 128) * KT + kt) * 128 + (n % 128));
+        for (int j = 0; j < TB; ++j) {
+          const size_t byte = (size_t)kt * TB + j;
+          if (byte < row_bytes) dd[(size_t)n * row_bytes + byte] = td[src * TB + j];
+        }
+        for (int hh = 0; hh < 2; ++hh) {
+          const size_t b = (size_t)kt * 2 + hh;
+          if (b < nb) scales_host[(size_t)n * nb + b] = ts[src * 2 + hh];
+        }
+      }
+    return MXQ_OK;
+  })
+}
+
 int mxq_weight_shape(mxq_weight w, int* fmt, size_t* n, size_t* k) {
   if (!w) return fail(nullptr, MXQ_ERR_INVALID_ARGUMENT, "null weight handle");
   if (fmt) *fmt = w->v.fmt;
@@ -1727,6 +1758,15 @@ int mxq_gae_ring(mxq_ctx c, const float* rewards, const float* values, const uin
 }  // extern "C"
 
 namespace mxq {
+cudaStream_t ctx_stream(mxq_context* c) { return c->stream; }
+int ctx_fail(mxq_context* c, int code, const char* msg) { return fail(c, code, "%s", msg); }
+int ctx_cuda_fail(mxq_context* c, cudaError_t e, const char* what) { return cuda_fail(c, e, what); }
+void ctx_add_launches(mxq_context* c, uint64_t n) { c->launches += n; }
+uint64_t ctx_ws_gen(mxq_context* c) { return c->ws_gen; }
+uint64_t ctx_launches(mxq_context* c) { return c->launches; }
+void ctx_set_launches(mxq_context* c, uint64_t n) { c->launches = n; }
+const WeightView* weight_view(mxq_weight w) { return w ? &w->v : nullptr; }
+
 cudaError_t launch_scale_range(const uint8_t* scales, size_t count, uint32_t* out2, cudaStream_t st) {
   size_t ctas = (count + 255) / 256;
   if (ctas > 1024) ctas = 1024;

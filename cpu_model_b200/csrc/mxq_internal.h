@@ -144,6 +144,38 @@ struct PairArgs {
 bool pair_supported(const WeightView& w1, const WeightView& w2);
 cudaError_t launch_pair(const PairArgs& a, cudaStream_t st, bool pdl);
 
+// Context internals for the other host translation units (mxq_api.cu).
+cudaStream_t ctx_stream(mxq_context* c);
+int ctx_fail(mxq_context* c, int code, const char* msg);
+int ctx_cuda_fail(mxq_context* c, cudaError_t e, const char* what);
+void ctx_add_launches(mxq_context* c, uint64_t n);
+uint64_t ctx_ws_gen(mxq_context* c);
+uint64_t ctx_launches(mxq_context* c);
+void ctx_set_launches(mxq_context* c, uint64_t n);
+const WeightView* weight_view(mxq_weight w);
+
+// Dense decoder steps (mxq_decoder_kernels.cu).
+cudaError_t dk_embed(const int32_t* tok, const float* table, int R, int d, int vocab, float* h, cudaStream_t s);
+cudaError_t dk_rmsnorm(const float* x, const float* g, int R, int d, float eps, float* y, cudaStream_t s);
+cudaError_t dk_add(float* h, const float* y, size_t n, cudaStream_t s);
+cudaError_t dk_swiglu(const float* gu, int R, int F, float* act, cudaStream_t s);
+cudaError_t dk_rope_kv(float* qkv, int R, int T, int d, int H, int pos0, const int32_t* pos_dev, const float* cs,
+                       int max_ctx, __nv_bfloat16* kc, __nv_bfloat16* vc, cudaStream_t s);
+size_t dk_attn_prompt_smem();
+cudaError_t dk_attn_prompt(const float* qkv, int B, int T, int d, int H, int pos0, const __nv_bfloat16* kc,
+                           const __nv_bfloat16* vc, int max_ctx, float* att, cudaStream_t s);
+int dk_decode_chunks(int max_ctx);
+cudaError_t dk_attn_decode(const float* qkv, int B, int d, int H, const int32_t* pos_dev, const __nv_bfloat16* kc,
+                           const __nv_bfloat16* vc, int max_ctx, float* part, float* att, cudaStream_t s);
+cudaError_t dk_pos_advance(int32_t* pos, int by, cudaStream_t s);
+cudaError_t dk_logprob(const float* logits, int R, int ld, int V, const int32_t* target, float* logp, cudaStream_t s);
+cudaError_t dk_column(const float* x, int R, int ld, int col, float* out, cudaStream_t s);
+cudaError_t dk_last_rows(const float* x, int B, int T, int n, float* y, cudaStream_t s);
+cudaError_t dk_synth_weight(uint8_t* data, size_t data_bytes, uint8_t* scales, size_t nscales, int fmt, int emin,
+                            int emax, uint64_t seed, cudaStream_t s);
+cudaError_t dk_synth_normal(float* out, size_t n, uint64_t seed, float sd, cudaStream_t s);
+cudaError_t dk_fill(float* out, size_t n, float v, cudaStream_t s);
+
 // MoE bookkeeping (mxq_moe.cu): per-expert route counts, slot offsets, the
 // token row gathered into each slot, the slot of each route; the weighted
 // combine of the k expert outputs per token.

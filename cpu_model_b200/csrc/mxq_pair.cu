@@ -137,51 +137,64 @@ __device__ __forceinline__ void stage_scales(const WeightView& w, int KT, int n0
 // This warp's K-slice of an fp32 row, MX-quantised exactly as quantize_kernel
 // does, into act (int8, int4 layouts store each 8-group even elements first)
 // and fa (block scales as floats).  8-lane groups share a 32-element block.
-template <int WFMT, bool CG>
+// The loads of NB rounds are issued before any of them is used, so a slice
+// costs one memory round trip per NB rounds, not one per round.
+template <int WFMT, bool CG, int NB>
 __device__ __forceinline__ void quant_slice(const float* x, int K, int kt0, int nblk, int8_t* act, float* fa,
                                             int lane) {
   const int kb = K / kBlock;
-  for (int c = lane; c < nblk * 8; c += 32) {
-    const int bl = c / 8, p4 = c % 8;
-    const int b = kt0 * 2 + bl;
-    const bool live = b < kb;
-    float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-    if (live) {
-      const float4* src = reinterpret_cast<const float4*>(x + b * kBlock + p4 * 4);
-      v = CG ? __ldcg(src) : *src;
-    }
-    const float e4[4] = {v.x, v.y, v.z, v.w};
-    float m = 0.0f;
-    bool nf = false;
+  for (int base = lane; base < nblk * 8; base += 32 * NB) {
+    float4 vv[NB];
 #pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      const float av = fabsf(e4[e]);
-      nf |= !(av <= 3.402823466e38f);
-      m = fmaxf(m, nf ? 0.0f : av);
+    for (int u = 0; u < NB; ++u) {
+      const int c = base + 32 * u;
+      const int b = kt0 * 2 + c / 8;
+      vv[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (c < nblk * 8 && b < kb) {
+        const float4* src = reinterpret_cast<const float4*>(x + b * kBlock + (c % 8) * 4);
+        vv[u] = CG ? __ldcg(src) : *src;
+      }
     }
 #pragma unroll
-    for (int o = 4; o > 0; o >>= 1) {
-      m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-      nf |= __shfl_xor_sync(0xffffffffu, (int)nf, o) != 0;
-    }
-    uint32_t s8 = 0;
-    int e = 0;
-    if (live) {
-      if (nf) s8 = 255;
-      else if (m != 0.0f) { e = e8m0_exponent<127>(m); s8 = (uint32_t)(e + 127); }
-    }
-    uint32_t packed = 0;
+    for (int u = 0; u < NB; ++u) {
+      const int c = base + 32 * u;          // warp-uniform: nblk * 8 is a multiple of 32
+      if (c - lane >= nblk * 8) break;
+      const int bl = c / 8, p4 = c % 8;
+      const int b = kt0 * 2 + bl;
+      const bool live = b < kb;
+      const float e4[4] = {vv[u].x, vv[u].y, vv[u].z, vv[u].w};
+      float m = 0.0f;
+      bool nf = false;
 #pragma unroll
-    for (int k = 0; k < 4; ++k) {
-      const int q = (s8 != 0 && s8 != 255) ? quant_value(e4[k], e) : 0;
-      packed |= ((uint32_t)q & 0xFFu) << (8 * k);
+      for (int e = 0; e < 4; ++e) {
+        const float av = fabsf(e4[e]);
+        nf |= !(av <= 3.402823466e38f);
+        m = fmaxf(m, nf ? 0.0f : av);
+      }
+#pragma unroll
+      for (int o = 4; o > 0; o >>= 1) {
+        m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+        nf |= __shfl_xor_sync(0xffffffffu, (int)nf, o) != 0;
+      }
+      uint32_t s8 = 0;
+      int e = 0;
+      if (live) {
+        if (nf) s8 = 255;
+        else if (m != 0.0f) { e = e8m0_exponent<127>(m); s8 = (uint32_t)(e + 127); }
+      }
+      uint32_t packed = 0;
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const int q = (s8 != 0 && s8 != 255) ? quant_value(e4[k], e) : 0;
+        packed |= ((uint32_t)q & 0xFFu) << (8 * k);
+      }
+      if (WFMT == 4) {
+        const uint32_t other = __shfl_xor_sync(0xffffffffu, packed, 1);
+        packed = (p4 & 1) ? __byte_perm(other, packed, 0x7531) : __byte_perm(packed, other, 0x6420);
+      }
+      *reinterpret_cast<uint32_t*>(act + bl * kBlock + p4 * 4) = packed;
+      if (p4 == 0) fa[bl] = live ? e8m0_to_float(s8) : 0.0f;
     }
-    if (WFMT == 4) {
-      const uint32_t other = __shfl_xor_sync(0xffffffffu, packed, 1);
-      packed = (p4 & 1) ? __byte_perm(other, packed, 0x7531) : __byte_perm(packed, other, 0x6420);
-    }
-    *reinterpret_cast<uint32_t*>(act + bl * kBlock + p4 * 4) = packed;
-    if (p4 == 0) fa[bl] = live ? e8m0_to_float(s8) : 0.0f;
   }
 }
 
@@ -338,7 +351,7 @@ __global__ void __launch_bounds__(kPThreads, 1) pair_kernel(PairArgs a) {
   // ---- 2. up: quantise x's K-slice, dot products from registers
   const int a_nblk = g1.kts * 2;
   float* fa = reinterpret_cast<float*>(act + g1.kts * kTileK);
-  quant_slice<WFMT, false>(a.x, a.w1.K, a_kt0, a_nblk, act, fa, lane);
+  quant_slice<WFMT, false, 2>(a.x, a.w1.K, a_kt0, a_nblk, act, fa, lane);
   asm volatile("cp.async.wait_group 1;" ::: "memory");   // every thread's scale copies have landed
   __syncthreads();
   {
@@ -392,7 +405,7 @@ __global__ void __launch_bounds__(kPThreads, 1) pair_kernel(PairArgs a) {
   if (ok) {
     const int b_nblk = g2.kts * 2;
     float* fb = reinterpret_cast<float*>(act + g2.kts * kTileK);
-    quant_slice<WFMT, true>(a.y1, a.w2.K, b_kt0, b_nblk, act, fb, lane);
+    quant_slice<WFMT, true, 8>(a.y1, a.w2.K, b_kt0, b_nblk, act, fb, lane);
     __syncwarp();
     const int8_t* xrow = act + kto * kTileK + (WFMT == 4 ? sub * 32 : sub * 16);
     const float* frow = fb + kto * 2 + bh;

@@ -538,3 +538,120 @@ def ppo_rollout_forward(states, actions, w_proj, w_policy, w_value=None, ctx=Non
         values = mx_linear(latent, w_value, ctx)[:, 0]
     lp, alp, ent = policy_head(logits, actions, ctx)
     return lp, alp, ent, values
+
+
+# ------------------------------------------------------------------ decoder ---
+DEC_QKV, DEC_O, DEC_GATE_UP, DEC_DOWN, DEC_LM_HEAD = 0, 1, 2, 3, 4
+TRACE = {"in": 0, "norm1": 1, "qkv": 2, "rope": 3, "att": 4, "h1": 5, "norm2": 6, "gu": 7, "out": 8}
+
+
+class DecoderConfig(ctypes.Structure):
+    """mxq_decoder_config (include/mxq.h)."""
+    _fields_ = [("n_layers", ctypes.c_int), ("d_model", ctypes.c_int), ("n_heads", ctypes.c_int),
+                ("ffn", ctypes.c_int), ("vocab", ctypes.c_int), ("fmt", ctypes.c_int), ("max_batch", ctypes.c_int),
+                ("max_ctx", ctypes.c_int), ("max_rows", ctypes.c_int), ("value_head", ctypes.c_int),
+                ("rope_theta", ctypes.c_float), ("norm_eps", ctypes.c_float)]
+
+
+class Decoder:
+    """The dense decoder on the MX linears (mxq_decoder_*): prefill a prompt,
+    decode one token per sequence per step (CUDA-graph replayed), or score
+    whole sequences (per-token log-probs and values, the rollout forward).
+    Weights are synthetic, generated from `seed` on the device."""
+
+    def __init__(self, n_layers, d_model, n_heads, ffn, vocab, fmt=FMT_INT4, max_batch=1, max_ctx=2048,
+                 max_rows=8192, value_head=False, rope_theta=10000.0, norm_eps=1e-5, seed=0, ctx=None):
+        self.ctx = ctx or context()
+        self.cfg = DecoderConfig(n_layers, d_model, n_heads, ffn, vocab, fmt, max_batch, max_ctx, max_rows,
+                                 1 if value_head else 0, rope_theta, norm_eps)
+        h = ctypes.c_void_p()
+        self.ctx._bind()
+        check(self.ctx.lib.mxq_decoder_create(self.ctx.h, ctypes.byref(self.cfg), seed, ctypes.byref(h)), self.ctx.h)
+        self.h = h
+
+    def _tokens(self, tokens):
+        if not isinstance(tokens, torch.Tensor) or tokens.dtype != torch.int32 or not tokens.is_contiguous():
+            raise ValueError("tokens must be a contiguous int32 tensor")
+        return tokens
+
+    def prefill(self, tokens):
+        """tokens [B][T] -> logits of the last position [B][vocab]."""
+        tokens = self._tokens(tokens)
+        b, t = tokens.shape
+        logits = torch.empty((b, self.cfg.vocab), dtype=torch.float32, device="cuda")
+        self.ctx._bind()
+        check(self.ctx.lib.mxq_decoder_prefill(self.h, _ptr(tokens), b, t, _ptr(logits)), self.ctx.h)
+        return logits
+
+    def decode(self, tokens):
+        """tokens [B] (one per sequence) -> logits [B][vocab]."""
+        tokens = self._tokens(tokens)
+        b = tokens.numel()
+        logits = torch.empty((b, self.cfg.vocab), dtype=torch.float32, device="cuda")
+        self.ctx._bind()
+        check(self.ctx.lib.mxq_decoder_decode(self.h, _ptr(tokens), b, _ptr(logits)), self.ctx.h)
+        return logits
+
+    def score(self, tokens):
+        """tokens [B][T] -> (logp [B][T-1], values [B][T] or None)."""
+        tokens = self._tokens(tokens)
+        b, t = tokens.shape
+        logp = torch.empty((b, t - 1), dtype=torch.float32, device="cuda")
+        values = torch.empty((b, t), dtype=torch.float32, device="cuda") if self.cfg.value_head else None
+        self.ctx._bind()
+        check(self.ctx.lib.mxq_decoder_score(self.h, _ptr(tokens), b, t, _ptr(logp), _ptr(values)), self.ctx.h)
+        return logp, values
+
+    def reset(self):
+        check(self.ctx.lib.mxq_decoder_reset(self.h), self.ctx.h)
+
+    def length(self):
+        v = ctypes.c_int()
+        check(self.ctx.lib.mxq_decoder_length(self.h, ctypes.byref(v)), self.ctx.h)
+        return v.value
+
+    def weight_handle(self, layer, which):
+        w = ctypes.c_void_p()
+        check(self.ctx.lib.mxq_decoder_weight(self.h, layer, which, ctypes.byref(w)), self.ctx.h)
+        return w
+
+    def download(self, layer, which):
+        """(data, scales) of one weight in the MXINT8Tensor layout (numpy)."""
+        import numpy as np
+        w = self.weight_handle(layer, which)
+        fmt, n, k = ctypes.c_int(), ctypes.c_size_t(), ctypes.c_size_t()
+        check(self.ctx.lib.mxq_weight_shape(w, ctypes.byref(fmt), ctypes.byref(n), ctypes.byref(k)), self.ctx.h)
+        data = np.empty((n.value, k.value // 2), np.uint8) if fmt.value == FMT_INT4 else \
+            np.empty((n.value, k.value), np.int8)
+        scales = np.empty((n.value, k.value // 32), np.uint8)
+        check(self.ctx.lib.mxq_weight_download(w, data.ctypes.data_as(ctypes.c_void_p),
+                                               scales.ctypes.data_as(ctypes.c_void_p)), self.ctx.h)
+        return data, scales
+
+    def embedding_rows(self, row0, nrows):
+        import numpy as np
+        out = np.empty((nrows, self.cfg.d_model), np.float32)
+        check(self.ctx.lib.mxq_decoder_embedding(self.h, row0, nrows, out.ctypes.data_as(ctypes.c_void_p)),
+              self.ctx.h)
+        return out
+
+    def set_trace(self, layer):
+        check(self.ctx.lib.mxq_decoder_set_trace(self.h, layer), self.ctx.h)
+
+    def get_trace(self, name, shape):
+        import numpy as np
+        out = np.empty(shape, np.float32)
+        check(self.ctx.lib.mxq_decoder_get_trace(self.h, TRACE[name], out.ctypes.data_as(ctypes.c_void_p),
+                                                 out.size), self.ctx.h)
+        return out
+
+    def close(self):
+        if getattr(self, "h", None):
+            self.ctx.lib.mxq_decoder_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass

@@ -343,6 +343,96 @@ MXQ_API int mxq_gae_ring(mxq_ctx ctx, const float* rewards, const float* values,
                          size_t e, float gamma, float lambda, float* adv,
                          float* ret);
 
+/* ------------------------------------------------------------ decoder --- */
+/* A dense decoder assembled from the MX linears -- the execution graph the
+ * hot path drops into (the caller of nca::linalg::mx_gemv in a model's
+ * forward; the 16-row expert slicing of training/fidelity_test.cpp:57-62
+ * and the rollout forward of training/ppo_trainer.cpp:57-63 are its
+ * reference-side counterparts).  No reference counterpart exists for the
+ * decoder itself: the reference's model code is not a transformer.  Per
+ * layer: RMSNorm (nn/core/normalization.cpp:16-47) -> QKV linear -> rotary
+ * embedding, K/V into a bf16 cache -> causal softmax attention -> O linear ->
+ * residual -> RMSNorm -> gate|up linear -> SwiGLU -> down linear -> residual;
+ * then RMSNorm and the vocabulary head.  Head dim is 128.  Weights are MX
+ * (int4 exponents uniform in [-8, -3], int8 in [-10, -4]) generated from
+ * `seed` on the device; the embedding table fp32 ~ N(0, 1); RMSNorm weights
+ * 1.  All sequences of a batch share one position. */
+typedef struct mxq_decoder_config {
+  int n_layers, d_model, n_heads, ffn, vocab;
+  int fmt;          /* MXQ_FMT_INT4 or MXQ_FMT_INT8 */
+  int max_batch;    /* sequences (K/V cache slots) */
+  int max_ctx;      /* positions per sequence */
+  int max_rows;     /* token rows per pass (prompt chunking), >= max_batch */
+  int value_head;   /* 1: one more head row after the vocabulary (a value) */
+  float rope_theta; /* e.g. 10000 */
+  float norm_eps;   /* e.g. 1e-5 */
+} mxq_decoder_config;
+typedef struct mxq_decoder_s* mxq_decoder;
+
+#define MXQ_DEC_QKV 0     /* [3d][d]: q rows, then k, then v */
+#define MXQ_DEC_O 1       /* [d][d] */
+#define MXQ_DEC_GATE_UP 2 /* [2F][d]: gate rows, then up */
+#define MXQ_DEC_DOWN 3    /* [d][F] */
+#define MXQ_DEC_LM_HEAD 4 /* [vocab (+1)][d] */
+
+/* Trace points of one layer (mxq_decoder_set_trace): the layer input, the
+ * first RMSNorm, QKV before and after the rotary embedding, the attention
+ * output, the residual after attention, the second RMSNorm, gate|up, the
+ * layer output.  Layer n_layers records its input (the last layer's output)
+ * as MXQ_TRACE_IN. */
+#define MXQ_TRACE_IN 0
+#define MXQ_TRACE_NORM1 1
+#define MXQ_TRACE_QKV 2
+#define MXQ_TRACE_ROPE 3
+#define MXQ_TRACE_ATT 4
+#define MXQ_TRACE_H1 5
+#define MXQ_TRACE_NORM2 6
+#define MXQ_TRACE_GU 7
+#define MXQ_TRACE_OUT 8
+#define MXQ_TRACE_COUNT 9
+
+MXQ_API int mxq_decoder_create(mxq_ctx ctx, const mxq_decoder_config* cfg,
+                               uint64_t seed, mxq_decoder* out);
+MXQ_API int mxq_decoder_destroy(mxq_decoder dec);
+/* Forget every cached position. */
+MXQ_API int mxq_decoder_reset(mxq_decoder dec);
+MXQ_API int mxq_decoder_length(mxq_decoder dec, int* len);
+/* Prompt tokens int32 [b][t] (host or device) from position 0; fills the
+ * cache and writes the last position's logits fp32 [b][vocab] (device or
+ * host; may be null). */
+MXQ_API int mxq_decoder_prefill(mxq_decoder dec, const int32_t* tokens,
+                                size_t b, size_t t, float* logits);
+/* One new token per sequence at the current position; logits [b][vocab].
+ * The first call for a batch size runs plain launches and records the step
+ * as a CUDA graph; later calls replay it. */
+MXQ_API int mxq_decoder_decode(mxq_decoder dec, const int32_t* tokens,
+                               size_t b, float* logits);
+/* Teacher-forced scoring (the PPO rollout forward): tokens [b][t] ->
+ * logp [b][t-1] = log p(token i+1 | tokens 0..i) and, with a value head,
+ * values [b][t] (may be null).  Sequences go through max_rows / t at a time;
+ * the cache is reset afterwards. */
+MXQ_API int mxq_decoder_score(mxq_decoder dec, const int32_t* tokens, size_t b,
+                              size_t t, float* logp, float* values);
+/* The decoder's weight handles (MXQ_DEC_*; layer ignored for the head). */
+MXQ_API int mxq_decoder_weight(mxq_decoder dec, int layer, int which,
+                               mxq_weight* out);
+/* Rows [row0, row0 + nrows) of the embedding table fp32 [vocab][d] into
+ * `out` (device or host memory). */
+MXQ_API int mxq_decoder_embedding(mxq_decoder dec, size_t row0, size_t nrows,
+                                  float* out);
+/* Record the trace points of `layer` (-1: off) on the following passes;
+ * mxq_decoder_get_trace copies `count` floats of trace `id` (the last pass's
+ * rows) to device or host memory. */
+MXQ_API int mxq_decoder_set_trace(mxq_decoder dec, int layer);
+MXQ_API int mxq_decoder_get_trace(mxq_decoder dec, int id, float* out,
+                                  size_t count);
+
+/* The MX bytes of a dense weight back in the MXINT8Tensor layout: data int8
+ * [N][K] or packed int4 [N][K/2], scales [N][K/32] (host memory).  The
+ * inverse of mxq_weight_create (for serialisation and checking). */
+MXQ_API int mxq_weight_download(mxq_weight w, void* data_host,
+                                uint8_t* scales_host);
+
 #ifdef __cplusplus
 }
 #endif

@@ -312,3 +312,70 @@ def baseline_gemv(fmt, xq, xs, w, ws, wsums, n, k, threads=0):
 
 def max_threads():
     return lib().mxb_max_threads()
+
+
+# ----------------------------------------------- dense decoder (numpy) ---
+# The steps around the MX linears in cpu_model_b200's dense decoder, stated
+# in float64 (the exactly rounded references the GPU's fp32 steps are held
+# to).  The reference has no transformer; RMSNorm follows
+# nn/core/normalization.cpp:16-47 (out = in * (1 / sqrt(sum(in^2) / n + eps))
+# * weight).
+def rmsnorm(x, g, eps):
+    x = np.asarray(x, np.float64)
+    inv = 1.0 / np.sqrt((x * x).sum(-1, keepdims=True) / x.shape[-1] + eps)
+    return (x * inv * np.asarray(g, np.float64)).astype(np.float32)
+
+
+def rope_table(max_ctx, theta, hd=128):
+    """cos/sin [max_ctx][hd/2] computed in double, rounded once (the table
+    the library builds on the host)."""
+    j = np.arange(hd // 2, dtype=np.float64)
+    p = np.arange(max_ctx, dtype=np.float64)[:, None]
+    ang = p * np.power(float(theta), -2.0 * j / hd)[None, :]
+    return np.cos(ang).astype(np.float32), np.sin(ang).astype(np.float32)
+
+
+def rope_rotate(x, pos, cos, sin):
+    """x [..., n_heads, hd] float32 at positions pos [...] -> rotated, with
+    the GPU's float32 operations (x1 c - x2 s, x2 c + x1 s)."""
+    half = x.shape[-1] // 2
+    c = cos[pos][..., None, :]
+    s = sin[pos][..., None, :]
+    x1, x2 = x[..., :half], x[..., half:]
+    return np.concatenate([x1 * c - x2 * s, x2 * c + x1 * s], axis=-1).astype(np.float32)
+
+
+def bf16_round(x):
+    """float32 -> nearest bfloat16 (ties to even), returned as float32."""
+    u = np.ascontiguousarray(x, np.float32).view(np.uint32).astype(np.uint64)
+    r = ((u + 0x7FFF + ((u >> 16) & 1)) >> 16) << 16
+    return r.astype(np.uint32).view(np.float32)
+
+
+def attention(q, k, v, qpos):
+    """q [Tq][H][hd] at positions qpos [Tq]; k, v [Tk][H][hd] at positions
+    0..Tk-1; causal softmax(q k^T / sqrt(hd)) v in float64 -> [Tq][H*hd]."""
+    q = np.asarray(q, np.float64)
+    k = np.asarray(k, np.float64)
+    v = np.asarray(v, np.float64)
+    hd = q.shape[-1]
+    s = np.einsum("qhd,khd->hqk", q, k) / np.sqrt(hd)
+    mask = np.arange(k.shape[0])[None, :] > np.asarray(qpos)[:, None]
+    s = np.where(mask[None], -np.inf, s)
+    s -= s.max(-1, keepdims=True)
+    p = np.exp(s)
+    p /= p.sum(-1, keepdims=True)
+    o = np.einsum("hqk,khd->qhd", p, v)
+    return o.reshape(q.shape[0], -1)
+
+
+def silu_mul(g, u):
+    g = np.asarray(g, np.float64)
+    return g / (1.0 + np.exp(-g)) * np.asarray(u, np.float64)
+
+
+def log_softmax_at(logits, target):
+    x = np.asarray(logits, np.float64)
+    m = x.max(-1, keepdims=True)
+    lse = m[:, 0] + np.log(np.exp(x - m).sum(-1))
+    return x[np.arange(x.shape[0]), target] - lse
