@@ -1759,6 +1759,7 @@ int mxq_gae_ring(mxq_ctx c, const float* rewards, const float* values, const uin
 
 namespace mxq {
 cudaStream_t ctx_stream(mxq_context* c) { return c->stream; }
+void ctx_set_stream_raw(mxq_context* c, cudaStream_t s) { c->stream = s; }
 int ctx_fail(mxq_context* c, int code, const char* msg) { return fail(c, code, "%s", msg); }
 int ctx_cuda_fail(mxq_context* c, cudaError_t e, const char* what) { return cuda_fail(c, e, what); }
 void ctx_add_launches(mxq_context* c, uint64_t n) { c->launches += n; }

@@ -50,6 +50,10 @@ struct mxq_decoder_s {
     cudaGraphExec_t exec;
   };
   std::vector<StepGraph> graphs;
+  // decode steps run on a private stream (capturable even when the caller's
+  // is the legacy default stream), ordered after and before the caller's
+  cudaStream_t dstream = nullptr;
+  cudaEvent_t ev_in = nullptr, ev_out = nullptr;
 };
 
 namespace {
@@ -198,6 +202,9 @@ int mxq_decoder_destroy(mxq_decoder D) {
     if (t) cudaFree(t);
   for (auto& g : D->graphs)
     if (g.exec) cudaGraphExecDestroy(g.exec);
+  if (D->dstream) cudaStreamSynchronize(D->dstream), cudaStreamDestroy(D->dstream);
+  if (D->ev_in) cudaEventDestroy(D->ev_in);
+  if (D->ev_out) cudaEventDestroy(D->ev_out);
   delete D;
   return MXQ_OK;
 }
@@ -280,6 +287,9 @@ int mxq_decoder_create(mxq_ctx c, const mxq_decoder_config* cfg, uint64_t seed, 
     if (e == cudaSuccess) e = dalloc(D->part, (size_t)D->Bmax * D->H * D->nch * (128 + 2));
     if (e == cudaSuccess) e = dalloc(D->tok, R + 1);
     if (e == cudaSuccess) e = cudaMemsetAsync(D->tok, 0, (R + 1) * 4, st);
+    if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&D->dstream, cudaStreamNonBlocking);
+    if (e == cudaSuccess) e = cudaEventCreateWithFlags(&D->ev_in, cudaEventDisableTiming);
+    if (e == cudaSuccess) e = cudaEventCreateWithFlags(&D->ev_out, cudaEventDisableTiming);
     if (e == cudaSuccess) e = cudaStreamSynchronize(st);
     if (e != cudaSuccess) return bail(ctx_cuda_fail(c, e, "decoder buffers"));
     *out = D;
@@ -336,9 +346,25 @@ int mxq_decoder_decode(mxq_decoder D, const int32_t* tokens, size_t b, float* lo
     if (b == 0 || (int)b > D->Bmax) return dfail(D, MXQ_ERR_INVALID_ARGUMENT, "decode: batch in [1, max_batch]");
     if (D->len >= D->Cmax) return dfail(D, MXQ_ERR_INVALID_ARGUMENT, "decode: the context is full (max_ctx)");
     mxq_context* c = D->c;
-    cudaStream_t st = ctx_stream(c);
+    const cudaStream_t user = ctx_stream(c);
+    // the step runs on the decoder's stream, after the caller's queued work
+    cudaError_t e = cudaEventRecord(D->ev_in, user);
+    if (e == cudaSuccess) e = cudaStreamWaitEvent(D->dstream, D->ev_in, 0);
+    if (e != cudaSuccess) return ctx_cuda_fail(c, e, "decode ordering");
+    // on every exit: the caller's stream waits for the step, and gets its
+    // stream back
+    struct Swap {
+      mxq_decoder_s* D;
+      cudaStream_t user;
+      ~Swap() {
+        if (cudaEventRecord(D->ev_out, D->dstream) == cudaSuccess) cudaStreamWaitEvent(user, D->ev_out, 0);
+        ctx_set_stream_raw(D->c, user);
+      }
+    } swap{D, user};
+    ctx_set_stream_raw(c, D->dstream);
+    cudaStream_t st = D->dstream;
     const int B = (int)b;
-    cudaError_t e = cudaMemcpyAsync(D->tok, tokens, (size_t)B * 4, cudaMemcpyDefault, st);
+    e = cudaMemcpyAsync(D->tok, tokens, (size_t)B * 4, cudaMemcpyDefault, st);
     if (e != cudaSuccess) return ctx_cuda_fail(c, e, "decode tokens");
     int rc;
     mxq_decoder_s::StepGraph* g = nullptr;

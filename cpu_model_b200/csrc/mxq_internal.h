@@ -146,6 +146,7 @@ cudaError_t launch_pair(const PairArgs& a, cudaStream_t st, bool pdl);
 
 // Context internals for the other host translation units (mxq_api.cu).
 cudaStream_t ctx_stream(mxq_context* c);
+void ctx_set_stream_raw(mxq_context* c, cudaStream_t s);
 int ctx_fail(mxq_context* c, int code, const char* msg);
 int ctx_cuda_fail(mxq_context* c, cudaError_t e, const char* what);
 void ctx_add_launches(mxq_context* c, uint64_t n);
