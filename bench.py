@@ -352,6 +352,126 @@ def time_cfg1(ctx, dev, args, world, max_over_ranks, barrier, peaks, rank, captu
     return out
 
 
+# 7B dense decoder: 32 layers, d 4096, 32 heads x 128, SwiGLU 11008, vocab
+# 32000, MX-int4 weights; 2048-token prompts of uniform ids, then 256 decode
+# steps, batch 1 / 8 / 32
+DEC7B = {"n_layers": 32, "d_model": 4096, "n_heads": 32, "ffn": 11008, "vocab": 32000, "prompt": 2048,
+         "decode": 256, "batches": [1, 8, 32]}
+# 1B rollout policy: 16 layers, d 2048, 16 heads, FFN 5632, vocab 32000,
+# MX-int8, value head; 256 rollouts x 512 tokens, GAE gamma 0.99 lambda 0.95
+PPO1B = {"n_layers": 16, "d_model": 2048, "n_heads": 16, "ffn": 5632, "vocab": 32000, "rollouts": 256,
+         "tokens": 512}
+
+
+def decoder_weight_bytes(cfg, fmt):
+    """MX bytes of every linear of the decoder (data + E8M0 scales)."""
+    d, F, L, V = cfg["d_model"], cfg["ffn"], cfg["n_layers"], cfg["vocab"]
+    per = 1.0 / (2 if fmt == 4 else 1) + 1.0 / 32
+    return (L * (3 * d * d + d * d + 2 * F * d + d * F) + V * d) * per
+
+
+def time_decoder_7b(ctx, dev, args, world, max_over_ranks, barrier, peaks, rank):
+    """The 7B decoder: per batch size, the prompt (chunked prefill) timed as
+    one call, then 256 one-token steps (each a replayed CUDA graph) timed
+    with CUDA events around the loop.  Decode tokens are uniform ids drawn
+    ahead of time (no sampling step).  Roofline: the weights (3.6 GB MX-int4)
+    plus the bf16 K/V read by every step, against the HBM peak."""
+    import torch
+    from cpu_model_b200 import mx
+    c = DEC7B
+    D = mx.Decoder(c["n_layers"], c["d_model"], c["n_heads"], c["ffn"], c["vocab"], fmt=4,
+                   max_batch=max(c["batches"]), max_ctx=c["prompt"] + c["decode"], max_rows=8192, seed=3, ctx=ctx)
+    g = torch.Generator(device=dev)
+    out = {"config": dict({k: v for k, v in c.items() if k != "batches"}, weights="mx-int4, E8M0 exp [-8,-3]",
+                          kv_cache="bf16", data="uniform-random token ids"), "api": "mxq_decoder_prefill/decode",
+           "batches": {}}
+    wbytes = decoder_weight_bytes(c, 4)
+    for b in c["batches"]:
+        g.manual_seed(100 + b)
+        prompt = torch.randint(0, c["vocab"], (b, c["prompt"]), dtype=torch.int32, device=dev, generator=g)
+        steps = torch.randint(0, c["vocab"], (c["decode"], b), dtype=torch.int32, device=dev, generator=g)
+        D.reset()
+        D.prefill(prompt)                                  # warm-up (workspaces, graphs)
+        for i in range(3):
+            D.decode(steps[i].contiguous())
+        torch.cuda.synchronize()
+        D.reset()
+        barrier()
+        e0, e1, e2 = (torch.cuda.Event(enable_timing=True) for _ in range(3))
+        e0.record()
+        D.prefill(prompt)
+        e1.record()
+        for i in range(c["decode"]):
+            D.decode(steps[i])
+        e2.record()
+        torch.cuda.synchronize()
+        pre_ms = max_over_ranks(e0.elapsed_time(e1))
+        dec_ms = max_over_ranks(e1.elapsed_time(e2))
+        step_ms = dec_ms / c["decode"]
+        avg_ctx = c["prompt"] + (c["decode"] + 1) / 2.0
+        kv = b * c["n_layers"] * 2 * avg_ctx * c["d_model"] * 2
+        gbs = (wbytes + kv) / (step_ms / 1e3) / 1e9
+        out["batches"][str(b)] = {
+            "decode_tokens_per_s": world * b * c["decode"] / (dec_ms / 1e3), "decode_ms_per_step": step_ms,
+            "prefill_tokens_per_s": world * b * c["prompt"] / (pre_ms / 1e3), "prefill_ms": pre_ms,
+            "roofline": {"bound": "hbm", "achieved": gbs, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                         "frac": gbs / peaks["hbm_gbs"], "bytes_per_step": wbytes + kv,
+                         "bytes": "MX weights %.2f GB + bf16 K/V %.2f GB (mean context %.0f)" % (
+                             wbytes / 1e9, kv / 1e9, avg_ctx)}}
+    D.close()
+    return out
+
+
+def time_ppo_1b(ctx, dev, args, world, max_over_ranks, barrier, peaks, rank):
+    """The 1B MX-int8 rollout policy: 256 rollouts x 512 tokens scored
+    (per-token log-probs of the next token, a value per token), then GAE over
+    the [512][256] trajectory with rewards ~ N(0, 1) at each rollout's last
+    token (done there); data parallel (each rank its own batch)."""
+    import torch
+    from cpu_model_b200 import mx
+    c = PPO1B
+    D = mx.Decoder(c["n_layers"], c["d_model"], c["n_heads"], c["ffn"], c["vocab"], fmt=8, max_batch=16,
+                   max_ctx=c["tokens"], max_rows=8192, value_head=True, seed=4, ctx=ctx)
+    g = torch.Generator(device=dev)
+    g.manual_seed(500 + rank)
+    R, T = c["rollouts"], c["tokens"]
+    tok = torch.randint(0, c["vocab"], (R, T), dtype=torch.int32, device=dev, generator=g)
+    rewards = torch.zeros((T, R), device=dev)
+    rewards[-1] = torch.randn(R, generator=g, device=dev)
+    dones = torch.zeros((T, R), dtype=torch.uint8, device=dev)
+    dones[-1] = 1
+    nv = torch.zeros(R, device=dev)
+
+    def step():
+        logp, values = D.score(tok)
+        return mx.fused_compute_gae(rewards, values.t().contiguous(), dones, nv, 0.99, 0.95, ctx)
+
+    step()
+    torch.cuda.synchronize()
+    barrier()
+    n = 2
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(n):
+        step()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = max_over_ranks(e0.elapsed_time(e1) / n)
+    d, F, L, V = c["d_model"], c["ffn"], c["n_layers"], c["vocab"]
+    lin_flops = 2.0 * R * T * (L * (4 * d * d + 3 * d * F) + (V + 1) * d)
+    att_flops = 4.0 * R * L * d * T * T / 2
+    tf = (lin_flops + att_flops) / (ms / 1e3) / 1e12
+    D.close()
+    return {"tokens_per_s": world * R * T / (ms / 1e3), "ms_per_batch": ms, "batches": n,
+            "tflops": tf, "linear_tflop_per_batch": lin_flops / 1e12, "attention_tflop_per_batch": att_flops / 1e12,
+            "roofline": {"bound": "tensor", "achieved": tf, "unit": "TFLOP/s", "peak": peaks["bf16_tflops_sustained"],
+                         "frac": tf / peaks["bf16_tflops_sustained"], "frac_of_int8_spec": tf / INT8_SPEC_TOPS,
+                         "peak_src": peaks["src"] + " bf16_tflops_sustained"},
+            "config": dict(c, weights="mx-int8, E8M0 exp [-10,-4]", value_head=True, gae="gamma 0.99, lambda 0.95",
+                           data="uniform-random token ids, rewards N(0,1) at rollout ends"),
+            "api": "mxq_decoder_score + mxq_gae"}
+
+
 def time_moe(ctx, dev, args, world, max_over_ranks, barrier, peaks, rank):
     """The block-sparse MoE layer (mxq_moe_swiglu) at its full size: whole
     layer calls timed with CUDA events (each call reads the per-expert token
@@ -761,6 +881,12 @@ def run_ours(args):
     ppo = None
     if not args.no_ppo:
         ppo = time_ppo(ctx, dev, args, world, max_over_ranks, barrier, peaks, rank)
+    dec7b = None
+    if not args.no_decoder:
+        dec7b = time_decoder_7b(ctx, dev, args, world, max_over_ranks, barrier, peaks, rank)
+    ppo1b = None
+    if not args.no_ppo:
+        ppo1b = time_ppo_1b(ctx, dev, args, world, max_over_ranks, barrier, peaks, rank)
     sharded = None
     if world > 1 and not args.no_shard:
         sharded = time_sharded(ctx, dev, args, world, rank, max_over_ranks, barrier)
@@ -795,6 +921,10 @@ def run_ours(args):
             line["moe"] = moe
         if ppo is not None:
             line["ppo_rollout"] = ppo
+        if dec7b is not None:
+            line["decoder_7b"] = dec7b
+        if ppo1b is not None:
+            line["ppo_policy_1b"] = ppo1b
         if sharded is not None:
             line["sharded"] = sharded
         if world == 1 and not args.no_cpu:
@@ -820,6 +950,7 @@ def main():
     ap.add_argument("--no-sweep", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-moe", action="store_true")
+    ap.add_argument("--no-decoder", action="store_true", help="skip the 7B decoder line")
     ap.add_argument("--no-cfg1", action="store_true", help="skip the single MX-int8 4096x4096 linear line")
     ap.add_argument("--no-ppo", action="store_true")
     ap.add_argument("--no-shard", action="store_true", help="N > 1: skip the column-sharded / expert-parallel forms")

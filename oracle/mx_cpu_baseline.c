@@ -4,8 +4,8 @@
  * snapshot; design described in nn/user.md:17 and
  * research_paper/HARDWARE_SATURATION.md:7-13): _mm512_dpbusd_epi32 over u8
  * activations (q+128) and s8 weights, two 32-element blocks per instruction,
- * each block's sum minus 128 * w_sum, scaled by 2^(e_x + e_w) and summed in
- * fp32.  OpenMP over output rows.
+ * each block scaled by 2^(e_x + e_w) in fp32 vector lanes with the
+ * 128 * w_sum correction per block.  OpenMP over output rows.
  *
  * TEST INFRASTRUCTURE / BASELINE ONLY: timed beside the GPU as the reference
  * CPU arm; never part of the product path.
@@ -83,37 +83,61 @@ static inline int32_t hsum8(__m256i d)
 }
 
 /* Two blocks per _mm512_dpbusd_epi32 (u8 activations x s8 weights, 64 bytes
- * each); the low and high eight int32 lanes are the two blocks' dpbusd sums. */
+ * each).  The 16 int32 lanes are converted to float and multiplied by their
+ * block's scale 2^(e_x + e_w) into a float accumulator vector; the w_sums
+ * correction (-128 * w_sum * scale per block) goes into a scalar; one
+ * horizontal sum per output. */
 __attribute__((target("avx2,avx512f,avx512bw,avx512vl,avx512vnni")))
 static void gemv_vnni(int fmt, const uint8_t* xq, const uint8_t* xs,
                       const void* w, const uint8_t* ws, const int32_t* w_sums,
                       size_t B, size_t N, size_t K, float* y)
 {
     size_t nb = K / BLK;
+    const __m256i lo_mask = _mm256_set1_epi8(0x0F);
+    const __m512i eight = _mm512_set1_epi8(8);
 #pragma omp parallel for schedule(static)
     for (size_t n = 0; n < N; ++n) {
+        const int32_t* zs = w_sums + n * nb;
+        const uint8_t* sw = ws + n * nb;
         for (size_t r = 0; r < B; ++r) {
             const uint8_t* x = xq + r * K;
             const uint8_t* sx = xs + r * nb;
-            float acc = 0.0f;
+            __m512 acc = _mm512_setzero_ps();
+            float corr = 0.0f;
             size_t b = 0;
             for (; b + 2 <= nb; b += 2) {
-                __m512i vw = _mm512_inserti64x4(_mm512_castsi256_si512(load_w_block(fmt, w, K, n, b)),
-                                                load_w_block(fmt, w, K, n, b + 1), 1);
-                __m512i vx = _mm512_loadu_si512((const void*)(x + b * BLK));
-                __m512i d = _mm512_dpbusd_epi32(_mm512_setzero_si512(), vx, vw);
-                int32_t d0 = hsum8(_mm512_castsi512_si256(d)) - 128 * w_sums[n * nb + b];
-                int32_t d1 = hsum8(_mm512_extracti64x4_epi64(d, 1)) - 128 * w_sums[n * nb + b + 1];
-                acc += (float)d0 * pow2f_i((int)sx[b] + (int)ws[n * nb + b] - 254);
-                acc += (float)d1 * pow2f_i((int)sx[b + 1] + (int)ws[n * nb + b + 1] - 254);
+                __m512i vw, vx = _mm512_loadu_si512((const void*)(x + b * BLK));
+                __mmask16 second;
+                if (fmt == 8) {
+                    /* natural order: lanes 0-7 block b, 8-15 block b+1 */
+                    vw = _mm512_loadu_si512((const void*)((const int8_t*)w + n * K + b * BLK));
+                    second = 0xFF00;
+                } else {
+                    /* [b:0-15 | b+1:0-15 | b:16-31 | b+1:16-31]; x's 16-byte
+                     * chunks reordered to match: lanes 4-7 and 12-15 block b+1 */
+                    __m256i p = _mm256_loadu_si256((const __m256i*)((const uint8_t*)w + n * (K / 2) + b * 16));
+                    __m256i lo = _mm256_and_si256(p, lo_mask);
+                    __m256i hi = _mm256_and_si256(_mm256_srli_epi16(p, 4), lo_mask);
+                    vw = _mm512_inserti64x4(_mm512_castsi256_si512(_mm256_unpacklo_epi8(lo, hi)),
+                                            _mm256_unpackhi_epi8(lo, hi), 1);
+                    vw = _mm512_sub_epi8(_mm512_xor_si512(vw, eight), eight);
+                    vx = _mm512_shuffle_i64x2(vx, vx, _MM_SHUFFLE(3, 1, 2, 0));
+                    second = 0xF0F0;
+                }
+                const __m512i d = _mm512_dpbusd_epi32(_mm512_setzero_si512(), vx, vw);
+                const float s0 = pow2f_i((int)sx[b] + (int)sw[b] - 254);
+                const float s1 = pow2f_i((int)sx[b + 1] + (int)sw[b + 1] - 254);
+                const __m512 sc = _mm512_mask_blend_ps(second, _mm512_set1_ps(s0), _mm512_set1_ps(s1));
+                acc = _mm512_fmadd_ps(_mm512_cvtepi32_ps(d), sc, acc);
+                corr += (float)(-128 * zs[b]) * s0 + (float)(-128 * zs[b + 1]) * s1;
             }
+            float tail = 0.0f;
             for (; b < nb; ++b) {
                 __m256i vx = _mm256_loadu_si256((const __m256i*)(x + b * BLK));
                 __m256i d = _mm256_dpbusd_epi32(_mm256_setzero_si256(), vx, load_w_block(fmt, w, K, n, b));
-                int32_t dot = hsum8(d) - 128 * w_sums[n * nb + b];
-                acc += (float)dot * pow2f_i((int)sx[b] + (int)ws[n * nb + b] - 254);
+                tail += (float)(hsum8(d) - 128 * zs[b]) * pow2f_i((int)sx[b] + (int)sw[b] - 254);
             }
-            y[r * N + n] = acc;
+            y[r * N + n] = _mm512_reduce_add_ps(acc) + corr + tail;
         }
     }
 }
