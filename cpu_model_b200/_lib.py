@@ -71,6 +71,10 @@ SIGNATURES = {
     "mxq_decoder_set_trace": [_vp, _i],
     "mxq_decoder_get_trace": [_vp, _i, _vp, _sz],
     "mxq_weight_download": [_vp, _vp, _vp],
+    "mxq_weight_save": [_vp, ctypes.c_char_p],
+    "mxq_update_gaussian_moment": [_vp, _vp, _vp, _vp, _f],
+    "mxq_activation_norm": [_vp, _vp, _vp, _sz, _sz, _vp],
+    "mxq_weight_load": [_vp, ctypes.c_char_p, ctypes.POINTER(_vp)],
     "mxq_quantize_w": [_vp, _i, _vp, _sz, _sz, _vp, _vp, _vp],
     "mxq_weight_quantize": [_vp, _i, _sz, _sz, _vp, _i, ctypes.POINTER(_vp)],
     "mxq_halting_step_host": [_vp, _vp, _vp, _vp, _f, _vp, _vp, _vp],

@@ -893,6 +893,58 @@ int mxq_weight_download(mxq_weight w, void* data_host, uint8_t* scales_host) {
   })
 }
 
+namespace {
+struct MxqwHeader {
+  char magic[4];
+  uint32_t version, fmt, flags;
+  uint64_t n, k;
+};
+static_assert(sizeof(MxqwHeader) == 32, "MXQW header layout");
+}  // namespace
+
+int mxq_weight_save(mxq_weight w, const char* path) {
+  MXQ_TRY({
+    if (!w || !path) return fail(nullptr, MXQ_ERR_INVALID_ARGUMENT, "null pointer");
+    if (w->v.kt_ptr) return fail(w->ctx, MXQ_ERR_UNSUPPORTED, "weight_save: block-sparse weights are not supported");
+    const size_t n = (size_t)w->v.N, k = (size_t)w->v.K;
+    const size_t db = w->v.fmt == 4 ? n * k / 2 : n * k, sb = n * k / kBlock;
+    std::vector<uint8_t> data(db), scales(sb);
+    if (int rc = mxq_weight_download(w, data.data(), scales.data())) return rc;
+    MxqwHeader h{{'M', 'X', 'Q', 'W'}, 1u, (uint32_t)w->v.fmt, 0u, n, k};
+    FILE* f = std::fopen(path, "wb");
+    if (!f) return fail(w->ctx, MXQ_ERR_INVALID_ARGUMENT, "weight_save: cannot open %s", path);
+    const bool ok = std::fwrite(&h, sizeof(h), 1, f) == 1 && std::fwrite(data.data(), 1, db, f) == db &&
+                    std::fwrite(scales.data(), 1, sb, f) == sb;
+    const bool closed = std::fclose(f) == 0;
+    if (!ok || !closed) return fail(w->ctx, MXQ_ERR_CUDA, "weight_save: write to %s failed", path);
+    return MXQ_OK;
+  })
+}
+
+int mxq_weight_load(mxq_ctx c, const char* path, mxq_weight* out) {
+  MXQ_TRY({
+    if (int rc = check_ctx(c)) return rc;
+    if (!path || !out) return fail(c, MXQ_ERR_INVALID_ARGUMENT, "null pointer");
+    *out = nullptr;
+    FILE* f = std::fopen(path, "rb");
+    if (!f) return fail(c, MXQ_ERR_INVALID_ARGUMENT, "weight_load: cannot open %s", path);
+    MxqwHeader h{};
+    bool ok = std::fread(&h, sizeof(h), 1, f) == 1 && std::memcmp(h.magic, "MXQW", 4) == 0 && h.version == 1 &&
+              (h.fmt == 4 || h.fmt == 8) && h.n > 0 && h.k > 0 && h.k % kBlock == 0 && h.n <= (1u << 24) &&
+              h.k <= (1u << 24) && h.flags == 0;
+    if (!ok) {
+      std::fclose(f);
+      return fail(c, MXQ_ERR_INVALID_ARGUMENT, "weight_load: %s is not an MXQW v1 dense weight", path);
+    }
+    const size_t db = h.fmt == 4 ? h.n * h.k / 2 : h.n * h.k, sb = h.n * h.k / kBlock;
+    std::vector<uint8_t> data(db), scales(sb);
+    ok = std::fread(data.data(), 1, db, f) == db && std::fread(scales.data(), 1, sb, f) == sb;
+    std::fclose(f);
+    if (!ok) return fail(c, MXQ_ERR_INVALID_ARGUMENT, "weight_load: %s is truncated", path);
+    return mxq_weight_create(c, (int)h.fmt, (size_t)h.n, (size_t)h.k, data.data(), scales.data(), 0, out);
+  })
+}
+
 int mxq_weight_shape(mxq_weight w, int* fmt, size_t* n, size_t* k) {
   if (!w) return fail(nullptr, MXQ_ERR_INVALID_ARGUMENT, "null weight handle");
   if (fmt) *fmt = w->v.fmt;
@@ -1725,6 +1777,26 @@ int mxq_hashed_route_host(mxq_ctx c, const float* x, size_t t, size_t d, size_t 
     if (e != cudaSuccess) return cuda_fail(c, e, "copy out");
     return mxq_synchronize(c);
   })
+}
+
+int mxq_update_gaussian_moment(mxq_ctx c, mxq_weight w, const float* g, const float* x, float step) {
+  if (int rc = check_ctx(c)) return rc;
+  if (int rc = check_weight(c, w)) return rc;
+  if (!g || !x) return fail(c, MXQ_ERR_INVALID_ARGUMENT, "null pointer");
+  if (int rc = reject_sparse(c, w, "update_gaussian_moment")) return rc;
+  if (!(step == step) || step - step != 0.0f) return fail(c, MXQ_ERR_INVALID_ARGUMENT, "update: step must be finite");
+  DeviceGuard g_(c->device);
+  // every cached host-call graph stays valid: the weight's buffers do not move
+  return after_launch(c, launch_moment_update(w->v, g, x, step, w->data, c->stream), "update_gaussian_moment");
+}
+
+int mxq_activation_norm(mxq_ctx c, const uint8_t* xq, const uint8_t* xs, size_t b, size_t k, float* norms) {
+  if (int rc = check_ctx(c)) return rc;
+  if (!xq || !xs || !norms || b == 0) return fail(c, MXQ_ERR_INVALID_ARGUMENT, "null pointer or empty batch");
+  if (k == 0 || k % kBlock || k > (1u << 24) || b > (1u << 24))
+    return fail(c, MXQ_ERR_INVALID_ARGUMENT, "activation_norm: K a positive multiple of 32");
+  DeviceGuard g(c->device);
+  return after_launch(c, launch_act_norm(xq, xs, (int)b, (int)k, norms, c->stream), "activation_norm");
 }
 
 int mxq_gae_ring(mxq_ctx c, const float* rewards, const float* values, const uint8_t* dones,

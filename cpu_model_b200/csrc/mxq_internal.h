@@ -194,6 +194,13 @@ cudaError_t launch_scale_range(const uint8_t* scales, size_t count, uint32_t* ou
 // [N][K/32] + optional w_sums int32 [N][K/32].
 cudaError_t launch_quantize_w(int fmt, const float* w, int N, int K, uint8_t* data, uint8_t* scales,
                               int32_t* wsums, cudaStream_t st);
+// Online weight update (mx_update_gaussian_moment): w += step * g x^T in
+// the weight's own E8M0 grid, re-clamped to the int8 / int4 range; `data` is
+// the weight's tiled bytes (w.data, written in place).
+cudaError_t launch_moment_update(const WeightView& w, const float* g, const float* x, float step, uint8_t* data,
+                                 cudaStream_t st);
+// L2 norm of MX activation rows (mx_compute_activation_norm).
+cudaError_t launch_act_norm(const uint8_t* xq, const uint8_t* xs, int B, int K, float* out, cudaStream_t st);
 // ACT halting step on a 1-row weight, one state per token.
 constexpr float kHaltEps = 0.01f;
 cudaError_t launch_halting(const WeightView& w, const uint8_t* xq, const uint8_t* xs, int B, float bias,

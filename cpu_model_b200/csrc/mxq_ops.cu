@@ -263,7 +263,92 @@ __global__ void hashed_route_kernel(const float* __restrict__ x, int T, int D, i
   }
 }
 
+// ------------------------------------------------ Gaussian moment update ---
+// One thread per 16-byte piece of the tiled weight: every element w (int8,
+// or an int4 nibble) of row n, column k becomes
+//   clamp(rint(w + ((step * g[n]) * x[k]) * 2^-e), -QMAX, QMAX)
+// with e the element's E8M0 block exponent (kept), QMAX 127 (int8) or 8 / 7
+// (int4: [-8, 7]).  Padding rows and columns stay zero; a NaN-scale block
+// (0xFF) is left as it is.
+template <int WFMT>
+__global__ void moment_update_kernel(WeightView w, const float* __restrict__ g, const float* __restrict__ x,
+                                     float step, uint8_t* __restrict__ data) {
+  constexpr int TB = WFMT == 4 ? 32 : 64;
+  const int KT = w.Kpad / kTileK;
+  const long pieces = (long)(w.Npad / 128) * KT * 128 * (TB / 16);
+  for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < pieces; i += (long)gridDim.x * blockDim.x) {
+    const int p = (int)(i % (TB / 16));
+    const long tr = i / (TB / 16);                 // tiled row index ((rt * KT + kt) * 128 + row)
+    const int row = (int)(tr % 128), kt = (int)((tr / 128) % KT), rt = (int)(tr / (128L * KT));
+    const int n = rt * 128 + row;
+    if (n >= w.N) continue;
+    uint4 v = *reinterpret_cast<const uint4*>(data + tr * TB + p * 16);
+    uint8_t* b = reinterpret_cast<uint8_t*>(&v);
+    const float gn = __fmul_rn(step, g[n]);
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      const int k0 = kt * kTileK + (WFMT == 4 ? (p * 16 + j) * 2 : p * 16 + j);
+#pragma unroll
+      for (int h = 0; h < (WFMT == 4 ? 2 : 1); ++h) {
+        const int k = k0 + h;
+        if (k >= w.K) continue;
+        const uint32_t s = w.scales[tr * 2 + ((k % kTileK) >> 5)];
+        if (s == 255u) continue;
+        const int old = WFMT == 4 ? (((int)(b[j] >> (4 * h)) & 0xF) ^ 8) - 8 : (int)(int8_t)b[j];
+        const float delta = __fmul_rn(__fmul_rn(gn, x[k]), pow2_exact(127 - (int)s));
+        int q = __float2int_rn(__fadd_rn((float)old, delta));
+        const int lo = WFMT == 4 ? -8 : -127, hi = WFMT == 4 ? 7 : 127;
+        q = q < lo ? lo : (q > hi ? hi : q);
+        if (WFMT == 4) b[j] = (uint8_t)((b[j] & (h ? 0x0F : 0xF0)) | ((q & 0xF) << (4 * h)));
+        else b[j] = (uint8_t)(int8_t)q;
+      }
+    }
+    *reinterpret_cast<uint4*>(data + tr * TB + p * 16) = v;
+  }
+}
+
+// ------------------------------------------------ activation norm ---
+// ||x||_2 of an MX activation row: per block the exact int sum of q^2,
+// times 2^(2 e) in fp32, summed in the lanes-then-butterfly order.
+__global__ void act_norm_kernel(const uint8_t* __restrict__ xq, const uint8_t* __restrict__ xs, int B, int K,
+                                float* __restrict__ out) {
+  const int lane = threadIdx.x & 31;
+  const int t = (int)(((long)blockIdx.x * blockDim.x + threadIdx.x) >> 5);
+  if (t >= B) return;
+  const int nb = K / kBlock;
+  float acc = 0.0f;
+  for (int b = lane; b < nb; b += 32) {
+    const uint8_t* q = xq + (size_t)t * K + (size_t)b * kBlock;
+    int ss = 0;
+#pragma unroll 8
+    for (int i = 0; i < kBlock; ++i) {
+      const int v = (int)q[i] - 128;
+      ss += v * v;
+    }
+    const float sc = e8m0_to_float(xs[(size_t)t * nb + b]);
+    acc = __fadd_rn(acc, __fmul_rn(__fmul_rn((float)ss, sc), sc));
+  }
+  acc = butterfly_sum(acc);
+  if (lane == 0) out[t] = __fsqrt_rn(acc);
+}
+
 }  // namespace
+
+cudaError_t launch_moment_update(const WeightView& w, const float* g, const float* x, float step, uint8_t* data,
+                                 cudaStream_t st) {
+  const long pieces = (long)(w.Npad / 128) * (w.Kpad / kTileK) * 128 * ((w.fmt == 4 ? 32 : 64) / 16);
+  long ctas = (pieces + 255) / 256;
+  if (ctas > 148L * 16) ctas = 148L * 16;
+  if (w.fmt == 4) moment_update_kernel<4><<<(unsigned)ctas, 256, 0, st>>>(w, g, x, step, data);
+  else moment_update_kernel<8><<<(unsigned)ctas, 256, 0, st>>>(w, g, x, step, data);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_act_norm(const uint8_t* xq, const uint8_t* xs, int B, int K, float* out, cudaStream_t st) {
+  const long threads = (long)B * 32;
+  act_norm_kernel<<<(unsigned)((threads + 127) / 128), 128, 0, st>>>(xq, xs, B, K, out);
+  return cudaGetLastError();
+}
 
 cudaError_t launch_quantize_w(int fmt, const float* w, int N, int K, uint8_t* data, uint8_t* scales,
                               int32_t* wsums, cudaStream_t st) {

@@ -157,6 +157,42 @@ class MXWeight:
         except Exception:
             pass
 
+    def download(self):
+        """(data, scales) in the MXINT8Tensor layout (numpy); dense only."""
+        import numpy as np
+        data = np.empty((self.n, self.k // 2), np.uint8) if self.fmt == FMT_INT4 else \
+            np.empty((self.n, self.k), np.int8)
+        scales = np.empty((self.n, self.k // 32), np.uint8)
+        check(self.ctx.lib.mxq_weight_download(self.h, data.ctypes.data_as(ctypes.c_void_p),
+                                               scales.ctypes.data_as(ctypes.c_void_p)), self.ctx.h)
+        return data, scales
+
+    def save(self, path):
+        """Write the weight as an MXQW file (mxq_weight_save)."""
+        check(self.ctx.lib.mxq_weight_save(self.h, str(path).encode()), self.ctx.h)
+
+    @classmethod
+    def load(cls, path, ctx=None):
+        """Read an MXQW file into a new weight (mxq_weight_load)."""
+        ctx = ctx or context()
+        h = ctypes.c_void_p()
+        ctx._bind()
+        check(ctx.lib.mxq_weight_load(ctx.h, str(path).encode(), ctypes.byref(h)), ctx.h)
+        obj = cls.__new__(cls)
+        obj.ctx, obj.h, obj.block_sparse = ctx, h, False
+        fmt, n, k = ctypes.c_int(), ctypes.c_size_t(), ctypes.c_size_t()
+        check(ctx.lib.mxq_weight_shape(h, ctypes.byref(fmt), ctypes.byref(n), ctypes.byref(k)), ctx.h)
+        obj.fmt, obj.n, obj.k = fmt.value, n.value, k.value
+        return obj
+
+    @classmethod
+    def from_float(cls, w, fmt, ctx=None):
+        """fp32 rows (a CUDA tensor [N][K], K a multiple of 32) quantised on
+        the device (mx_quantize_w) into a new weight."""
+        ctx = ctx or context()
+        data, scales, _ = mx_quantize_w(w.contiguous(), fmt, ctx, with_sums=False)
+        return cls(data, scales, fmt, w.shape[0], w.shape[1], ctx)
+
 
 def _quant(x, act, ctx):
     ctx = ctx or context()
@@ -411,6 +447,29 @@ def halting_step(x, w_halt, bias, state, ctx=None):
     check(ctx.lib.mxq_halting_step(ctx.h, w_halt.h, _ptr(x.q), _ptr(x.s), x.batch, float(bias), _ptr(state.raw),
                                    _ptr(p), _ptr(h)), ctx.h)
     return p, h
+
+
+def mx_update_gaussian_moment(w, g, x, step, ctx=None):
+    """nca::linalg::mx_update_gaussian_moment: in place, w += step * g x^T in
+    the weight's own E8M0 grid, re-clamped to the int8 / int4 range
+    (mxq_update_gaussian_moment).  g [N], x [K] fp32 CUDA tensors."""
+    ctx = ctx or w.ctx
+    _need_cuda(g, torch.float32, "g")
+    _need_cuda(x, torch.float32, "x")
+    if g.numel() != w.n or x.numel() != w.k:
+        raise ValueError("update: g needs %d values and x %d" % (w.n, w.k))
+    ctx._bind()
+    check(ctx.lib.mxq_update_gaussian_moment(ctx.h, w.h, _ptr(g), _ptr(x), float(step)), ctx.h)
+
+
+def mx_compute_activation_norm(x, ctx=None):
+    """nca::linalg::mx_compute_activation_norm: L2 norm per MX activation row."""
+    ctx = ctx or context()
+    _need_cuda(x.q, torch.uint8, "activation q")
+    out = torch.empty(x.batch, dtype=torch.float32, device=x.q.device)
+    ctx._bind()
+    check(ctx.lib.mxq_activation_norm(ctx.h, _ptr(x.q), _ptr(x.s), x.batch, x.k, _ptr(out)), ctx.h)
+    return out
 
 
 def mx_quantize_w(w, fmt, ctx=None, with_sums=True):

@@ -228,6 +228,25 @@ MXQ_API int mxq_linear_noalloc(mxq_ctx ctx, mxq_weight w, const float* x,
 MXQ_API int mxq_debug_gemm_stall(mxq_ctx ctx, mxq_weight w, const float* x,
                                  size_t b, float* y, uint32_t wait_us);
 
+/* ---------------------------------------------------- online update --- */
+/* nca::linalg::mx_update_gaussian_moment (nn/tests/test_auto_generated.cpp:49;
+ * described in research_paper/MATH_FOUNDATIONS.md:33-40 as "dW = eta * A_t *
+ * grad_W log pi, then re-clamp to the MX boundary"; its code is absent, so
+ * this is the library's statement of it): in place, every element of w
+ * becomes clamp(rint(w + ((step * g[n]) * x[k]) * 2^-e), lo, hi) with e its
+ * block's E8M0 exponent (unchanged) and [lo, hi] = [-127, 127] (int8) or
+ * [-8, 7] (int4); step = eta * advantage, g [N] and x [K] (device) the
+ * output gradient and the input of the linear (grad_W = g x^T).  Blocks with
+ * scale 0xFF are left as they are; dense weights only. */
+MXQ_API int mxq_update_gaussian_moment(mxq_ctx ctx, mxq_weight w, const float* g,
+                                       const float* x, float step);
+/* nca::linalg::mx_compute_activation_norm (nn/tests/test_auto_generated.cpp:50):
+ * norms[b] = ||dequant(x_b)||_2 of MX activations xq [B][K], xs [B][K/32]
+ * (per block the exact int sum of q^2 times 2^(2e), fp32 sum in a fixed
+ * order). */
+MXQ_API int mxq_activation_norm(mxq_ctx ctx, const uint8_t* xq, const uint8_t* xs,
+                                size_t b, size_t k, float* norms);
+
 /* ------------------------------------------------------------ halting --- */
 /* nca::layers::halting_step (nn/core/layers/halting.hpp:24-30), batched: per
  * token b, p = sigmoid(w_halt . x_b + bias) with the 1-row MX dot of
@@ -432,6 +451,16 @@ MXQ_API int mxq_decoder_get_trace(mxq_decoder dec, int id, float* out,
  * inverse of mxq_weight_create (for serialisation and checking). */
 MXQ_API int mxq_weight_download(mxq_weight w, void* data_host,
                                 uint8_t* scales_host);
+
+/* On-disk MX weight (no counterpart in the reference, whose MX containers
+ * lived only in memory; its checkpoints were LibTorch archives,
+ * training/offline_trainer.cpp:105-128).  Little-endian file: magic "MXQW",
+ * u32 version 1, u32 fmt (4 or 8), u32 flags (0), u64 N, u64 K, then
+ * the MXINT8Tensor bytes (data [N][K] int8 or [N][K/2] packed int4), then the
+ * E8M0 scales [N][K/32].  Dense weights only (block-sparse:
+ * MXQ_ERR_UNSUPPORTED). */
+MXQ_API int mxq_weight_save(mxq_weight w, const char* path);
+MXQ_API int mxq_weight_load(mxq_ctx ctx, const char* path, mxq_weight* out);
 
 #ifdef __cplusplus
 }

@@ -341,6 +341,58 @@ void mxo_halting_step(int fmt, const uint8_t* xq, const uint8_t* xs, const void*
     }
 }
 
+/* mx_update_gaussian_moment as the library states it: w = clamp(rint(w +
+ * ((step * g[n]) * x[k]) * 2^-e), lo, hi), scales kept, blocks with scale
+ * 0xFF untouched; data in the MXINT8Tensor layout, updated in place. */
+void mxo_update_gaussian_moment(int fmt, void* data, const uint8_t* scales, size_t N, size_t K,
+                                const float* g, const float* x, float step)
+{
+    size_t nb = K / MXO_BLOCK;
+    int lo = fmt == MXO_FMT_INT4 ? -8 : -127, hi = fmt == MXO_FMT_INT4 ? 7 : 127;
+    for (size_t n = 0; n < N; ++n) {
+        float gn = step * g[n];
+        for (size_t k = 0; k < K; ++k) {
+            uint8_t s = scales[n * nb + k / MXO_BLOCK];
+            if (s == 0xFF) continue;
+            int old = mxo_weight_at(fmt, data, K, n, k);
+            float delta = (gn * x[k]) * pow2x(127 - (int)s);
+            float r = rintf((float)old + delta);
+            int q = r < (float)lo ? lo : (r > (float)hi ? hi : (int)r);
+            if (fmt == MXO_FMT_INT8) {
+                ((int8_t*)data)[n * K + k] = (int8_t)q;
+            } else {
+                uint8_t* p = (uint8_t*)data + n * (K / 2) + k / 2;
+                *p = (k & 1) ? (uint8_t)((*p & 0x0F) | ((q & 0xF) << 4)) : (uint8_t)((*p & 0xF0) | (q & 0xF));
+            }
+        }
+    }
+}
+
+/* ||dequant(x_b)||_2 in the GPU's order (lanes, then the butterfly). */
+void mxo_activation_norm(const uint8_t* xq, const uint8_t* xs, size_t B, size_t K, float* out)
+{
+    size_t nb = K / MXO_BLOCK;
+    for (size_t r = 0; r < B; ++r) {
+        float v[32];
+        for (int l = 0; l < 32; ++l) v[l] = 0.0f;
+        for (size_t b = 0; b < nb; ++b) {
+            int32_t ss = 0;
+            for (int i = 0; i < MXO_BLOCK; ++i) {
+                int q = (int)xq[r * K + b * MXO_BLOCK + i] - 128;
+                ss += q * q;
+            }
+            float sc = e8m0_f32(xs[r * nb + b]);
+            v[b % 32] = v[b % 32] + ((float)ss * sc) * sc;
+        }
+        for (int o = 16; o > 0; o >>= 1) {
+            float u[32];
+            for (int l = 0; l < 32; ++l) u[l] = v[l] + v[l ^ o];
+            for (int l = 0; l < 32; ++l) v[l] = u[l];
+        }
+        out[r] = sqrtf(v[0]);
+    }
+}
+
 /* splitmix64 finaliser (the router's hyperplane and code generator) */
 static uint64_t mix64(uint64_t z)
 {

@@ -106,6 +106,15 @@ void mxo_halting_step(int fmt, const uint8_t* xq, const uint8_t* xs, const void*
                       const uint8_t* ws, size_t B, size_t K, float bias, float eps,
                       float* p_sum, float* remainder, uint64_t* steps, float* p, uint8_t* halt);
 
+/* mx_update_gaussian_moment (nn/tests/test_auto_generated.cpp:49;
+ * research_paper/MATH_FOUNDATIONS.md:33-40) as the library states it:
+ * w = clamp(rint(w + ((step * g[n]) * x[k]) * 2^-e), lo, hi), scales kept. */
+void mxo_update_gaussian_moment(int fmt, void* data, const uint8_t* scales, size_t N, size_t K,
+                                const float* g, const float* x, float step);
+/* mx_compute_activation_norm (nn/tests/test_auto_generated.cpp:50): the L2
+ * norm of each MX activation row, in the GPU's summation order. */
+void mxo_activation_norm(const uint8_t* xq, const uint8_t* xs, size_t B, size_t K, float* out);
+
 /* linalg::HashedRouter::route (nn/tests/test_robustness.cpp:13-35) as the
  * library defines it (the reference's algorithm is absent): sign-of-
  * projection LSH over the MX-quantised input with H seeded +-1 hyperplanes,

@@ -130,6 +130,25 @@ def halting_step(fmt, xq, xs, w, ws, k, bias, p_sum, remainder, steps, eps=0.01)
     return p, h
 
 
+def update_gaussian_moment(fmt, data, scales, g, x, step):
+    """Returns the updated copy of data (MXINT8Tensor layout)."""
+    out = np.array(data, copy=True)
+    n = scales.shape[0]
+    k = scales.shape[1] * 32
+    lib().mxo_update_gaussian_moment(ctypes.c_int(fmt), _p(out), _p(np.ascontiguousarray(scales, np.uint8)),
+                                     *_sz(n, k), _p(np.ascontiguousarray(g, np.float32)),
+                                     _p(np.ascontiguousarray(x, np.float32)), ctypes.c_float(step))
+    return out
+
+
+def activation_norm(xq, xs):
+    xq = np.ascontiguousarray(xq, np.uint8)
+    b, k = xq.shape
+    out = np.empty(b, np.float32)
+    lib().mxo_activation_norm(_p(xq), _p(np.ascontiguousarray(xs, np.uint8)), *_sz(b, k), _p(out))
+    return out
+
+
 def hashed_route(x, n_experts, top_k, n_hashes, seed):
     """(idx [T][top_k], score [T][top_k]) of the LSH router; ValueError for
     top_k > n_experts (the reference's invalid_argument)."""

@@ -187,3 +187,38 @@ def test_hashed_router_remainder_and_bounds(ctx):
                                   mx._ptr(out), mx._ptr(out))
     assert rc == _lib.MXQ_ERR_INVALID_ARGUMENT
     ctx.synchronize()
+
+
+# ------------------------------------------- online update / activation norm ---
+@pytest.mark.parametrize("fmt,n,k", [(8, 200, 448), (4, 130, 1024)])
+def test_update_gaussian_moment_bit_exact(ctx, fmt, n, k):
+    """mx_update_gaussian_moment against the oracle: the tiled device weight,
+    read back, equals the oracle's update of the MXINT8Tensor bytes; a large
+    step saturates at the range ends."""
+    w, ws = synth.weights(fmt, n, k, -9, -5, 90 + k)
+    ws[3, 2] = 255                                      # a NaN block stays as it is
+    W = mx.MXWeight(torch.from_numpy(w), torch.from_numpy(ws), fmt, n, k, ctx)
+    g = synth.normal((n,), 91)
+    x = synth.normal((k,), 92)
+    cur = w
+    for step in (0.37, -1e3):
+        mx.mx_update_gaussian_moment(W, cuda(g), cuda(x), step, ctx)
+        ctx.synchronize()
+        cur = oracle.update_gaussian_moment(fmt, cur, ws, g, x, step)
+        d, s = W.download()
+        assert np.array_equal(d, cur) and np.array_equal(s, ws)
+    vals = synth.unpack_int4(cur) if fmt == 4 else cur
+    assert vals.min() == (-8 if fmt == 4 else -127) and vals.max() == (7 if fmt == 4 else 127)
+    W.close()
+
+
+@pytest.mark.parametrize("b,k", [(1, 32), (5, 4096), (3, 11008)])
+def test_activation_norm_bit_exact(ctx, b, k):
+    x = synth.normal((b, k), 93 + k)
+    if k >= 64:
+        x[0, 32:64] = 0.0
+    xq, xs = oracle.quantize_x(x)
+    nrm = host(mx.mx_compute_activation_norm(mx.MXActivation(cuda(xq), cuda(xs)), ctx))
+    assert np.array_equal(nrm, oracle.activation_norm(xq, xs))
+    deq = (xq.astype(np.float64) - 128) * np.exp2(xs.astype(np.float64) - 127).repeat(32, axis=1)
+    assert np.allclose(nrm, np.linalg.norm(deq, axis=1), rtol=1e-6)
