@@ -74,6 +74,7 @@ SIGNATURES = {
     "mxq_weight_save": [_vp, ctypes.c_char_p],
     "mxq_update_gaussian_moment": [_vp, _vp, _vp, _vp, _f],
     "mxq_activation_norm": [_vp, _vp, _vp, _sz, _sz, _vp],
+    "mxq_micro_moe": [_vp, _vp, _vp, _vp, _sz, _sz, _vp, _vp, _vp, _sz, _sz, _vp],
     "mxq_weight_load": [_vp, ctypes.c_char_p, ctypes.POINTER(_vp)],
     "mxq_quantize_w": [_vp, _i, _vp, _sz, _sz, _vp, _vp, _vp],
     "mxq_weight_quantize": [_vp, _i, _sz, _sz, _vp, _i, ctypes.POINTER(_vp)],

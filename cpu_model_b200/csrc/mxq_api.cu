@@ -1799,6 +1799,32 @@ int mxq_activation_norm(mxq_ctx c, const uint8_t* xq, const uint8_t* xs, size_t 
   return after_launch(c, launch_act_norm(xq, xs, (int)b, (int)k, norms, c->stream), "activation_norm");
 }
 
+int mxq_micro_moe(mxq_ctx c, mxq_weight wg, mxq_weight wu, mxq_weight wd, size_t n_routed, size_t n_shared,
+                  const float* x, const int32_t* idx, const float* gate, size_t t, size_t k, float* y) {
+  if (int rc = check_ctx(c)) return rc;
+  if (int rc = check_weight(c, wg)) return rc;
+  if (int rc = check_weight(c, wu)) return rc;
+  if (int rc = check_weight(c, wd)) return rc;
+  if (!x || !y || (k > 0 && !idx)) return fail(c, MXQ_ERR_INVALID_ARGUMENT, "null pointer");
+  if (int rc = reject_sparse(c, wg, "micro_moe")) return rc;
+  if (int rc = reject_sparse(c, wu, "micro_moe")) return rc;
+  if (int rc = reject_sparse(c, wd, "micro_moe")) return rc;
+  if (k > n_routed) return fail(c, MXQ_ERR_INVALID_ARGUMENT, "micro_moe: top_k (%zu) exceeds n_experts (%zu)", k, n_routed);
+  if (k > 64 || n_shared > 8 || k + n_shared == 0)
+    return fail(c, MXQ_ERR_INVALID_ARGUMENT, "micro_moe: top_k <= 64, n_shared <= 8, at least one expert");
+  const size_t E = n_routed + n_shared;
+  const WeightView &g = wg->v, &u = wu->v, &d = wd->v;
+  if ((size_t)g.N != E * 16 || (size_t)u.N != E * 16 || g.K != u.K || (size_t)d.K != E * 16 || d.N != g.K)
+    return fail(c, MXQ_ERR_INVALID_ARGUMENT,
+                "micro_moe: gate/up pools must be [%zu][D], down [D][%zu] (16 rows per expert)", E * 16, E * 16);
+  if (E % 2) return fail(c, MXQ_ERR_INVALID_ARGUMENT, "micro_moe: the expert count (routed + shared) must be even");
+  if (t == 0) return MXQ_OK;
+  if (t > (1u << 24)) return fail(c, MXQ_ERR_INVALID_ARGUMENT, "micro_moe: too many tokens");
+  DeviceGuard g_(c->device);
+  return after_launch(c, launch_micro_moe(g, u, d, (int)n_routed, (int)n_shared, x, idx, gate, (int)t, (int)k, y,
+                                          c->stream), "micro_moe");
+}
+
 int mxq_gae_ring(mxq_ctx c, const float* rewards, const float* values, const uint8_t* dones,
                  const float* next_values, size_t capacity, size_t size, size_t cursor, size_t t,
                  size_t e, float gamma, float lambda, float* adv, float* ret) {

@@ -201,6 +201,11 @@ cudaError_t launch_moment_update(const WeightView& w, const float* g, const floa
                                  cudaStream_t st);
 // L2 norm of MX activation rows (mx_compute_activation_norm).
 cudaError_t launch_act_norm(const uint8_t* xq, const uint8_t* xs, int B, int K, float* out, cudaStream_t st);
+// Micro-expert layer (16-row experts, top-k routed + shared), one CTA per token.
+size_t micro_moe_smem(int D, int nsel);
+cudaError_t launch_micro_moe(const WeightView& wg, const WeightView& wu, const WeightView& wd, int n_routed,
+                             int n_shared, const float* x, const int32_t* idx, const float* gate, int T, int k,
+                             float* y, cudaStream_t st);
 // ACT halting step on a 1-row weight, one state per token.
 constexpr float kHaltEps = 0.01f;
 cudaError_t launch_halting(const WeightView& w, const uint8_t* xq, const uint8_t* xs, int B, float bias,

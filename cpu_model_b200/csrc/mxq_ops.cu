@@ -332,7 +332,141 @@ __global__ void act_norm_kernel(const uint8_t* __restrict__ xq, const uint8_t* _
   if (lane == 0) out[t] = __fsqrt_rn(acc);
 }
 
+// ------------------------------------------------ micro-expert layer ---
+// The reference's expert pool (1024 micro-experts of 16 rows, top-16 routed
+// plus 2 shared, nn/config/model_config.hpp:23-25; 16-row slices of the
+// gate/up matrices, training/fidelity_test.cpp:57-59).  Expert e owns rows
+// 16e .. 16e+15 of the gate and up pools [(E_r + E_s) * 16][D] and columns
+// 16e .. 16e+15 of the down pool [D][(E_r + E_s) * 16]; shared experts are
+// e = E_r .. E_r + E_s - 1.  Per token (one CTA of 256 threads):
+//   x -> MX (quantize_kernel's arithmetic) in shared memory;
+//   the 16 gate and 16 up rows of each chosen expert: row dots in the fixed
+//   lane order (one warp per row);
+//   h = det_swiglu(g, u) * gate weight (1 for shared experts), placed in the
+//   32-element blocks of the down pool's K (expert e's 16 values are half of
+//   block e / 2; a block's other half is 0 unless its expert is chosen too),
+//   each block MX-quantised;
+//   y[j] = sum over the chosen blocks in ascending order of
+//   (dot * 2^e_h) * 2^e_w, fp32.
+constexpr int kMicroMaxSel = 64 + 8;   // routed k <= 64, shared <= 8
+
+__global__ void __launch_bounds__(256) micro_moe_kernel(WeightView wg, WeightView wu, WeightView wd, int n_routed,
+                                                        int n_shared, const float* __restrict__ x,
+                                                        const int32_t* __restrict__ idx,
+                                                        const float* __restrict__ gate, int k,
+                                                        float* __restrict__ y) {
+  extern __shared__ __align__(16) uint8_t sm[];
+  const int D = wg.K, t = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int nsel = k + n_shared;
+  uint8_t* xq = sm;                                     // [D] u8
+  uint8_t* xs = xq + D;                                 // [D/32]
+  float* hv = reinterpret_cast<float*>(sm + ((D + D / 32 + 15) / 16) * 16);   // [nsel][32]: g then u
+  int* sel = reinterpret_cast<int*>(hv + nsel * 32);    // [nsel] expert ids
+  float* wsel = reinterpret_cast<float*>(sel + nsel);   // [nsel] weights
+  int* blk = reinterpret_cast<int*>(wsel + nsel);       // [nsel] distinct blocks, ascending
+  int* nblk = blk + nsel;
+  uint8_t* hq = reinterpret_cast<uint8_t*>(nblk + 4);   // [nsel][32] (16-byte aligned below)
+  hq = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(hq) + 15) & ~(uintptr_t)15);
+  uint8_t* hs = hq + nsel * 32;                         // [nsel]
+  // 1. the token's x to MX bytes
+  for (int b = warp; b < D / kBlock; b += 8) {
+    const float v = x[(size_t)t * D + b * kBlock + lane];
+    const float av = fabsf(v);
+    const bool nonfinite = !(av <= 3.402823466e38f);
+    const bool any_nf = __any_sync(0xffffffffu, nonfinite);
+    const float m = warp_max(nonfinite ? 0.0f : av, 32);
+    int q = 0;
+    uint32_t sb = 0;
+    if (any_nf) sb = 255;
+    else if (m != 0.0f) {
+      const int e = e8m0_exponent<127>(m);
+      sb = (uint32_t)(e + 127);
+      q = quant_value(v, e);
+    }
+    xq[b * kBlock + lane] = (uint8_t)(q + 128);
+    if (lane == 0) xs[b] = (uint8_t)sb;
+  }
+  if (tid < nsel) {
+    int e = tid < k ? idx[(size_t)t * k + tid] : n_routed + (tid - k);
+    if (tid < k) e = e < 0 ? 0 : (e >= n_routed ? n_routed - 1 : e);   // ids outside the pool: clamped
+    sel[tid] = e;
+    wsel[tid] = tid < k ? (gate ? gate[(size_t)t * k + tid] : 1.0f) : 1.0f;
+  }
+  __syncthreads();
+  // 2. gate and up rows of the chosen experts, one warp per row
+  for (int r = warp; r < nsel * 32; r += 8) {
+    const int s = r >> 5, j = r & 31;                   // j < 16: gate row j, else up row j - 16
+    const int row = sel[s] * 16 + (j & 15);
+    const float v = row_dot(j < 16 ? wg : wu, row, xq, xs, lane);
+    if (lane == 0) hv[s * 32 + j] = v;
+  }
+  // the distinct down blocks, ascending (one thread; at most nsel entries)
+  if (tid == 0) {
+    int n = 0;
+    for (int s2 = 0; s2 < nsel; ++s2) {
+      const int b = sel[s2] >> 1;
+      int pos = 0;
+      while (pos < n && blk[pos] < b) ++pos;
+      if (pos < n && blk[pos] == b) continue;
+      for (int q2 = n; q2 > pos; --q2) blk[q2] = blk[q2 - 1];
+      blk[pos] = b;
+      ++n;
+    }
+    *nblk = n;
+  }
+  __syncthreads();
+  // 3. h per block (one warp per block, lane = element) -> MX
+  const int nb = *nblk;
+  for (int i = warp; i < nb; i += 8) {
+    const int e = blk[i] * 2 + (lane >> 4), slot = lane & 15;
+    float v = 0.0f;
+    for (int s2 = 0; s2 < nsel; ++s2)
+      if (sel[s2] == e) v = __fmul_rn(det_swiglu(hv[s2 * 32 + slot], hv[s2 * 32 + 16 + slot]), wsel[s2]);
+    const float av = fabsf(v);
+    const bool nonfinite = !(av <= 3.402823466e38f);
+    const bool any_nf = __any_sync(0xffffffffu, nonfinite);
+    const float m = warp_max(nonfinite ? 0.0f : av, 32);
+    int q = 0;
+    uint32_t sb = 0;
+    if (any_nf) sb = 255;
+    else if (m != 0.0f) {
+      const int ee = e8m0_exponent<127>(m);
+      sb = (uint32_t)(ee + 127);
+      q = quant_value(v, ee);
+    }
+    hq[i * 32 + lane] = (uint8_t)(q + 128);
+    if (lane == 0) hs[i] = (uint8_t)sb;
+  }
+  __syncthreads();
+  // 4. down: one thread per output row, the chosen blocks in ascending order
+  for (int j = tid; j < wd.N; j += 256) {
+    float acc = 0.0f;
+    for (int i = 0; i < nb; ++i) {
+      const int d = block_dot(wd, j, blk[i], hq + i * 32);
+      acc = __fadd_rn(acc, __fmul_rn(__fmul_rn((float)d, e8m0_to_float(hs[i])),
+                                     e8m0_to_float(weight_scale(wd, j, blk[i]))));
+    }
+    y[(size_t)t * wd.N + j] = acc;
+  }
+}
+
 }  // namespace
+
+size_t micro_moe_smem(int D, int nsel) {
+  return (size_t)((D + D / 32 + 15) / 16) * 16 + (size_t)nsel * 32 * 4 + (size_t)nsel * 4 * 3 + 16 + 16 +
+         (size_t)nsel * 33 + 16;
+}
+
+cudaError_t launch_micro_moe(const WeightView& wg, const WeightView& wu, const WeightView& wd, int n_routed,
+                             int n_shared, const float* x, const int32_t* idx, const float* gate, int T, int k,
+                             float* y, cudaStream_t st) {
+  if (k + n_shared > kMicroMaxSel) return cudaErrorInvalidValue;
+  const size_t smem = micro_moe_smem(wg.K, k + n_shared);
+  static SmemAttr smem_attr;
+  if (cudaError_t e = smem_attr.ensure(micro_moe_kernel, smem)) return e;
+  micro_moe_kernel<<<(unsigned)T, 256, smem, st>>>(wg, wu, wd, n_routed, n_shared, x, idx, gate, k, y);
+  return cudaGetLastError();
+}
 
 cudaError_t launch_moment_update(const WeightView& w, const float* g, const float* x, float step, uint8_t* data,
                                  cudaStream_t st) {

@@ -462,6 +462,26 @@ def mx_update_gaussian_moment(w, g, x, step, ctx=None):
     check(ctx.lib.mxq_update_gaussian_moment(ctx.h, w.h, _ptr(g), _ptr(x), float(step)), ctx.h)
 
 
+def micro_moe(x, w_gate, w_up, w_down, n_routed, n_shared, idx, gate=None, ctx=None):
+    """The micro-expert pool layer (mxq_micro_moe): x [T][D], 16-row experts
+    in the gate/up pools [(n_routed + n_shared) * 16][D] and the down pool
+    [D][(n_routed + n_shared) * 16]; idx/gate [T][k] from a router (gate None
+    = weight 1); shared experts always active.  Returns y [T][D]."""
+    ctx = ctx or w_gate.ctx
+    _need_cuda(x, torch.float32, "x")
+    t, d = x.shape
+    k = 0 if idx is None else idx.shape[1]
+    if idx is not None:
+        _need_cuda(idx, torch.int32, "idx")
+    if gate is not None:
+        _need_cuda(gate, torch.float32, "gate")
+    y = torch.empty((t, w_down.n), dtype=torch.float32, device=x.device)
+    ctx._bind()
+    check(ctx.lib.mxq_micro_moe(ctx.h, w_gate.h, w_up.h, w_down.h, n_routed, n_shared, _ptr(x), _ptr(idx),
+                                _ptr(gate), t, k, _ptr(y)), ctx.h)
+    return y
+
+
 def mx_compute_activation_norm(x, ctx=None):
     """nca::linalg::mx_compute_activation_norm: L2 norm per MX activation row."""
     ctx = ctx or context()

@@ -325,6 +325,25 @@ MXQ_API int mxq_moe_swiglu(mxq_ctx ctx, const mxq_weight* w_gate,
                            const float* logits, size_t t, size_t k,
                            float* y);
 
+/* The reference's micro-expert pool (nn/config/model_config.hpp:23-25:
+ * 1024 experts, top-16 routed, 2 shared always active; 16-row expert slices
+ * of the gate/up matrices, training/fidelity_test.cpp:57-59; executed by
+ * mx_rank16_dot_ptrs over the 16 gathered rows, nn/tests/autotest.hpp:
+ * 126-136).  The pool's code is absent; this is the library's statement:
+ * E = n_routed + n_shared experts (E even), expert e owning rows 16e..16e+15
+ * of wg and wu [E*16][D] and columns 16e..16e+15 of wd [D][E*16], shared
+ * experts e = n_routed .. E-1.  Per token: h_e = silu(gate rows . x) * (up
+ * rows . x) * w_e (w_e = gate[t][j] for routed expert idx[t][j], 1 for
+ * shared; gate may be null = 1), MX-quantised per 32-block of wd's K,
+ * y[t] = wd . h over the chosen blocks.  Every sum runs in a fixed order, so
+ * results are bit-reproducible.  idx/gate [T][k] come from mxq_route_topk or
+ * mxq_hashed_route; k > n_routed is MXQ_ERR_INVALID_ARGUMENT.  x [T][D],
+ * y [T][D] device pointers; dense weights. */
+MXQ_API int mxq_micro_moe(mxq_ctx ctx, mxq_weight wg, mxq_weight wu, mxq_weight wd,
+                          size_t n_routed, size_t n_shared, const float* x,
+                          const int32_t* idx, const float* gate, size_t t,
+                          size_t k, float* y);
+
 /* --------------------------------------------------------- PPO head --- */
 /* The rollout head of PPOTrainer::update_step (training/ppo_trainer.cpp:64-66
  * and :77) after its three MX linears (states -> latent -> logits, latent ->

@@ -393,6 +393,75 @@ void mxo_activation_norm(const uint8_t* xq, const uint8_t* xs, size_t B, size_t 
     }
 }
 
+/* The micro-expert layer in the GPU's operation order (see mxq_micro_moe):
+ * per token, x quantised; each chosen expert's 16 gate and 16 up row dots by
+ * lane_tree_dot; h = silu(g) * u * weight placed in the down pool's 32-blocks
+ * and quantised; y[j] = sum over the chosen blocks, ascending, of
+ * (d * 2^e_h) * 2^e_w in fp32.  Pools in the MXINT8Tensor layout. */
+void mxo_micro_moe(int fmt, const void* wg, const uint8_t* sg, const void* wu, const uint8_t* su,
+                   const void* wd, const uint8_t* sd, size_t n_routed, size_t n_shared, size_t D,
+                   const float* x, const int32_t* idx, const float* gate, size_t T, size_t k, float* y)
+{
+    size_t E = n_routed + n_shared, nsel = k + n_shared, KD = E * 16;
+    size_t rb = fmt == MXO_FMT_INT4 ? D / 2 : D;          /* bytes per pool row */
+    uint8_t* xq = (uint8_t*)malloc(D);
+    uint8_t* xs = (uint8_t*)malloc(D / 32);
+    float* hv = (float*)malloc(nsel * 32 * sizeof(float));
+    int* sel = (int*)malloc(nsel * sizeof(int));
+    float* wsel = (float*)malloc(nsel * sizeof(float));
+    int* blk = (int*)malloc(nsel * sizeof(int));
+    uint8_t* hq = (uint8_t*)malloc(nsel * 32);
+    uint8_t* hs = (uint8_t*)malloc(nsel);
+    float blkv[32];
+    for (size_t t = 0; t < T; ++t) {
+        mxo_quantize_x(x + t * D, 1, D, 0, xq, xs);
+        for (size_t s = 0; s < nsel; ++s) {
+            int e = s < k ? idx[t * k + s] : (int)(n_routed + (s - k));
+            if (s < k) e = e < 0 ? 0 : (e >= (int)n_routed ? (int)n_routed - 1 : e);
+            sel[s] = e;
+            wsel[s] = s < k ? (gate ? gate[t * k + s] : 1.0f) : 1.0f;
+            for (int j = 0; j < 16; ++j) {
+                size_t row = (size_t)e * 16 + j;
+                const uint8_t* pg = (const uint8_t*)wg + row * rb;
+                const uint8_t* pu = (const uint8_t*)wu + row * rb;
+                hv[s * 32 + j] = lane_tree_dot(fmt, xq, xs, pg, sg + row * (D / 32), D, 0);
+                hv[s * 32 + 16 + j] = lane_tree_dot(fmt, xq, xs, pu, su + row * (D / 32), D, 0);
+            }
+        }
+        size_t nb = 0;
+        for (size_t s = 0; s < nsel; ++s) {
+            int b = sel[s] >> 1;
+            size_t pos = 0;
+            while (pos < nb && blk[pos] < b) ++pos;
+            if (pos < nb && blk[pos] == b) continue;
+            for (size_t q = nb; q > pos; --q) blk[q] = blk[q - 1];
+            blk[pos] = b;
+            ++nb;
+        }
+        for (size_t i = 0; i < nb; ++i) {
+            for (int l = 0; l < 32; ++l) {
+                int e = blk[i] * 2 + (l >> 4), slot = l & 15;
+                float v = 0.0f;
+                for (size_t s = 0; s < nsel; ++s)
+                    if (sel[s] == e) v = (mxo_silu(hv[s * 32 + slot]) * hv[s * 32 + 16 + slot]) * wsel[s];
+                blkv[l] = v;
+            }
+            mxo_quantize_x(blkv, 1, 32, 0, hq + i * 32, hs + i);
+        }
+        for (size_t j = 0; j < D; ++j) {
+            float acc = 0.0f;
+            for (size_t i = 0; i < nb; ++i) {
+                int32_t d = 0;
+                for (int l = 0; l < 32; ++l)
+                    d += ((int32_t)hq[i * 32 + l] - 128) * mxo_weight_at(fmt, wd, KD, j, (size_t)blk[i] * 32 + l);
+                acc = acc + ((float)d * e8m0_f32(hs[i])) * e8m0_f32(sd[j * (KD / 32) + blk[i]]);
+            }
+            y[t * D + j] = acc;
+        }
+    }
+    free(xq); free(xs); free(hv); free(sel); free(wsel); free(blk); free(hq); free(hs);
+}
+
 /* splitmix64 finaliser (the router's hyperplane and code generator) */
 static uint64_t mix64(uint64_t z)
 {

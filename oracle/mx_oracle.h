@@ -106,6 +106,12 @@ void mxo_halting_step(int fmt, const uint8_t* xq, const uint8_t* xs, const void*
                       const uint8_t* ws, size_t B, size_t K, float bias, float eps,
                       float* p_sum, float* remainder, uint64_t* steps, float* p, uint8_t* halt);
 
+/* The micro-expert pool (nn/config/model_config.hpp:23-25) as the library
+ * states it (mxq_micro_moe), in the GPU's operation order. */
+void mxo_micro_moe(int fmt, const void* wg, const uint8_t* sg, const void* wu, const uint8_t* su,
+                   const void* wd, const uint8_t* sd, size_t n_routed, size_t n_shared, size_t D,
+                   const float* x, const int32_t* idx, const float* gate, size_t T, size_t k, float* y);
+
 /* mx_update_gaussian_moment (nn/tests/test_auto_generated.cpp:49;
  * research_paper/MATH_FOUNDATIONS.md:33-40) as the library states it:
  * w = clamp(rint(w + ((step * g[n]) * x[k]) * 2^-e), lo, hi), scales kept. */

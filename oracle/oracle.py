@@ -141,6 +141,22 @@ def update_gaussian_moment(fmt, data, scales, g, x, step):
     return out
 
 
+def micro_moe(fmt, wg, sg, wu, su, wd, sd, n_routed, n_shared, x, idx, gate):
+    """The micro-expert layer (mxo_micro_moe); idx/gate [T][k] (gate may be
+    None = 1)."""
+    x = np.ascontiguousarray(x, np.float32)
+    t, d = x.shape
+    idx = np.ascontiguousarray(idx, np.int32)
+    k = idx.shape[1] if idx.ndim == 2 else 0
+    y = np.empty((t, d), np.float32)
+    g = None if gate is None else np.ascontiguousarray(gate, np.float32)
+    c = lambda a: np.ascontiguousarray(a)
+    lib().mxo_micro_moe(ctypes.c_int(fmt), _p(c(wg)), _p(c(sg)), _p(c(wu)), _p(c(su)), _p(c(wd)), _p(c(sd)),
+                        *_sz(n_routed, n_shared, d), _p(x), _p(idx), _p(g) if g is not None else None,
+                        *_sz(t, k), _p(y))
+    return y
+
+
 def activation_norm(xq, xs):
     xq = np.ascontiguousarray(xq, np.uint8)
     b, k = xq.shape

@@ -222,3 +222,39 @@ def test_activation_norm_bit_exact(ctx, b, k):
     assert np.array_equal(nrm, oracle.activation_norm(xq, xs))
     deq = (xq.astype(np.float64) - 128) * np.exp2(xs.astype(np.float64) - 127).repeat(32, axis=1)
     assert np.allclose(nrm, np.linalg.norm(deq, axis=1), rtol=1e-6)
+
+
+# ---------------------------------------------------- micro-expert pool ---
+@pytest.mark.parametrize("fmt,router", [(4, "logits"), (8, "hashed")])
+def test_micro_moe_reference_shape_bit_exact(ctx, fmt, router):
+    """The reference's expert pool shape (nn/config/model_config.hpp:23-25):
+    1024 routed 16-row experts, top-16, 2 shared, d 2048; routing by softmax
+    top-k over logits or by the LSH HashedRouter (unit weights).  The layer is
+    bit-identical to the oracle's restatement of its operation order."""
+    E, S, D, K, T = 1024, 2, 2048, 16, 24
+    wg, sg = synth.weights(fmt, (E + S) * 16, D, -9, -6, 71)
+    wu, su = synth.weights(fmt, (E + S) * 16, D, -9, -6, 72)
+    wd, sd = synth.weights(fmt, D, (E + S) * 16, -9, -6, 73)
+    Wg, Wu, Wd = (mx.MXWeight(torch.from_numpy(a), torch.from_numpy(b), fmt, n, k, ctx)
+                  for a, b, n, k in ((wg, sg, (E + S) * 16, D), (wu, su, (E + S) * 16, D), (wd, sd, D, (E + S) * 16)))
+    x = synth.normal((T, D), 74)
+    if router == "logits":
+        logits = synth.normal((T, E), 75)
+        idx_d, gate_d = mx.route_topk(cuda(logits), K, ctx)
+        i0, g0 = oracle.route_topk(logits, K)
+        assert np.array_equal(host(idx_d), i0) and np.array_equal(host(gate_d), g0)
+    else:
+        idx_d, _ = mx.HashedRouter(D, E, K, 16, seed=5).route(cuda(x), ctx)
+        gate_d, g0 = None, None
+        i0, _ = oracle.hashed_route(x, E, K, 16, 5)
+        assert np.array_equal(host(idx_d), i0)
+    y = host(mx.micro_moe(cuda(x), Wg, Wu, Wd, E, S, idx_d, gate_d, ctx))
+    ctx.synchronize()
+    ref = oracle.micro_moe(fmt, wg, sg, wu, su, wd, sd, E, S, x, i0, g0)
+    assert np.all(np.isfinite(y)) and np.linalg.norm(y) > 0
+    assert np.array_equal(y, ref)
+    with pytest.raises(ValueError):                       # top-k beyond the pool
+        mx.micro_moe(cuda(x), Wg, Wu, Wd, 8, E + S - 8, cuda(np.zeros((T, 9), np.int32)), None, ctx)
+    ctx.synchronize()
+    for W in (Wg, Wu, Wd):
+        W.close()
