@@ -38,6 +38,7 @@ SIGNATURES = {
     "mxq_set_stream": [_vp, _vp],
     "mxq_set_path": [_vp, _i],
     "mxq_reserve": [_vp, _sz, _sz],
+    "mxq_set_fused_pair": [_vp, _i],
     "mxq_synchronize": [_vp],
     "mxq_last_error": [_vp],
     "mxq_launch_count": [_vp, ctypes.POINTER(ctypes.c_uint64)],

@@ -20,6 +20,7 @@ struct mxq_context {
   int device = 0;
   cudaStream_t stream = nullptr;
   int path = MXQ_PATH_AUTO;
+  bool fused_pair = false;     // batch-1 pairs as one kernel (mxq_set_fused_pair)
   uint32_t* status = nullptr;  // device status word; status[1..2]: the pair kernel's grid barrier
   uint32_t* status_host = nullptr;  // pinned mirror, read after one stream sync
   uint64_t launches = 0;
@@ -622,6 +623,12 @@ int mxq_set_path(mxq_ctx c, int path) {
   return MXQ_OK;
 }
 
+int mxq_set_fused_pair(mxq_ctx c, int on) {
+  if (int rc = check_ctx(c)) return rc;
+  c->fused_pair = on != 0;
+  return MXQ_OK;
+}
+
 int mxq_launch_count(mxq_ctx c, uint64_t* out) {
   if (int rc = check_ctx(c)) return rc;
   if (!out) return fail(c, MXQ_ERR_INVALID_ARGUMENT, "null output pointer");
@@ -1068,7 +1075,7 @@ int mxq_linear_pair(mxq_ctx c, mxq_weight w1, mxq_weight w2, const float* x,
     int rc;
     if ((rc = ensure(c, c->ws_f0, c->ws_f0_bytes, b * w1->v.N * 4, "workspace mid"))) return rc;
     if (use_gemv(c, b, w1) && use_gemv(c, b, w2)) {
-      if (b == 1 && pair_supported(w1->v, w2->v)) {
+      if (b == 1 && c->fused_pair && pair_supported(w1->v, w2->v)) {
         // batch 1: both projections in one kernel, every weight byte of the
         // pair in flight from its start
         PairArgs pa{};

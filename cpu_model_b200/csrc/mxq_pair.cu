@@ -247,10 +247,11 @@ __device__ __forceinline__ void fold_store(float (&acc)[kGB], int lane, int warp
 }
 
 // Grid-wide barrier on {count, flag} (one launch at a time per context):
-// the last CTA to arrive resets the count and advances the flag; the others
-// poll the flag with a time limit.  Returns false (status set) on timeout.
+// the CTA's stores are ordered before its thread 0 by the CTA barrier; thread
+// 0 fences and arrives; the last CTA to arrive resets the count and advances
+// the flag; the others poll the flag with a time limit.  Returns false
+// (status set) on timeout.  `arrive` false (test hook) skips the arrival.
 __device__ bool grid_barrier(uint32_t* bar, uint32_t nctas, uint32_t* status, uint64_t lim, bool arrive) {
-  __threadfence();                      // this thread's y1 stores, device-wide
   __syncthreads();
   __shared__ int ok_s;
   if (threadIdx.x == 0) {
@@ -267,8 +268,7 @@ __device__ bool grid_barrier(uint32_t* bar, uint32_t nctas, uint32_t* status, ui
       const uint64_t t0 = globaltimer_ns();
       for (uint32_t it = 0;; ++it) {
         if (ld_acquire(flag) != gen) break;
-        __nanosleep(64);
-        if ((it & 63u) == 63u && globaltimer_ns() - t0 > lim) {
+        if ((it & 15u) == 15u && globaltimer_ns() - t0 > lim) {
           atomicOr(status, kStatusTimeout);
           ok = 0;
           break;

@@ -98,6 +98,14 @@ MXQ_API int mxq_set_stream(mxq_ctx ctx, void* cuda_stream);
  * kernel, 3-8 int8-MMA kernel where it fits, register-blocked otherwise) and
  * batch <= 16 where the int8-MMA kernel fits the shape. */
 MXQ_API int mxq_set_path(mxq_ctx ctx, int path);
+/* Batch-1 mxq_linear_pair / _host as ONE kernel (on != 0): each CTA issues
+ * both projections' weight shares (the first into registers, the second into
+ * shared memory) before waiting, and a bounded grid-wide barrier separates
+ * the projections.  Bit-identical to the default two launches; off by
+ * default, as it measured slower on the 7B MLP pair (about 20 us against
+ * 18.4 us: the phases after the weights land -- compute, barrier, the
+ * intermediate's requantisation, compute -- run one after another). */
+MXQ_API int mxq_set_fused_pair(mxq_ctx ctx, int on);
 MXQ_API int mxq_reserve(mxq_ctx ctx, size_t max_batch, size_t max_k);
 MXQ_API int mxq_synchronize(mxq_ctx ctx);
 MXQ_API const char* mxq_last_error(mxq_ctx ctx);

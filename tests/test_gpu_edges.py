@@ -169,11 +169,15 @@ def test_pair_barrier_timeout_is_reported_and_context_recovers(ctx):
     rc = ctx.lib.mxq_debug_pair_stall(ctx.h, W1.h, W2.h, mx._ptr(x), mx._ptr(y), 2000)
     assert rc == _lib.MXQ_ERR_TIMEOUT, rc
     ctx.synchronize()
-    for _ in range(2):
-        yp = host(mx.mx_linear_pair(x, W1, W2, ctx))
-        y1 = mx.mx_linear(x, W1, ctx)
-        y2 = host(mx.mx_linear(y1, W2, ctx))
-        ctx.synchronize()
-        assert np.array_equal(yp, y2)
+    ctx.set_fused_pair(True)
+    try:
+        for _ in range(2):
+            yp = host(mx.mx_linear_pair(x, W1, W2, ctx))
+            y1 = mx.mx_linear(x, W1, ctx)
+            y2 = host(mx.mx_linear(y1, W2, ctx))
+            ctx.synchronize()
+            assert np.array_equal(yp, y2)
+    finally:
+        ctx.set_fused_pair(False)
     W1.close()
     W2.close()
