@@ -32,7 +32,7 @@ struct mxq_decoder_s {
   std::vector<mxq_weight> qkv, o, gu, down;
   mxq_weight lm = nullptr;
   float* embed = nullptr;      // [V][d]
-  float* gains = nullptr;      // [2L + 1][d]: attention, MLP, final RMSNorm weights
+  float* gains = nullptr;      // [2L + 1][d]: per layer the attention then the MLP RMSNorm weights, then the final
   float* cs = nullptr;         // [Cmax][hd/2][2] rotary cos, sin
   __nv_bfloat16* kc = nullptr; // [L][Bmax][H][Cmax][hd]
   __nv_bfloat16* vc = nullptr;
@@ -120,7 +120,9 @@ int layers(mxq_decoder_s* D, int B, int T, int pos0, bool decode) {
     __nv_bfloat16* kc = D->kc + (size_t)l * kv_layer_elems(D);
     __nv_bfloat16* vc = D->vc + (size_t)l * kv_layer_elems(D);
     if ((rc = trace_copy(D, l, MXQ_TRACE_IN, D->h, (size_t)R * d))) return rc;
-    if ((rc = dcheck(D, dk_rmsnorm(D->h, D->gains + (size_t)(2 * l) * d, R, d, eps, D->hn, st), "rmsnorm"))) return rc;
+    // layer 0 normalises the embeddings; later layers received D->hn from the
+    // previous layer's fused residual + RMSNorm
+    if (l == 0 && (rc = dcheck(D, dk_rmsnorm(D->h, D->gains, R, d, eps, D->hn, st), "rmsnorm"))) return rc;
     if ((rc = trace_copy(D, l, MXQ_TRACE_NORM1, D->hn, (size_t)R * d))) return rc;
     if ((rc = mxq_linear(c, D->qkv[l], D->hn, (size_t)R, D->qkvb))) return rc;
     if ((rc = trace_copy(D, l, MXQ_TRACE_QKV, D->qkvb, (size_t)R * 3 * d))) return rc;
@@ -139,20 +141,22 @@ int layers(mxq_decoder_s* D, int B, int T, int pos0, bool decode) {
     }
     if ((rc = trace_copy(D, l, MXQ_TRACE_ATT, D->att, (size_t)R * d))) return rc;
     if ((rc = mxq_linear(c, D->o[l], D->att, (size_t)R, D->tmp))) return rc;
-    if ((rc = dcheck(D, dk_add(D->h, D->tmp, (size_t)R * d, st), "residual"))) return rc;
-    if ((rc = trace_copy(D, l, MXQ_TRACE_H1, D->h, (size_t)R * d))) return rc;
-    if ((rc = dcheck(D, dk_rmsnorm(D->h, D->gains + (size_t)(2 * l + 1) * d, R, d, eps, D->hn, st), "rmsnorm")))
+    if ((rc = dcheck(D, dk_add_rmsnorm(D->h, D->tmp, D->gains + (size_t)(2 * l + 1) * d, R, d, eps, D->hn, st),
+                     "residual + rmsnorm")))
       return rc;
+    if ((rc = trace_copy(D, l, MXQ_TRACE_H1, D->h, (size_t)R * d))) return rc;
     if ((rc = trace_copy(D, l, MXQ_TRACE_NORM2, D->hn, (size_t)R * d))) return rc;
     if ((rc = mxq_linear(c, D->gu[l], D->hn, (size_t)R, D->gub))) return rc;
     if ((rc = trace_copy(D, l, MXQ_TRACE_GU, D->gub, (size_t)R * 2 * D->F))) return rc;
     if ((rc = dcheck(D, dk_swiglu(D->gub, R, D->F, D->act, st), "swiglu"))) return rc;
     if ((rc = mxq_linear(c, D->down[l], D->act, (size_t)R, D->tmp))) return rc;
-    if ((rc = dcheck(D, dk_add(D->h, D->tmp, (size_t)R * d, st), "residual"))) return rc;
+    // residual, then the next layer's (or the final) RMSNorm, in one kernel
+    if ((rc = dcheck(D, dk_add_rmsnorm(D->h, D->tmp, D->gains + (size_t)(2 * l + 2) * d, R, d, eps, D->hn, st),
+                     "residual + rmsnorm")))
+      return rc;
     if ((rc = trace_copy(D, l, MXQ_TRACE_OUT, D->h, (size_t)R * d))) return rc;
   }
-  if ((rc = trace_copy(D, D->L, MXQ_TRACE_IN, D->h, (size_t)R * d))) return rc;
-  return dcheck(D, dk_rmsnorm(D->h, D->gains + (size_t)(2 * D->L) * d, R, d, eps, D->hn, st), "rmsnorm");
+  return trace_copy(D, D->L, MXQ_TRACE_IN, D->h, (size_t)R * d);
 }
 
 // logits of rows `hrows` [B][d] -> user [B][V] (the value row, if any, dropped)

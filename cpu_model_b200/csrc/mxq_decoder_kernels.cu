@@ -14,9 +14,18 @@ namespace mxq {
 
 namespace {
 
+// Every kernel here waits for its predecessor's results (programmatic
+// dependent launch) and lets its own dependents launch at once: the MX
+// linear that follows streams its weights while this kernel runs, and reads
+// this kernel's output only after its own wait.
+#define DK_PDL_PROLOGUE()                                   \
+  asm volatile("griddepcontrol.wait;" ::: "memory");        \
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory")
+
 // ------------------------------------------------------------ embedding ---
 __global__ void embed_kernel(const int32_t* __restrict__ tok, const float* __restrict__ table, int R, int d,
                              int vocab, float* __restrict__ h) {
+  DK_PDL_PROLOGUE();
   const int r = blockIdx.x;
   if (r >= R) return;
   int t = tok[r];
@@ -30,6 +39,7 @@ __global__ void embed_kernel(const int32_t* __restrict__ tok, const float* __res
 // One CTA of 256 threads per row; the square sum in a fixed tree.
 __global__ void __launch_bounds__(256) rmsnorm_kernel(const float* __restrict__ x, const float* __restrict__ g,
                                                       int d, float eps, float* __restrict__ y) {
+  DK_PDL_PROLOGUE();
   __shared__ float ws[8];
   const int r = blockIdx.x;
   const float* xr = x + (size_t)r * d;
@@ -47,8 +57,37 @@ __global__ void __launch_bounds__(256) rmsnorm_kernel(const float* __restrict__ 
   for (int i = threadIdx.x; i < d; i += 256) yr[i] = __fmul_rn(__fmul_rn(xr[i], inv), g[i]);
 }
 
+// Residual add fused with the next RMSNorm: h += y, then out = RMSNorm(h)
+// (the same arithmetic as add_kernel followed by rmsnorm_kernel).
+__global__ void __launch_bounds__(256) add_rmsnorm_kernel(float* __restrict__ h, const float* __restrict__ y,
+                                                          const float* __restrict__ g, int d, float eps,
+                                                          float* __restrict__ out) {
+  DK_PDL_PROLOGUE();
+  __shared__ float ws[8];
+  const int r = blockIdx.x;
+  float* hr = h + (size_t)r * d;
+  const float* yr = y + (size_t)r * d;
+  float s = 0.0f;
+  for (int i = threadIdx.x; i < d; i += 256) {
+    const float v = __fadd_rn(hr[i], yr[i]);
+    hr[i] = v;
+    s = __fmaf_rn(v, v, s);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) s = __fadd_rn(s, __shfl_xor_sync(0xffffffffu, s, o));
+  if ((threadIdx.x & 31) == 0) ws[threadIdx.x >> 5] = s;
+  __syncthreads();
+  float tot = 0.0f;
+#pragma unroll
+  for (int w = 0; w < 8; ++w) tot = __fadd_rn(tot, ws[w]);
+  const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(tot, (float)d), eps)));
+  float* o = out + (size_t)r * d;
+  for (int i = threadIdx.x; i < d; i += 256) o[i] = __fmul_rn(__fmul_rn(hr[i], inv), g[i]);
+}
+
 // ----------------------------------------------------------- residual ---
 __global__ void add_kernel(float* __restrict__ h, const float* __restrict__ y, size_t n4) {
+  DK_PDL_PROLOGUE();
   for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += (size_t)gridDim.x * blockDim.x) {
     float4 a = reinterpret_cast<float4*>(h)[i];
     const float4 b = reinterpret_cast<const float4*>(y)[i];
@@ -63,6 +102,7 @@ __global__ void add_kernel(float* __restrict__ h, const float* __restrict__ y, s
 // ------------------------------------------------------------- SwiGLU ---
 // gu [R][2F] holds gate | up; act [R][F] = silu(gate) * up.
 __global__ void swiglu_kernel(const float* __restrict__ gu, int R, int F, float* __restrict__ act) {
+  DK_PDL_PROLOGUE();
   const size_t n = (size_t)R * F;
   for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
     const size_t r = i / F, j = i % F;
@@ -79,6 +119,7 @@ __global__ void swiglu_kernel(const float* __restrict__ gu, int R, int F, float*
 __global__ void rope_kv_kernel(float* __restrict__ qkv, int T, int d, int H, int hd, int pos0,
                                const int32_t* __restrict__ pos_dev, const float* __restrict__ cs, int max_ctx,
                                __nv_bfloat16* __restrict__ kc, __nv_bfloat16* __restrict__ vc, int R) {
+  DK_PDL_PROLOGUE();
   const int half = hd / 2;
   const long total = (long)R * H * half;
   const int p0 = pos_dev ? *pos_dev : pos0;
@@ -117,6 +158,7 @@ __global__ void __launch_bounds__(256) attn_prompt_kernel(const float* __restric
                                                           int pos0, const __nv_bfloat16* __restrict__ kc,
                                                           const __nv_bfloat16* __restrict__ vc, int max_ctx,
                                                           float scale, float* __restrict__ att) {
+  DK_PDL_PROLOGUE();
   extern __shared__ __align__(16) float sm[];
   float* Qt = sm;                          // [hd][kQB]      queries, transposed, pre-scaled
   float* Kt = Qt + kHD * kQB;              // [hd][kKB + 4]  keys, transposed
@@ -246,6 +288,7 @@ __global__ void __launch_bounds__(128) attn_decode_kernel(const float* __restric
                                                           const __nv_bfloat16* __restrict__ kc,
                                                           const __nv_bfloat16* __restrict__ vc, int max_ctx,
                                                           float scale, int nch, float* __restrict__ part) {
+  DK_PDL_PROLOGUE();
   __shared__ float q[kHD];
   __shared__ float p[kDC];
   __shared__ float red[4];
@@ -303,6 +346,7 @@ __global__ void __launch_bounds__(128) attn_decode_kernel(const float* __restric
 
 __global__ void attn_combine_kernel(const float* __restrict__ part, int H, int nch, const int32_t* __restrict__ pos_dev,
                                     int d, float* __restrict__ att) {
+  DK_PDL_PROLOGUE();
   const int h = blockIdx.x, b = blockIdx.y, tid = threadIdx.x;
   const int used = (*pos_dev + 1 + kDC - 1) / kDC;
   const float* pp = part + ((size_t)b * H + h) * nch * (kHD + 2);
@@ -318,6 +362,7 @@ __global__ void attn_combine_kernel(const float* __restrict__ part, int H, int n
 }
 
 __global__ void pos_advance_kernel(int32_t* pos, int by) {
+  DK_PDL_PROLOGUE();
   if (threadIdx.x == 0 && blockIdx.x == 0) *pos += by;
 }
 
@@ -328,6 +373,7 @@ __global__ void pos_advance_kernel(int32_t* pos, int by) {
 __global__ void __launch_bounds__(256) logprob_kernel(const float* __restrict__ logits, int ld, int V,
                                                       const int32_t* __restrict__ target,
                                                       float* __restrict__ logp) {
+  DK_PDL_PROLOGUE();
   __shared__ float red[8];
   const int r = blockIdx.x, tid = threadIdx.x;
   const float* x = logits + (size_t)r * ld;
@@ -359,12 +405,14 @@ __global__ void __launch_bounds__(256) logprob_kernel(const float* __restrict__ 
 
 // column `col` of a [R][ld] matrix -> out [R]
 __global__ void column_kernel(const float* __restrict__ x, int R, int ld, int col, float* __restrict__ out) {
+  DK_PDL_PROLOGUE();
   const int r = blockIdx.x * blockDim.x + threadIdx.x;
   if (r < R) out[r] = x[(size_t)r * ld + col];
 }
 
 // rows r * T + T - 1 (the last token of each sequence) of x [B*T][n] -> y [B][n]
 __global__ void last_rows_kernel(const float* __restrict__ x, int B, int T, int n, float* __restrict__ y) {
+  DK_PDL_PROLOGUE();
   const int b = blockIdx.y;
   for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x)
     y[(size_t)b * n + i] = x[((size_t)b * T + T - 1) * n + i];
@@ -410,6 +458,23 @@ __global__ void fill_kernel(float* __restrict__ out, size_t n, float v) {
   for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) out[i] = v;
 }
 
+// <<<grid, block, smem, stream>>> with the programmatic-dependent-launch
+// attribute.
+template <typename... P, typename... A>
+cudaError_t pdl_launch(void (*k)(P...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, A... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, k, static_cast<P>(args)...);
+}
+
 unsigned grid_for(size_t n, unsigned threads) {
   size_t g = (n + threads - 1) / threads;
   if (g > 148u * 32u) g = 148u * 32u;
@@ -420,26 +485,26 @@ unsigned grid_for(size_t n, unsigned threads) {
 
 // ------------------------------------------------------------ launchers ---
 cudaError_t dk_embed(const int32_t* tok, const float* table, int R, int d, int vocab, float* h, cudaStream_t s) {
-  embed_kernel<<<R, 256, 0, s>>>(tok, table, R, d, vocab, h);
-  return cudaGetLastError();
+  return pdl_launch(embed_kernel, dim3(R), dim3(256), 0, s, tok, table, R, d, vocab, h);
 }
 cudaError_t dk_rmsnorm(const float* x, const float* g, int R, int d, float eps, float* y, cudaStream_t s) {
-  rmsnorm_kernel<<<R, 256, 0, s>>>(x, g, d, eps, y);
-  return cudaGetLastError();
+  return pdl_launch(rmsnorm_kernel, dim3(R), dim3(256), 0, s, x, g, d, eps, y);
 }
 cudaError_t dk_add(float* h, const float* y, size_t n, cudaStream_t s) {
-  add_kernel<<<grid_for(n / 4, 256), 256, 0, s>>>(h, y, n / 4);
-  return cudaGetLastError();
+  return pdl_launch(add_kernel, dim3(grid_for(n / 4, 256)), dim3(256), 0, s, h, y, n / 4);
+}
+cudaError_t dk_add_rmsnorm(float* h, const float* y, const float* g, int R, int d, float eps, float* out,
+                           cudaStream_t s) {
+  return pdl_launch(add_rmsnorm_kernel, dim3(R), dim3(256), 0, s, h, y, g, d, eps, out);
 }
 cudaError_t dk_swiglu(const float* gu, int R, int F, float* act, cudaStream_t s) {
-  swiglu_kernel<<<grid_for((size_t)R * F, 256), 256, 0, s>>>(gu, R, F, act);
-  return cudaGetLastError();
+  return pdl_launch(swiglu_kernel, dim3(grid_for((size_t)R * F, 256)), dim3(256), 0, s, gu, R, F, act);
 }
 cudaError_t dk_rope_kv(float* qkv, int R, int T, int d, int H, int pos0, const int32_t* pos_dev, const float* cs,
                        int max_ctx, __nv_bfloat16* kc, __nv_bfloat16* vc, cudaStream_t s) {
   const size_t n = (size_t)R * H * (d / H / 2);
-  rope_kv_kernel<<<grid_for(n, 256), 256, 0, s>>>(qkv, T, d, H, d / H, pos0, pos_dev, cs, max_ctx, kc, vc, R);
-  return cudaGetLastError();
+  return pdl_launch(rope_kv_kernel, dim3(grid_for(n, 256)), dim3(256), 0, s, qkv, T, d, H, d / H, pos0, pos_dev, cs,
+                    max_ctx, kc, vc, R);
 }
 size_t dk_attn_prompt_smem() {
   return (size_t)(kHD * kQB + kHD * (kKB + 4) + kKB * kHD + kQB * (kKB + 4)) * sizeof(float);
@@ -450,35 +515,30 @@ cudaError_t dk_attn_prompt(const float* qkv, int B, int T, int d, int H, int pos
   const size_t smem = dk_attn_prompt_smem();
   if (cudaError_t e = smem_attr.ensure(attn_prompt_kernel, smem)) return e;
   const dim3 grid((unsigned)((T + kQB - 1) / kQB), (unsigned)H, (unsigned)B);
-  attn_prompt_kernel<<<grid, 256, smem, s>>>(qkv, T, d, H, pos0, kc, vc, max_ctx, 1.0f / sqrtf((float)kHD), att);
-  return cudaGetLastError();
+  return pdl_launch(attn_prompt_kernel, grid, dim3(256), smem, s, qkv, T, d, H, pos0, kc, vc, max_ctx,
+                    1.0f / sqrtf((float)kHD), att);
 }
 int dk_decode_chunks(int max_ctx) { return (max_ctx + kDC - 1) / kDC; }
 cudaError_t dk_attn_decode(const float* qkv, int B, int d, int H, const int32_t* pos_dev, const __nv_bfloat16* kc,
                            const __nv_bfloat16* vc, int max_ctx, float* part, float* att, cudaStream_t s) {
   const int nch = dk_decode_chunks(max_ctx);
-  attn_decode_kernel<<<dim3((unsigned)nch, (unsigned)H, (unsigned)B), 128, 0, s>>>(
-      qkv, d, H, pos_dev, kc, vc, max_ctx, 1.0f / sqrtf((float)kHD), nch, part);
-  cudaError_t e = cudaGetLastError();
+  cudaError_t e = pdl_launch(attn_decode_kernel, dim3((unsigned)nch, (unsigned)H, (unsigned)B), dim3(128), 0, s,
+                             qkv, d, H, pos_dev, kc, vc, max_ctx, 1.0f / sqrtf((float)kHD), nch, part);
   if (e != cudaSuccess) return e;
-  attn_combine_kernel<<<dim3((unsigned)H, (unsigned)B), kHD, 0, s>>>(part, H, nch, pos_dev, d, att);
-  return cudaGetLastError();
+  return pdl_launch(attn_combine_kernel, dim3((unsigned)H, (unsigned)B), dim3(kHD), 0, s, part, H, nch, pos_dev, d,
+                    att);
 }
 cudaError_t dk_pos_advance(int32_t* pos, int by, cudaStream_t s) {
-  pos_advance_kernel<<<1, 32, 0, s>>>(pos, by);
-  return cudaGetLastError();
+  return pdl_launch(pos_advance_kernel, dim3(1), dim3(32), 0, s, pos, by);
 }
 cudaError_t dk_logprob(const float* logits, int R, int ld, int V, const int32_t* target, float* logp, cudaStream_t s) {
-  logprob_kernel<<<R, 256, 0, s>>>(logits, ld, V, target, logp);
-  return cudaGetLastError();
+  return pdl_launch(logprob_kernel, dim3(R), dim3(256), 0, s, logits, ld, V, target, logp);
 }
 cudaError_t dk_column(const float* x, int R, int ld, int col, float* out, cudaStream_t s) {
-  column_kernel<<<(R + 255) / 256, 256, 0, s>>>(x, R, ld, col, out);
-  return cudaGetLastError();
+  return pdl_launch(column_kernel, dim3((R + 255) / 256), dim3(256), 0, s, x, R, ld, col, out);
 }
 cudaError_t dk_last_rows(const float* x, int B, int T, int n, float* y, cudaStream_t s) {
-  last_rows_kernel<<<dim3((unsigned)((n + 255) / 256), (unsigned)B), 256, 0, s>>>(x, B, T, n, y);
-  return cudaGetLastError();
+  return pdl_launch(last_rows_kernel, dim3((unsigned)((n + 255) / 256), (unsigned)B), dim3(256), 0, s, x, B, T, n, y);
 }
 cudaError_t dk_synth_weight(uint8_t* data, size_t data_bytes, uint8_t* scales, size_t nscales, int fmt, int emin,
                             int emax, uint64_t seed, cudaStream_t s) {

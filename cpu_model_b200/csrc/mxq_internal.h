@@ -159,6 +159,8 @@ const WeightView* weight_view(mxq_weight w);
 cudaError_t dk_embed(const int32_t* tok, const float* table, int R, int d, int vocab, float* h, cudaStream_t s);
 cudaError_t dk_rmsnorm(const float* x, const float* g, int R, int d, float eps, float* y, cudaStream_t s);
 cudaError_t dk_add(float* h, const float* y, size_t n, cudaStream_t s);
+cudaError_t dk_add_rmsnorm(float* h, const float* y, const float* g, int R, int d, float eps, float* out,
+                           cudaStream_t s);
 cudaError_t dk_swiglu(const float* gu, int R, int F, float* act, cudaStream_t s);
 cudaError_t dk_rope_kv(float* qkv, int R, int T, int d, int H, int pos0, const int32_t* pos_dev, const float* cs,
                        int max_ctx, __nv_bfloat16* kc, __nv_bfloat16* vc, cudaStream_t s);
