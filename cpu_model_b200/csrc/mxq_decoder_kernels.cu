@@ -36,53 +36,68 @@ __global__ void embed_kernel(const int32_t* __restrict__ tok, const float* __res
 }
 
 // --------------------------------------------------------------- RMSNorm ---
-// One CTA of 256 threads per row; the square sum in a fixed tree.
-__global__ void __launch_bounds__(256) rmsnorm_kernel(const float* __restrict__ x, const float* __restrict__ g,
-                                                      int d, float eps, float* __restrict__ y) {
-  DK_PDL_PROLOGUE();
-  __shared__ float ws[8];
-  const int r = blockIdx.x;
-  const float* xr = x + (size_t)r * d;
-  float s = 0.0f;
-  for (int i = threadIdx.x; i < d; i += 256) s = __fmaf_rn(xr[i], xr[i], s);
+// One CTA of 1024 threads per row, each thread a few float4 chunks held in
+// registers (one pass over memory), the square sum in a fixed tree: the
+// per-thread chunks in order, the 32 lanes by a xor-butterfly, the 32 warps
+// in order.  kNormVec chunks per thread cover d <= 16384.
+constexpr int kNormThreads = 1024, kNormVec = 4;
+
+__device__ __forceinline__ float norm_block_sum(float s, float* ws) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) s = __fadd_rn(s, __shfl_xor_sync(0xffffffffu, s, o));
   if ((threadIdx.x & 31) == 0) ws[threadIdx.x >> 5] = s;
   __syncthreads();
   float tot = 0.0f;
 #pragma unroll
-  for (int w = 0; w < 8; ++w) tot = __fadd_rn(tot, ws[w]);
-  const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(tot, (float)d), eps)));
-  float* yr = y + (size_t)r * d;
-  for (int i = threadIdx.x; i < d; i += 256) yr[i] = __fmul_rn(__fmul_rn(xr[i], inv), g[i]);
+  for (int w = 0; w < kNormThreads / 32; ++w) tot = __fadd_rn(tot, ws[w]);
+  return tot;
 }
 
-// Residual add fused with the next RMSNorm: h += y, then out = RMSNorm(h)
-// (the same arithmetic as add_kernel followed by rmsnorm_kernel).
-__global__ void __launch_bounds__(256) add_rmsnorm_kernel(float* __restrict__ h, const float* __restrict__ y,
-                                                          const float* __restrict__ g, int d, float eps,
-                                                          float* __restrict__ out) {
+// RESID: h += y first (written back), then out = RMSNorm(h) * g.
+template <bool RESID>
+__global__ void __launch_bounds__(kNormThreads) norm_kernel(float* __restrict__ h, const float* __restrict__ y,
+                                                            const float* __restrict__ g, int d, float eps,
+                                                            float* __restrict__ out) {
   DK_PDL_PROLOGUE();
-  __shared__ float ws[8];
-  const int r = blockIdx.x;
-  float* hr = h + (size_t)r * d;
-  const float* yr = y + (size_t)r * d;
+  __shared__ float ws[kNormThreads / 32];
+  const int r = blockIdx.x, d4 = d / 4;
+  float4* hr = reinterpret_cast<float4*>(h + (size_t)r * d);
+  const float4* yr = reinterpret_cast<const float4*>(y + (size_t)r * d);
+  float4 v[kNormVec];
   float s = 0.0f;
-  for (int i = threadIdx.x; i < d; i += 256) {
-    const float v = __fadd_rn(hr[i], yr[i]);
-    hr[i] = v;
-    s = __fmaf_rn(v, v, s);
+#pragma unroll
+  for (int u = 0; u < kNormVec; ++u) {
+    const int i = threadIdx.x + u * kNormThreads;
+    v[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (i < d4) {
+      v[u] = hr[i];
+      if (RESID) {
+        const float4 b = yr[i];
+        v[u].x = __fadd_rn(v[u].x, b.x);
+        v[u].y = __fadd_rn(v[u].y, b.y);
+        v[u].z = __fadd_rn(v[u].z, b.z);
+        v[u].w = __fadd_rn(v[u].w, b.w);
+        hr[i] = v[u];
+      }
+    }
+    s = __fmaf_rn(v[u].x, v[u].x, s);
+    s = __fmaf_rn(v[u].y, v[u].y, s);
+    s = __fmaf_rn(v[u].z, v[u].z, s);
+    s = __fmaf_rn(v[u].w, v[u].w, s);
   }
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) s = __fadd_rn(s, __shfl_xor_sync(0xffffffffu, s, o));
-  if ((threadIdx.x & 31) == 0) ws[threadIdx.x >> 5] = s;
-  __syncthreads();
-  float tot = 0.0f;
-#pragma unroll
-  for (int w = 0; w < 8; ++w) tot = __fadd_rn(tot, ws[w]);
+  const float tot = norm_block_sum(s, ws);
   const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(tot, (float)d), eps)));
-  float* o = out + (size_t)r * d;
-  for (int i = threadIdx.x; i < d; i += 256) o[i] = __fmul_rn(__fmul_rn(hr[i], inv), g[i]);
+  float4* o = reinterpret_cast<float4*>(out + (size_t)r * d);
+  const float4* g4 = reinterpret_cast<const float4*>(g);
+#pragma unroll
+  for (int u = 0; u < kNormVec; ++u) {
+    const int i = threadIdx.x + u * kNormThreads;
+    if (i < d4) {
+      const float4 gg = g4[i];
+      o[i] = make_float4(__fmul_rn(__fmul_rn(v[u].x, inv), gg.x), __fmul_rn(__fmul_rn(v[u].y, inv), gg.y),
+                         __fmul_rn(__fmul_rn(v[u].z, inv), gg.z), __fmul_rn(__fmul_rn(v[u].w, inv), gg.w));
+    }
+  }
 }
 
 // ----------------------------------------------------------- residual ---
@@ -488,14 +503,17 @@ cudaError_t dk_embed(const int32_t* tok, const float* table, int R, int d, int v
   return pdl_launch(embed_kernel, dim3(R), dim3(256), 0, s, tok, table, R, d, vocab, h);
 }
 cudaError_t dk_rmsnorm(const float* x, const float* g, int R, int d, float eps, float* y, cudaStream_t s) {
-  return pdl_launch(rmsnorm_kernel, dim3(R), dim3(256), 0, s, x, g, d, eps, y);
+  if (d % 4 || d / 4 > kNormThreads * kNormVec) return cudaErrorInvalidValue;
+  return pdl_launch(norm_kernel<false>, dim3(R), dim3(kNormThreads), 0, s, const_cast<float*>(x),
+                    static_cast<const float*>(nullptr), g, d, eps, y);
 }
 cudaError_t dk_add(float* h, const float* y, size_t n, cudaStream_t s) {
   return pdl_launch(add_kernel, dim3(grid_for(n / 4, 256)), dim3(256), 0, s, h, y, n / 4);
 }
 cudaError_t dk_add_rmsnorm(float* h, const float* y, const float* g, int R, int d, float eps, float* out,
                            cudaStream_t s) {
-  return pdl_launch(add_rmsnorm_kernel, dim3(R), dim3(256), 0, s, h, y, g, d, eps, out);
+  if (d % 4 || d / 4 > kNormThreads * kNormVec) return cudaErrorInvalidValue;
+  return pdl_launch(norm_kernel<true>, dim3(R), dim3(kNormThreads), 0, s, h, y, g, d, eps, out);
 }
 cudaError_t dk_swiglu(const float* gu, int R, int F, float* act, cudaStream_t s) {
   return pdl_launch(swiglu_kernel, dim3(grid_for((size_t)R * F, 256)), dim3(256), 0, s, gu, R, F, act);
