@@ -950,6 +950,42 @@ def run_ours(args):
         dist.destroy_process_group()
 
 
+def run_case(args):
+    """Small single-workload runs for profiling (ncu) on one GPU: a few
+    launches of one kernel family, nothing timed.
+      gemm512   3 up-projection linears at batch 512 (tcgen05 GEMM)
+      gemv1     3 up-projection linears at batch 1 (weight-resident GEMV)
+      moe       one full-size block-sparse MoE layer
+      decode7b  the 7B decoder: a 2048-token prompt, then 3 decode steps"""
+    import torch
+    from cpu_model_b200 import mx, synth
+    ctx = mx.MXContext(0)
+    if args.case in ("gemm512", "gemv1"):
+        b = 512 if args.case == "gemm512" else 1
+        wu, su = synth.weights(4, UP[0], UP[1], EMIN, EMAX, 1000)
+        W = mx.MXWeight(torch.from_numpy(wu), torch.from_numpy(su), 4, UP[0], UP[1], ctx)
+        x = torch.from_numpy(synth.normal((b, UP[1]), 9)).cuda()
+        for _ in range(3):
+            mx.mx_linear(x, W, ctx)
+        W.close()
+    elif args.case == "moe":
+        experts = moe_weights(ctx, torch.device("cuda", 0))
+        x = torch.from_numpy(synth.normal((MOE["tokens"], MOE["d"]), 201)).cuda()
+        logits = torch.from_numpy(synth.normal((MOE["tokens"], MOE["experts"]), 202)).cuda()
+        mx.moe_swiglu(x, logits, [m[0][0] for m in experts], [m[1][0] for m in experts],
+                      [m[2][0] for m in experts], MOE["top_k"], ctx)
+    elif args.case == "decode7b":
+        c = DEC7B
+        D = mx.Decoder(c["n_layers"], c["d_model"], c["n_heads"], c["ffn"], c["vocab"], fmt=4, max_batch=1,
+                       max_ctx=c["prompt"] + 8, max_rows=8192, seed=3, ctx=ctx)
+        D.prefill(torch.randint(0, c["vocab"], (1, c["prompt"]), dtype=torch.int32, device="cuda"))
+        for i in range(3):
+            D.decode(torch.full((1,), i, dtype=torch.int32, device="cuda"))
+        D.close()
+    ctx.synchronize()
+    print(json.dumps({"case": args.case, "ok": True}), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -967,10 +1003,14 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--copies", type=int, default=COPIES,
                     help="distinct weight-pair copies rotated per step (default 8 = 383 MB)")
+    ap.add_argument("--case", choices=["gemm512", "gemv1", "moe", "decode7b"],
+                    help="profiling: run one small workload (nothing timed) and exit")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
-    if args.impl == "reference":
+    if args.case:
+        run_case(args)
+    elif args.impl == "reference":
         run_reference(args)
     else:
         run_ours(args)
