@@ -41,6 +41,7 @@ struct mxq_decoder_s {
   float *h = nullptr, *hn = nullptr, *qkvb = nullptr, *att = nullptr, *tmp = nullptr, *gub = nullptr,
         *act = nullptr, *logits = nullptr, *part = nullptr, *hl = nullptr;
   int32_t* tok = nullptr;      // [Rmax + 1]
+  uint32_t* done = nullptr;    // [Bmax][H] one-token attention chunk counters (zero between calls)
   int trace_layer = -1;
   float* trace[MXQ_TRACE_COUNT] = {};
   size_t trace_elems[MXQ_TRACE_COUNT] = {};
@@ -131,10 +132,10 @@ int layers(mxq_decoder_s* D, int B, int T, int pos0, bool decode) {
       return rc;
     if ((rc = trace_copy(D, l, MXQ_TRACE_ROPE, D->qkvb, (size_t)R * 3 * d))) return rc;
     if (decode) {
-      if ((rc = dcheck(D, dk_attn_decode(D->qkvb, B, d, D->H, D->pos_dev, kc, vc, D->Cmax, D->part, D->att, st),
+      if ((rc = dcheck(D, dk_attn_decode(D->qkvb, B, d, D->H, D->pos_dev, kc, vc, D->Cmax, D->part, D->done,
+                                         D->att, st),
                        "attention")))
         return rc;
-      ctx_add_launches(c, 1);
     } else {
       if ((rc = dcheck(D, dk_attn_prompt(D->qkvb, B, T, d, D->H, pos0, kc, vc, D->Cmax, D->att, st), "attention")))
         return rc;
@@ -200,7 +201,7 @@ int mxq_decoder_destroy(mxq_decoder D) {
   if (D->lm) mxq_weight_destroy(D->lm);
   for (void* p : {(void*)D->embed, (void*)D->gains, (void*)D->cs, (void*)D->kc, (void*)D->vc, (void*)D->pos_dev,
                   (void*)D->h, (void*)D->hn, (void*)D->qkvb, (void*)D->att, (void*)D->tmp, (void*)D->gub,
-                  (void*)D->act, (void*)D->logits, (void*)D->part, (void*)D->hl, (void*)D->tok})
+                  (void*)D->act, (void*)D->logits, (void*)D->part, (void*)D->hl, (void*)D->tok, (void*)D->done})
     if (p) cudaFree(p);
   for (float* t : D->trace)
     if (t) cudaFree(t);
@@ -290,6 +291,8 @@ int mxq_decoder_create(mxq_ctx c, const mxq_decoder_config* cfg, uint64_t seed, 
     if (e == cudaSuccess) e = dalloc(D->hl, (size_t)D->Bmax * d);
     if (e == cudaSuccess) e = dalloc(D->part, (size_t)D->Bmax * D->H * D->nch * (128 + 2));
     if (e == cudaSuccess) e = dalloc(D->tok, R + 1);
+    if (e == cudaSuccess) e = dalloc(D->done, (size_t)D->Bmax * D->H);
+    if (e == cudaSuccess) e = cudaMemsetAsync(D->done, 0, (size_t)D->Bmax * D->H * 4 + 16, st);
     if (e == cudaSuccess) e = cudaMemsetAsync(D->tok, 0, (R + 1) * 4, st);
     if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&D->dstream, cudaStreamNonBlocking);
     if (e == cudaSuccess) e = cudaEventCreateWithFlags(&D->ev_in, cudaEventDisableTiming);
@@ -305,6 +308,7 @@ int mxq_decoder_reset(mxq_decoder D) {
   if (!D) return MXQ_ERR_INVALID_ARGUMENT;
   D->len = 0;
   cudaError_t e = cudaMemsetAsync(D->pos_dev, 0, 4, ctx_stream(D->c));
+  if (e == cudaSuccess) e = cudaMemsetAsync(D->done, 0, (size_t)D->Bmax * D->H * 4, ctx_stream(D->c));
   return e == cudaSuccess ? MXQ_OK : ctx_cuda_fail(D->c, e, "decoder reset");
 }
 

@@ -293,87 +293,119 @@ __global__ void __launch_bounds__(256) attn_prompt_kernel(const float* __restric
 
 // ------------------------------------------------- one-token attention ---
 // The new token of each sequence (position pos = *pos_dev) against keys
-// 0 .. pos, split into chunks of kDC keys: one CTA of 128 threads per
-// (chunk, head, sequence) writes (max, sum, o[hd]) for its chunk; a second
-// kernel combines the chunks in order.
+// 0 .. pos, split into chunks of kDC keys: one CTA of 256 threads per
+// (chunk, head, sequence).  Scores: one key per thread (its bf16 row in
+// 16-byte loads, q from shared memory).  Output: warp w takes keys 32w ..
+// 32w+31 of the chunk, lane l dims 4l .. 4l+3 (one 8-byte load per key, a
+// 256-byte row per warp and key), and the 8 warps' partial outputs are added
+// in warp order.  Each CTA writes (max, sum, o[hd]) for its chunk; the last
+// CTA of a (sequence, head) to finish (a counter, reset by that CTA) combines
+// the chunks in chunk order, so the result does not depend on which CTA it is.
 constexpr int kDC = 256;
 
-__global__ void __launch_bounds__(128) attn_decode_kernel(const float* __restrict__ qkv, int d, int H,
+__global__ void __launch_bounds__(256) attn_decode_kernel(const float* __restrict__ qkv, int d, int H,
                                                           const int32_t* __restrict__ pos_dev,
                                                           const __nv_bfloat16* __restrict__ kc,
                                                           const __nv_bfloat16* __restrict__ vc, int max_ctx,
-                                                          float scale, int nch, float* __restrict__ part) {
+                                                          float scale, int nch, float* __restrict__ part,
+                                                          uint32_t* __restrict__ done, float* __restrict__ att) {
   DK_PDL_PROLOGUE();
   __shared__ float q[kHD];
   __shared__ float p[kDC];
-  __shared__ float red[4];
-  const int ch = blockIdx.x, h = blockIdx.y, b = blockIdx.z, tid = threadIdx.x;
+  __shared__ float red[8];
+  __shared__ float4 po[8][kHD / 4];
+  __shared__ int last;
+  const int ch = blockIdx.x, h = blockIdx.y, b = blockIdx.z, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int nkeys = *pos_dev + 1;
+  const int used = (nkeys + kDC - 1) / kDC;
+  if (ch >= used) return;                               // chunk past the context (CTA-uniform)
   const int c0 = ch * kDC, c1 = c0 + kDC < nkeys ? c0 + kDC : nkeys;
   float* out = part + (((size_t)b * H + h) * nch + ch) * (kHD + 2);
-  if (c0 >= nkeys) {                      // chunk past the context: an empty partial
-    if (tid == 0) { out[0] = -3.402823466e38f; out[1] = 0.0f; }
-    out[2 + tid] = 0.0f;
-    return;
-  }
-  q[tid] = __fmul_rn(qkv[(size_t)b * 3 * d + h * kHD + tid], scale);
+  if (tid < kHD) q[tid] = __fmul_rn(qkv[(size_t)b * 3 * d + h * kHD + tid], scale);
   __syncthreads();
   const size_t cbase = ((size_t)b * H + h) * max_ctx * kHD;
-  float mx = -3.402823466e38f;
-  for (int c = c0 + tid; c < c1; c += 128) {
-    const __nv_bfloat16* kr = kc + cbase + (size_t)c * kHD;
-    float s = 0.0f;
-#pragma unroll 4
-    for (int d8 = 0; d8 < kHD; d8 += 8) {
-      const uint4 kv = *reinterpret_cast<const uint4*>(kr + d8);
-      const __nv_bfloat16* k16 = reinterpret_cast<const __nv_bfloat16*>(&kv);
+  // scores, one key per thread
+  const int c = c0 + tid;
+  float s = -3.402823466e38f;
+  if (c < c1) {
+    const uint4* kr = reinterpret_cast<const uint4*>(kc + cbase + (size_t)c * kHD);
+    uint4 kv[kHD / 8];
 #pragma unroll
-      for (int u = 0; u < 8; ++u) s = __fmaf_rn(q[d8 + u], __bfloat162float(k16[u]), s);
+    for (int u = 0; u < kHD / 8; ++u) kv[u] = kr[u];
+    s = 0.0f;
+#pragma unroll
+    for (int u = 0; u < kHD / 8; ++u) {
+      const __nv_bfloat16* k16 = reinterpret_cast<const __nv_bfloat16*>(&kv[u]);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) s = __fmaf_rn(q[u * 8 + e], __bfloat162float(k16[e]), s);
     }
-    p[c - c0] = s;
-    mx = fmaxf(mx, s);
   }
+  float mx = s;
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-  if ((tid & 31) == 0) red[tid >> 5] = mx;
+  if (lane == 0) red[warp] = mx;
   __syncthreads();
-  mx = fmaxf(fmaxf(red[0], red[1]), fmaxf(red[2], red[3]));
-  __syncthreads();
-  float sum = 0.0f;
-  for (int c = c0 + tid; c < c1; c += 128) {
-    const float e = det_expf(__fsub_rn(p[c - c0], mx));
-    p[c - c0] = e;
-    sum = __fadd_rn(sum, e);
-  }
+  mx = red[0];
+#pragma unroll
+  for (int w = 1; w < 8; ++w) mx = fmaxf(mx, red[w]);
+  const float e = c < c1 ? det_expf(__fsub_rn(s, mx)) : 0.0f;
+  p[tid] = e;
+  float sum = e;
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) sum = __fadd_rn(sum, __shfl_xor_sync(0xffffffffu, sum, o));
-  if ((tid & 31) == 0) red[tid >> 5] = sum;
+  __syncthreads();                                      // p written, red[] read
+  if (lane == 0) red[warp] = sum;
+  // o partial of this warp's 32 keys, dims 4 lane .. 4 lane + 3
+  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+  const int k0 = c0 + warp * 32, k1 = k0 + 32 < c1 ? k0 + 32 : c1;
+#pragma unroll 8
+  for (int cc = k0; cc < k1; ++cc) {
+    const uint2 vv = *reinterpret_cast<const uint2*>(vc + cbase + (size_t)cc * kHD + 4 * lane);
+    const __nv_bfloat16* v16 = reinterpret_cast<const __nv_bfloat16*>(&vv);
+    const float pc = p[cc - c0];
+    acc.x = __fmaf_rn(pc, __bfloat162float(v16[0]), acc.x);
+    acc.y = __fmaf_rn(pc, __bfloat162float(v16[1]), acc.y);
+    acc.z = __fmaf_rn(pc, __bfloat162float(v16[2]), acc.z);
+    acc.w = __fmaf_rn(pc, __bfloat162float(v16[3]), acc.w);
+  }
+  po[warp][lane] = acc;
+  __syncthreads();
+  if (tid < kHD) {
+    float o = 0.0f;
+#pragma unroll
+    for (int w = 0; w < 8; ++w) o = __fadd_rn(o, reinterpret_cast<const float*>(po[w])[tid]);
+    out[2 + tid] = o;
+  }
+  if (tid == 0) {
+    float tot = 0.0f;
+#pragma unroll
+    for (int w = 0; w < 8; ++w) tot = __fadd_rn(tot, red[w]);
+    out[0] = mx;
+    out[1] = tot;
+  }
+  // the last chunk of this (sequence, head) to finish combines
+  __threadfence();
   __syncthreads();
   if (tid == 0) {
-    out[0] = mx;
-    out[1] = __fadd_rn(__fadd_rn(red[0], red[1]), __fadd_rn(red[2], red[3]));
+    const uint32_t prev = atomicAdd(&done[b * H + h], 1u);
+    last = prev == (uint32_t)used - 1;
+    if (last) done[b * H + h] = 0u;                     // ready for the next step
   }
-  // o[tid] = sum_c p_c V[c][tid]
-  float acc = 0.0f;
-  for (int c = c0; c < c1; ++c) acc = __fmaf_rn(p[c - c0], __bfloat162float(vc[cbase + (size_t)c * kHD + tid]), acc);
-  out[2 + tid] = acc;
-}
-
-__global__ void attn_combine_kernel(const float* __restrict__ part, int H, int nch, const int32_t* __restrict__ pos_dev,
-                                    int d, float* __restrict__ att) {
-  DK_PDL_PROLOGUE();
-  const int h = blockIdx.x, b = blockIdx.y, tid = threadIdx.x;
-  const int used = (*pos_dev + 1 + kDC - 1) / kDC;
-  const float* pp = part + ((size_t)b * H + h) * nch * (kHD + 2);
-  float M = -3.402823466e38f;
-  for (int c = 0; c < used; ++c) M = fmaxf(M, pp[c * (kHD + 2)]);
-  float L = 0.0f, acc = 0.0f;
-  for (int c = 0; c < used; ++c) {
-    const float w = det_expf(__fsub_rn(pp[c * (kHD + 2)], M));
-    L = __fmaf_rn(w, pp[c * (kHD + 2) + 1], L);
-    acc = __fmaf_rn(w, pp[c * (kHD + 2) + 2 + tid], acc);
+  __syncthreads();
+  if (!last) return;
+  __threadfence();
+  if (tid < kHD) {
+    const volatile float* pp = part + ((size_t)b * H + h) * nch * (kHD + 2);
+    float M = -3.402823466e38f;
+    for (int cc = 0; cc < used; ++cc) M = fmaxf(M, pp[cc * (kHD + 2)]);
+    float L = 0.0f, a = 0.0f;
+    for (int cc = 0; cc < used; ++cc) {
+      const float w = det_expf(__fsub_rn(pp[cc * (kHD + 2)], M));
+      L = __fmaf_rn(w, pp[cc * (kHD + 2) + 1], L);
+      a = __fmaf_rn(w, pp[cc * (kHD + 2) + 2 + tid], a);
+    }
+    att[(size_t)b * d + h * kHD + tid] = __fdiv_rn(a, L);
   }
-  att[(size_t)b * d + h * kHD + tid] = __fdiv_rn(acc, L);
 }
 
 __global__ void pos_advance_kernel(int32_t* pos, int by) {
@@ -538,13 +570,11 @@ cudaError_t dk_attn_prompt(const float* qkv, int B, int T, int d, int H, int pos
 }
 int dk_decode_chunks(int max_ctx) { return (max_ctx + kDC - 1) / kDC; }
 cudaError_t dk_attn_decode(const float* qkv, int B, int d, int H, const int32_t* pos_dev, const __nv_bfloat16* kc,
-                           const __nv_bfloat16* vc, int max_ctx, float* part, float* att, cudaStream_t s) {
+                           const __nv_bfloat16* vc, int max_ctx, float* part, uint32_t* done, float* att,
+                           cudaStream_t s) {
   const int nch = dk_decode_chunks(max_ctx);
-  cudaError_t e = pdl_launch(attn_decode_kernel, dim3((unsigned)nch, (unsigned)H, (unsigned)B), dim3(128), 0, s,
-                             qkv, d, H, pos_dev, kc, vc, max_ctx, 1.0f / sqrtf((float)kHD), nch, part);
-  if (e != cudaSuccess) return e;
-  return pdl_launch(attn_combine_kernel, dim3((unsigned)H, (unsigned)B), dim3(kHD), 0, s, part, H, nch, pos_dev, d,
-                    att);
+  return pdl_launch(attn_decode_kernel, dim3((unsigned)nch, (unsigned)H, (unsigned)B), dim3(256), 0, s, qkv, d, H,
+                    pos_dev, kc, vc, max_ctx, 1.0f / sqrtf((float)kHD), nch, part, done, att);
 }
 cudaError_t dk_pos_advance(int32_t* pos, int by, cudaStream_t s) {
   return pdl_launch(pos_advance_kernel, dim3(1), dim3(32), 0, s, pos, by);

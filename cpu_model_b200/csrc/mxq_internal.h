@@ -168,8 +168,10 @@ size_t dk_attn_prompt_smem();
 cudaError_t dk_attn_prompt(const float* qkv, int B, int T, int d, int H, int pos0, const __nv_bfloat16* kc,
                            const __nv_bfloat16* vc, int max_ctx, float* att, cudaStream_t s);
 int dk_decode_chunks(int max_ctx);
+// `done` [B][H] counters, zero before the first call (each call leaves them zero).
 cudaError_t dk_attn_decode(const float* qkv, int B, int d, int H, const int32_t* pos_dev, const __nv_bfloat16* kc,
-                           const __nv_bfloat16* vc, int max_ctx, float* part, float* att, cudaStream_t s);
+                           const __nv_bfloat16* vc, int max_ctx, float* part, uint32_t* done, float* att,
+                           cudaStream_t s);
 cudaError_t dk_pos_advance(int32_t* pos, int by, cudaStream_t s);
 cudaError_t dk_logprob(const float* logits, int R, int ld, int V, const int32_t* target, float* logp, cudaStream_t s);
 cudaError_t dk_column(const float* x, int R, int ld, int col, float* out, cudaStream_t s);
