@@ -848,14 +848,6 @@ def run_ours(args):
     with Clocks(local) as clk:
         ms, launches = time_pairs(b, args.steps, args.warmup)
     clocks = clk.summary()
-    fused = None
-    if b == 1:
-        # the opt-in one-kernel pair (mxq_set_fused_pair), for comparison
-        ctx.set_fused_pair(True)
-        fms, _ = time_pairs(1, ROOFLINE_LAUNCHES, 3)
-        ctx.set_fused_pair(False)
-        fused = {"ms_per_step": fms, "tokens_per_s": world / (fms / 1e3),
-                 "hbm_gbs": pair_bytes(1) / (fms / 1e3) / 1e9, "api": "mxq_linear_pair with mxq_set_fused_pair(1)"}
     value = world * b / (ms / 1e3)
     gemv_ms = time_gemv(b, ROOFLINE_LAUNCHES)
     gbytes = gemv_bytes(UP[0], UP[1], b)
@@ -923,8 +915,6 @@ def run_ours(args):
             "clocks": clocks,
             "sweep": sweep,
         }
-        if fused is not None:
-            line["fused_pair_b1"] = fused
         if cfg1 is not None:
             line["int8_linear_4096"] = cfg1
         if moe is not None:

@@ -38,7 +38,6 @@ SIGNATURES = {
     "mxq_set_stream": [_vp, _vp],
     "mxq_set_path": [_vp, _i],
     "mxq_reserve": [_vp, _sz, _sz],
-    "mxq_set_fused_pair": [_vp, _i],
     "mxq_synchronize": [_vp],
     "mxq_last_error": [_vp],
     "mxq_launch_count": [_vp, ctypes.POINTER(ctypes.c_uint64)],
@@ -58,7 +57,6 @@ SIGNATURES = {
     "mxq_mlp_swiglu": [_vp, _vp, _vp, _vp, _vp, _sz, _vp],
     "mxq_linear_noalloc": [_vp, _vp, _vp, _sz, _vp],
     "mxq_debug_gemm_stall": [_vp, _vp, _vp, _sz, _vp, ctypes.c_uint32],
-    "mxq_debug_pair_stall": [_vp, _vp, _vp, _vp, _vp, ctypes.c_uint32],
     "mxq_route_topk": [_vp, _vp, _sz, _sz, _sz, _vp, _vp],
     "mxq_decoder_create": [_vp, _vp, ctypes.c_uint64, ctypes.POINTER(_vp)],
     "mxq_decoder_destroy": [_vp],

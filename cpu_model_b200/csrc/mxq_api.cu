@@ -20,8 +20,7 @@ struct mxq_context {
   int device = 0;
   cudaStream_t stream = nullptr;
   int path = MXQ_PATH_AUTO;
-  bool fused_pair = false;     // batch-1 pairs as one kernel (mxq_set_fused_pair)
-  uint32_t* status = nullptr;  // device status word; status[1..2]: the pair kernel's grid barrier
+  uint32_t* status = nullptr;  // device status word (bounded waits that gave up)
   uint32_t* status_host = nullptr;  // pinned mirror, read after one stream sync
   uint64_t launches = 0;
   std::string err;
@@ -31,6 +30,7 @@ struct mxq_context {
   uint8_t* ws_op = nullptr;  size_t ws_op_bytes = 0;   // GEMM operand
   float* ws_f0 = nullptr;    size_t ws_f0_bytes = 0;   // fp32 intermediates
   float* ws_f1 = nullptr;    size_t ws_f1_bytes = 0;
+  uint32_t* ws_cnt = nullptr; size_t ws_cnt_bytes = 0; // block counters of MX-output GEMVs (kept zero)
   float* ws_in = nullptr;    size_t ws_in_bytes = 0;   // host-call staging
   float* ws_out = nullptr;   size_t ws_out_bytes = 0;
   // MoE: routing bookkeeping, per-route expert outputs, pinned route counts
@@ -123,6 +123,15 @@ int ensure(mxq_context* c, T*& p, size_t& cap, size_t bytes, const char* what) {
   p = static_cast<T*>(q);
   cap = bytes;
   return MXQ_OK;
+}
+
+// A workspace of counters that the kernels using it leave zero: zeroed once
+// when (re)allocated, in stream order before its first use.
+int ensure_zeroed(mxq_context* c, uint32_t*& p, size_t& cap, size_t bytes, const char* what) {
+  if (bytes <= cap) return MXQ_OK;
+  if (int rc = ensure(c, p, cap, bytes, what)) return rc;
+  const cudaError_t e = cudaMemsetAsync(p, 0, cap, c->stream);
+  return e == cudaSuccess ? MXQ_OK : cuda_fail(c, e, what);
 }
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
@@ -390,6 +399,28 @@ int after_launch(mxq_context* c, cudaError_t e, const char* what) {
 // (optional) is the weight the following call will read: its bytes are
 // prefetched into L2 while this GEMV streams, so the next layer starts warm.
 int gemv_f32(mxq_context* c, mxq_weight w, const float* x, size_t b, float* y, mxq_weight next) {
+  if (b == 1 && !cogemv_supported(w->v, 1, true, false) && cogemv_supported(w->v, 1, false, false)) {
+    // batch 1, the fp32 row too long to stage next to the resident weights:
+    // quantise it first, then the co-resident GEMV on MX input
+    const int K = w->v.K;
+    int rc;
+    if ((rc = ensure(c, c->ws_q, c->ws_q_bytes, (size_t)K, "workspace q"))) return rc;
+    if ((rc = ensure(c, c->ws_s, c->ws_s_bytes, (size_t)K / kBlock, "workspace s"))) return rc;
+    QuantArgs qa{};
+    qa.x = x;
+    qa.B = 1;
+    qa.K = K;
+    qa.out_q = c->ws_q;
+    qa.out_s = c->ws_s;
+    if ((rc = after_launch(c, launch_quantize(qa, MXQ_ACT_NONE, c->stream, true), "quantize"))) return rc;
+    GemvArgs ga{};
+    ga.w = w->v;
+    ga.xq = c->ws_q;
+    ga.xs = c->ws_s;
+    ga.y = y;
+    ga.B = 1;
+    return after_launch(c, launch_cogemv(ga, c->stream, true), "gemv");
+  }
   if (bgemv_supported(w->v, (int)b)) {
     // small batch: MX-quantise the rows, then the MMA GEMV
     const int K = w->v.K;
@@ -584,6 +615,7 @@ int mxq_destroy(mxq_ctx c) {
     cudaFree(c->ws_op);
     cudaFree(c->ws_f0);
     cudaFree(c->ws_f1);
+    cudaFree(c->ws_cnt);
     cudaFree(c->ws_in);
     cudaFree(c->ws_out);
     cudaFree(c->ws_moe);
@@ -620,12 +652,6 @@ int mxq_set_path(mxq_ctx c, int path) {
   if (path < MXQ_PATH_AUTO || path > MXQ_PATH_GEMM)
     return fail(c, MXQ_ERR_INVALID_ARGUMENT, "unknown path %d", path);
   c->path = path;
-  return MXQ_OK;
-}
-
-int mxq_set_fused_pair(mxq_ctx c, int on) {
-  if (int rc = check_ctx(c)) return rc;
-  c->fused_pair = on != 0;
   return MXQ_OK;
 }
 
@@ -666,7 +692,7 @@ int mxq_synchronize(mxq_ctx c) {
   if (e != cudaSuccess) return cuda_fail(c, e, "synchronize");
   const uint32_t st = *c->status_host;
   if (st) {
-    // the status word and the grid barrier a timed-out kernel may have left mid-way
+    // the status word a timed-out kernel left set
     cudaMemset(c->status, 0, 4 * sizeof(uint32_t));
     return fail(c, MXQ_ERR_TIMEOUT, "a device-side bounded wait gave up (status 0x%x)", st);
   }
@@ -1075,18 +1101,29 @@ int mxq_linear_pair(mxq_ctx c, mxq_weight w1, mxq_weight w2, const float* x,
     int rc;
     if ((rc = ensure(c, c->ws_f0, c->ws_f0_bytes, b * w1->v.N * 4, "workspace mid"))) return rc;
     if (use_gemv(c, b, w1) && use_gemv(c, b, w2)) {
-      if (b == 1 && c->fused_pair && pair_supported(w1->v, w2->v)) {
-        // batch 1: both projections in one kernel, every weight byte of the
-        // pair in flight from its start
-        PairArgs pa{};
-        pa.w1 = w1->v;
-        pa.w2 = w2->v;
-        pa.x = x;
-        pa.y1 = c->ws_f0;
-        pa.y = y;
-        pa.bar = c->status + 1;
-        pa.status = c->status;
-        return after_launch(c, launch_pair(pa, c->stream, true), "pair");
+      if (b == 1 && cogemv_supported(w1->v, 1, true, true) && cogemv_supported(w2->v, 1, false, false)) {
+        // batch 1, two co-resident GEMVs: the first also writes its output as
+        // MX bytes, which the second reads (its weights stream meanwhile)
+        const size_t m = (size_t)w1->v.N;
+        if ((rc = ensure(c, c->ws_q, c->ws_q_bytes, m, "workspace q"))) return rc;
+        if ((rc = ensure(c, c->ws_s, c->ws_s_bytes, m / kBlock, "workspace s"))) return rc;
+        if ((rc = ensure_zeroed(c, c->ws_cnt, c->ws_cnt_bytes, m / kBlock * 4, "workspace counters"))) return rc;
+        GemvArgs up{};
+        up.w = w1->v;
+        up.xf = x;
+        up.y = c->ws_f0;
+        up.B = 1;
+        up.yq = c->ws_q;
+        up.ys = c->ws_s;
+        up.ycnt = c->ws_cnt;
+        if ((rc = after_launch(c, launch_cogemv(up, c->stream, true), "gemv"))) return rc;
+        GemvArgs dn{};
+        dn.w = w2->v;
+        dn.xq = c->ws_q;
+        dn.xs = c->ws_s;
+        dn.y = y;
+        dn.B = 1;
+        return after_launch(c, launch_cogemv(dn, c->stream, true), "gemv");
       }
       // decode: two launches; each GEMV quantises its fp32 input itself and
       // the first warms L2 with the second's weights while it streams
@@ -1564,35 +1601,6 @@ int mxq_debug_gemm_stall(mxq_ctx c, mxq_weight w, const float* x, size_t b, floa
     ga.wait_ns = (uint64_t)wait_us * 1000ull;
     ga.withhold_x0 = 1;
     if ((rc = after_launch(c, launch_gemm(ga, c->stream, false), "gemm"))) return rc;
-    return mxq_synchronize(c);
-  })
-}
-
-int mxq_debug_pair_stall(mxq_ctx c, mxq_weight w1, mxq_weight w2, const float* x, float* y, uint32_t wait_us) {
-  MXQ_TRY({
-    if (int rc = check_ctx(c)) return rc;
-    if (int rc = check_weight(c, w1)) return rc;
-    if (int rc = check_weight(c, w2)) return rc;
-    if (!x || !y) return fail(c, MXQ_ERR_INVALID_ARGUMENT, "null pointer");
-    if (!aligned16(x)) return fail(c, MXQ_ERR_INVALID_ARGUMENT, "fp32 input must be 16-byte aligned (it is read in 16-byte vectors)");
-    if (wait_us == 0 || wait_us > 1000000u)
-      return fail(c, MXQ_ERR_INVALID_ARGUMENT, "debug stall: wait limit must be in [1, 1e6] microseconds");
-    if (!pair_supported(w1->v, w2->v))
-      return fail(c, MXQ_ERR_UNSUPPORTED, "debug pair stall: the one-kernel pair does not support these weights");
-    DeviceGuard g(c->device);
-    int rc;
-    if ((rc = ensure(c, c->ws_f0, c->ws_f0_bytes, (size_t)w1->v.N * 4, "workspace mid"))) return rc;
-    PairArgs pa{};
-    pa.w1 = w1->v;
-    pa.w2 = w2->v;
-    pa.x = x;
-    pa.y1 = c->ws_f0;
-    pa.y = y;
-    pa.bar = c->status + 1;
-    pa.status = c->status;
-    pa.wait_ns = (uint64_t)wait_us * 1000ull;
-    pa.withhold_arrive = 1;
-    if ((rc = after_launch(c, launch_pair(pa, c->stream, false), "pair"))) return rc;
     return mxq_synchronize(c);
   })
 }

@@ -85,6 +85,11 @@ struct GemvArgs {
   const int32_t* rows;   // optional gathered row ids (mx_rank16_dot_ptrs)
   int nrows;
   int32_t* block_dots;   // optional debug output [B][N][K/32]
+  // Optional MX output of y (co-resident batch-1 GEMV, N a multiple of 32):
+  // u8 q+128 [N], E8M0 [N/32], and N/32 zeroed counters the kernel leaves zero.
+  uint8_t* yq;
+  uint8_t* ys;
+  uint32_t* ycnt;
 };
 
 cudaError_t launch_gemv(const GemvArgs& a, cudaStream_t st, bool pdl);
@@ -125,24 +130,10 @@ constexpr int kRgemvMaxBatch = 4;
 bool rgemv_supported(const WeightView& w, int B);
 cudaError_t launch_rgemv(const GemvArgs& a, cudaStream_t st, bool pdl);
 
-// Decode linear pair in one kernel (mxq_pair.cu): batch 1, fp32 x [w1.K] ->
-// y1 [w1.N] (also written out, fp32) -> y [w2.N]; bit-identical to two
-// weight-resident GEMV launches.  `bar` = two zeroed words of device memory
-// (grid barrier count and generation) owned by the caller's context.
-struct PairArgs {
-  WeightView w1, w2;
-  const float* x;
-  float* y1;
-  float* y;
-  uint32_t* bar;
-  uint32_t* status;
-  uint64_t wait_ns;   // barrier limit; 0 = kWaitLimitNs
-  // Test hook (mxq_debug_pair_stall): CTA 0 does not arrive at the grid
-  // barrier, so every CTA's wait runs out and the error path is exercised.
-  int withhold_arrive;
-};
-bool pair_supported(const WeightView& w1, const WeightView& w2);
-cudaError_t launch_pair(const PairArgs& a, cudaStream_t st, bool pdl);
+// Batch-1 GEMV with two launches resident per SM (mxq_cogemv.cu): MX or fp32
+// input, fp32 output, optionally also MX bytes of the output (GemvArgs.yq).
+bool cogemv_supported(const WeightView& w, int B, bool inf32, bool qout);
+cudaError_t launch_cogemv(const GemvArgs& a, cudaStream_t st, bool pdl);
 
 // Context internals for the other host translation units (mxq_api.cu).
 cudaStream_t ctx_stream(mxq_context* c);

@@ -787,6 +787,9 @@ bool rgemv_supported(const WeightView& w, int B) {
 cudaError_t launch_rgemv(const GemvArgs& a, cudaStream_t st, bool pdl) {
   if (!rgemv_supported(a.w, a.B) || a.rows || a.block_dots) return cudaErrorInvalidValue;
   const bool f32 = a.xf != nullptr;
+  // batch 1: two launches resident per SM where the shape fits (mxq_cogemv.cu)
+  if (cogemv_supported(a.w, a.B, f32, a.yq != nullptr)) return launch_cogemv(a, st, pdl);
+  if (a.yq) return cudaErrorInvalidValue;
   if (a.w.fmt == 4 && res_ok<4>(a.w, a.B, f32)) return f32 ? launch_res<4, true>(a, st, pdl) : launch_res<4, false>(a, st, pdl);
   if (a.w.fmt == 8 && res_ok<8>(a.w, a.B, f32)) return f32 ? launch_res<8, true>(a, st, pdl) : launch_res<8, false>(a, st, pdl);
   if (a.w.fmt == 4) return f32 ? launch_fast<4, true>(a, st, pdl) : launch_fast<4, false>(a, st, pdl);

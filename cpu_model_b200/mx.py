@@ -59,10 +59,6 @@ class MXContext:
     def set_path(self, path):
         check(self.lib.mxq_set_path(self.h, path), self.h)
 
-    def set_fused_pair(self, on):
-        """Batch-1 linear pairs as one kernel (mxq_set_fused_pair)."""
-        check(self.lib.mxq_set_fused_pair(self.h, 1 if on else 0), self.h)
-
     def reserve(self, max_batch, max_k):
         check(self.lib.mxq_reserve(self.h, max_batch, max_k), self.h)
 

@@ -98,14 +98,6 @@ MXQ_API int mxq_set_stream(mxq_ctx ctx, void* cuda_stream);
  * kernel, 3-8 int8-MMA kernel where it fits, register-blocked otherwise) and
  * batch <= 16 where the int8-MMA kernel fits the shape. */
 MXQ_API int mxq_set_path(mxq_ctx ctx, int path);
-/* Batch-1 mxq_linear_pair / _host as ONE kernel (on != 0): each CTA issues
- * both projections' weight shares (the first into registers, the second into
- * shared memory) before waiting, and a bounded grid-wide barrier separates
- * the projections.  Bit-identical to the default two launches; off by
- * default, as it measured slower on the 7B MLP pair (about 20 us against
- * 18.4 us: the phases after the weights land -- compute, barrier, the
- * intermediate's requantisation, compute -- run one after another). */
-MXQ_API int mxq_set_fused_pair(mxq_ctx ctx, int on);
 MXQ_API int mxq_reserve(mxq_ctx ctx, size_t max_batch, size_t max_k);
 MXQ_API int mxq_synchronize(mxq_ctx ctx);
 MXQ_API const char* mxq_last_error(mxq_ctx ctx);
@@ -275,16 +267,6 @@ MXQ_API int mxq_halting_step_host(mxq_ctx ctx, mxq_weight w_halt,
                                   const uint8_t* xq, const uint8_t* xs,
                                   float bias, mxq_halting_state* state_host,
                                   float* p_host, uint8_t* should_halt_host);
-
-/* Test hook, no counterpart in the reference: the one-kernel batch-1 pair of
- * mxq_linear_pair with one CTA kept from arriving at its grid barrier and the
- * barrier's wait limited to wait_us microseconds (1 .. 1e6): every CTA's wait
- * runs out, the down projection is skipped, the timeout lands in the status
- * word, and the call returns mxq_synchronize's status, MXQ_ERR_TIMEOUT, with
- * the barrier reset so the context stays usable.  MXQ_ERR_UNSUPPORTED when
- * the pair does not take the one-kernel path. */
-MXQ_API int mxq_debug_pair_stall(mxq_ctx ctx, mxq_weight w1, mxq_weight w2,
-                                 const float* x, float* y, uint32_t wait_us);
 
 /* ------------------------------------------------------------ routing --- */
 /* Top-k expert selection with the HashedRouter contract

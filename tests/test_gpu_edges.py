@@ -151,33 +151,3 @@ def test_bounded_wait_timeout_is_reported_and_context_recovers(ctx, fmt, n, k, b
     with pytest.raises(ValueError):          # the limit is bounded on the host
         mx.check(ctx.lib.mxq_debug_gemm_stall(ctx.h, W.h, mx._ptr(xd), b, mx._ptr(y), 0), ctx.h)
     W.close()
-
-
-def test_pair_barrier_timeout_is_reported_and_context_recovers(ctx):
-    """The one-kernel batch-1 pair with one CTA kept from its grid barrier and
-    a 2 ms limit (mxq_debug_pair_stall): every CTA's wait runs out, the call
-    reports MXQ_ERR_TIMEOUT, the barrier is reset, and the next pairs are
-    correct and bit-identical to two separate linears."""
-    k, m, n = 4096, 11008, 4096
-    w1, s1 = synth.weights(4, m, k, -8, -3, 61)
-    w2, s2 = synth.weights(4, n, m, -8, -3, 62)
-    W1 = mx.MXWeight(torch.from_numpy(w1), torch.from_numpy(s1), 4, m, k, ctx)
-    W2 = mx.MXWeight(torch.from_numpy(w2), torch.from_numpy(s2), 4, n, m, ctx)
-    x = cuda(synth.normal((1, k), 63))
-    y = torch.empty((1, n), dtype=torch.float32, device="cuda")
-    ctx._bind()
-    rc = ctx.lib.mxq_debug_pair_stall(ctx.h, W1.h, W2.h, mx._ptr(x), mx._ptr(y), 2000)
-    assert rc == _lib.MXQ_ERR_TIMEOUT, rc
-    ctx.synchronize()
-    ctx.set_fused_pair(True)
-    try:
-        for _ in range(2):
-            yp = host(mx.mx_linear_pair(x, W1, W2, ctx))
-            y1 = mx.mx_linear(x, W1, ctx)
-            y2 = host(mx.mx_linear(y1, W2, ctx))
-            ctx.synchronize()
-            assert np.array_equal(yp, y2)
-    finally:
-        ctx.set_fused_pair(False)
-    W1.close()
-    W2.close()

@@ -288,36 +288,6 @@ def test_int4_mlp_pair_7b_shape(ctx, b):
     assert np.array_equal(yp, y2)
 
 
-@pytest.mark.parametrize("fmt,k,m,n", [(4, 4096, 11008, 4096), (8, 4096, 4096, 4096), (4, 1024, 992, 2000),
-                                      (8, 2048, 5632, 2048), (4, 11008, 4096, 11008)])
-def test_pair_one_kernel_matches_two_launches(ctx, fmt, k, m, n):
-    """Batch-1 mxq_linear_pair as one kernel (mxq_set_fused_pair; grid
-    barrier between the projections): its y is bit-identical to the default
-    two launches and to two mxq_linear calls on the GPU's own intermediate,
-    and each stage agrees with the oracle."""
-    w1, s1, W1 = weight(ctx, fmt, m, k, 400 + m, -8, -3)
-    w2, s2, W2 = weight(ctx, fmt, n, m, 401 + n, -8, -3)
-    x = synth.normal((1, k), 402)
-    xd = cuda(x)
-    ctx.set_fused_pair(True)
-    try:
-        yp = host(mx.mx_linear_pair(xd, W1, W2, ctx))
-        for _ in range(3):                       # repeated calls reuse the grid barrier
-            assert np.array_equal(host(mx.mx_linear_pair(xd, W1, W2, ctx)), yp)
-    finally:
-        ctx.set_fused_pair(False)
-    assert np.array_equal(host(mx.mx_linear_pair(xd, W1, W2, ctx)), yp)   # two launches, same bits
-    y1 = host(mx.mx_linear(xd, W1, ctx))
-    y2 = host(mx.mx_linear(cuda(y1), W2, ctx))
-    ctx.synchronize()
-    assert np.array_equal(yp, y2)
-    xq, xs = oracle.quantize_x(x)
-    assert rel_l2(y1, oracle.gemv(fmt, xq, xs, w1, s1, m, k)) <= REL_TOL
-    hq, hs = oracle.quantize_x(y1)
-    assert rel_l2(y2, oracle.gemv(fmt, hq, hs, w2, s2, n, m)) <= REL_TOL
-    ctx.synchronize()
-
-
 # ---------------------------------------------------- gather / MLP ---
 @pytest.mark.parametrize("fmt", [8, 4])
 def test_rank16_dot_ptrs(ctx, fmt):
