@@ -395,11 +395,17 @@ int after_launch(mxq_context* c, cudaError_t e, const char* what) {
   return MXQ_OK;
 }
 
+// The batch-1 co-resident GEMV (mxq_cogemv.cu) takes this weight and input.
+static bool gemv1_ok(const mxq_weight_s* w, bool inf32, bool qout) {
+  return cogemv_supported(w->v, 1, inf32, qout);
+}
+
 // Decode GEMV straight from fp32 rows (quantised inside the kernel).  `next`
 // (optional) is the weight the following call will read: its bytes are
-// prefetched into L2 while this GEMV streams, so the next layer starts warm.
+// prefetched into L2 while this GEMV streams (cp.async-ring and weight-
+// resident kernels), so the next layer starts warm.
 int gemv_f32(mxq_context* c, mxq_weight w, const float* x, size_t b, float* y, mxq_weight next) {
-  if (b == 1 && !cogemv_supported(w->v, 1, true, false) && cogemv_supported(w->v, 1, false, false)) {
+  if (b == 1 && !gemv1_ok(w, true, false) && gemv1_ok(w, false, false)) {
     // batch 1, the fp32 row too long to stage next to the resident weights:
     // quantise it first, then the co-resident GEMV on MX input
     const int K = w->v.K;
@@ -419,7 +425,7 @@ int gemv_f32(mxq_context* c, mxq_weight w, const float* x, size_t b, float* y, m
     ga.xs = c->ws_s;
     ga.y = y;
     ga.B = 1;
-    return after_launch(c, launch_cogemv(ga, c->stream, true), "gemv");
+    return after_launch(c, launch_rgemv(ga, c->stream, true), "gemv");
   }
   if (bgemv_supported(w->v, (int)b)) {
     // small batch: MX-quantise the rows, then the MMA GEMV
@@ -1101,7 +1107,7 @@ int mxq_linear_pair(mxq_ctx c, mxq_weight w1, mxq_weight w2, const float* x,
     int rc;
     if ((rc = ensure(c, c->ws_f0, c->ws_f0_bytes, b * w1->v.N * 4, "workspace mid"))) return rc;
     if (use_gemv(c, b, w1) && use_gemv(c, b, w2)) {
-      if (b == 1 && cogemv_supported(w1->v, 1, true, true) && cogemv_supported(w2->v, 1, false, false)) {
+      if (b == 1 && gemv1_ok(w1, true, true) && gemv1_ok(w2, false, false)) {
         // batch 1, two co-resident GEMVs: the first also writes its output as
         // MX bytes, which the second reads (its weights stream meanwhile)
         const size_t m = (size_t)w1->v.N;
@@ -1116,14 +1122,14 @@ int mxq_linear_pair(mxq_ctx c, mxq_weight w1, mxq_weight w2, const float* x,
         up.yq = c->ws_q;
         up.ys = c->ws_s;
         up.ycnt = c->ws_cnt;
-        if ((rc = after_launch(c, launch_cogemv(up, c->stream, true), "gemv"))) return rc;
+        if ((rc = after_launch(c, launch_rgemv(up, c->stream, true), "gemv"))) return rc;
         GemvArgs dn{};
         dn.w = w2->v;
         dn.xq = c->ws_q;
         dn.xs = c->ws_s;
         dn.y = y;
         dn.B = 1;
-        return after_launch(c, launch_cogemv(dn, c->stream, true), "gemv");
+        return after_launch(c, launch_rgemv(dn, c->stream, true), "gemv");
       }
       // decode: two launches; each GEMV quantises its fp32 input itself and
       // the first warms L2 with the second's weights while it streams
