@@ -343,7 +343,7 @@ def time_cfg1(ctx, dev, args, world, max_over_ranks, barrier, peaks, rank, captu
            "roofline": {"bound": "hbm", "achieved": gbs, "peak": peaks["hbm_gbs"], "unit": "GB/s",
                         "frac": gbs / peaks["hbm_gbs"], "algorithmic_bytes_per_launch": nbytes,
                         "peak_src": peaks["src"] + " hbm_gbs (burst copy)",
-                        "kernel": "rgemv_res_kernel<int8, fp32 in> (weight-resident decode GEMV)"},
+                        "kernel": "cogemv_kernel<int8, fp32 in> (batch-1 GEMV, two launches resident per SM)"},
            "api": "mxq_linear"}
     if rank == 0 and world == 1 and not args.no_cpu:
         out["cpu_baseline"] = cpu_int8_sample(seconds=min(5.0, args.cpu_seconds))
@@ -902,9 +902,9 @@ def run_ours(args):
                          "frac": achieved / peaks["hbm_gbs"],
                          "traffic": ROOFLINE_TRAFFIC_B1 if b == 1 else None,
                          "traffic_src": ("ncu dram__bytes_read.sum + dram__bytes_write.sum of one "
-                                         "rgemv_res_kernel<int4, MX in> launch (up 4096->11008)")
+                                         "cogemv_kernel<int4, MX in> launch (up 4096->11008)")
                                         if b == 1 else None,
-                         "kernel": ("rgemv_res_kernel<int4> (up 4096->11008, weight-resident)" if b == 1 else
+                         "kernel": ("cogemv_kernel<int4, MX in> (up 4096->11008, two launches resident per SM)" if b == 1 else
                                     "rgemv_kernel<int4> (up 4096->11008)" if b <= 4 else "gemm_tc_kernel<int4> (up 4096->11008)"),
                          "algorithmic_bytes_per_launch": gbytes, "launch_ms": gemv_ms,
                          "peak_src": peaks["src"] + " hbm_gbs (burst copy)"},
@@ -944,7 +944,7 @@ def run_case(args):
     """Small single-workload runs for profiling (ncu) on one GPU: a few
     launches of one kernel family, nothing timed.
       gemm512   3 up-projection linears at batch 512 (tcgen05 GEMM)
-      gemv1     3 up-projection linears at batch 1 (weight-resident GEMV)
+      gemv1     3 up-projection GEMVs at batch 1 on MX input (co-resident GEMV)
       moe       one full-size block-sparse MoE layer
       decode7b  the 7B decoder: a 2048-token prompt, then 3 decode steps"""
     import torch
@@ -955,8 +955,14 @@ def run_case(args):
         wu, su = synth.weights(4, UP[0], UP[1], EMIN, EMAX, 1000)
         W = mx.MXWeight(torch.from_numpy(wu), torch.from_numpy(su), 4, UP[0], UP[1], ctx)
         x = torch.from_numpy(synth.normal((b, UP[1]), 9)).cuda()
-        for _ in range(3):
-            mx.mx_linear(x, W, ctx)
+        if b == 1:
+            # the roofline leg's kernel: the batch-1 GEMV on MX input
+            a = mx.mx_quantize_x(x, ctx)
+            for _ in range(3):
+                mx.mx_gemv(a, W, ctx)
+        else:
+            for _ in range(3):
+                mx.mx_linear(x, W, ctx)
         W.close()
     elif args.case == "moe":
         experts = moe_weights(ctx, torch.device("cuda", 0))

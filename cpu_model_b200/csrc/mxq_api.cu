@@ -395,6 +395,13 @@ int after_launch(mxq_context* c, cudaError_t e, const char* what) {
   return MXQ_OK;
 }
 
+// launch_rgemv, counting every kernel it launched
+static int rgemv_call(mxq_context* c, const GemvArgs& ga) {
+  const int rc = after_launch(c, launch_rgemv(ga, c->stream, true), "gemv");
+  if (rc == MXQ_OK) c->launches += (uint64_t)(rgemv_launches(ga) - 1);
+  return rc;
+}
+
 // The batch-1 co-resident GEMV (mxq_cogemv.cu) takes this weight and input.
 static bool gemv1_ok(const mxq_weight_s* w, bool inf32, bool qout) {
   return cogemv_supported(w->v, 1, inf32, qout);
@@ -425,7 +432,7 @@ int gemv_f32(mxq_context* c, mxq_weight w, const float* x, size_t b, float* y, m
     ga.xs = c->ws_s;
     ga.y = y;
     ga.B = 1;
-    return after_launch(c, launch_rgemv(ga, c->stream, true), "gemv");
+    return rgemv_call(c, ga);
   }
   if (bgemv_supported(w->v, (int)b)) {
     // small batch: MX-quantise the rows, then the MMA GEMV
@@ -459,7 +466,7 @@ int gemv_f32(mxq_context* c, mxq_weight w, const float* x, size_t b, float* y, m
     ga.pf_ptr2 = next->scales;
     ga.pf_bytes2 = (size_t)next->v.Npad * next->v.Kpad / kBlock;
   }
-  if (rgemv_supported(w->v, (int)b)) return after_launch(c, launch_rgemv(ga, c->stream, true), "gemv");
+  if (rgemv_supported(w->v, (int)b)) return rgemv_call(c, ga);
   return after_launch(c, launch_gemv(ga, c->stream, true), "gemv");
 }
 
@@ -530,7 +537,7 @@ int gemv_dev(mxq_context* c, mxq_weight w, const uint8_t* xq, const uint8_t* xs,
     ga.y = y;
     ga.B = (int)b;
     if (bgemv_supported(w->v, (int)b)) return after_launch(c, launch_bgemv(ga, c->stream, true), "gemv");
-    if (rgemv_supported(w->v, (int)b)) return after_launch(c, launch_rgemv(ga, c->stream, true), "gemv");
+    if (rgemv_supported(w->v, (int)b)) return rgemv_call(c, ga);
     return after_launch(c, launch_gemv(ga, c->stream, true), "gemv");
   }
   const int BN = gemm_pick_bn((int)b);

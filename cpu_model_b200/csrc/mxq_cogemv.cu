@@ -9,10 +9,10 @@
 // boundary.  Here a CTA is 256 threads at <= 128 registers and <= 113 KB of
 // shared memory, so two fit an SM: the CTA issues every weight load of its
 // share -- 24 rounds of 16 bytes a thread into registers, the rest into
-// shared memory with cp.async -- and the scale bytes of its rows, then lets
-// the next launch start (griddepcontrol.launch_dependents) and waits for its
-// predecessor.  While it computes, the next launch's CTA on the same SM
-// streams that launch's weights.
+// shared memory with cp.async -- and the scale bytes of its rows, and waits
+// for its predecessor; the next launch is let in (griddepcontrol.
+// launch_dependents) before or after the activation lands, and while this
+// CTA computes, the next launch's CTA on the same SM streams its weights.
 //
 // Work split.  Output rows are taken in groups of 4, a contiguous balanced
 // range of groups per CTA.  A quad is (block of 4 groups, warp load): the
@@ -233,6 +233,15 @@ __global__ void __launch_bounds__(kCoThreads, 2) cogemv_kernel(GemvArgs a) {
     cp_async_commit();
   }
   for (int e = tid; e < kCoWarps * g.max_ng * 4; e += kCoThreads) part[e] = 0.0f;
+  // The next launch may take this SM's other slot and stream its own weights
+  // while this one computes (its griddepcontrol.wait still waits for this
+  // whole grid).  With a small activation (<= 8 KB) it is let in now; with a
+  // larger one only once the activation has landed, so that the next
+  // launch's weight requests do not queue ahead of it (measured on the 7B
+  // MLP shapes: 4 KB MX rows 6.0 vs 6.4 us a launch, 11 KB MX and 16 KB fp32
+  // rows 6.7 vs 6.9 and 6.9 vs 7.1 us).
+  const bool early = a.w.K * (INF32 ? 4 : 1) <= 8192;
+  if (early) asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   asm volatile("griddepcontrol.wait;" ::: "memory");
 
   // ---- the activation row
@@ -260,11 +269,7 @@ __global__ void __launch_bounds__(kCoThreads, 2) cogemv_kernel(GemvArgs a) {
   }
   cp_async_wait_all();
   __syncthreads();
-  // The next launch may take this SM's other slot now and stream its own
-  // weights while this one computes (its griddepcontrol.wait still waits for
-  // this whole grid).  Triggered only once the activation has landed, so the
-  // next launch's weight requests do not queue ahead of it.
-  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  if (!early) asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 
   if (INF32) {
     // 8 lanes per block, 4 values a lane (quantize_kernel's arithmetic)
@@ -570,6 +575,44 @@ cudaError_t launch_cogemv(const GemvArgs& a, cudaStream_t st, bool pdl) {
     return cudaErrorInvalidValue;
   if (a.yq && (!a.ys || !a.ycnt)) return cudaErrorInvalidValue;
   return a.w.fmt == 4 ? launch_co_t<4>(a, st, pdl) : launch_co_t<8>(a, st, pdl);
+}
+
+// Rows [rt0 * 128, rt0 * 128 + n) of a dense weight as a weight of its own:
+// the tiled layout keeps each 128-row tile's k-tiles together, so a slice at
+// tile boundaries is a pointer offset.
+static WeightView row_slice(const WeightView& w, int rt0, int n) {
+  WeightView v = w;
+  const size_t kt = (size_t)w.Kpad / kTileK;
+  v.data = w.data + (size_t)rt0 * kt * 128 * (w.fmt == 4 ? 32 : 64);
+  v.scales = w.scales + (size_t)rt0 * kt * 128 * 2;
+  v.N = n;
+  v.Npad = (n + 127) / 128 * 128;
+  return v;
+}
+
+int cogemv_row_parts(const WeightView& w, int B, bool inf32) {
+  if (B != 1 || w.kt_ptr || cogemv_supported(w, B, inf32, false)) return 0;
+  const int tiles = (w.N + 127) / 128;
+  for (int parts = 2; parts <= 8 && parts <= tiles; ++parts) {
+    const int per = (tiles + parts - 1) / parts;
+    if (cogemv_supported(row_slice(w, 0, per * 128 < w.N ? per * 128 : w.N), 1, inf32, false)) return parts;
+  }
+  return 0;
+}
+
+cudaError_t launch_cogemv_rows(const GemvArgs& a, int parts, cudaStream_t st, bool pdl) {
+  if (parts < 2 || a.yq || a.rows || a.block_dots || a.B != 1) return cudaErrorInvalidValue;
+  const int tiles = (a.w.N + 127) / 128;
+  const int per = (tiles + parts - 1) / parts;
+  for (int rt = 0; rt < tiles; rt += per) {
+    const int n = ((rt + per) * 128 < a.w.N ? (rt + per) * 128 : a.w.N) - rt * 128;
+    GemvArgs p = a;
+    p.w = row_slice(a.w, rt, n);
+    p.y = a.y + (size_t)rt * 128;
+    if (!cogemv_supported(p.w, 1, a.xf != nullptr, false)) return cudaErrorInvalidValue;
+    if (cudaError_t e = p.w.fmt == 4 ? launch_co_t<4>(p, st, pdl) : launch_co_t<8>(p, st, pdl)) return e;
+  }
+  return cudaSuccess;
 }
 
 }  // namespace mxq

@@ -129,11 +129,18 @@ cudaError_t launch_bgemv(const GemvArgs& a, cudaStream_t st, bool pdl);
 constexpr int kRgemvMaxBatch = 4;
 bool rgemv_supported(const WeightView& w, int B);
 cudaError_t launch_rgemv(const GemvArgs& a, cudaStream_t st, bool pdl);
+// kernels one launch_rgemv call launches (batch-1 row slices: several)
+int rgemv_launches(const GemvArgs& a);
 
 // Batch-1 GEMV with two launches resident per SM (mxq_cogemv.cu): MX or fp32
 // input, fp32 output, optionally also MX bytes of the output (GemvArgs.yq).
 bool cogemv_supported(const WeightView& w, int B, bool inf32, bool qout);
 cudaError_t launch_cogemv(const GemvArgs& a, cudaStream_t st, bool pdl);
+// Batch 1, a weight too tall for one co-resident launch: the number of
+// 128-row-tile slices (2-8) that each fit, 0 if none; and the launches (one
+// per slice, in row order, each writing its rows of y).
+int cogemv_row_parts(const WeightView& w, int B, bool inf32);
+cudaError_t launch_cogemv_rows(const GemvArgs& a, int parts, cudaStream_t st, bool pdl);
 
 // Context internals for the other host translation units (mxq_api.cu).
 cudaStream_t ctx_stream(mxq_context* c);

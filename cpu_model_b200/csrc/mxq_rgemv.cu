@@ -778,6 +778,13 @@ bool res_ok(const WeightView& w, int B, bool inf32) {
 }
 }  // namespace
 
+int rgemv_launches(const GemvArgs& a) {
+  const bool f32 = a.xf != nullptr;
+  if (cogemv_supported(a.w, a.B, f32, a.yq != nullptr)) return 1;
+  const int parts = a.yq ? 0 : cogemv_row_parts(a.w, a.B, f32);
+  return parts ? parts : 1;
+}
+
 bool rgemv_supported(const WeightView& w, int B) {
   if (B < 1 || B > kRgemvMaxBatch) return false;
   const size_t smem = w.fmt == 4 ? smem_bytes<4>(w, B) : smem_bytes<8>(w, B);
@@ -790,6 +797,7 @@ cudaError_t launch_rgemv(const GemvArgs& a, cudaStream_t st, bool pdl) {
   // batch 1: two launches resident per SM where the shape fits (mxq_cogemv.cu)
   if (cogemv_supported(a.w, a.B, f32, a.yq != nullptr)) return launch_cogemv(a, st, pdl);
   if (a.yq) return cudaErrorInvalidValue;
+  if (const int parts = cogemv_row_parts(a.w, a.B, f32)) return launch_cogemv_rows(a, parts, st, pdl);
   if (a.w.fmt == 4 && res_ok<4>(a.w, a.B, f32)) return f32 ? launch_res<4, true>(a, st, pdl) : launch_res<4, false>(a, st, pdl);
   if (a.w.fmt == 8 && res_ok<8>(a.w, a.B, f32)) return f32 ? launch_res<8, true>(a, st, pdl) : launch_res<8, false>(a, st, pdl);
   if (a.w.fmt == 4) return f32 ? launch_fast<4, true>(a, st, pdl) : launch_fast<4, false>(a, st, pdl);

@@ -288,6 +288,48 @@ def test_int4_mlp_pair_7b_shape(ctx, b):
     assert np.array_equal(yp, y2)
 
 
+@pytest.mark.parametrize("fmt,n,k", [(4, 22016, 4096), (4, 32000, 4096), (8, 12288, 2048), (4, 12288, 4096)])
+def test_tall_batch1_linear_row_slices(ctx, fmt, n, k):
+    """Batch-1 linears too tall for one co-resident launch (the 7B decoder's
+    fused gate/up, LM head and QKV shapes) run as consecutive launches over
+    128-row-tile slices; every row agrees with the oracle, fp32 and MX input."""
+    w, ws, W = weight(ctx, fmt, n, k, 70 + n, -8, -3)
+    x = synth.normal((1, k), 71)
+    xq, xs = oracle.quantize_x(x)
+    ref = oracle.gemv(fmt, xq, xs, w, ws, n, k)
+    y = host(mx.mx_linear(cuda(x), W, ctx))
+    y2 = host(mx.mx_gemv(mx.MXActivation(cuda(xq), cuda(xs)), W, ctx))
+    ctx.synchronize()
+    assert rel_l2(y, ref) <= REL_TOL
+    assert rel_l2(y2, ref) <= REL_TOL
+    W.close()
+
+
+@pytest.mark.parametrize("fmt,k,m,n", [(4, 2048, 2048, 1024), (8, 1024, 1184, 2048), (4, 4096, 4096, 4096)])
+def test_pair_mx_output_blocks_across_ctas(ctx, fmt, k, m, n):
+    """Batch-1 pairs whose first projection has fewer than 32 rows a CTA, so
+    one 32-row MX block of the intermediate is shared by two or three CTAs
+    (the last of them to finish quantises it): the pair is bit-identical to
+    two mxq_linear calls on the GPU's own intermediate, each vs the oracle."""
+    w1, s1, W1 = weight(ctx, fmt, m, k, 80 + m, -8, -3)
+    w2, s2, W2 = weight(ctx, fmt, n, m, 81 + n, -8, -3)
+    x = synth.normal((1, k), 82)
+    xd = cuda(x)
+    yp = host(mx.mx_linear_pair(xd, W1, W2, ctx))
+    for _ in range(3):                       # the block counters are left zero
+        assert np.array_equal(host(mx.mx_linear_pair(xd, W1, W2, ctx)), yp)
+    y1 = host(mx.mx_linear(xd, W1, ctx))
+    y2 = host(mx.mx_linear(cuda(y1), W2, ctx))
+    ctx.synchronize()
+    assert np.array_equal(yp, y2)
+    xq, xs = oracle.quantize_x(x)
+    assert rel_l2(y1, oracle.gemv(fmt, xq, xs, w1, s1, m, k)) <= REL_TOL
+    hq, hs = oracle.quantize_x(y1)
+    assert rel_l2(y2, oracle.gemv(fmt, hq, hs, w2, s2, n, m)) <= REL_TOL
+    W1.close()
+    W2.close()
+
+
 # ---------------------------------------------------- gather / MLP ---
 @pytest.mark.parametrize("fmt", [8, 4])
 def test_rank16_dot_ptrs(ctx, fmt):
