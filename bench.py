@@ -19,6 +19,7 @@ HBM.
 """
 import argparse
 import json
+import math
 import os
 import statistics
 import subprocess
@@ -615,6 +616,67 @@ def time_ppo(ctx, dev, args, world, max_over_ranks, barrier, peaks, rank):
     return out
 
 
+def time_sharded_peer(ctx, dev, args, world, rank, max_over_ranks, barrier, up_full, dn_full):
+    """N > 1: the batch-1 pair column-sharded through mxq_linear_pair_sharded
+    (no NCCL on the data path: each linear's rows go straight into every
+    rank's mailbox over NVLink).  Each rank holds 1/N of both matrices;
+    enough distinct shard copies rotate that a step's weights come from HBM,
+    not L2; CUDA graph of the steps, CUDA events, max over ranks."""
+    import torch
+    import torch.distributed as dist
+    from cpu_model_b200 import mx, synth
+    n1, n2 = UP[0], DOWN[0]
+    n1s, n2s = n1 // world, n2 // world
+    shard_bytes = pair_bytes(1) / world
+    copies = max(2, int(math.ceil(4 * 126e6 / shard_bytes)))
+    (wu, su), (wd, sd) = up_full, dn_full
+    w1 = (np.ascontiguousarray(wu[rank * n1s:(rank + 1) * n1s]), np.ascontiguousarray(su[rank * n1s:(rank + 1) * n1s]))
+    w2 = (np.ascontiguousarray(wd[rank * n2s:(rank + 1) * n2s]), np.ascontiguousarray(sd[rank * n2s:(rank + 1) * n2s]))
+    shards = [(mx.MXWeight(torch.from_numpy(w1[0]), torch.from_numpy(w1[1]), 4, n1s, UP[1], ctx),
+               mx.MXWeight(torch.from_numpy(w2[0]), torch.from_numpy(w2[1]), 4, n2s, DOWN[1], ctx))
+              for _ in range(copies)]
+    P = mx.PeerGroup(rank, world, n1, n2, ctx)
+    handles = [None] * world
+    dist.all_gather_object(handles, P.handle())
+    P.connect(handles)
+    barrier()
+    x = torch.from_numpy(synth.normal((1, UP[1]), 303)).to(dev)
+    y = torch.empty((1, n2), dtype=torch.float32, device=dev)
+    for i in range(max(3, args.warmup)):
+        P.linear_pair(x, *shards[i % copies], out=y)
+    ctx.synchronize()
+    steps = max(20, args.steps)
+    stream = torch.cuda.Stream(dev)
+    with torch.cuda.stream(stream):
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            for i in range(steps):
+                P.linear_pair(x, *shards[i % copies], out=y)
+    torch.cuda.synchronize()
+    g.replay()
+    torch.cuda.synchronize()
+    barrier()
+    torch.cuda.synchronize()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    g.replay()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms = max_over_ranks(e0.elapsed_time(e1) / steps)
+    del g
+    ctx.synchronize()
+    barrier()
+    P.close()
+    for a, b in shards:
+        a.close()
+        b.close()
+    return {"1": {"ms_per_step": ms, "tokens_per_s": 1.0 / (ms / 1e3)}, "scaling": "strong",
+            "weight_copies": copies, "api": "mxq_linear_pair_sharded",
+            "collective": "none: rows stored into every rank's mailbox over NVLink by the GEMV epilogues, "
+                          "bounded flag waits"}
+
+
 def time_sharded(ctx, dev, args, world, rank, max_over_ranks, barrier):
     """N > 1 only: the multi-GPU forms of the path, over NCCL.
     pair -- the MLP pair column-sharded (each rank owns F/N rows of up and
@@ -659,6 +721,8 @@ def time_sharded(ctx, dev, args, world, rank, max_over_ranks, barrier):
     up.w.close()
     down.w.close()
     out["pair_column_sharded"] = dict(pair, scaling="strong", collective="all_gather (NCCL) after each linear")
+    out["pair_column_sharded_peer"] = time_sharded_peer(ctx, dev, args, world, rank, max_over_ranks, barrier,
+                                                        up_full, dn_full)
 
     e_lo, e_hi = shard.row_shards(MOE["experts"], world)[rank]
     experts = moe_weights(ctx, dev, experts_range=(e_lo, e_hi))

@@ -24,6 +24,7 @@ ACT_SILU = 1
 PATH_AUTO = 0
 PATH_GEMV = 1
 PATH_GEMM = 2
+PEER_HANDLE_BYTES = 64
 
 _vp = ctypes.c_void_p
 _sz = ctypes.c_size_t
@@ -54,6 +55,12 @@ SIGNATURES = {
     "mxq_linear_host": [_vp, _vp, _vp, _sz, _vp],
     "mxq_linear_pair": [_vp, _vp, _vp, _vp, _sz, _vp],
     "mxq_linear_pair_host": [_vp, _vp, _vp, _vp, _sz, _vp],
+    "mxq_peers_create": [_vp, _i, _i, _sz, _sz, ctypes.POINTER(_vp), _vp],
+    "mxq_peers_connect": [_vp, _vp],
+    "mxq_peers_set_wait_limit": [_vp, ctypes.c_uint32],
+    "mxq_peers_destroy": [_vp],
+    "mxq_linear_pair_sharded": [_vp, _vp, _vp, _vp, _vp, _vp],
+    "mxq_debug_peer_stall": [_vp, _vp, _vp, ctypes.c_uint32],
     "mxq_mlp_swiglu": [_vp, _vp, _vp, _vp, _vp, _sz, _vp],
     "mxq_linear_noalloc": [_vp, _vp, _vp, _sz, _vp],
     "mxq_debug_gemm_stall": [_vp, _vp, _vp, _sz, _vp, ctypes.c_uint32],

@@ -1311,6 +1311,226 @@ int mxq_linear_host(mxq_ctx c, mxq_weight w, const float* x_host, size_t b, floa
   })
 }
 
+// ---------------------------------------------- column-sharded pair ---
+// One rank's side of a batch-1 pair column-sharded over `world` GPUs.  The
+// mailbox (device memory exported over CUDA IPC, opened by every other
+// rank) holds, twice over (the device epoch's parity picks the half):
+//   flags  [2 kinds][kMaxPeers] u32 at 0 (kind 0: first linear's rows
+//          landed, kind 1: second's), written by the ranks over NVLink;
+//   q      [2][n1] MX bytes of the intermediate, s [2][n1/32] its scales;
+//   f      [2][n2] fp32 output rows.
+// Local words (not exported): epoch, and one finished-CTA counter per role.
+struct mxq_peers_s {
+  mxq_context* ctx = nullptr;
+  int rank = 0, world = 1;
+  size_t n1 = 0, n2 = 0;
+  uint8_t* mbox = nullptr;
+  size_t off_q = 0, off_s = 0, off_f = 0, bytes = 0;
+  uint8_t* base[kMaxPeers] = {};   // every rank's mailbox as mapped here
+  bool opened[kMaxPeers] = {};
+  uint32_t* local = nullptr;       // [0] epoch, [1] role-1 counter, [2] role-2 counter
+  uint64_t wait_ns = kWaitLimitNs;
+};
+
+int mxq_peers_create(mxq_ctx c, int rank, int world, size_t n1, size_t n2, mxq_peers* out, void* handle_out) {
+  MXQ_TRY({
+    if (int rc = check_ctx(c)) return rc;
+    if (!out || !handle_out) return fail(c, MXQ_ERR_INVALID_ARGUMENT, "null pointer");
+    *out = nullptr;
+    if (world < 1 || world > kMaxPeers || rank < 0 || rank >= world)
+      return fail(c, MXQ_ERR_INVALID_ARGUMENT, "peer group: rank %d of world %d (1..%d ranks)", rank, world, kMaxPeers);
+    if (n1 == 0 || n2 == 0 || n1 % ((size_t)world * kBlock) || n2 % (size_t)world)
+      return fail(c, MXQ_ERR_INVALID_ARGUMENT,
+                  "peer group: n1=%zu must split into whole 32-row blocks per rank and n2=%zu into equal shards", n1, n2);
+    DeviceGuard g(c->device);
+    auto* P = new mxq_peers_s();
+    P->ctx = c;
+    P->rank = rank;
+    P->world = world;
+    P->n1 = n1;
+    P->n2 = n2;
+    P->off_q = 256;
+    P->off_s = P->off_q + 2 * n1;
+    P->off_f = (P->off_s + 2 * (n1 / kBlock) + 15) / 16 * 16;
+    P->bytes = P->off_f + 2 * n2 * sizeof(float);
+    cudaError_t e = cudaMalloc(&P->mbox, P->bytes);
+    if (e == cudaSuccess) e = cudaMemset(P->mbox, 0, P->bytes);
+    if (e == cudaSuccess) e = cudaMalloc(&P->local, 4 * sizeof(uint32_t));
+    if (e == cudaSuccess) e = cudaMemset(P->local, 0, 4 * sizeof(uint32_t));
+    cudaIpcMemHandle_t h{};
+    if (e == cudaSuccess) e = cudaIpcGetMemHandle(&h, P->mbox);
+    if (e == cudaSuccess) e = cudaDeviceSynchronize();
+    if (e != cudaSuccess) {
+      cudaFree(P->mbox);
+      cudaFree(P->local);
+      delete P;
+      return cuda_fail(c, e, "peer mailbox");
+    }
+    static_assert(sizeof(cudaIpcMemHandle_t) == MXQ_PEER_HANDLE_BYTES, "IPC handle size");
+    std::memcpy(handle_out, &h, sizeof(h));
+    P->base[rank] = P->mbox;
+    *out = P;
+    return MXQ_OK;
+  })
+}
+
+int mxq_peers_connect(mxq_peers P, const void* handles) {
+  MXQ_TRY({
+    if (!P || !handles) return fail(nullptr, MXQ_ERR_INVALID_ARGUMENT, "null pointer");
+    mxq_context* c = P->ctx;
+    DeviceGuard g(c->device);
+    for (int r = 0; r < P->world; ++r) {
+      if (r == P->rank || P->base[r]) continue;
+      cudaIpcMemHandle_t h;
+      std::memcpy(&h, static_cast<const uint8_t*>(handles) + (size_t)r * sizeof(h), sizeof(h));
+      void* p = nullptr;
+      const cudaError_t e = cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess);
+      if (e != cudaSuccess) return cuda_fail(c, e, "open a peer's mailbox");
+      P->base[r] = static_cast<uint8_t*>(p);
+      P->opened[r] = true;
+    }
+    return MXQ_OK;
+  })
+}
+
+int mxq_peers_set_wait_limit(mxq_peers P, uint32_t wait_us) {
+  if (!P) return fail(nullptr, MXQ_ERR_INVALID_ARGUMENT, "null peer group");
+  if (wait_us == 0 || wait_us > 10000000u)
+    return fail(P->ctx, MXQ_ERR_INVALID_ARGUMENT, "peer wait limit must be in [1, 1e7] microseconds");
+  P->wait_ns = (uint64_t)wait_us * 1000ull;
+  return MXQ_OK;
+}
+
+int mxq_peers_destroy(mxq_peers P) {
+  if (!P) return fail(nullptr, MXQ_ERR_INVALID_ARGUMENT, "null peer group");
+  DeviceGuard g(P->ctx->device);
+  cudaDeviceSynchronize();
+  for (int r = 0; r < P->world; ++r)
+    if (P->opened[r]) cudaIpcCloseMemHandle(P->base[r]);
+  cudaFree(P->mbox);
+  cudaFree(P->local);
+  delete P;
+  return MXQ_OK;
+}
+
+int mxq_linear_pair_sharded(mxq_ctx c, mxq_peers P, mxq_weight w1, mxq_weight w2, const float* x, float* y) {
+  MXQ_TRY({
+    if (int rc = check_ctx(c)) return rc;
+    if (int rc = check_weight(c, w1)) return rc;
+    if (int rc = check_weight(c, w2)) return rc;
+    if (!P || !x || !y) return fail(c, MXQ_ERR_INVALID_ARGUMENT, "null pointer");
+    if (P->ctx != c) return fail(c, MXQ_ERR_INVALID_ARGUMENT, "peer group belongs to another context");
+    for (int r = 0; r < P->world; ++r)
+      if (!P->base[r]) return fail(c, MXQ_ERR_INVALID_ARGUMENT, "peer group not connected (mxq_peers_connect)");
+    if (!aligned16(x)) return fail(c, MXQ_ERR_INVALID_ARGUMENT, "fp32 input must be 16-byte aligned (it is read in 16-byte vectors)");
+    const size_t n1s = P->n1 / P->world, n2s = P->n2 / P->world;
+    if ((size_t)w1->v.N != n1s || (size_t)w2->v.N != n2s || (size_t)w2->v.K != P->n1)
+      return fail(c, MXQ_ERR_INVALID_ARGUMENT,
+                  "sharded pair: shards must be %zu x K and %zu x %zu rows (got %d x %d, %d x %d)", n1s, n2s, P->n1,
+                  w1->v.N, w1->v.K, w2->v.N, w2->v.K);
+    if (!cogemv_supported(w1->v, 1, true, true) || !cogemv_supported(w2->v, 1, false, false))
+      return fail(c, MXQ_ERR_UNSUPPORTED, "sharded pair: a shard does not fit the batch-1 co-resident GEMV");
+    DeviceGuard g(c->device);
+    int rc;
+    if ((rc = ensure(c, c->ws_f0, c->ws_f0_bytes, n1s * 4, "workspace mid"))) return rc;
+    if ((rc = ensure(c, c->ws_q, c->ws_q_bytes, n1s, "workspace q"))) return rc;
+    if ((rc = ensure(c, c->ws_s, c->ws_s_bytes, n1s / kBlock, "workspace s"))) return rc;
+    if ((rc = ensure_zeroed(c, c->ws_cnt, c->ws_cnt_bytes, n1s / kBlock * 4, "workspace counters"))) return rc;
+    PeerArgs pa{};
+    pa.world = P->world;
+    pa.rank = P->rank;
+    pa.epoch = P->local;
+    pa.status = c->status;
+    pa.wait_ns = P->wait_ns;
+    auto flags = [&](int r, int kind) { return reinterpret_cast<uint32_t*>(P->base[r]) + kind * kMaxPeers; };
+    // first linear: this rank's rows of the intermediate, as MX bytes, into every mailbox
+    PeerArgs p1 = pa;
+    p1.grid_cnt = P->local + 1;
+    for (int r = 0; r < P->world; ++r) {
+      p1.flag_out[r] = flags(r, 0) + P->rank;
+      p1.q_out[r] = P->base[r] + P->off_q;
+      p1.s_out[r] = P->base[r] + P->off_s;
+    }
+    p1.q_stride = P->n1;
+    p1.s_stride = P->n1 / kBlock;
+    p1.row_off = (int)(P->rank * n1s);
+    GemvArgs up{};
+    up.w = w1->v;
+    up.xf = x;
+    up.y = c->ws_f0;
+    up.B = 1;
+    up.yq = c->ws_q;
+    up.ys = c->ws_s;
+    up.ycnt = c->ws_cnt;
+    if ((rc = after_launch(c, launch_cogemv_peer(up, p1, 1, c->stream, true), "sharded gemv 1"))) return rc;
+    // second linear: waits for every rank's rows, reads the full MX
+    // intermediate from the local mailbox, its fp32 rows into every mailbox
+    PeerArgs p2 = pa;
+    p2.grid_cnt = P->local + 2;
+    p2.wait_flags = flags(P->rank, 0);
+    p2.xq_base = P->mbox + P->off_q;
+    p2.xs_base = P->mbox + P->off_s;
+    p2.xq_stride = P->n1;
+    p2.xs_stride = P->n1 / kBlock;
+    for (int r = 0; r < P->world; ++r) {
+      p2.flag_out[r] = flags(r, 1) + P->rank;
+      p2.f_out[r] = reinterpret_cast<float*>(P->base[r] + P->off_f);
+    }
+    p2.f_stride = P->n2;
+    p2.row_off = (int)(P->rank * n2s);
+    GemvArgs dn{};
+    dn.w = w2->v;
+    dn.B = 1;
+    if ((rc = after_launch(c, launch_cogemv_peer(dn, p2, 2, c->stream, true), "sharded gemv 2"))) return rc;
+    // every rank's output rows -> y, and the epoch advances
+    PeerArgs p3 = pa;
+    p3.wait_flags = flags(P->rank, 1);
+    p3.f_in = reinterpret_cast<const float*>(P->mbox + P->off_f);
+    p3.f_in_stride = P->n2;
+    return after_launch(c, launch_peer_gather(p3, y, (int)P->n2, c->stream, true), "sharded gather");
+  })
+}
+
+int mxq_debug_peer_stall(mxq_ctx c, mxq_peers P, mxq_weight w2, uint32_t wait_us) {
+  MXQ_TRY({
+    if (int rc = check_ctx(c)) return rc;
+    if (int rc = check_weight(c, w2)) return rc;
+    if (!P || P->ctx != c) return fail(c, MXQ_ERR_INVALID_ARGUMENT, "null or foreign peer group");
+    if (P->world != 1) return fail(c, MXQ_ERR_UNSUPPORTED, "debug peer stall: one-rank groups only");
+    if (wait_us == 0 || wait_us > 1000000u)
+      return fail(c, MXQ_ERR_INVALID_ARGUMENT, "debug stall: wait limit must be in [1, 1e6] microseconds");
+    if ((size_t)w2->v.N != P->n2 || (size_t)w2->v.K != P->n1 || !cogemv_supported(w2->v, 1, false, false))
+      return fail(c, MXQ_ERR_INVALID_ARGUMENT, "debug peer stall: w2 must be n2 x n1");
+    DeviceGuard g(c->device);
+    // the second linear waiting on a flag word that nothing sets (local[3]);
+    // its own flag goes to the same scratch word and the epoch is not
+    // advanced, so the group stays consistent
+    PeerArgs p2{};
+    p2.world = 1;
+    p2.rank = 0;
+    p2.epoch = P->local;
+    p2.grid_cnt = P->local + 2;
+    p2.wait_flags = P->local + 3;
+    p2.flag_out[0] = P->local + 3;
+    p2.xq_base = P->mbox + P->off_q;
+    p2.xs_base = P->mbox + P->off_s;
+    p2.xq_stride = P->n1;
+    p2.xs_stride = P->n1 / kBlock;
+    p2.f_out[0] = reinterpret_cast<float*>(P->mbox + P->off_f);
+    p2.f_stride = P->n2;
+    p2.status = c->status;
+    p2.wait_ns = (uint64_t)wait_us * 1000ull;
+    GemvArgs dn{};
+    dn.w = w2->v;
+    dn.B = 1;
+    int rc;
+    if ((rc = after_launch(c, launch_cogemv_peer(dn, p2, 2, c->stream, false), "sharded gemv 2"))) return rc;
+    const int st = mxq_synchronize(c);
+    cudaMemset(P->local + 3, 0, sizeof(uint32_t));
+    return st;
+  })
+}
+
 int mxq_linear_pair_host(mxq_ctx c, mxq_weight w1, mxq_weight w2, const float* x_host,
                          size_t b, float* y_host) {
   MXQ_TRY({

@@ -170,8 +170,41 @@ __device__ __forceinline__ int owner_cta(int q, int G4, int G) {
   return (int)(((long long)(q + 1) * G - 1) / G4);
 }
 
-template <int WFMT, bool FAST, bool INF32, bool QOUT>
-__global__ void __launch_bounds__(kCoThreads, 2) cogemv_kernel(GemvArgs a) {
+// --- peer mailboxes (column-sharded linears across GPUs) -----------------
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+// Bounded wait until every rank's flag has reached this call's epoch (the
+// flags are written over NVLink by the other GPUs).  Returns 0, with the
+// timeout recorded in the status word, once `limit_ns` have passed.
+__device__ int peer_wait(const uint32_t* flags, int world, uint32_t ep, uint64_t limit_ns, uint32_t* status) {
+  const uint64_t t0 = globaltimer_ns();
+  for (int r = 0; r < world; ++r) {
+    for (uint32_t it = 0;; ++it) {
+      if ((int)(ld_acquire_sys(flags + r) - ep) >= 0) break;
+      if (it > (1u << 26) || globaltimer_ns() - t0 > limit_ns) {
+        if (status) atomicOr(status, kStatusTimeout);
+        return 0;
+      }
+      __nanosleep(100);
+    }
+  }
+  return 1;
+}
+
+// ROLE 0: a plain GEMV.  ROLE 1: the first linear of a column-sharded pair
+// (fp32 input, MX output written into every rank's mailbox at this rank's
+// rows, then this rank's flag set on every rank).  ROLE 2: the second
+// linear (waits for every rank's flag, reads the full MX activation from the
+// local mailbox, writes its fp32 rows into every rank's mailbox, sets flags).
+template <int WFMT, bool FAST, bool INF32, bool QOUT, int ROLE>
+__global__ void __launch_bounds__(kCoThreads, 2) cogemv_kernel(GemvArgs a, PeerArgs p) {
+  static_assert(ROLE == 0 || (ROLE == 1 && INF32 && QOUT) || (ROLE == 2 && !INF32 && !QOUT), "role");
   using C = CoCfg<WFMT>;
   extern __shared__ __align__(16) uint8_t smem[];
   const int G = gridDim.x;
@@ -244,6 +277,21 @@ __global__ void __launch_bounds__(kCoThreads, 2) cogemv_kernel(GemvArgs a) {
   if (early) asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   asm volatile("griddepcontrol.wait;" ::: "memory");
 
+  // this call's epoch (peer roles): parity selects the mailbox half
+  uint32_t ep = 0;
+  const uint8_t* xq_in = a.xq;
+  const uint8_t* xs_in = a.xs;
+  if (ROLE != 0) {
+    ep = *reinterpret_cast<volatile const uint32_t*>(p.epoch) + 1u;
+    if (ROLE == 2) {
+      xq_in = p.xq_base + (size_t)(ep & 1u) * p.xq_stride;
+      xs_in = p.xs_base + (size_t)(ep & 1u) * p.xs_stride;
+      int* okf = reinterpret_cast<int*>(smem + g.off_flag) + 2;
+      if (tid == 0) okf[0] = peer_wait(p.wait_flags, p.world, ep, p.wait_ns, p.status);
+      __syncthreads();
+    }
+  }
+
   // ---- the activation row
   const int K = a.w.K;
   const int kb = K / kBlock;
@@ -253,7 +301,7 @@ __global__ void __launch_bounds__(kCoThreads, 2) cogemv_kernel(GemvArgs a) {
   if (INF32) {
     for (int c = tid; c < K / 4; c += kCoThreads) cp_async16(sm + g.off_xin + c * 16, a.xf + c * 4, 16u);
   } else {
-    for (int c = tid; c < K / 16; c += kCoThreads) cp_async16(sm + g.off_act + c * 16, a.xq + c * 16, 16u);
+    for (int c = tid; c < K / 16; c += kCoThreads) cp_async16(sm + g.off_act + c * 16, xq_in + c * 16, 16u);
   }
   cp_async_commit();
   // MX input: the scale bytes of the (at most kXsRegs) blocks this thread
@@ -264,7 +312,7 @@ __global__ void __launch_bounds__(kCoThreads, 2) cogemv_kernel(GemvArgs a) {
 #pragma unroll
     for (int k = 0; k < kXsRegs; ++k) {
       const int c = tid + k * kCoThreads, blk = c >> 1;
-      if (!(c & 1) && blk < kb) xsr[k] = a.xs[blk];
+      if (!(c & 1) && blk < kb) xsr[k] = __ldcg(xs_in + blk);
     }
   }
   cp_async_wait_all();
@@ -343,7 +391,7 @@ __global__ void __launch_bounds__(kCoThreads, 2) cogemv_kernel(GemvArgs a) {
       qs += __shfl_xor_sync(0xffffffffu, qs, 1);   // chunks c and c ^ 1 are lanes l and l ^ 1
       if (in && !(c & 1)) {
         const int blk = c >> 1;
-        const uint32_t sb = pre ? sb_pre : (blk < kb ? (uint32_t)a.xs[blk] : 0u);
+        const uint32_t sb = pre ? sb_pre : (blk < kb ? (uint32_t)__ldcg(xs_in + blk) : 0u);
         fab[blk] = make_uint2(__float_as_uint(blk < kb ? e8m0_to_float(sb) : 0.0f),
                               (uint32_t)(kMagic - (WFMT == 4 ? 128 * qs : 0)));
       }
@@ -453,13 +501,36 @@ __global__ void __launch_bounds__(kCoThreads, 2) cogemv_kernel(GemvArgs a) {
     float s = 0.0f;
 #pragma unroll
     for (int w = 0; w < kCoWarps; ++w) s += part[w * g.max_ng * 4 + e];
-    if (n < N) a.y[n] = s;
+    if (n < N) {
+      if (ROLE == 2) {
+        const size_t o = (size_t)(ep & 1u) * p.f_stride + p.row_off + n;
+        for (int r = 0; r < p.world; ++r) p.f_out[r][o] = s;
+      } else {
+        a.y[n] = s;
+      }
+    }
     if (QOUT) yv[e] = s;
   }
-  if (QOUT) {
+  // MX bytes out: local, or (ROLE 1) into every rank's mailbox at this rank's rows
+  auto put_q = [&](int i, uint8_t v) {
+    if (ROLE == 1) {
+      const size_t o = (size_t)(ep & 1u) * p.q_stride + p.row_off + i;
+      for (int r = 0; r < p.world; ++r) p.q_out[r][o] = v;
+    } else {
+      a.yq[i] = v;
+    }
+  };
+  auto put_s = [&](int b, uint8_t v) {
+    if (ROLE == 1) {
+      const size_t o = (size_t)(ep & 1u) * p.s_stride + p.row_off / kBlock + b;
+      for (int r = 0; r < p.world; ++r) p.s_out[r][o] = v;
+    } else {
+      a.ys[b] = v;
+    }
+  };
+  const int R0 = g_lo * 4, R1 = min((g_lo + ng) * 4, N);
+  if (QOUT && R1 > R0) {
     // MX bytes of the 32-row blocks this CTA's rows touch (N is a multiple of 32)
-    const int R0 = g_lo * 4, R1 = min((g_lo + ng) * 4, N);
-    if (R1 <= R0) return;
     const int b0 = R0 / kBlock, b1 = (R1 - 1) / kBlock;
     __syncthreads();   // every row of y written by this CTA ...
     int* flag = reinterpret_cast<int*>(smem + g.off_flag);
@@ -490,13 +561,43 @@ __global__ void __launch_bounds__(kCoThreads, 2) cogemv_kernel(GemvArgs a) {
       }
       uint32_t sb = 0;
       const int q = quant_lane(v, sb);
-      a.yq[b * kBlock + lane] = (uint8_t)(q + 128);
+      put_q(b * kBlock + lane, (uint8_t)(q + 128));
       if (lane == 0) {
-        a.ys[b] = (uint8_t)sb;
+        put_s(b, (uint8_t)sb);
         if (!inside) a.ycnt[b] = 0u;   // every contributor has counted itself in
       }
     }
   }
+  if (ROLE != 0) {
+    // the last CTA of the grid to finish publishes this rank's rows: every
+    // CTA's stores to the mailboxes are made visible system-wide first
+    __threadfence_system();
+    __syncthreads();
+    if (tid == 0) {
+      const unsigned old = atomicAdd(p.grid_cnt, 1u);
+      if (old == (unsigned)G - 1u) {
+        *p.grid_cnt = 0u;
+        __threadfence_system();
+        for (int r = 0; r < p.world; ++r) st_release_sys(p.flag_out[r], ep);
+      }
+    }
+  }
+}
+
+// The end of a column-sharded pair (one CTA): waits (bounded) for every
+// rank's second-linear rows, copies the full fp32 vector out of the local
+// mailbox and advances the epoch.
+__global__ void __launch_bounds__(1024, 1) peer_gather_kernel(PeerArgs p, float* y, int n) {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  const uint32_t ep = *reinterpret_cast<volatile const uint32_t*>(p.epoch) + 1u;
+  __shared__ int ok;
+  if (threadIdx.x == 0) ok = peer_wait(p.wait_flags, p.world, ep, p.wait_ns, p.status);
+  __syncthreads();
+  const float* src = p.f_in + (size_t)(ep & 1u) * p.f_in_stride;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) y[i] = __ldcg(src + i);
+  __syncthreads();
+  if (threadIdx.x == 0) *p.epoch = ep;
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
 
 int co_sms() {
@@ -509,23 +610,25 @@ int co_sms() {
   return n;
 }
 
-template <int WFMT, bool FAST, bool INF32, bool QOUT>
+template <int WFMT, bool FAST, bool INF32, bool QOUT, int ROLE>
 struct CoKernel {
   static cudaError_t prepare(size_t smem) {
     static SmemAttr attr;
-    static bool carve = false;
-    auto fn = cogemv_kernel<WFMT, FAST, INF32, QOUT>;
+    static bool carve[SmemAttr::kMaxDevices] = {};
+    auto fn = cogemv_kernel<WFMT, FAST, INF32, QOUT, ROLE>;
     if (cudaError_t e = attr.ensure(fn, smem)) return e;
-    if (!carve) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= SmemAttr::kMaxDevices) dev = 0;
+    if (!carve[dev]) {
       // two CTAs of up to 113 KB share an SM: the largest shared carveout
       if (cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributePreferredSharedMemoryCarveout,
                                                (int)cudaSharedmemCarveoutMaxShared))
         return e;
-      carve = true;
+      carve[dev] = true;
     }
     return cudaSuccess;
   }
-  static cudaError_t launch(const GemvArgs& a, cudaStream_t st, bool pdl) {
+  static cudaError_t launch(const GemvArgs& a, const PeerArgs& pa, cudaStream_t st, bool pdl) {
     const int G4 = (a.w.N + 3) / 4;
     const int grid = G4 < co_sms() ? G4 : co_sms();
     const CoGeom g = co_geom<WFMT>(a.w, grid, INF32, QOUT);
@@ -540,15 +643,15 @@ struct CoKernel {
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = pdl ? 1 : 0;
-    return cudaLaunchKernelEx(&cfg, cogemv_kernel<WFMT, FAST, INF32, QOUT>, a);
+    return cudaLaunchKernelEx(&cfg, cogemv_kernel<WFMT, FAST, INF32, QOUT, ROLE>, a, pa);
   }
 };
 
-template <int WFMT, bool INF32, bool QOUT>
-cudaError_t launch_co_fast(const GemvArgs& a, cudaStream_t st, bool pdl) {
+template <int WFMT, bool INF32, bool QOUT, int ROLE = 0>
+cudaError_t launch_co_fast(const GemvArgs& a, cudaStream_t st, bool pdl, const PeerArgs& pa = PeerArgs{}) {
   const bool fast = a.w.scale_lo >= (WFMT == 4 ? 5 : 1) && a.w.scale_hi <= 254;
-  return fast ? CoKernel<WFMT, true, INF32, QOUT>::launch(a, st, pdl)
-              : CoKernel<WFMT, false, INF32, QOUT>::launch(a, st, pdl);
+  return fast ? CoKernel<WFMT, true, INF32, QOUT, ROLE>::launch(a, pa, st, pdl)
+              : CoKernel<WFMT, false, INF32, QOUT, ROLE>::launch(a, pa, st, pdl);
 }
 
 template <int WFMT>
@@ -613,6 +716,36 @@ cudaError_t launch_cogemv_rows(const GemvArgs& a, int parts, cudaStream_t st, bo
     if (cudaError_t e = p.w.fmt == 4 ? launch_co_t<4>(p, st, pdl) : launch_co_t<8>(p, st, pdl)) return e;
   }
   return cudaSuccess;
+}
+
+cudaError_t launch_cogemv_peer(const GemvArgs& a, const PeerArgs& pa, int role, cudaStream_t st, bool pdl) {
+  if (pa.world < 1 || pa.world > kMaxPeers || !pa.epoch || !pa.grid_cnt) return cudaErrorInvalidValue;
+  if (role == 1) {
+    if (!a.xf || !a.yq || !a.ys || !a.ycnt || !a.y || !cogemv_supported(a.w, 1, true, true)) return cudaErrorInvalidValue;
+    return a.w.fmt == 4 ? launch_co_fast<4, true, true, 1>(a, st, pdl, pa) : launch_co_fast<8, true, true, 1>(a, st, pdl, pa);
+  }
+  if (role == 2) {
+    if (a.xf || a.yq || !pa.wait_flags || !pa.xq_base || !cogemv_supported(a.w, 1, false, false))
+      return cudaErrorInvalidValue;
+    return a.w.fmt == 4 ? launch_co_fast<4, false, false, 2>(a, st, pdl, pa)
+                        : launch_co_fast<8, false, false, 2>(a, st, pdl, pa);
+  }
+  return cudaErrorInvalidValue;
+}
+
+cudaError_t launch_peer_gather(const PeerArgs& pa, float* y, int n, cudaStream_t st, bool pdl) {
+  if (pa.world < 1 || pa.world > kMaxPeers || !pa.epoch || !pa.wait_flags || !pa.f_in || !y || n <= 0)
+    return cudaErrorInvalidValue;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(1);
+  cfg.blockDim = dim3(1024);
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, peer_gather_kernel, pa, y, n);
 }
 
 }  // namespace mxq

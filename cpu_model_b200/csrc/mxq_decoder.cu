@@ -149,8 +149,23 @@ int layers(mxq_decoder_s* D, int B, int T, int pos0, bool decode) {
     if ((rc = trace_copy(D, l, MXQ_TRACE_NORM2, D->hn, (size_t)R * d))) return rc;
     if ((rc = mxq_linear(c, D->gu[l], D->hn, (size_t)R, D->gub))) return rc;
     if ((rc = trace_copy(D, l, MXQ_TRACE_GU, D->gub, (size_t)R * 2 * D->F))) return rc;
-    if ((rc = dcheck(D, dk_swiglu(D->gub, R, D->F, D->act, st), "swiglu"))) return rc;
-    if ((rc = mxq_linear(c, D->down[l], D->act, (size_t)R, D->tmp))) return rc;
+    if (R == 1) {
+      // one token: silu(gate) * up straight to MX bytes (one kernel, the
+      // fused SwiGLU quantiser), which the down GEMV reads as its activation
+      uint8_t* hq = reinterpret_cast<uint8_t*>(D->act);
+      QuantArgs qa{};
+      qa.x = D->gub;
+      qa.up = D->gub + D->F;
+      qa.B = 1;
+      qa.K = D->F;
+      qa.out_q = hq;
+      qa.out_s = hq + D->F;
+      if ((rc = dcheck(D, launch_quantize(qa, 2, st, true), "swiglu quantize"))) return rc;
+      if ((rc = mxq_gemv(c, D->down[l], hq, hq + D->F, 1, D->tmp))) return rc;
+    } else {
+      if ((rc = dcheck(D, dk_swiglu(D->gub, R, D->F, D->act, st), "swiglu"))) return rc;
+      if ((rc = mxq_linear(c, D->down[l], D->act, (size_t)R, D->tmp))) return rc;
+    }
     // residual, then the next layer's (or the final) RMSNorm, in one kernel
     if ((rc = dcheck(D, dk_add_rmsnorm(D->h, D->tmp, D->gains + (size_t)(2 * l + 2) * d, R, d, eps, D->hn, st),
                      "residual + rmsnorm")))

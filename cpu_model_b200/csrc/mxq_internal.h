@@ -132,6 +132,33 @@ cudaError_t launch_rgemv(const GemvArgs& a, cudaStream_t st, bool pdl);
 // kernels one launch_rgemv call launches (batch-1 row slices: several)
 int rgemv_launches(const GemvArgs& a);
 
+// Peer mailboxes of a column-sharded batch-1 pair (mxq_cogemv.cu): where a
+// launch writes into every rank's mailbox, the flags it waits on and sets,
+// and the device epoch whose parity selects the mailbox half in use.
+constexpr int kMaxPeers = 8;
+struct PeerArgs {
+  int world, rank;
+  uint32_t* epoch;                 // local: calls completed (advanced by the gather)
+  uint32_t* grid_cnt;              // local: CTAs of this launch that have finished
+  const uint32_t* wait_flags;      // local flags this launch waits on, [world]
+  uint32_t* flag_out[kMaxPeers];   // per rank: the flag slot this launch sets
+  uint8_t* q_out[kMaxPeers];       // per rank: MX bytes [2][q_stride] (role 1)
+  uint8_t* s_out[kMaxPeers];       // per rank: MX scales [2][s_stride] (role 1)
+  float* f_out[kMaxPeers];         // per rank: fp32 rows [2][f_stride] (role 2)
+  size_t q_stride, s_stride, f_stride;
+  int row_off;                     // this rank's first row in the full vector
+  const uint8_t* xq_base;          // local MX input [2][xq_stride] (role 2)
+  const uint8_t* xs_base;
+  size_t xq_stride, xs_stride;
+  const float* f_in;               // local fp32 rows [2][f_in_stride] (gather)
+  size_t f_in_stride;
+  uint32_t* status;
+  uint64_t wait_ns;
+};
+// role 1 / 2: the first / second linear of the pair (see the kernel)
+cudaError_t launch_cogemv_peer(const GemvArgs& a, const PeerArgs& p, int role, cudaStream_t st, bool pdl);
+cudaError_t launch_peer_gather(const PeerArgs& p, float* y, int n, cudaStream_t st, bool pdl);
+
 // Batch-1 GEMV with two launches resident per SM (mxq_cogemv.cu): MX or fp32
 // input, fp32 output, optionally also MX bytes of the output (GemvArgs.yq).
 bool cogemv_supported(const WeightView& w, int B, bool inf32, bool qout);

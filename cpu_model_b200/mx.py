@@ -343,6 +343,51 @@ def mx_linear_pair(x, w1, w2, ctx=None):
     return y
 
 
+class PeerGroup:
+    """One rank of a batch-1 linear pair column-sharded over `world` GPUs
+    (mxq_peers_*): the first linear's rows of the MX intermediate and the
+    second's fp32 rows go straight into every rank's mailbox over NVLink.
+
+    handle() gives this rank's 64-byte mailbox handle; the caller gathers
+    every rank's (e.g. torch.distributed.all_gather_object) and passes the
+    list, in rank order, to connect()."""
+
+    def __init__(self, rank, world, n1, n2, ctx=None):
+        self.ctx = ctx or context()
+        self.rank, self.world, self.n1, self.n2 = rank, world, n1, n2
+        h = ctypes.c_void_p()
+        self._handle = ctypes.create_string_buffer(_lib.PEER_HANDLE_BYTES)
+        self.ctx._bind()
+        check(self.ctx.lib.mxq_peers_create(self.ctx.h, rank, world, n1, n2, ctypes.byref(h),
+                                            ctypes.cast(self._handle, ctypes.c_void_p)), self.ctx.h)
+        self.h = h
+
+    def handle(self):
+        return bytes(self._handle.raw)
+
+    def connect(self, handles):
+        assert len(handles) == self.world and all(len(b) == _lib.PEER_HANDLE_BYTES for b in handles)
+        buf = ctypes.create_string_buffer(b"".join(handles), _lib.PEER_HANDLE_BYTES * self.world)
+        check(self.ctx.lib.mxq_peers_connect(self.h, ctypes.cast(buf, ctypes.c_void_p)), self.ctx.h)
+
+    def set_wait_limit(self, us):
+        check(self.ctx.lib.mxq_peers_set_wait_limit(self.h, int(us)), self.ctx.h)
+
+    def linear_pair(self, x, w1, w2, out=None):
+        """x [K] or [1, K] fp32 on this rank's GPU; w1 / w2 this rank's
+        shards; returns the full [1, n2] output (the same on every rank)."""
+        _need_cuda(x, torch.float32, "x")
+        y = out if out is not None else torch.empty((1, self.n2), dtype=torch.float32, device=x.device)
+        self.ctx._bind()
+        check(self.ctx.lib.mxq_linear_pair_sharded(self.ctx.h, self.h, w1.h, w2.h, _ptr(x), _ptr(y)), self.ctx.h)
+        return y
+
+    def close(self):
+        if getattr(self, "h", None):
+            self.ctx.lib.mxq_peers_destroy(self.h)
+            self.h = None
+
+
 def gated_mlp_step(x, w_gate, w_up, w_down, ctx=None):
     """nca::layers::gated_mlp_step: down(quant(silu(gate x) * up x))."""
     ctx = ctx or w_gate.ctx

@@ -74,6 +74,7 @@ extern "C" {
 
 typedef struct mxq_context* mxq_ctx;
 typedef struct mxq_weight_s* mxq_weight;
+typedef struct mxq_peers_s* mxq_peers;
 
 /* nca::layers::HaltingState (nn/core/layers/halting.hpp:16-20): the same
  * members and, with size_t of 8 bytes, the same layout. */
@@ -194,6 +195,46 @@ MXQ_API int mxq_linear_pair(mxq_ctx ctx, mxq_weight w1, mxq_weight w2,
                             const float* x, size_t b, float* y);
 MXQ_API int mxq_linear_pair_host(mxq_ctx ctx, mxq_weight w1, mxq_weight w2,
                                  const float* x_host, size_t b, float* y_host);
+
+/* ------------------------------------------- column-sharded pair (GPUs) ---
+ * The batch-1 pair above column-sharded over `world` GPUs of one node, one
+ * process (context) per GPU: output-feature sharding of mx_gemv
+ * (nn/tests/test_auto_generated.cpp:56; each rank owns whole rows, full K,
+ * so a row's block sums are untouched).  No NCCL on the data path: the first linear writes its rows of
+ * the MX intermediate straight into every rank's mailbox (peer stores over
+ * NVLink into CUDA IPC memory) and sets its flag there; the second waits
+ * (bounded) for every rank's flag, reads the whole intermediate locally and
+ * writes its fp32 rows the same way; a one-CTA kernel waits for those and
+ * copies the full output.  Usage:
+ *   mxq_peers_create(ctx, rank, world, n1, n2, &p, handle)   -- n1: the
+ *     intermediate's length (a multiple of 32 * world), n2: the output's
+ *     (a multiple of world); handle: MXQ_PEER_HANDLE_BYTES to exchange;
+ *   (the caller gathers every rank's handle, in rank order)
+ *   mxq_peers_connect(p, handles)       -- handles: world * 64 bytes
+ *   mxq_linear_pair_sharded(ctx, p, w1, w2, x, y) -- w1: this rank's
+ *     n1/world x K rows, w2: its n2/world x n1 rows, x: [K] fp32 (device),
+ *     y: [n2] fp32 (device), the full output on every rank.
+ * Every rank must make the same calls in the same order.  A wait that runs
+ * out (a rank that never calls; limit mxq_peers_set_wait_limit, default 2 s)
+ * sets the context's status word: mxq_synchronize then returns
+ * MXQ_ERR_TIMEOUT, and the group must be destroyed and created again (its
+ * ranks' epochs no longer agree).  CUDA-graph capture of the call is
+ * supported (the mailbox half is chosen on the device). */
+#define MXQ_PEER_HANDLE_BYTES 64
+MXQ_API int mxq_peers_create(mxq_ctx ctx, int rank, int world, size_t n1, size_t n2,
+                             mxq_peers* out, void* handle_out);
+MXQ_API int mxq_peers_connect(mxq_peers peers, const void* handles);
+MXQ_API int mxq_peers_set_wait_limit(mxq_peers peers, uint32_t wait_us);
+MXQ_API int mxq_peers_destroy(mxq_peers peers);
+MXQ_API int mxq_linear_pair_sharded(mxq_ctx ctx, mxq_peers peers, mxq_weight w1, mxq_weight w2,
+                                    const float* x, float* y);
+/* Test hook, no counterpart in the reference: on a one-rank group, the
+ * second linear of the sharded pair (w2: n2 x n1) waiting on a flag that
+ * nothing sets, with its wait limited to wait_us (1 .. 1e6) microseconds:
+ * the wait runs out, the timeout lands in the status word, and the call
+ * returns mxq_synchronize's MXQ_ERR_TIMEOUT.  The group and the context
+ * stay usable. */
+MXQ_API int mxq_debug_peer_stall(mxq_ctx ctx, mxq_peers peers, mxq_weight w2, uint32_t wait_us);
 /* nca::layers::gated_mlp_step (nn/tests/test_auto_generated.cpp:42):
  * y = down(quant(silu(gate(x)) * up(x))). */
 MXQ_API int mxq_mlp_swiglu(mxq_ctx ctx, mxq_weight gate, mxq_weight up,

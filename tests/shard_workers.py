@@ -72,3 +72,66 @@ def moe_worker(rank, world, port, fmt, t, d, f, e, k, outdir):
     np.save(os.path.join(outdir, "moe_%d.npy" % rank), y.numpy())
     dist.barrier()
     dist.destroy_process_group()
+
+
+def peer_pair_worker(rank, world, port, fmt, k, m, n, steps, outdir):
+    """One GPU rank of mxq_linear_pair_sharded: the handles travel over a
+    gloo group; the result (every step) and a local re-computation from the
+    plain linears on every rank's shard are saved for the parent."""
+    from cpu_model_b200 import mx
+    _init(rank, world, port)
+    torch.cuda.set_device(rank)
+    ctx = mx.MXContext(rank)
+    w1, s1 = synth.weights(fmt, m, k, -8, -3, 91)
+    w2, s2 = synth.weights(fmt, n, m, -8, -3, 92)
+    m_s, n_s = m // world, n // world
+    W1 = [mx.MXWeight(torch.from_numpy(np.ascontiguousarray(w1[r * m_s:(r + 1) * m_s])),
+                      torch.from_numpy(np.ascontiguousarray(s1[r * m_s:(r + 1) * m_s])), fmt, m_s, k, ctx)
+          for r in range(world)]
+    W2 = [mx.MXWeight(torch.from_numpy(np.ascontiguousarray(w2[r * n_s:(r + 1) * n_s])),
+                      torch.from_numpy(np.ascontiguousarray(s2[r * n_s:(r + 1) * n_s])), fmt, n_s, m, ctx)
+          for r in range(world)]
+    P = mx.PeerGroup(rank, world, m, n, ctx)
+    handles = [None] * world
+    dist.all_gather_object(handles, P.handle())
+    P.connect(handles)
+    dist.barrier()
+    outs = []
+    for i in range(steps):
+        x = torch.from_numpy(synth.normal((1, k), 93 + i)).cuda()
+        outs.append(P.linear_pair(x, W1[rank], W2[rank]).cpu().numpy())
+    # CUDA-graph capture of two calls, replayed twice
+    xg = torch.from_numpy(synth.normal((1, k), 99)).cuda()
+    yg = torch.empty((1, n), dtype=torch.float32, device="cuda")
+    ctx.synchronize()
+    s = torch.cuda.Stream()
+    with torch.cuda.stream(s):
+        P.linear_pair(xg, W1[rank], W2[rank], out=yg)       # warm (sizes workspaces)
+        ctx.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=s):
+            P.linear_pair(xg, W1[rank], W2[rank], out=yg)
+            P.linear_pair(xg, W1[rank], W2[rank], out=yg)
+    torch.cuda.synchronize()
+    graph_outs = []
+    for _ in range(2):
+        g.replay()
+        torch.cuda.synchronize()
+        graph_outs.append(yg.cpu().numpy())
+    ctx.synchronize()
+    del g
+    # the same values from the plain linears on every shard
+    refs = []
+    for i in list(range(steps)) + [None]:
+        x = torch.from_numpy(synth.normal((1, k), 93 + i if i is not None else 99)).cuda()
+        y1 = torch.cat([mx.mx_linear(x, W1[r], ctx) for r in range(world)], dim=1)
+        refs.append(torch.cat([mx.mx_linear(y1, W2[r], ctx) for r in range(world)], dim=1).cpu().numpy())
+    ctx.synchronize()
+    np.savez(os.path.join(outdir, "peer_%d.npz" % rank), outs=np.stack(outs), graph=np.stack(graph_outs),
+             refs=np.stack(refs))
+    dist.barrier()
+    P.close()
+    for w in W1 + W2:
+        w.close()
+    ctx.close()
+    dist.destroy_process_group()
