@@ -653,15 +653,16 @@ def time_sharded_peer(ctx, dev, args, world, rank, max_over_ranks, barrier, up_f
             for i in range(steps):
                 P.linear_pair(x, *shards[i % copies], out=y)
     torch.cuda.synchronize()
-    g.replay()
-    torch.cuda.synchronize()
-    barrier()
-    torch.cuda.synchronize()
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
-    e0.record(stream)
-    g.replay()
-    e1.record(stream)
+    with torch.cuda.stream(stream):          # replay and events on the same stream
+        g.replay()
+        torch.cuda.synchronize()
+        barrier()
+        torch.cuda.synchronize()
+        e0.record(stream)
+        g.replay()
+        e1.record(stream)
     torch.cuda.synchronize()
     ms = max_over_ranks(e0.elapsed_time(e1) / steps)
     del g

@@ -179,6 +179,20 @@ __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
 __device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
   asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
+__device__ __forceinline__ void st_release_gpu(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+// Publishes this launch's mailbox stores and sets every rank's flag: the
+// peers are other GPUs (system scope), or with one rank this GPU itself.
+__device__ __forceinline__ void publish_flags(const PeerArgs& p, uint32_t ep) {
+  if (p.world == 1) {
+    asm volatile("fence.acq_rel.gpu;" ::: "memory");
+    st_release_gpu(p.flag_out[0], ep);
+  } else {
+    asm volatile("fence.acq_rel.sys;" ::: "memory");
+    for (int r = 0; r < p.world; ++r) st_release_sys(p.flag_out[r], ep);
+  }
+}
 // Bounded wait until every rank's flag has reached this call's epoch (the
 // flags are written over NVLink by the other GPUs).  Returns 0, with the
 // timeout recorded in the status word, once `limit_ns` have passed.
@@ -569,16 +583,18 @@ __global__ void __launch_bounds__(kCoThreads, 2) cogemv_kernel(GemvArgs a, PeerA
     }
   }
   if (ROLE != 0) {
-    // the last CTA of the grid to finish publishes this rank's rows: every
-    // CTA's stores to the mailboxes are made visible system-wide first
-    __threadfence_system();
+    // the last CTA of the grid to finish publishes this rank's rows: the CTA
+    // barrier orders every thread's mailbox stores before thread 0's
+    // GPU-scope fence and count; the last CTA's one system-scope fence is
+    // cumulative over every store it has observed through the counts, so the
+    // peers see all of them before the flag
     __syncthreads();
     if (tid == 0) {
+      __threadfence();
       const unsigned old = atomicAdd(p.grid_cnt, 1u);
       if (old == (unsigned)G - 1u) {
         *p.grid_cnt = 0u;
-        __threadfence_system();
-        for (int r = 0; r < p.world; ++r) st_release_sys(p.flag_out[r], ep);
+        publish_flags(p, ep);
       }
     }
   }
