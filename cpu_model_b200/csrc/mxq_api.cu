@@ -1478,16 +1478,16 @@ int mxq_linear_pair_sharded(mxq_ctx c, mxq_peers P, mxq_weight w1, mxq_weight w2
     }
     p2.f_stride = P->n2;
     p2.row_off = (int)(P->rank * n2s);
+    // ... then its last CTA: every rank's output rows -> y, epoch advanced
+    p2.done_flags = flags(P->rank, 1);
+    p2.f_in = reinterpret_cast<const float*>(P->mbox + P->off_f);
+    p2.f_in_stride = P->n2;
+    p2.n_out = (int)P->n2;
     GemvArgs dn{};
     dn.w = w2->v;
     dn.B = 1;
-    if ((rc = after_launch(c, launch_cogemv_peer(dn, p2, 2, c->stream, true), "sharded gemv 2"))) return rc;
-    // every rank's output rows -> y, and the epoch advances
-    PeerArgs p3 = pa;
-    p3.wait_flags = flags(P->rank, 1);
-    p3.f_in = reinterpret_cast<const float*>(P->mbox + P->off_f);
-    p3.f_in_stride = P->n2;
-    return after_launch(c, launch_peer_gather(p3, y, (int)P->n2, c->stream, true), "sharded gather");
+    dn.y = y;
+    return after_launch(c, launch_cogemv_peer(dn, p2, 2, c->stream, true), "sharded gemv 2");
   })
 }
 
@@ -1503,8 +1503,9 @@ int mxq_debug_peer_stall(mxq_ctx c, mxq_peers P, mxq_weight w2, uint32_t wait_us
       return fail(c, MXQ_ERR_INVALID_ARGUMENT, "debug peer stall: w2 must be n2 x n1");
     DeviceGuard g(c->device);
     // the second linear waiting on a flag word that nothing sets (local[3]);
-    // its own flag goes to the same scratch word and the epoch is not
-    // advanced, so the group stays consistent
+    // its own flag goes to the same scratch word, its output to a scratch
+    // buffer; a one-rank group needs no agreement with other ranks' epochs,
+    // so it stays usable
     PeerArgs p2{};
     p2.world = 1;
     p2.rank = 0;
@@ -1518,14 +1519,23 @@ int mxq_debug_peer_stall(mxq_ctx c, mxq_peers P, mxq_weight w2, uint32_t wait_us
     p2.xs_stride = P->n1 / kBlock;
     p2.f_out[0] = reinterpret_cast<float*>(P->mbox + P->off_f);
     p2.f_stride = P->n2;
+    p2.done_flags = P->local + 3;
+    p2.f_in = reinterpret_cast<const float*>(P->mbox + P->off_f);
+    p2.f_in_stride = P->n2;
+    p2.n_out = (int)P->n2;
     p2.status = c->status;
     p2.wait_ns = (uint64_t)wait_us * 1000ull;
+    float* scratch = nullptr;
+    cudaError_t e = cudaMalloc(&scratch, P->n2 * sizeof(float));
+    if (e != cudaSuccess) return cuda_fail(c, e, "debug peer stall");
     GemvArgs dn{};
     dn.w = w2->v;
     dn.B = 1;
-    int rc;
-    if ((rc = after_launch(c, launch_cogemv_peer(dn, p2, 2, c->stream, false), "sharded gemv 2"))) return rc;
-    const int st = mxq_synchronize(c);
+    dn.y = scratch;
+    int rc = after_launch(c, launch_cogemv_peer(dn, p2, 2, c->stream, false), "sharded gemv 2");
+    const int st = rc ? rc : mxq_synchronize(c);
+    cudaDeviceSynchronize();
+    cudaFree(scratch);
     cudaMemset(P->local + 3, 0, sizeof(uint32_t));
     return st;
   })

@@ -215,7 +215,9 @@ __device__ int peer_wait(const uint32_t* flags, int world, uint32_t ep, uint64_t
 // (fp32 input, MX output written into every rank's mailbox at this rank's
 // rows, then this rank's flag set on every rank).  ROLE 2: the second
 // linear (waits for every rank's flag, reads the full MX activation from the
-// local mailbox, writes its fp32 rows into every rank's mailbox, sets flags).
+// local mailbox, writes its fp32 rows into every rank's mailbox, sets flags;
+// its last CTA then waits for every rank's rows and copies the whole output
+// to y).
 template <int WFMT, bool FAST, bool INF32, bool QOUT, int ROLE>
 __global__ void __launch_bounds__(kCoThreads, 2) cogemv_kernel(GemvArgs a, PeerArgs p) {
   static_assert(ROLE == 0 || (ROLE == 1 && INF32 && QOUT) || (ROLE == 2 && !INF32 && !QOUT), "role");
@@ -585,35 +587,36 @@ __global__ void __launch_bounds__(kCoThreads, 2) cogemv_kernel(GemvArgs a, PeerA
   if (ROLE != 0) {
     // the last CTA of the grid to finish publishes this rank's rows: the CTA
     // barrier orders every thread's mailbox stores before thread 0's
-    // GPU-scope fence and count; the last CTA's one system-scope fence is
-    // cumulative over every store it has observed through the counts, so the
-    // peers see all of them before the flag
+    // GPU-scope fence and count; the last CTA's one release at system scope
+    // is cumulative over every store it has observed through the counts, so
+    // the peers see all of them before the flag
+    int* lastf = reinterpret_cast<int*>(smem + g.off_flag) + 3;
     __syncthreads();
     if (tid == 0) {
       __threadfence();
       const unsigned old = atomicAdd(p.grid_cnt, 1u);
-      if (old == (unsigned)G - 1u) {
+      const int last = old == (unsigned)G - 1u;
+      if (last) {
         *p.grid_cnt = 0u;
         publish_flags(p, ep);
       }
+      *lastf = last;
+    }
+    if (ROLE == 2) {
+      // the same CTA then waits for every rank's rows, copies the whole
+      // output out of the local mailbox and advances the epoch
+      __syncthreads();
+      if (*lastf) {   // CTA-uniform
+        int* okf = reinterpret_cast<int*>(smem + g.off_flag) + 2;
+        if (tid == 0) okf[0] = peer_wait(p.done_flags, p.world, ep, p.wait_ns, p.status);
+        __syncthreads();
+        const float* src = p.f_in + (size_t)(ep & 1u) * p.f_in_stride;
+        for (int i = tid; i < p.n_out; i += kCoThreads) a.y[i] = __ldcg(src + i);
+        __syncthreads();
+        if (tid == 0) *p.epoch = ep;
+      }
     }
   }
-}
-
-// The end of a column-sharded pair (one CTA): waits (bounded) for every
-// rank's second-linear rows, copies the full fp32 vector out of the local
-// mailbox and advances the epoch.
-__global__ void __launch_bounds__(1024, 1) peer_gather_kernel(PeerArgs p, float* y, int n) {
-  asm volatile("griddepcontrol.wait;" ::: "memory");
-  const uint32_t ep = *reinterpret_cast<volatile const uint32_t*>(p.epoch) + 1u;
-  __shared__ int ok;
-  if (threadIdx.x == 0) ok = peer_wait(p.wait_flags, p.world, ep, p.wait_ns, p.status);
-  __syncthreads();
-  const float* src = p.f_in + (size_t)(ep & 1u) * p.f_in_stride;
-  for (int i = threadIdx.x; i < n; i += blockDim.x) y[i] = __ldcg(src + i);
-  __syncthreads();
-  if (threadIdx.x == 0) *p.epoch = ep;
-  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
 
 int co_sms() {
@@ -741,27 +744,13 @@ cudaError_t launch_cogemv_peer(const GemvArgs& a, const PeerArgs& pa, int role, 
     return a.w.fmt == 4 ? launch_co_fast<4, true, true, 1>(a, st, pdl, pa) : launch_co_fast<8, true, true, 1>(a, st, pdl, pa);
   }
   if (role == 2) {
-    if (a.xf || a.yq || !pa.wait_flags || !pa.xq_base || !cogemv_supported(a.w, 1, false, false))
+    if (a.xf || a.yq || !a.y || !pa.wait_flags || !pa.done_flags || !pa.xq_base || !pa.f_in || pa.n_out <= 0 ||
+        !cogemv_supported(a.w, 1, false, false))
       return cudaErrorInvalidValue;
     return a.w.fmt == 4 ? launch_co_fast<4, false, false, 2>(a, st, pdl, pa)
                         : launch_co_fast<8, false, false, 2>(a, st, pdl, pa);
   }
   return cudaErrorInvalidValue;
-}
-
-cudaError_t launch_peer_gather(const PeerArgs& pa, float* y, int n, cudaStream_t st, bool pdl) {
-  if (pa.world < 1 || pa.world > kMaxPeers || !pa.epoch || !pa.wait_flags || !pa.f_in || !y || n <= 0)
-    return cudaErrorInvalidValue;
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(1);
-  cfg.blockDim = dim3(1024);
-  cfg.stream = st;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = pdl ? 1 : 0;
-  return cudaLaunchKernelEx(&cfg, peer_gather_kernel, pa, y, n);
 }
 
 }  // namespace mxq

@@ -138,7 +138,7 @@ int rgemv_launches(const GemvArgs& a);
 constexpr int kMaxPeers = 8;
 struct PeerArgs {
   int world, rank;
-  uint32_t* epoch;                 // local: calls completed (advanced by the gather)
+  uint32_t* epoch;                 // local: calls completed (advanced at the end of role 2)
   uint32_t* grid_cnt;              // local: CTAs of this launch that have finished
   const uint32_t* wait_flags;      // local flags this launch waits on, [world]
   uint32_t* flag_out[kMaxPeers];   // per rank: the flag slot this launch sets
@@ -150,14 +150,15 @@ struct PeerArgs {
   const uint8_t* xq_base;          // local MX input [2][xq_stride] (role 2)
   const uint8_t* xs_base;
   size_t xq_stride, xs_stride;
-  const float* f_in;               // local fp32 rows [2][f_in_stride] (gather)
+  const uint32_t* done_flags;      // local flags of the second linear's rows, [world] (role 2)
+  const float* f_in;               // local fp32 rows [2][f_in_stride] (role 2's copy out)
   size_t f_in_stride;
+  int n_out;                       // full output length (role 2)
   uint32_t* status;
   uint64_t wait_ns;
 };
 // role 1 / 2: the first / second linear of the pair (see the kernel)
 cudaError_t launch_cogemv_peer(const GemvArgs& a, const PeerArgs& p, int role, cudaStream_t st, bool pdl);
-cudaError_t launch_peer_gather(const PeerArgs& p, float* y, int n, cudaStream_t st, bool pdl);
 
 // Batch-1 GEMV with two launches resident per SM (mxq_cogemv.cu): MX or fp32
 // input, fp32 output, optionally also MX bytes of the output (GemvArgs.yq).

@@ -200,12 +200,13 @@ MXQ_API int mxq_linear_pair_host(mxq_ctx ctx, mxq_weight w1, mxq_weight w2,
  * The batch-1 pair above column-sharded over `world` GPUs of one node, one
  * process (context) per GPU: output-feature sharding of mx_gemv
  * (nn/tests/test_auto_generated.cpp:56; each rank owns whole rows, full K,
- * so a row's block sums are untouched).  No NCCL on the data path: the first linear writes its rows of
- * the MX intermediate straight into every rank's mailbox (peer stores over
- * NVLink into CUDA IPC memory) and sets its flag there; the second waits
- * (bounded) for every rank's flag, reads the whole intermediate locally and
- * writes its fp32 rows the same way; a one-CTA kernel waits for those and
- * copies the full output.  Usage:
+ * so a row's block sums are untouched).  No NCCL on the data path: the
+ * first linear writes its rows of the MX intermediate straight into every
+ * rank's mailbox (peer stores over NVLink into CUDA IPC memory) and sets its
+ * flag there; the second waits (bounded) for every rank's flag, reads the
+ * whole intermediate locally and writes its fp32 rows the same way, and its
+ * last CTA waits for every rank's rows and copies the full output.  Two
+ * kernels a call.  Usage:
  *   mxq_peers_create(ctx, rank, world, n1, n2, &p, handle)   -- n1: the
  *     intermediate's length (a multiple of 32 * world), n2: the output's
  *     (a multiple of world); handle: MXQ_PEER_HANDLE_BYTES to exchange;
