@@ -1010,6 +1010,7 @@ def run_case(args):
     launches of one kernel family, nothing timed.
       gemm512   3 up-projection linears at batch 512 (tcgen05 GEMM)
       gemv1     3 up-projection GEMVs at batch 1 on MX input (co-resident GEMV)
+      pair1     8 batch-1 MLP pair steps (mxq_linear_pair)
       moe       one full-size block-sparse MoE layer
       decode7b  the 7B decoder: a 2048-token prompt, then 3 decode steps"""
     import torch
@@ -1029,6 +1030,16 @@ def run_case(args):
             for _ in range(3):
                 mx.mx_linear(x, W, ctx)
         W.close()
+    elif args.case == "pair1":
+        wu, su = synth.weights(4, UP[0], UP[1], EMIN, EMAX, 1000)
+        wd, sd = synth.weights(4, DOWN[0], DOWN[1], EMIN, EMAX, 1001)
+        Wu = mx.MXWeight(torch.from_numpy(wu), torch.from_numpy(su), 4, UP[0], UP[1], ctx)
+        Wd = mx.MXWeight(torch.from_numpy(wd), torch.from_numpy(sd), 4, DOWN[0], DOWN[1], ctx)
+        x = torch.from_numpy(synth.normal((1, UP[1]), 9)).cuda()
+        for _ in range(8):
+            mx.mx_linear_pair(x, Wu, Wd, ctx)
+        Wu.close()
+        Wd.close()
     elif args.case == "moe":
         experts = moe_weights(ctx, torch.device("cuda", 0))
         x = torch.from_numpy(synth.normal((MOE["tokens"], MOE["d"]), 201)).cuda()
@@ -1064,7 +1075,7 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--copies", type=int, default=COPIES,
                     help="distinct weight-pair copies rotated per step (default 8 = 383 MB)")
-    ap.add_argument("--case", choices=["gemm512", "gemv1", "moe", "decode7b"],
+    ap.add_argument("--case", choices=["gemm512", "gemv1", "pair1", "moe", "decode7b"],
                     help="profiling: run one small workload (nothing timed) and exit")
     args = ap.parse_args()
     if args.warmup < 3:
