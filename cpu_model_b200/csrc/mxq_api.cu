@@ -66,8 +66,12 @@ struct mxq_context {
     cudaStream_t stream;
     cudaGraphExec_t exec;   // null: capture failed, run uncaptured
     bool mapped;            // copies by kernels through mapped memory, completion by a flag
+    uint64_t used;          // last call that used it (LRU)
   };
+  // at most kMaxHostGraphs recorded calls; the least recently used goes
+  static constexpr size_t kMaxHostGraphs = 64;
   std::vector<HostGraph> graphs;
+  uint64_t graph_clock = 0;
 };
 
 struct mxq_weight_s {
@@ -1196,9 +1200,10 @@ static int host_call(mxq_context* c, int kind, uint64_t w1, uint64_t w2, size_t 
   mxq_context::HostGraph* hg = nullptr;
   for (auto& g : c->graphs)
     if (g.kind == kind && g.w1 == w1 && g.w2 == w2 && g.b == b) hg = &g;
+  if (hg) hg->used = ++c->graph_clock;
   if (hg && (hg->gen != c->ws_gen || hg->stream != c->stream)) {
     if (hg->exec) cudaGraphExecDestroy(hg->exec);
-    *hg = mxq_context::HostGraph{kind, w1, w2, b, 0, nullptr, nullptr, false};
+    *hg = mxq_context::HostGraph{kind, w1, w2, b, 0, nullptr, nullptr, false, 0};
   }
   std::memcpy(c->pin_in, x_host, in_bytes);
   if (hg && hg->gen == c->ws_gen && hg->exec) {
@@ -1246,7 +1251,14 @@ static int host_call(mxq_context* c, int kind, uint64_t w1, uint64_t w2, size_t 
   if ((rc = mxq_synchronize(c))) return rc;
   std::memcpy(y_host, c->pin_out, out_bytes);
   if (!hg) {
-    c->graphs.push_back(mxq_context::HostGraph{kind, w1, w2, b, 0, c->stream, nullptr, false});
+    if (c->graphs.size() >= mxq_context::kMaxHostGraphs) {
+      auto lru = c->graphs.begin();
+      for (auto it = c->graphs.begin(); it != c->graphs.end(); ++it)
+        if (it->used < lru->used) lru = it;
+      if (lru->exec) cudaGraphExecDestroy(lru->exec);
+      c->graphs.erase(lru);
+    }
+    c->graphs.push_back(mxq_context::HostGraph{kind, w1, w2, b, 0, c->stream, nullptr, false, 0});
     hg = &c->graphs.back();
   }
   if (c->ws_gen == gen0 && hg->gen == 0) {

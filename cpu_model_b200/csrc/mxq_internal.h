@@ -2,6 +2,7 @@
 // (mxq_api.cu) and the kernel translation units.
 #pragma once
 #include <cstdint>
+#include <mutex>
 #include <cuda_runtime.h>
 #include "../../include/mxq.h"
 #include "mxq_common.cuh"
@@ -37,18 +38,23 @@ struct WeightView {
 
 // The largest dynamic shared memory already allowed for one kernel, per
 // device: cudaFuncSetAttribute applies to the current device only, so a
-// process with contexts on several devices sets it once on each.
+// process with contexts on several devices sets it once on each.  The value
+// only grows (a smaller request never lowers it), under a lock, so threads
+// launching the same kernel cannot leave it below what one of them needs.
 struct SmemAttr {
   static constexpr int kMaxDevices = 64;
   size_t bytes[kMaxDevices] = {};
+  std::mutex mu;
   template <typename F>
   cudaError_t ensure(F* fn, size_t smem) {
     if (smem <= 48 * 1024) return cudaSuccess;
     int dev = -1;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) dev = -1;
+    std::lock_guard<std::mutex> lock(mu);
     if (dev >= 0 && bytes[dev] >= smem) return cudaSuccess;
-    const cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (e == cudaSuccess && dev >= 0) bytes[dev] = smem;
+    const size_t want = dev >= 0 && bytes[dev] > smem ? bytes[dev] : smem;
+    const cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)want);
+    if (e == cudaSuccess && dev >= 0) bytes[dev] = want;
     return e;
   }
 };
