@@ -423,6 +423,66 @@ def time_decoder_7b(ctx, dev, args, world, max_over_ranks, barrier, peaks, rank)
     return out
 
 
+def time_decoder_7b_tp(ctx, dev, args, world, max_over_ranks, barrier, peaks, rank):
+    """N > 1: the same 7B decoder tensor-parallel over the N GPUs
+    (mxq_decoder_create_sharded): each rank holds 32/N heads and 1/N of every
+    linear's rows, four peer all-gathers a layer.  Every rank serves the same
+    sequences, so tokens/s counts them once.  Roofline: each rank's share of
+    the weights and K/V (the head is replicated) against one GPU's HBM peak."""
+    import torch
+    import torch.distributed as dist
+    from cpu_model_b200 import mx
+    c = DEC7B
+    D = mx.Decoder(c["n_layers"], c["d_model"], c["n_heads"], c["ffn"], c["vocab"], fmt=4,
+                   max_batch=max(c["batches"]), max_ctx=c["prompt"] + c["decode"], max_rows=8192, seed=3, ctx=ctx,
+                   rank=rank, world=world)
+    handles = [None] * world
+    dist.all_gather_object(handles, D.handle())
+    D.connect(handles)
+    barrier()
+    g = torch.Generator(device=dev)
+    out = {"config": dict({k: v for k, v in c.items() if k != "batches"}, weights="mx-int4, E8M0 exp [-8,-3]",
+                          kv_cache="bf16", data="uniform-random token ids", parallelism="tp%d" % world,
+                          exchange="peer all-gather over NVLink x4 per layer"),
+           "api": "mxq_decoder_create_sharded + prefill/decode", "batches": {}}
+    head = c["vocab"] * c["d_model"] * (0.5 + 1.0 / 32)
+    wbytes = (decoder_weight_bytes(c, 4) - head) / world + head
+    for b in c["batches"]:
+        g.manual_seed(100 + b)                             # the same tokens on every rank
+        prompt = torch.randint(0, c["vocab"], (b, c["prompt"]), dtype=torch.int32, device=dev, generator=g)
+        steps = torch.randint(0, c["vocab"], (c["decode"], b), dtype=torch.int32, device=dev, generator=g)
+        D.reset()
+        D.prefill(prompt)
+        for i in range(3):
+            D.decode(steps[i].contiguous())
+        torch.cuda.synchronize()
+        D.reset()
+        barrier()
+        e0, e1, e2 = (torch.cuda.Event(enable_timing=True) for _ in range(3))
+        e0.record()
+        D.prefill(prompt)
+        e1.record()
+        for i in range(c["decode"]):
+            D.decode(steps[i])
+        e2.record()
+        torch.cuda.synchronize()
+        pre_ms = max_over_ranks(e0.elapsed_time(e1))
+        dec_ms = max_over_ranks(e1.elapsed_time(e2))
+        step_ms = dec_ms / c["decode"]
+        avg_ctx = c["prompt"] + (c["decode"] + 1) / 2.0
+        kv = b * c["n_layers"] * 2 * avg_ctx * c["d_model"] * 2 / world
+        gbs = (wbytes + kv) / (step_ms / 1e3) / 1e9
+        out["batches"][str(b)] = {
+            "decode_tokens_per_s": b * c["decode"] / (dec_ms / 1e3), "decode_ms_per_step": step_ms,
+            "prefill_tokens_per_s": b * c["prompt"] / (pre_ms / 1e3), "prefill_ms": pre_ms,
+            "roofline": {"bound": "hbm", "achieved_per_gpu": gbs, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                         "frac": gbs / peaks["hbm_gbs"], "bytes_per_step_per_gpu": wbytes + kv}}
+    torch.cuda.synchronize()
+    barrier()
+    D.close()
+    return out
+
+
 def time_ppo_1b(ctx, dev, args, world, max_over_ranks, barrier, peaks, rank):
     """The 1B MX-int8 rollout policy: 256 rollouts x 512 tokens scored
     (per-token log-probs of the next token, a value per token), then GAE over
@@ -955,6 +1015,9 @@ def run_ours(args):
     sharded = None
     if world > 1 and not args.no_shard:
         sharded = time_sharded(ctx, dev, args, world, rank, max_over_ranks, barrier)
+        if not args.no_decoder:
+            sharded["decoder_7b_tensor_parallel"] = time_decoder_7b_tp(ctx, dev, args, world, max_over_ranks,
+                                                                       barrier, peaks, rank)
 
     if rank == 0:
         line = {

@@ -66,6 +66,9 @@ SIGNATURES = {
     "mxq_debug_gemm_stall": [_vp, _vp, _vp, _sz, _vp, ctypes.c_uint32],
     "mxq_route_topk": [_vp, _vp, _sz, _sz, _sz, _vp, _vp],
     "mxq_decoder_create": [_vp, _vp, ctypes.c_uint64, ctypes.POINTER(_vp)],
+    "mxq_decoder_create_sharded": [_vp, _vp, ctypes.c_uint64, _i, _i, ctypes.POINTER(_vp), _vp],
+    "mxq_decoder_connect": [_vp, _vp],
+    "mxq_decoder_set_wait_limit": [_vp, ctypes.c_uint32],
     "mxq_decoder_destroy": [_vp],
     "mxq_decoder_reset": [_vp],
     "mxq_decoder_length": [_vp, ctypes.POINTER(_i)],

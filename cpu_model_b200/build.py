@@ -12,7 +12,8 @@ import sys
 HERE = os.path.dirname(os.path.abspath(__file__))
 ROOT = os.path.dirname(HERE)
 SOURCES = ["mxq_api.cu", "mxq_quant.cu", "mxq_gemv.cu", "mxq_rgemv.cu", "mxq_bgemv.cu", "mxq_gemm.cu", "mxq_moe.cu",
-           "mxq_ops.cu", "mxq_decoder_kernels.cu", "mxq_decoder.cu", "mxq_cogemv.cu"]
+           "mxq_ops.cu", "mxq_decoder_kernels.cu", "mxq_decoder.cu", "mxq_cogemv.cu",
+           "mxq_tp.cu"]
 LIB = os.path.join(HERE, "libmxq.so")
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 FLAGS = [

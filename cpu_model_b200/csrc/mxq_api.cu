@@ -2130,6 +2130,8 @@ cudaStream_t ctx_stream(mxq_context* c) { return c->stream; }
 void ctx_set_stream_raw(mxq_context* c, cudaStream_t s) { c->stream = s; }
 int ctx_fail(mxq_context* c, int code, const char* msg) { return fail(c, code, "%s", msg); }
 int ctx_cuda_fail(mxq_context* c, cudaError_t e, const char* what) { return cuda_fail(c, e, what); }
+uint32_t* ctx_status_word(mxq_context* c) { return c->status; }
+int ctx_device(mxq_context* c) { return c->device; }
 void ctx_add_launches(mxq_context* c, uint64_t n) { c->launches += n; }
 uint64_t ctx_ws_gen(mxq_context* c) { return c->ws_gen; }
 uint64_t ctx_launches(mxq_context* c) { return c->launches; }

@@ -171,17 +171,6 @@ __device__ __forceinline__ int owner_cta(int q, int G4, int G) {
 }
 
 // --- peer mailboxes (column-sharded linears across GPUs) -----------------
-__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
-  uint32_t v;
-  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
-}
-__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
-  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
-__device__ __forceinline__ void st_release_gpu(uint32_t* p, uint32_t v) {
-  asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
 // Publishes this launch's mailbox stores and sets every rank's flag: the
 // peers are other GPUs (system scope), or with one rank this GPU itself.
 __device__ __forceinline__ void publish_flags(const PeerArgs& p, uint32_t ep) {
@@ -193,24 +182,6 @@ __device__ __forceinline__ void publish_flags(const PeerArgs& p, uint32_t ep) {
     for (int r = 0; r < p.world; ++r) st_release_sys(p.flag_out[r], ep);
   }
 }
-// Bounded wait until every rank's flag has reached this call's epoch (the
-// flags are written over NVLink by the other GPUs).  Returns 0, with the
-// timeout recorded in the status word, once `limit_ns` have passed.
-__device__ int peer_wait(const uint32_t* flags, int world, uint32_t ep, uint64_t limit_ns, uint32_t* status) {
-  const uint64_t t0 = globaltimer_ns();
-  for (int r = 0; r < world; ++r) {
-    for (uint32_t it = 0;; ++it) {
-      if ((int)(ld_acquire_sys(flags + r) - ep) >= 0) break;
-      if (it > (1u << 26) || globaltimer_ns() - t0 > limit_ns) {
-        if (status) atomicOr(status, kStatusTimeout);
-        return 0;
-      }
-      __nanosleep(100);
-    }
-  }
-  return 1;
-}
-
 // ROLE 0: a plain GEMV.  ROLE 1: the first linear of a column-sharded pair
 // (fp32 input, MX output written into every rank's mailbox at this rank's
 // rows, then this rank's flag set on every rank).  ROLE 2: the second

@@ -199,6 +199,36 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint32
   return false;
 }
 
+// --- flags in peer memory (mailboxes over NVLink) ------------------------
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ void st_release_gpu(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+// Bounded wait until every rank's flag has reached this call's epoch (the
+// flags are written over NVLink by the other GPUs).  Returns 0, with the
+// timeout recorded in the status word, once `limit_ns` have passed.
+__device__ inline int peer_wait(const uint32_t* flags, int world, uint32_t ep, uint64_t limit_ns, uint32_t* status) {
+  const uint64_t t0 = globaltimer_ns();
+  for (int r = 0; r < world; ++r) {
+    for (uint32_t it = 0;; ++it) {
+      if ((int)(ld_acquire_sys(flags + r) - ep) >= 0) break;
+      if (it > (1u << 26) || globaltimer_ns() - t0 > limit_ns) {
+        if (status) atomicOr(status, kStatusTimeout);
+        return 0;
+      }
+      __nanosleep(100);
+    }
+  }
+  return 1;
+}
+
 // 1-D bulk copy global -> shared, completing bytes on an mbarrier.
 // Both addresses 16-byte aligned and bytes a multiple of 16.
 __device__ __forceinline__ void bulk_g2s(void* dst_smem, const void* src,

@@ -15,8 +15,19 @@
 // graph and replayed.  Weights are synthetic (seeded, generated on the
 // device), as no checkpoint is available; mxq_decoder_weight exposes the
 // handles, so real weights can be uploaded into the same shapes.
+//
+// Tensor parallel (mxq_decoder_create_sharded): rank r of p holds heads
+// [r H/p, (r+1) H/p) -- their q, k, v rows, their K/V cache and attention --
+// and rows [r n/p, (r+1) n/p) of the O, gate, up and down weights (whole
+// rows, full K: output-feature sharding).  Embedding, RMSNorm, residual and
+// the vocabulary head are replicated.  Four peer all-gathers a layer
+// (mxq_tp.cu) rebuild the full activation in every rank's mailbox: the
+// attention output, the O output, the SwiGLU activation (MX bytes at one
+// token row) and the down output.  Every row's arithmetic is that of the
+// unsharded decoder.
 #include <cmath>
 #include <cstring>
+#include <initializer_list>
 #include <new>
 #include <vector>
 
@@ -29,19 +40,29 @@ struct mxq_decoder_s {
   mxq_context* c = nullptr;
   mxq_decoder_config cfg{};
   int d = 0, H = 0, hd = 0, F = 0, V = 0, Vo = 0, L = 0, Bmax = 0, Cmax = 0, Rmax = 0, nch = 0;
+  // tensor parallel: this rank of `world`; its width, heads and FFN columns
+  // (dl = d, Hl = H, Fl = F unsharded)
+  bool tp = false;
+  int rank = 0, world = 1, dl = 0, Hl = 0, Fl = 0;
+  uint8_t* mbox = nullptr;            // flags [2 slots][8 ranks] u32, then slot 0, slot 1
+  size_t slot_bytes = 0, mbox_bytes = 0;
+  uint8_t* peer[kMaxPeers] = {};      // every rank's mailbox as mapped here
+  bool opened[kMaxPeers] = {};
+  uint32_t* tpw = nullptr;            // local: slot sequence numbers [2], grid counters [2]
+  uint64_t wait_ns = kWaitLimitNs;
   std::vector<mxq_weight> qkv, o, gu, down;
   mxq_weight lm = nullptr;
   float* embed = nullptr;      // [V][d]
   float* gains = nullptr;      // [2L + 1][d]: per layer the attention then the MLP RMSNorm weights, then the final
   float* cs = nullptr;         // [Cmax][hd/2][2] rotary cos, sin
-  __nv_bfloat16* kc = nullptr; // [L][Bmax][H][Cmax][hd]
+  __nv_bfloat16* kc = nullptr; // [L][Bmax][Hl][Cmax][hd]
   __nv_bfloat16* vc = nullptr;
   int32_t* pos_dev = nullptr;  // position of the next token (all sequences)
   int len = 0;                 // host mirror of *pos_dev
   float *h = nullptr, *hn = nullptr, *qkvb = nullptr, *att = nullptr, *tmp = nullptr, *gub = nullptr,
         *act = nullptr, *logits = nullptr, *part = nullptr, *hl = nullptr;
   int32_t* tok = nullptr;      // [Rmax + 1]
-  uint32_t* done = nullptr;    // [Bmax][H] one-token attention chunk counters (zero between calls)
+  uint32_t* done = nullptr;    // [Bmax][Hl] one-token attention chunk counters (zero between calls)
   int trace_layer = -1;
   float* trace[MXQ_TRACE_COUNT] = {};
   size_t trace_elems[MXQ_TRACE_COUNT] = {};
@@ -59,7 +80,7 @@ struct mxq_decoder_s {
 
 namespace {
 
-size_t kv_layer_elems(const mxq_decoder_s* D) { return (size_t)D->Bmax * D->H * D->Cmax * D->hd; }
+size_t kv_layer_elems(const mxq_decoder_s* D) { return (size_t)D->Bmax * D->Hl * D->Cmax * D->hd; }
 
 int dfail(mxq_decoder_s* D, int code, const char* msg) { return ctx_fail(D->c, code, msg); }
 
@@ -77,18 +98,45 @@ cudaError_t dalloc(T*& p, size_t count) {
   return e;
 }
 
-// Synthetic MX weight [n][k] on the device (seeded), uploaded as a handle.
-int synth_weight(mxq_decoder_s* D, int n, int k, uint64_t seed, mxq_weight* out) {
+struct RowRange {
+  int row0, rows;
+};
+
+// Synthetic MX weight [n][k] on the device (seeded), uploaded as a handle;
+// with row ranges, only those rows of it, in range order (a rank's shard:
+// the same bytes the unsharded weight has in those rows).
+int synth_weight(mxq_decoder_s* D, int n, int k, uint64_t seed, mxq_weight* out,
+                 std::initializer_list<RowRange> ranges = {}) {
   const int fmt = D->cfg.fmt;
-  const size_t db = fmt == 4 ? (size_t)n * k / 2 : (size_t)n * k, sb = (size_t)n * k / 32;
+  const size_t rb = fmt == 4 ? (size_t)k / 2 : (size_t)k, rs = (size_t)k / 32;   // data, scale bytes a row
+  const size_t db = rb * n, sb = rs * n;
+  size_t ns = 0;
+  for (const RowRange& r : ranges) ns += (size_t)r.rows;
   uint8_t* tmp = nullptr;
-  cudaError_t e = cudaMalloc(&tmp, db + sb + 16);
+  cudaError_t e = cudaMalloc(&tmp, db + sb + (ns ? (rb + rs) * ns : 0) + 16);
   if (e != cudaSuccess) return ctx_cuda_fail(D->c, e, "decoder weight scratch");
+  cudaStream_t st = ctx_stream(D->c);
   const int emin = fmt == 4 ? -8 : -10, emax = fmt == 4 ? -3 : -4;
-  e = dk_synth_weight(tmp, db, tmp + db, sb, fmt, emin, emax, seed, ctx_stream(D->c));
-  int rc = e == cudaSuccess ? mxq_weight_create(D->c, fmt, (size_t)n, (size_t)k, tmp, tmp + db, 1, out)
+  e = dk_synth_weight(tmp, db, tmp + db, sb, fmt, emin, emax, seed, st);
+  const uint8_t *wd = tmp, *ws = tmp + db;
+  size_t rows = (size_t)n;
+  if (ns && e == cudaSuccess) {
+    uint8_t *sd = tmp + db + sb, *ss = sd + rb * ns;
+    size_t at = 0;
+    for (const RowRange& r : ranges) {
+      if (e == cudaSuccess)
+        e = cudaMemcpyAsync(sd + rb * at, wd + rb * r.row0, rb * r.rows, cudaMemcpyDeviceToDevice, st);
+      if (e == cudaSuccess)
+        e = cudaMemcpyAsync(ss + rs * at, ws + rs * r.row0, rs * r.rows, cudaMemcpyDeviceToDevice, st);
+      at += (size_t)r.rows;
+    }
+    wd = sd;
+    ws = ss;
+    rows = ns;
+  }
+  int rc = e == cudaSuccess ? mxq_weight_create(D->c, fmt, rows, (size_t)k, wd, ws, 1, out)
                             : ctx_cuda_fail(D->c, e, "decoder weight synth");
-  cudaStreamSynchronize(ctx_stream(D->c));
+  cudaStreamSynchronize(st);
   cudaFree(tmp);
   return rc;
 }
@@ -108,10 +156,137 @@ int trace_copy(mxq_decoder_s* D, int layer, int id, const float* src, size_t n) 
   return MXQ_OK;
 }
 
+// --- tensor parallel: the peer all-gathers --------------------------------
+constexpr size_t kTpFlagBytes = 256;
+
+uint32_t* tp_flags(const mxq_decoder_s* D, int r, int slot) {
+  return reinterpret_cast<uint32_t*>(D->peer[r]) + slot * kMaxPeers;
+}
+size_t tp_slot_off(const mxq_decoder_s* D, int slot) { return kTpFlagBytes + (size_t)slot * D->slot_bytes; }
+
+int tp_gather(mxq_decoder_s* D, int slot, int rows, std::initializer_list<TpSegment> segs) {
+  TpGatherArgs a{};
+  a.world = D->world;
+  a.rank = D->rank;
+  a.rows = rows;
+  a.nseg = 0;
+  for (const TpSegment& g : segs) {
+    if (g.dst_off + (size_t)(rows - 1) * g.dst_ld + g.row_bytes * (size_t)D->world > tp_slot_off(D, slot + 1))
+      return dfail(D, MXQ_ERR_INVALID_ARGUMENT, "tensor-parallel exchange larger than its mailbox slot");
+    a.seg[a.nseg++] = g;
+  }
+  for (int r = 0; r < D->world; ++r) {
+    a.base[r] = D->peer[r];
+    a.flag_out[r] = tp_flags(D, r, slot) + D->rank;
+  }
+  a.wait_flags = tp_flags(D, D->rank, slot);
+  a.seq = D->tpw + slot;
+  a.grid_cnt = D->tpw + 2 + slot;
+  a.status = ctx_status_word(D->c);
+  a.wait_ns = D->wait_ns;
+  return dcheck(D, launch_tp_gather(a, ctx_stream(D->c)), "tensor-parallel all-gather");
+}
+
+// this rank's columns [R][n] fp32 -> every rank's [R][n * world] in slot `slot`
+int tp_gather_f32(mxq_decoder_s* D, int slot, const float* src, int R, int n, const float** full) {
+  const size_t rb = (size_t)n * 4;
+  const size_t off = tp_slot_off(D, slot);
+  if (int rc = tp_gather(D, slot, R, {TpSegment{reinterpret_cast<const uint8_t*>(src), rb, rb, off, rb * D->world}}))
+    return rc;
+  *full = reinterpret_cast<const float*>(D->mbox + off);
+  return MXQ_OK;
+}
+
+// one row of MX bytes (q [n], scales [n/32]) -> every rank's [n * world] and
+// [n * world / 32] in slot `slot`
+int tp_gather_mx(mxq_decoder_s* D, int slot, const uint8_t* q, const uint8_t* sc, int n, const uint8_t** fq,
+                 const uint8_t** fs) {
+  const size_t off = tp_slot_off(D, slot), nf = (size_t)n * D->world;
+  const size_t soff = off + (nf + 15) / 16 * 16;
+  if (int rc = tp_gather(D, slot, 1, {TpSegment{q, (size_t)n, (size_t)n, off, nf},
+                                      TpSegment{sc, (size_t)n / 32, (size_t)n / 32, soff, nf / 32}}))
+    return rc;
+  *fq = D->mbox + off;
+  *fs = D->mbox + soff;
+  return MXQ_OK;
+}
+
+// The layers of a tensor-parallel decoder (see the file comment): as layers()
+// below, over this rank's heads and rows, with the four all-gathers.
+int layers_tp(mxq_decoder_s* D, int B, int T, int pos0, bool decode) {
+  mxq_context* c = D->c;
+  cudaStream_t st = ctx_stream(c);
+  const int R = B * T, d = D->d, dl = D->dl, Fl = D->Fl;
+  const float eps = D->cfg.norm_eps;
+  int rc;
+  const float* full = nullptr;
+  for (int l = 0; l < D->L; ++l) {
+    __nv_bfloat16* kc = D->kc + (size_t)l * kv_layer_elems(D);
+    __nv_bfloat16* vc = D->vc + (size_t)l * kv_layer_elems(D);
+    if ((rc = trace_copy(D, l, MXQ_TRACE_IN, D->h, (size_t)R * d))) return rc;
+    if (l == 0 && (rc = dcheck(D, dk_rmsnorm(D->h, D->gains, R, d, eps, D->hn, st), "rmsnorm"))) return rc;
+    if ((rc = trace_copy(D, l, MXQ_TRACE_NORM1, D->hn, (size_t)R * d))) return rc;
+    // this rank's heads: q, k, v rows [R][3 dl]
+    if ((rc = mxq_linear(c, D->qkv[l], D->hn, (size_t)R, D->qkvb))) return rc;
+    if ((rc = trace_copy(D, l, MXQ_TRACE_QKV, D->qkvb, (size_t)R * 3 * dl))) return rc;
+    if ((rc = dcheck(D, dk_rope_kv(D->qkvb, R, T, dl, D->Hl, pos0, decode ? D->pos_dev : nullptr, D->cs, D->Cmax,
+                                   kc, vc, st), "rope")))
+      return rc;
+    if ((rc = trace_copy(D, l, MXQ_TRACE_ROPE, D->qkvb, (size_t)R * 3 * dl))) return rc;
+    if (decode) {
+      if ((rc = dcheck(D, dk_attn_decode(D->qkvb, B, dl, D->Hl, D->pos_dev, kc, vc, D->Cmax, D->part, D->done,
+                                         D->att, st),
+                       "attention")))
+        return rc;
+    } else {
+      if ((rc = dcheck(D, dk_attn_prompt(D->qkvb, B, T, dl, D->Hl, pos0, kc, vc, D->Cmax, D->att, st),
+                       "attention")))
+        return rc;
+    }
+    if ((rc = tp_gather_f32(D, 0, D->att, R, dl, &full))) return rc;          // every head's output
+    if ((rc = trace_copy(D, l, MXQ_TRACE_ATT, full, (size_t)R * d))) return rc;
+    if ((rc = mxq_linear(c, D->o[l], full, (size_t)R, D->tmp))) return rc;
+    if ((rc = tp_gather_f32(D, 1, D->tmp, R, dl, &full))) return rc;          // the full O output
+    if ((rc = dcheck(D, dk_add_rmsnorm(D->h, full, D->gains + (size_t)(2 * l + 1) * d, R, d, eps, D->hn, st),
+                     "residual + rmsnorm")))
+      return rc;
+    if ((rc = trace_copy(D, l, MXQ_TRACE_H1, D->h, (size_t)R * d))) return rc;
+    if ((rc = trace_copy(D, l, MXQ_TRACE_NORM2, D->hn, (size_t)R * d))) return rc;
+    // this rank's gate rows, then its up rows: [R][2 Fl]
+    if ((rc = mxq_linear(c, D->gu[l], D->hn, (size_t)R, D->gub))) return rc;
+    if ((rc = trace_copy(D, l, MXQ_TRACE_GU, D->gub, (size_t)R * 2 * Fl))) return rc;
+    if (R == 1) {
+      uint8_t* hq = reinterpret_cast<uint8_t*>(D->act);
+      QuantArgs qa{};
+      qa.x = D->gub;
+      qa.up = D->gub + Fl;
+      qa.B = 1;
+      qa.K = Fl;
+      qa.out_q = hq;
+      qa.out_s = hq + (Fl + 15) / 16 * 16;
+      if ((rc = dcheck(D, launch_quantize(qa, 2, st, true), "swiglu quantize"))) return rc;
+      const uint8_t *fq = nullptr, *fs = nullptr;
+      if ((rc = tp_gather_mx(D, 0, qa.out_q, qa.out_s, Fl, &fq, &fs))) return rc;   // the whole MX activation
+      if ((rc = mxq_gemv(c, D->down[l], fq, fs, 1, D->tmp))) return rc;
+    } else {
+      if ((rc = dcheck(D, dk_swiglu(D->gub, R, Fl, D->act, st), "swiglu"))) return rc;
+      if ((rc = tp_gather_f32(D, 0, D->act, R, Fl, &full))) return rc;
+      if ((rc = mxq_linear(c, D->down[l], full, (size_t)R, D->tmp))) return rc;
+    }
+    if ((rc = tp_gather_f32(D, 1, D->tmp, R, dl, &full))) return rc;          // the full down output
+    if ((rc = dcheck(D, dk_add_rmsnorm(D->h, full, D->gains + (size_t)(2 * l + 2) * d, R, d, eps, D->hn, st),
+                     "residual + rmsnorm")))
+      return rc;
+    if ((rc = trace_copy(D, l, MXQ_TRACE_OUT, D->h, (size_t)R * d))) return rc;
+  }
+  return trace_copy(D, D->L, MXQ_TRACE_IN, D->h, (size_t)R * d);
+}
+
 // All layers over R = B * T rows already embedded in D->h.  decode: one token
 // per sequence at the device position (T == 1); otherwise a prompt chunk at
 // positions pos0 .. pos0 + T - 1.  Leaves the final RMSNorm output in D->hn.
 int layers(mxq_decoder_s* D, int B, int T, int pos0, bool decode) {
+  if (D->tp) return layers_tp(D, B, T, pos0, decode);
   mxq_context* c = D->c;
   cudaStream_t st = ctx_stream(c);
   const int R = B * T, d = D->d;
@@ -222,6 +397,13 @@ int mxq_decoder_destroy(mxq_decoder D) {
     if (t) cudaFree(t);
   for (auto& g : D->graphs)
     if (g.exec) cudaGraphExecDestroy(g.exec);
+  if (D->tp) {
+    cudaDeviceSynchronize();
+    for (int r = 0; r < D->world; ++r)
+      if (D->opened[r]) cudaIpcCloseMemHandle(D->peer[r]);
+    if (D->mbox) cudaFree(D->mbox);
+    if (D->tpw) cudaFree(D->tpw);
+  }
   if (D->dstream) cudaStreamSynchronize(D->dstream), cudaStreamDestroy(D->dstream);
   if (D->ev_in) cudaEventDestroy(D->ev_in);
   if (D->ev_out) cudaEventDestroy(D->ev_out);
@@ -229,9 +411,17 @@ int mxq_decoder_destroy(mxq_decoder D) {
   return MXQ_OK;
 }
 
-int mxq_decoder_create(mxq_ctx c, const mxq_decoder_config* cfg, uint64_t seed, mxq_decoder* out) {
+}  // extern "C"
+
+namespace {
+
+// world == 0: the unsharded decoder; otherwise rank `rank` of a
+// tensor-parallel group of `world` (one rank: the sharded code path on one
+// GPU, its exchanges through its own mailbox)
+int create_decoder(mxq_ctx c, const mxq_decoder_config* cfg, uint64_t seed, int rank, int world, mxq_decoder* out,
+                   void* handle_out) {
   DEC_TRY({
-    if (!c || !cfg || !out) return MXQ_ERR_INVALID_ARGUMENT;
+    if (!c || !cfg || !out || (world && !handle_out)) return MXQ_ERR_INVALID_ARGUMENT;
     *out = nullptr;
     const mxq_decoder_config& g = *cfg;
     if (g.n_layers < 1 || g.d_model < 128 || g.n_heads < 1 || g.d_model % g.n_heads || g.d_model / g.n_heads != 128 ||
@@ -240,6 +430,10 @@ int mxq_decoder_create(mxq_ctx c, const mxq_decoder_config* cfg, uint64_t seed, 
       return ctx_fail(c, MXQ_ERR_INVALID_ARGUMENT,
                       "decoder config: head dim 128, d and ffn multiples of 64, vocab >= 2, fmt 4/8, "
                       "max_rows >= max_batch >= 1, max_ctx >= 1");
+    if (world && (world > kMaxPeers || rank < 0 || rank >= world || g.n_heads % world || g.ffn % (32 * world)))
+      return ctx_fail(c, MXQ_ERR_INVALID_ARGUMENT,
+                      "sharded decoder: rank in [0, world), world in [1, 8] dividing the heads, ffn a multiple of "
+                      "32 * world");
     auto* D = new mxq_decoder_s();
     D->c = c;
     D->cfg = g;
@@ -254,20 +448,38 @@ int mxq_decoder_create(mxq_ctx c, const mxq_decoder_config* cfg, uint64_t seed, 
     D->Cmax = g.max_ctx;
     D->Rmax = g.max_rows;
     D->nch = dk_decode_chunks(g.max_ctx);
+    D->tp = world > 0;
+    D->rank = D->tp ? rank : 0;
+    D->world = D->tp ? world : 1;
+    D->dl = D->d / D->world;
+    D->Hl = D->H / D->world;
+    D->Fl = D->F / D->world;
     cudaStream_t st = ctx_stream(c);
     int rc = MXQ_OK;
     auto bail = [&](int code) {
       mxq_decoder_destroy(D);
       return code;
     };
-    const int d = D->d, F = D->F;
+    const int d = D->d, F = D->F, dl = D->dl, Fl = D->Fl, r0 = D->rank;
     for (int l = 0; l < D->L && rc == MXQ_OK; ++l) {
       mxq_weight w;
       const uint64_t s = seed * 1000003ull + (uint64_t)l * 16;
-      if ((rc = synth_weight(D, 3 * d, d, s + 1, &w)) == MXQ_OK) D->qkv.push_back(w);
-      if (rc == MXQ_OK && (rc = synth_weight(D, d, d, s + 2, &w)) == MXQ_OK) D->o.push_back(w);
-      if (rc == MXQ_OK && (rc = synth_weight(D, 2 * F, d, s + 3, &w)) == MXQ_OK) D->gu.push_back(w);
-      if (rc == MXQ_OK && (rc = synth_weight(D, d, F, s + 4, &w)) == MXQ_OK) D->down.push_back(w);
+      if (!D->tp) {
+        if ((rc = synth_weight(D, 3 * d, d, s + 1, &w)) == MXQ_OK) D->qkv.push_back(w);
+        if (rc == MXQ_OK && (rc = synth_weight(D, d, d, s + 2, &w)) == MXQ_OK) D->o.push_back(w);
+        if (rc == MXQ_OK && (rc = synth_weight(D, 2 * F, d, s + 3, &w)) == MXQ_OK) D->gu.push_back(w);
+        if (rc == MXQ_OK && (rc = synth_weight(D, d, F, s + 4, &w)) == MXQ_OK) D->down.push_back(w);
+        continue;
+      }
+      // this rank's rows of the same weights: its heads' q, k, v rows; its
+      // O rows; its gate rows then its up rows; its down rows
+      if ((rc = synth_weight(D, 3 * d, d, s + 1, &w, {{r0 * dl, dl}, {d + r0 * dl, dl}, {2 * d + r0 * dl, dl}})) ==
+          MXQ_OK)
+        D->qkv.push_back(w);
+      if (rc == MXQ_OK && (rc = synth_weight(D, d, d, s + 2, &w, {{r0 * dl, dl}})) == MXQ_OK) D->o.push_back(w);
+      if (rc == MXQ_OK && (rc = synth_weight(D, 2 * F, d, s + 3, &w, {{r0 * Fl, Fl}, {F + r0 * Fl, Fl}})) == MXQ_OK)
+        D->gu.push_back(w);
+      if (rc == MXQ_OK && (rc = synth_weight(D, d, F, s + 4, &w, {{r0 * dl, dl}})) == MXQ_OK) D->down.push_back(w);
     }
     if (rc == MXQ_OK) rc = synth_weight(D, D->Vo, d, seed * 1000003ull + 999983ull, &D->lm);
     if (rc) return bail(rc);
@@ -304,10 +516,27 @@ int mxq_decoder_create(mxq_ctx c, const mxq_decoder_config* cfg, uint64_t seed, 
     if (e == cudaSuccess) e = dalloc(D->act, R * F);
     if (e == cudaSuccess) e = dalloc(D->logits, R * D->Vo);
     if (e == cudaSuccess) e = dalloc(D->hl, (size_t)D->Bmax * d);
-    if (e == cudaSuccess) e = dalloc(D->part, (size_t)D->Bmax * D->H * D->nch * (128 + 2));
+    if (e == cudaSuccess) e = dalloc(D->part, (size_t)D->Bmax * D->Hl * D->nch * (128 + 2));
     if (e == cudaSuccess) e = dalloc(D->tok, R + 1);
-    if (e == cudaSuccess) e = dalloc(D->done, (size_t)D->Bmax * D->H);
-    if (e == cudaSuccess) e = cudaMemsetAsync(D->done, 0, (size_t)D->Bmax * D->H * 4 + 16, st);
+    if (e == cudaSuccess) e = dalloc(D->done, (size_t)D->Bmax * D->Hl);
+    if (e == cudaSuccess) e = cudaMemsetAsync(D->done, 0, (size_t)D->Bmax * D->Hl * 4 + 16, st);
+    if (D->tp) {
+      // mailbox: flags, then two slots of [max_rows][max(d, ffn)] fp32 each
+      const size_t wmax = (size_t)(d > F ? d : F);
+      D->slot_bytes = (R * wmax * 4 + 256 + 255) / 256 * 256;
+      D->mbox_bytes = kTpFlagBytes + 2 * D->slot_bytes;
+      if (e == cudaSuccess) e = cudaMalloc(&D->mbox, D->mbox_bytes);
+      if (e == cudaSuccess) e = cudaMemsetAsync(D->mbox, 0, D->mbox_bytes, st);
+      if (e == cudaSuccess) e = dalloc(D->tpw, 4);
+      if (e == cudaSuccess) e = cudaMemsetAsync(D->tpw, 0, 4 * sizeof(uint32_t), st);
+      cudaIpcMemHandle_t ih{};
+      if (e == cudaSuccess) e = cudaIpcGetMemHandle(&ih, D->mbox);
+      if (e == cudaSuccess) {
+        static_assert(sizeof(cudaIpcMemHandle_t) == MXQ_PEER_HANDLE_BYTES, "IPC handle size");
+        std::memcpy(handle_out, &ih, sizeof(ih));
+        D->peer[D->rank] = D->mbox;
+      }
+    }
     if (e == cudaSuccess) e = cudaMemsetAsync(D->tok, 0, (R + 1) * 4, st);
     if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&D->dstream, cudaStreamNonBlocking);
     if (e == cudaSuccess) e = cudaEventCreateWithFlags(&D->ev_in, cudaEventDisableTiming);
@@ -319,11 +548,58 @@ int mxq_decoder_create(mxq_ctx c, const mxq_decoder_config* cfg, uint64_t seed, 
   })
 }
 
+bool tp_ready(mxq_decoder_s* D) {
+  for (int r = 0; r < D->world; ++r)
+    if (!D->peer[r]) return false;
+  return true;
+}
+
+}  // namespace
+
+extern "C" {
+
+int mxq_decoder_create(mxq_ctx c, const mxq_decoder_config* cfg, uint64_t seed, mxq_decoder* out) {
+  return create_decoder(c, cfg, seed, 0, 0, out, nullptr);
+}
+
+int mxq_decoder_create_sharded(mxq_ctx c, const mxq_decoder_config* cfg, uint64_t seed, int rank, int world,
+                               mxq_decoder* out, void* handle_out) {
+  if (!c) return MXQ_ERR_INVALID_ARGUMENT;
+  if (world < 1) return ctx_fail(c, MXQ_ERR_INVALID_ARGUMENT, "sharded decoder: world >= 1");
+  return create_decoder(c, cfg, seed, rank, world, out, handle_out);
+}
+
+int mxq_decoder_connect(mxq_decoder D, const void* handles) {
+  DEC_TRY({
+    if (!D || !handles) return MXQ_ERR_INVALID_ARGUMENT;
+    if (!D->tp) return dfail(D, MXQ_ERR_INVALID_ARGUMENT, "connect: the decoder is not sharded");
+    for (int r = 0; r < D->world; ++r) {
+      if (r == D->rank || D->peer[r]) continue;
+      cudaIpcMemHandle_t h;
+      std::memcpy(&h, static_cast<const uint8_t*>(handles) + (size_t)r * sizeof(h), sizeof(h));
+      void* p = nullptr;
+      const cudaError_t e = cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess);
+      if (e != cudaSuccess) return ctx_cuda_fail(D->c, e, "open a peer's decoder mailbox");
+      D->peer[r] = static_cast<uint8_t*>(p);
+      D->opened[r] = true;
+    }
+    return MXQ_OK;
+  })
+}
+
+int mxq_decoder_set_wait_limit(mxq_decoder D, uint32_t wait_us) {
+  if (!D) return MXQ_ERR_INVALID_ARGUMENT;
+  if (wait_us == 0 || wait_us > 10000000u)
+    return dfail(D, MXQ_ERR_INVALID_ARGUMENT, "decoder wait limit must be in [1, 1e7] microseconds");
+  D->wait_ns = (uint64_t)wait_us * 1000ull;
+  return MXQ_OK;
+}
+
 int mxq_decoder_reset(mxq_decoder D) {
   if (!D) return MXQ_ERR_INVALID_ARGUMENT;
   D->len = 0;
   cudaError_t e = cudaMemsetAsync(D->pos_dev, 0, 4, ctx_stream(D->c));
-  if (e == cudaSuccess) e = cudaMemsetAsync(D->done, 0, (size_t)D->Bmax * D->H * 4, ctx_stream(D->c));
+  if (e == cudaSuccess) e = cudaMemsetAsync(D->done, 0, (size_t)D->Bmax * D->Hl * 4, ctx_stream(D->c));
   return e == cudaSuccess ? MXQ_OK : ctx_cuda_fail(D->c, e, "decoder reset");
 }
 
@@ -336,6 +612,8 @@ int mxq_decoder_length(mxq_decoder D, int* len) {
 int mxq_decoder_prefill(mxq_decoder D, const int32_t* tokens, size_t b, size_t t, float* logits) {
   DEC_TRY({
     if (!D || !tokens) return MXQ_ERR_INVALID_ARGUMENT;
+    if (D->tp && !tp_ready(D))
+      return dfail(D, MXQ_ERR_INVALID_ARGUMENT, "sharded decoder not connected (mxq_decoder_connect)");
     if (b == 0 || t == 0 || (int)b > D->Bmax || t > (size_t)D->Cmax)
       return dfail(D, MXQ_ERR_INVALID_ARGUMENT, "prefill: batch in [1, max_batch], prompt in [1, max_ctx]");
     cudaStream_t st = ctx_stream(D->c);
@@ -366,6 +644,8 @@ int mxq_decoder_prefill(mxq_decoder D, const int32_t* tokens, size_t b, size_t t
 int mxq_decoder_decode(mxq_decoder D, const int32_t* tokens, size_t b, float* logits) {
   DEC_TRY({
     if (!D || !tokens || !logits) return MXQ_ERR_INVALID_ARGUMENT;
+    if (D->tp && !tp_ready(D))
+      return dfail(D, MXQ_ERR_INVALID_ARGUMENT, "sharded decoder not connected (mxq_decoder_connect)");
     if (b == 0 || (int)b > D->Bmax) return dfail(D, MXQ_ERR_INVALID_ARGUMENT, "decode: batch in [1, max_batch]");
     if (D->len >= D->Cmax) return dfail(D, MXQ_ERR_INVALID_ARGUMENT, "decode: the context is full (max_ctx)");
     mxq_context* c = D->c;
@@ -434,6 +714,8 @@ int mxq_decoder_decode(mxq_decoder D, const int32_t* tokens, size_t b, float* lo
 int mxq_decoder_score(mxq_decoder D, const int32_t* tokens, size_t b, size_t t, float* logp, float* values) {
   DEC_TRY({
     if (!D || !tokens || !logp) return MXQ_ERR_INVALID_ARGUMENT;
+    if (D->tp && !tp_ready(D))
+      return dfail(D, MXQ_ERR_INVALID_ARGUMENT, "sharded decoder not connected (mxq_decoder_connect)");
     if (b == 0 || t < 2 || t > (size_t)D->Cmax || t > (size_t)D->Rmax)
       return dfail(D, MXQ_ERR_INVALID_ARGUMENT, "score: batch >= 1, sequence length in [2, min(max_ctx, max_rows)]");
     if (values && !D->cfg.value_head) return dfail(D, MXQ_ERR_INVALID_ARGUMENT, "score: the decoder has no value head");

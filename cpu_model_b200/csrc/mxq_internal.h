@@ -166,6 +166,29 @@ struct PeerArgs {
 // role 1 / 2: the first / second linear of the pair (see the kernel)
 cudaError_t launch_cogemv_peer(const GemvArgs& a, const PeerArgs& p, int role, cudaStream_t st, bool pdl);
 
+// Peer all-gather of the tensor-parallel decoder (mxq_tp.cu).  Each rank
+// holds its columns of `rows` rows (per segment: row_bytes a row, this
+// rank's slice); the launch stores them at column rank * row_bytes of every
+// rank's mailbox rows (dst_off + r * dst_ld), sets this rank's flag word in
+// every mailbox to the slot's next sequence number, and its last CTA waits
+// (bounded) until every rank's flag in the local mailbox has reached it.
+struct TpSegment {
+  const uint8_t* src;              // this rank's rows, src_ld bytes apart
+  size_t src_ld, row_bytes, dst_off, dst_ld;
+};
+struct TpGatherArgs {
+  int world, rank, rows, nseg;
+  TpSegment seg[2];
+  uint8_t* base[kMaxPeers];        // every rank's mailbox as mapped here
+  uint32_t* flag_out[kMaxPeers];   // per rank: this rank's flag word of the slot
+  const uint32_t* wait_flags;      // local mailbox: the slot's flags, [world]
+  uint32_t* seq;                   // local: the slot's completed exchanges
+  uint32_t* grid_cnt;              // local: CTAs of this launch that have finished
+  uint32_t* status;
+  uint64_t wait_ns;
+};
+cudaError_t launch_tp_gather(const TpGatherArgs& a, cudaStream_t st);
+
 // Batch-1 GEMV with two launches resident per SM (mxq_cogemv.cu): MX or fp32
 // input, fp32 output, optionally also MX bytes of the output (GemvArgs.yq).
 bool cogemv_supported(const WeightView& w, int B, bool inf32, bool qout);
@@ -181,6 +204,8 @@ cudaStream_t ctx_stream(mxq_context* c);
 void ctx_set_stream_raw(mxq_context* c, cudaStream_t s);
 int ctx_fail(mxq_context* c, int code, const char* msg);
 int ctx_cuda_fail(mxq_context* c, cudaError_t e, const char* what);
+uint32_t* ctx_status_word(mxq_context* c);
+int ctx_device(mxq_context* c);
 void ctx_add_launches(mxq_context* c, uint64_t n);
 uint64_t ctx_ws_gen(mxq_context* c);
 uint64_t ctx_launches(mxq_context* c);

@@ -681,17 +681,44 @@ class Decoder:
     """The dense decoder on the MX linears (mxq_decoder_*): prefill a prompt,
     decode one token per sequence per step (CUDA-graph replayed), or score
     whole sequences (per-token log-probs and values, the rollout forward).
-    Weights are synthetic, generated from `seed` on the device."""
+    Weights are synthetic, generated from `seed` on the device.
+
+    With `world` set, rank `rank` of a tensor-parallel decoder over `world`
+    GPUs (mxq_decoder_create_sharded): handle() gives this rank's 64-byte
+    mailbox handle; the caller gathers every rank's (e.g.
+    torch.distributed.all_gather_object) and passes the list, in rank order,
+    to connect() before the first pass."""
 
     def __init__(self, n_layers, d_model, n_heads, ffn, vocab, fmt=FMT_INT4, max_batch=1, max_ctx=2048,
-                 max_rows=8192, value_head=False, rope_theta=10000.0, norm_eps=1e-5, seed=0, ctx=None):
+                 max_rows=8192, value_head=False, rope_theta=10000.0, norm_eps=1e-5, seed=0, ctx=None,
+                 rank=0, world=None):
         self.ctx = ctx or context()
         self.cfg = DecoderConfig(n_layers, d_model, n_heads, ffn, vocab, fmt, max_batch, max_ctx, max_rows,
                                  1 if value_head else 0, rope_theta, norm_eps)
+        self.rank, self.world = rank, world
         h = ctypes.c_void_p()
         self.ctx._bind()
-        check(self.ctx.lib.mxq_decoder_create(self.ctx.h, ctypes.byref(self.cfg), seed, ctypes.byref(h)), self.ctx.h)
+        if world is None:
+            check(self.ctx.lib.mxq_decoder_create(self.ctx.h, ctypes.byref(self.cfg), seed, ctypes.byref(h)),
+                  self.ctx.h)
+        else:
+            self._handle = ctypes.create_string_buffer(_lib.PEER_HANDLE_BYTES)
+            check(self.ctx.lib.mxq_decoder_create_sharded(self.ctx.h, ctypes.byref(self.cfg), seed, rank, world,
+                                                          ctypes.byref(h),
+                                                          ctypes.cast(self._handle, ctypes.c_void_p)), self.ctx.h)
         self.h = h
+
+    def handle(self):
+        return bytes(self._handle.raw)
+
+    def connect(self, handles):
+        assert self.world is not None and len(handles) == self.world
+        assert all(len(b) == _lib.PEER_HANDLE_BYTES for b in handles)
+        buf = ctypes.create_string_buffer(b"".join(handles), _lib.PEER_HANDLE_BYTES * self.world)
+        check(self.ctx.lib.mxq_decoder_connect(self.h, ctypes.cast(buf, ctypes.c_void_p)), self.ctx.h)
+
+    def set_wait_limit(self, us):
+        check(self.ctx.lib.mxq_decoder_set_wait_limit(self.h, int(us)), self.ctx.h)
 
     def _tokens(self, tokens):
         if not isinstance(tokens, torch.Tensor) or tokens.dtype != torch.int32 or not tokens.is_contiguous():

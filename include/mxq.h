@@ -463,6 +463,36 @@ typedef struct mxq_decoder_s* mxq_decoder;
 
 MXQ_API int mxq_decoder_create(mxq_ctx ctx, const mxq_decoder_config* cfg,
                                uint64_t seed, mxq_decoder* out);
+/* The same decoder tensor-parallel over `world` GPUs of one node (one process
+ * and context per GPU; world 1..8 dividing n_heads, ffn a multiple of
+ * 32 * world).  Rank `rank` holds the q, k, v rows, K/V cache and attention
+ * of heads [rank * n_heads / world, (rank + 1) * n_heads / world) and rows
+ * [rank * n / world, (rank + 1) * n / world) of the O, gate, up and down
+ * weights (output-feature sharding of mx_gemv,
+ * nn/tests/test_auto_generated.cpp:56: whole rows, full K); the embedding,
+ * RMSNorm weights and vocabulary head are replicated, and every weight row
+ * is the unsharded decoder's for the same seed.  After the attention, the O
+ * linear, the SwiGLU and the down linear of every layer, one kernel stores
+ * this rank's columns into every rank's mailbox (peer stores over NVLink
+ * into CUDA IPC memory), sets its flag there and waits (bounded) for every
+ * rank's flag; no NCCL on the data path.  Usage:
+ *   mxq_decoder_create_sharded(ctx, cfg, seed, rank, world, &dec, handle)
+ *     -- handle: MXQ_PEER_HANDLE_BYTES to exchange;
+ *   (the caller gathers every rank's handle, in rank order)
+ *   mxq_decoder_connect(dec, handles)   -- world * 64 bytes
+ * then prefill / decode / score as on one GPU, with the same tokens in the
+ * same order on every rank; every rank returns the full logits.  A wait that
+ * runs out (mxq_decoder_set_wait_limit, default 2 s) sets the context's
+ * status word (mxq_synchronize returns MXQ_ERR_TIMEOUT) and the group must
+ * be created again.  With world 1 the sharded code path runs on one GPU,
+ * exchanging through its own mailbox.  Trace points QKV, ROPE and GU hold
+ * this rank's columns ([rows][3 d / world], [rows][2 ffn / world]); the
+ * others the full rows. */
+MXQ_API int mxq_decoder_create_sharded(mxq_ctx ctx, const mxq_decoder_config* cfg,
+                                       uint64_t seed, int rank, int world,
+                                       mxq_decoder* out, void* handle_out);
+MXQ_API int mxq_decoder_connect(mxq_decoder dec, const void* handles);
+MXQ_API int mxq_decoder_set_wait_limit(mxq_decoder dec, uint32_t wait_us);
 MXQ_API int mxq_decoder_destroy(mxq_decoder dec);
 /* Forget every cached position. */
 MXQ_API int mxq_decoder_reset(mxq_decoder dec);

@@ -135,3 +135,44 @@ def peer_pair_worker(rank, world, port, fmt, k, m, n, steps, outdir):
         w.close()
     ctx.close()
     dist.destroy_process_group()
+
+
+def decoder_tp_worker(rank, world, port, cfg, seed, steps, outdir):
+    """One GPU rank of the tensor-parallel decoder: handles over a gloo group;
+    a prompt, `steps` decode steps (graph-replayed after the first) and a
+    scoring pass, then the same calls on an unsharded decoder of the same
+    seed on this GPU; everything saved for the parent."""
+    from cpu_model_b200 import mx
+    _init(rank, world, port)
+    torch.cuda.set_device(rank)
+    ctx = mx.MXContext(rank)
+    b, vocab = cfg["max_batch"], cfg["vocab"]
+
+    def run(dec):
+        rng = np.random.default_rng(17)       # the same tokens on every rank
+        outs = [dec.prefill(torch.from_numpy(rng.integers(0, vocab, (b, 5), dtype=np.int32)).cuda()).cpu().numpy()]
+        for _ in range(steps):
+            tok = torch.from_numpy(rng.integers(0, vocab, (b,), dtype=np.int32)).cuda()
+            outs.append(dec.decode(tok).cpu().numpy())
+        dec.reset()
+        one = [dec.prefill(torch.from_numpy(rng.integers(0, vocab, (1, 3), dtype=np.int32)).cuda()).cpu().numpy()]
+        for _ in range(steps):
+            one.append(dec.decode(torch.from_numpy(rng.integers(0, vocab, (1,), dtype=np.int32)).cuda()).cpu().numpy())
+        dec.reset()
+        logp, _ = dec.score(torch.from_numpy(rng.integers(0, vocab, (b, 8), dtype=np.int32)).cuda())
+        return np.stack(outs), np.stack(one), logp.cpu().numpy()
+
+    dec = mx.Decoder(seed=seed, ctx=ctx, rank=rank, world=world, **cfg)
+    handles = [None] * world
+    dist.all_gather_object(handles, dec.handle())
+    dec.connect(handles)
+    dist.barrier()
+    tp = run(dec)
+    ctx.synchronize()
+    dist.barrier()
+    dec.close()
+    ref = run(mx.Decoder(seed=seed, ctx=ctx, **cfg))
+    np.savez(os.path.join(outdir, "dec_%d.npz" % rank), outs=tp[0], one=tp[1], logp=tp[2],
+             ref_outs=ref[0], ref_one=ref[1], ref_logp=ref[2])
+    dist.barrier()
+    dist.destroy_process_group()
