@@ -425,8 +425,9 @@ def time_decoder_7b(ctx, dev, args, world, max_over_ranks, barrier, peaks, rank)
 
 def time_decoder_7b_tp(ctx, dev, args, world, max_over_ranks, barrier, peaks, rank):
     """N > 1: the same 7B decoder tensor-parallel over the N GPUs
-    (mxq_decoder_create_sharded): each rank holds 32/N heads and 1/N of every
-    linear's rows, four peer all-gathers a layer.  Every rank serves the same
+    (mxq_decoder_create_sharded): each rank holds 32/N heads and 11008/N FFN
+    units (their QKV and gate/up rows, their O and down columns); two peer
+    exchanges of partial sums a layer.  Every rank serves the same
     sequences, so tokens/s counts them once.  Roofline: each rank's share of
     the weights and K/V (the head is replicated) against one GPU's HBM peak."""
     import torch
@@ -443,7 +444,7 @@ def time_decoder_7b_tp(ctx, dev, args, world, max_over_ranks, barrier, peaks, ra
     g = torch.Generator(device=dev)
     out = {"config": dict({k: v for k, v in c.items() if k != "batches"}, weights="mx-int4, E8M0 exp [-8,-3]",
                           kv_cache="bf16", data="uniform-random token ids", parallelism="tp%d" % world,
-                          exchange="peer all-gather over NVLink x4 per layer"),
+                          exchange="peer exchange of O / down partial sums over NVLink, 2 per layer"),
            "api": "mxq_decoder_create_sharded + prefill/decode", "batches": {}}
     head = c["vocab"] * c["d_model"] * (0.5 + 1.0 / 32)
     wbytes = (decoder_weight_bytes(c, 4) - head) / world + head

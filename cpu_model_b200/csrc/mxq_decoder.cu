@@ -17,14 +17,16 @@
 // handles, so real weights can be uploaded into the same shapes.
 //
 // Tensor parallel (mxq_decoder_create_sharded): rank r of p holds heads
-// [r H/p, (r+1) H/p) -- their q, k, v rows, their K/V cache and attention --
-// and rows [r n/p, (r+1) n/p) of the O, gate, up and down weights (whole
-// rows, full K: output-feature sharding).  Embedding, RMSNorm, residual and
-// the vocabulary head are replicated.  Four peer all-gathers a layer
-// (mxq_tp.cu) rebuild the full activation in every rank's mailbox: the
-// attention output, the O output, the SwiGLU activation (MX bytes at one
-// token row) and the down output.  Every row's arithmetic is that of the
-// unsharded decoder.
+// [r H/p, (r+1) H/p) -- their q, k, v rows, K/V cache and attention -- and
+// FFN units [r F/p, (r+1) F/p) -- their gate and up rows; the O and down
+// weights are split along K the same way (the columns of its heads and of
+// its units), so each rank's O and down outputs are partial sums of every
+// row.  Two peer all-gathers a layer (mxq_tp.cu) bring every rank's partial
+// sums into every rank's mailbox, and the residual kernel adds them in rank
+// order, so all ranks hold the same hidden state.  Embedding, RMSNorm and
+// the vocabulary head are replicated.  The MX block dots are the unsharded
+// decoder's (shards end on 32-blocks); only the fp32 order of the block sums
+// of O and down differs.
 #include <cmath>
 #include <cstring>
 #include <initializer_list>
@@ -44,7 +46,7 @@ struct mxq_decoder_s {
   // (dl = d, Hl = H, Fl = F unsharded)
   bool tp = false;
   int rank = 0, world = 1, dl = 0, Hl = 0, Fl = 0;
-  uint8_t* mbox = nullptr;            // flags [2 slots][8 ranks] u32, then slot 0, slot 1
+  uint8_t* mbox = nullptr;            // flags [2 slots][8 ranks] u32, then slot 0 (O), slot 1 (down)
   size_t slot_bytes = 0, mbox_bytes = 0;
   uint8_t* peer[kMaxPeers] = {};      // every rank's mailbox as mapped here
   bool opened[kMaxPeers] = {};
@@ -103,17 +105,18 @@ struct RowRange {
 };
 
 // Synthetic MX weight [n][k] on the device (seeded), uploaded as a handle;
-// with row ranges, only those rows of it, in range order (a rank's shard:
-// the same bytes the unsharded weight has in those rows).
+// with row ranges, only those rows of it, in range order; with cols > 0,
+// only columns [col0, col0 + cols) of every row (whole 32-blocks).  A
+// rank's shard: the same bytes the unsharded weight has there.
 int synth_weight(mxq_decoder_s* D, int n, int k, uint64_t seed, mxq_weight* out,
-                 std::initializer_list<RowRange> ranges = {}) {
+                 std::initializer_list<RowRange> ranges = {}, int col0 = 0, int cols = 0) {
   const int fmt = D->cfg.fmt;
   const size_t rb = fmt == 4 ? (size_t)k / 2 : (size_t)k, rs = (size_t)k / 32;   // data, scale bytes a row
   const size_t db = rb * n, sb = rs * n;
   size_t ns = 0;
   for (const RowRange& r : ranges) ns += (size_t)r.rows;
   uint8_t* tmp = nullptr;
-  cudaError_t e = cudaMalloc(&tmp, db + sb + (ns ? (rb + rs) * ns : 0) + 16);
+  cudaError_t e = cudaMalloc(&tmp, db + sb + (ns ? (rb + rs) * ns : 0) + (cols ? db + sb : 0) + 16);
   if (e != cudaSuccess) return ctx_cuda_fail(D->c, e, "decoder weight scratch");
   cudaStream_t st = ctx_stream(D->c);
   const int emin = fmt == 4 ? -8 : -10, emax = fmt == 4 ? -3 : -4;
@@ -134,7 +137,19 @@ int synth_weight(mxq_decoder_s* D, int n, int k, uint64_t seed, mxq_weight* out,
     ws = ss;
     rows = ns;
   }
-  int rc = e == cudaSuccess ? mxq_weight_create(D->c, fmt, rows, (size_t)k, wd, ws, 1, out)
+  size_t kk = (size_t)k;
+  if (cols && e == cudaSuccess) {
+    const size_t cb = fmt == 4 ? (size_t)cols / 2 : (size_t)cols, c0 = fmt == 4 ? (size_t)col0 / 2 : (size_t)col0;
+    uint8_t *cd = tmp + db + sb + (ns ? (rb + rs) * ns : 0), *cs = cd + cb * rows;
+    e = cudaMemcpy2DAsync(cd, cb, wd + c0, rb, cb, rows, cudaMemcpyDeviceToDevice, st);
+    if (e == cudaSuccess)
+      e = cudaMemcpy2DAsync(cs, (size_t)cols / 32, ws + col0 / 32, rs, (size_t)cols / 32, rows,
+                            cudaMemcpyDeviceToDevice, st);
+    wd = cd;
+    ws = cs;
+    kk = (size_t)cols;
+  }
+  int rc = e == cudaSuccess ? mxq_weight_create(D->c, fmt, rows, kk, wd, ws, 1, out)
                             : ctx_cuda_fail(D->c, e, "decoder weight synth");
   cudaStreamSynchronize(st);
   cudaFree(tmp);
@@ -164,17 +179,16 @@ uint32_t* tp_flags(const mxq_decoder_s* D, int r, int slot) {
 }
 size_t tp_slot_off(const mxq_decoder_s* D, int slot) { return kTpFlagBytes + (size_t)slot * D->slot_bytes; }
 
-int tp_gather(mxq_decoder_s* D, int slot, int rows, std::initializer_list<TpSegment> segs) {
+int tp_gather(mxq_decoder_s* D, int slot, int rows, const uint8_t* src, size_t row_bytes) {
   TpGatherArgs a{};
   a.world = D->world;
   a.rank = D->rank;
   a.rows = rows;
-  a.nseg = 0;
-  for (const TpSegment& g : segs) {
-    if (g.dst_off + (size_t)(rows - 1) * g.dst_ld + g.row_bytes * (size_t)D->world > tp_slot_off(D, slot + 1))
-      return dfail(D, MXQ_ERR_INVALID_ARGUMENT, "tensor-parallel exchange larger than its mailbox slot");
-    a.seg[a.nseg++] = g;
-  }
+  a.src = src;
+  a.row_bytes = row_bytes;
+  a.dst_off = tp_slot_off(D, slot);
+  if (a.dst_off + (size_t)rows * row_bytes * D->world > tp_slot_off(D, slot + 1))
+    return dfail(D, MXQ_ERR_INVALID_ARGUMENT, "tensor-parallel exchange larger than its mailbox slot");
   for (int r = 0; r < D->world; ++r) {
     a.base[r] = D->peer[r];
     a.flag_out[r] = tp_flags(D, r, slot) + D->rank;
@@ -187,32 +201,15 @@ int tp_gather(mxq_decoder_s* D, int slot, int rows, std::initializer_list<TpSegm
   return dcheck(D, launch_tp_gather(a, ctx_stream(D->c)), "tensor-parallel all-gather");
 }
 
-// this rank's columns [R][n] fp32 -> every rank's [R][n * world] in slot `slot`
+// this rank's [R][n] fp32 -> every rank's [R][world][n] in slot `slot`
 int tp_gather_f32(mxq_decoder_s* D, int slot, const float* src, int R, int n, const float** full) {
-  const size_t rb = (size_t)n * 4;
-  const size_t off = tp_slot_off(D, slot);
-  if (int rc = tp_gather(D, slot, R, {TpSegment{reinterpret_cast<const uint8_t*>(src), rb, rb, off, rb * D->world}}))
-    return rc;
-  *full = reinterpret_cast<const float*>(D->mbox + off);
-  return MXQ_OK;
-}
-
-// one row of MX bytes (q [n], scales [n/32]) -> every rank's [n * world] and
-// [n * world / 32] in slot `slot`
-int tp_gather_mx(mxq_decoder_s* D, int slot, const uint8_t* q, const uint8_t* sc, int n, const uint8_t** fq,
-                 const uint8_t** fs) {
-  const size_t off = tp_slot_off(D, slot), nf = (size_t)n * D->world;
-  const size_t soff = off + (nf + 15) / 16 * 16;
-  if (int rc = tp_gather(D, slot, 1, {TpSegment{q, (size_t)n, (size_t)n, off, nf},
-                                      TpSegment{sc, (size_t)n / 32, (size_t)n / 32, soff, nf / 32}}))
-    return rc;
-  *fq = D->mbox + off;
-  *fs = D->mbox + soff;
+  if (int rc = tp_gather(D, slot, R, reinterpret_cast<const uint8_t*>(src), (size_t)n * 4)) return rc;
+  *full = reinterpret_cast<const float*>(D->mbox + tp_slot_off(D, slot));
   return MXQ_OK;
 }
 
 // The layers of a tensor-parallel decoder (see the file comment): as layers()
-// below, over this rank's heads and rows, with the four all-gathers.
+// below, over this rank's heads and FFN units, with the two exchanges.
 int layers_tp(mxq_decoder_s* D, int B, int T, int pos0, bool decode) {
   mxq_context* c = D->c;
   cudaStream_t st = ctx_stream(c);
@@ -243,11 +240,14 @@ int layers_tp(mxq_decoder_s* D, int B, int T, int pos0, bool decode) {
                        "attention")))
         return rc;
     }
-    if ((rc = tp_gather_f32(D, 0, D->att, R, dl, &full))) return rc;          // every head's output
-    if ((rc = trace_copy(D, l, MXQ_TRACE_ATT, full, (size_t)R * d))) return rc;
-    if ((rc = mxq_linear(c, D->o[l], full, (size_t)R, D->tmp))) return rc;
-    if ((rc = tp_gather_f32(D, 1, D->tmp, R, dl, &full))) return rc;          // the full O output
-    if ((rc = dcheck(D, dk_add_rmsnorm(D->h, full, D->gains + (size_t)(2 * l + 1) * d, R, d, eps, D->hn, st),
+    if ((rc = trace_copy(D, l, MXQ_TRACE_ATT, D->att, (size_t)R * dl))) return rc;
+    // O over this rank's heads (its K columns): a partial sum of every
+    // output row; every rank's partials, added in rank order, then the
+    // residual and the RMSNorm
+    if ((rc = mxq_linear(c, D->o[l], D->att, (size_t)R, D->tmp))) return rc;
+    if ((rc = tp_gather_f32(D, 0, D->tmp, R, d, &full))) return rc;
+    if ((rc = dcheck(D, dk_add_parts_rmsnorm(D->h, full, D->world, D->gains + (size_t)(2 * l + 1) * d, R, d, eps,
+                                             D->hn, st),
                      "residual + rmsnorm")))
       return rc;
     if ((rc = trace_copy(D, l, MXQ_TRACE_H1, D->h, (size_t)R * d))) return rc;
@@ -255,6 +255,7 @@ int layers_tp(mxq_decoder_s* D, int B, int T, int pos0, bool decode) {
     // this rank's gate rows, then its up rows: [R][2 Fl]
     if ((rc = mxq_linear(c, D->gu[l], D->hn, (size_t)R, D->gub))) return rc;
     if ((rc = trace_copy(D, l, MXQ_TRACE_GU, D->gub, (size_t)R * 2 * Fl))) return rc;
+    // down over this rank's FFN units (its K columns): partial sums again
     if (R == 1) {
       uint8_t* hq = reinterpret_cast<uint8_t*>(D->act);
       QuantArgs qa{};
@@ -265,16 +266,14 @@ int layers_tp(mxq_decoder_s* D, int B, int T, int pos0, bool decode) {
       qa.out_q = hq;
       qa.out_s = hq + (Fl + 15) / 16 * 16;
       if ((rc = dcheck(D, launch_quantize(qa, 2, st, true), "swiglu quantize"))) return rc;
-      const uint8_t *fq = nullptr, *fs = nullptr;
-      if ((rc = tp_gather_mx(D, 0, qa.out_q, qa.out_s, Fl, &fq, &fs))) return rc;   // the whole MX activation
-      if ((rc = mxq_gemv(c, D->down[l], fq, fs, 1, D->tmp))) return rc;
+      if ((rc = mxq_gemv(c, D->down[l], qa.out_q, qa.out_s, 1, D->tmp))) return rc;
     } else {
       if ((rc = dcheck(D, dk_swiglu(D->gub, R, Fl, D->act, st), "swiglu"))) return rc;
-      if ((rc = tp_gather_f32(D, 0, D->act, R, Fl, &full))) return rc;
-      if ((rc = mxq_linear(c, D->down[l], full, (size_t)R, D->tmp))) return rc;
+      if ((rc = mxq_linear(c, D->down[l], D->act, (size_t)R, D->tmp))) return rc;
     }
-    if ((rc = tp_gather_f32(D, 1, D->tmp, R, dl, &full))) return rc;          // the full down output
-    if ((rc = dcheck(D, dk_add_rmsnorm(D->h, full, D->gains + (size_t)(2 * l + 2) * d, R, d, eps, D->hn, st),
+    if ((rc = tp_gather_f32(D, 1, D->tmp, R, d, &full))) return rc;
+    if ((rc = dcheck(D, dk_add_parts_rmsnorm(D->h, full, D->world, D->gains + (size_t)(2 * l + 2) * d, R, d, eps,
+                                             D->hn, st),
                      "residual + rmsnorm")))
       return rc;
     if ((rc = trace_copy(D, l, MXQ_TRACE_OUT, D->h, (size_t)R * d))) return rc;
@@ -471,15 +470,16 @@ int create_decoder(mxq_ctx c, const mxq_decoder_config* cfg, uint64_t seed, int 
         if (rc == MXQ_OK && (rc = synth_weight(D, d, F, s + 4, &w)) == MXQ_OK) D->down.push_back(w);
         continue;
       }
-      // this rank's rows of the same weights: its heads' q, k, v rows; its
-      // O rows; its gate rows then its up rows; its down rows
+      // this rank's parts of the same weights: its heads' q, k, v rows; the
+      // O columns of its heads; its gate rows then its up rows; the down
+      // columns of its FFN units
       if ((rc = synth_weight(D, 3 * d, d, s + 1, &w, {{r0 * dl, dl}, {d + r0 * dl, dl}, {2 * d + r0 * dl, dl}})) ==
           MXQ_OK)
         D->qkv.push_back(w);
-      if (rc == MXQ_OK && (rc = synth_weight(D, d, d, s + 2, &w, {{r0 * dl, dl}})) == MXQ_OK) D->o.push_back(w);
+      if (rc == MXQ_OK && (rc = synth_weight(D, d, d, s + 2, &w, {}, r0 * dl, dl)) == MXQ_OK) D->o.push_back(w);
       if (rc == MXQ_OK && (rc = synth_weight(D, 2 * F, d, s + 3, &w, {{r0 * Fl, Fl}, {F + r0 * Fl, Fl}})) == MXQ_OK)
         D->gu.push_back(w);
-      if (rc == MXQ_OK && (rc = synth_weight(D, d, F, s + 4, &w, {{r0 * dl, dl}})) == MXQ_OK) D->down.push_back(w);
+      if (rc == MXQ_OK && (rc = synth_weight(D, d, F, s + 4, &w, {}, r0 * Fl, Fl)) == MXQ_OK) D->down.push_back(w);
     }
     if (rc == MXQ_OK) rc = synth_weight(D, D->Vo, d, seed * 1000003ull + 999983ull, &D->lm);
     if (rc) return bail(rc);
@@ -521,9 +521,8 @@ int create_decoder(mxq_ctx c, const mxq_decoder_config* cfg, uint64_t seed, int 
     if (e == cudaSuccess) e = dalloc(D->done, (size_t)D->Bmax * D->Hl);
     if (e == cudaSuccess) e = cudaMemsetAsync(D->done, 0, (size_t)D->Bmax * D->Hl * 4 + 16, st);
     if (D->tp) {
-      // mailbox: flags, then two slots of [max_rows][max(d, ffn)] fp32 each
-      const size_t wmax = (size_t)(d > F ? d : F);
-      D->slot_bytes = (R * wmax * 4 + 256 + 255) / 256 * 256;
+      // mailbox: flags, then two slots of [max_rows][world][d] fp32 each
+      D->slot_bytes = (R * (size_t)D->world * d * 4 + 255) / 256 * 256;
       D->mbox_bytes = kTpFlagBytes + 2 * D->slot_bytes;
       if (e == cudaSuccess) e = cudaMalloc(&D->mbox, D->mbox_bytes);
       if (e == cudaSuccess) e = cudaMemsetAsync(D->mbox, 0, D->mbox_bytes, st);

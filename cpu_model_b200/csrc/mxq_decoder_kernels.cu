@@ -53,16 +53,18 @@ __device__ __forceinline__ float norm_block_sum(float s, float* ws) {
   return tot;
 }
 
-// RESID: h += y first (written back), then out = RMSNorm(h) * g.
+// RESID: h += y first (written back), then out = RMSNorm(h) * g.  y's row r
+// is `nparts` partial sums of d values side by side (y + r * y_ld), added
+// in order before the residual (one part: h + y).
 template <bool RESID>
 __global__ void __launch_bounds__(kNormThreads) norm_kernel(float* __restrict__ h, const float* __restrict__ y,
                                                             const float* __restrict__ g, int d, float eps,
-                                                            float* __restrict__ out) {
+                                                            float* __restrict__ out, int nparts, size_t y_ld) {
   DK_PDL_PROLOGUE();
   __shared__ float ws[kNormThreads / 32];
   const int r = blockIdx.x, d4 = d / 4;
   float4* hr = reinterpret_cast<float4*>(h + (size_t)r * d);
-  const float4* yr = reinterpret_cast<const float4*>(y + (size_t)r * d);
+  const float4* yr = reinterpret_cast<const float4*>(y + (size_t)r * y_ld);
   float4 v[kNormVec];
   float s = 0.0f;
 #pragma unroll
@@ -72,7 +74,14 @@ __global__ void __launch_bounds__(kNormThreads) norm_kernel(float* __restrict__ 
     if (i < d4) {
       v[u] = hr[i];
       if (RESID) {
-        const float4 b = yr[i];
+        float4 b = yr[i];
+        for (int q = 1; q < nparts; ++q) {
+          const float4 c = yr[(size_t)q * d4 + i];
+          b.x = __fadd_rn(b.x, c.x);
+          b.y = __fadd_rn(b.y, c.y);
+          b.z = __fadd_rn(b.z, c.z);
+          b.w = __fadd_rn(b.w, c.w);
+        }
         v[u].x = __fadd_rn(v[u].x, b.x);
         v[u].y = __fadd_rn(v[u].y, b.y);
         v[u].z = __fadd_rn(v[u].z, b.z);
@@ -537,7 +546,7 @@ cudaError_t dk_embed(const int32_t* tok, const float* table, int R, int d, int v
 cudaError_t dk_rmsnorm(const float* x, const float* g, int R, int d, float eps, float* y, cudaStream_t s) {
   if (d % 4 || d / 4 > kNormThreads * kNormVec) return cudaErrorInvalidValue;
   return pdl_launch(norm_kernel<false>, dim3(R), dim3(kNormThreads), 0, s, const_cast<float*>(x),
-                    static_cast<const float*>(nullptr), g, d, eps, y);
+                    static_cast<const float*>(nullptr), g, d, eps, y, 1, (size_t)d);
 }
 cudaError_t dk_add(float* h, const float* y, size_t n, cudaStream_t s) {
   return pdl_launch(add_kernel, dim3(grid_for(n / 4, 256)), dim3(256), 0, s, h, y, n / 4);
@@ -545,7 +554,13 @@ cudaError_t dk_add(float* h, const float* y, size_t n, cudaStream_t s) {
 cudaError_t dk_add_rmsnorm(float* h, const float* y, const float* g, int R, int d, float eps, float* out,
                            cudaStream_t s) {
   if (d % 4 || d / 4 > kNormThreads * kNormVec) return cudaErrorInvalidValue;
-  return pdl_launch(norm_kernel<true>, dim3(R), dim3(kNormThreads), 0, s, h, y, g, d, eps, out);
+  return pdl_launch(norm_kernel<true>, dim3(R), dim3(kNormThreads), 0, s, h, y, g, d, eps, out, 1, (size_t)d);
+}
+cudaError_t dk_add_parts_rmsnorm(float* h, const float* y, int nparts, const float* g, int R, int d, float eps,
+                                 float* out, cudaStream_t s) {
+  if (d % 4 || d / 4 > kNormThreads * kNormVec || nparts < 1) return cudaErrorInvalidValue;
+  return pdl_launch(norm_kernel<true>, dim3(R), dim3(kNormThreads), 0, s, h, y, g, d, eps, out, nparts,
+                    (size_t)nparts * d);
 }
 cudaError_t dk_swiglu(const float* gu, int R, int F, float* act, cudaStream_t s) {
   return pdl_launch(swiglu_kernel, dim3(grid_for((size_t)R * F, 256)), dim3(256), 0, s, gu, R, F, act);

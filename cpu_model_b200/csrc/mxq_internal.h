@@ -167,18 +167,15 @@ struct PeerArgs {
 cudaError_t launch_cogemv_peer(const GemvArgs& a, const PeerArgs& p, int role, cudaStream_t st, bool pdl);
 
 // Peer all-gather of the tensor-parallel decoder (mxq_tp.cu).  Each rank
-// holds its columns of `rows` rows (per segment: row_bytes a row, this
-// rank's slice); the launch stores them at column rank * row_bytes of every
-// rank's mailbox rows (dst_off + r * dst_ld), sets this rank's flag word in
-// every mailbox to the slot's next sequence number, and its last CTA waits
-// (bounded) until every rank's flag in the local mailbox has reached it.
-struct TpSegment {
-  const uint8_t* src;              // this rank's rows, src_ld bytes apart
-  size_t src_ld, row_bytes, dst_off, dst_ld;
-};
+// holds `rows` rows of row_bytes (a multiple of 16) at src, contiguous; the
+// launch stores row r at dst_off + (r * world + rank) * row_bytes of every
+// rank's mailbox, sets this rank's flag word in every mailbox to the slot's
+// next sequence number, and its last CTA waits (bounded) until every rank's
+// flag in the local mailbox has reached it.
 struct TpGatherArgs {
-  int world, rank, rows, nseg;
-  TpSegment seg[2];
+  int world, rank, rows;
+  const uint8_t* src;              // 16-byte aligned
+  size_t row_bytes, dst_off;
   uint8_t* base[kMaxPeers];        // every rank's mailbox as mapped here
   uint32_t* flag_out[kMaxPeers];   // per rank: this rank's flag word of the slot
   const uint32_t* wait_flags;      // local mailbox: the slot's flags, [world]
@@ -218,6 +215,9 @@ cudaError_t dk_rmsnorm(const float* x, const float* g, int R, int d, float eps, 
 cudaError_t dk_add(float* h, const float* y, size_t n, cudaStream_t s);
 cudaError_t dk_add_rmsnorm(float* h, const float* y, const float* g, int R, int d, float eps, float* out,
                            cudaStream_t s);
+// h += y[0] + ... + y[nparts - 1] (row r of y: nparts rows of d side by side), then RMSNorm
+cudaError_t dk_add_parts_rmsnorm(float* h, const float* y, int nparts, const float* g, int R, int d, float eps,
+                                 float* out, cudaStream_t s);
 cudaError_t dk_swiglu(const float* gu, int R, int F, float* act, cudaStream_t s);
 cudaError_t dk_rope_kv(float* qkv, int R, int T, int d, int H, int pos0, const int32_t* pos_dev, const float* cs,
                        int max_ctx, __nv_bfloat16* kc, __nv_bfloat16* vc, cudaStream_t s);

@@ -1,16 +1,17 @@
 // mxq_tp.cu -- the peer all-gather of the tensor-parallel decoder.
 //
-// Each rank of a sharded decoder owns whole output rows of every linear
-// (output-feature sharding of mx_gemv, nn/tests/test_auto_generated.cpp:56:
-// a row keeps its full K, so its block sums are those of the unsharded
-// weight), so after each linear it holds some columns of the activation.
-// One launch of tp_gather_kernel makes the full activation appear in every
-// rank's mailbox: every thread stores its 16-byte pieces of this rank's
-// columns into every rank's mailbox over NVLink (plain stores through CUDA
+// Each rank of a sharded decoder computes, for the O and down linears, a
+// partial sum of every output row over its part of K (whole 32-blocks, so
+// the MX block dots are those of the unsharded weight; the reference's
+// mx_gemv sums them per row, nn/tests/test_auto_generated.cpp:56).  One
+// launch of tp_gather_kernel makes every rank's partials appear in every
+// rank's mailbox, [row][rank][values]: every thread stores its 16-byte
+// pieces into every rank's mailbox over NVLink (plain stores through CUDA
 // IPC mappings), the grid's last CTA releases this rank's flag word in every
 // mailbox, then waits, bounded, until every rank's flag in its own mailbox
-// shows the same sequence number.  The kernel after it reads the gathered
-// rows from the local mailbox once this grid has completed.
+// shows the same sequence number.  The kernel after it (the residual) reads
+// the partials from the local mailbox once this grid has completed and adds
+// them in rank order.
 //
 // Ordering: the copy starts after griddepcontrol.wait, so the producer's
 // rows are complete; each CTA's stores are ordered before its arrival on the
@@ -34,29 +35,12 @@ __global__ void __launch_bounds__(kTpThreads) tp_gather_kernel(TpGatherArgs a) {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   asm volatile("griddepcontrol.wait;" ::: "memory");
   const long nth = (long)gridDim.x * kTpThreads;
-  const long t0 = (long)blockIdx.x * kTpThreads + threadIdx.x;
-  for (int s = 0; s < a.nseg; ++s) {
-    const TpSegment g = a.seg[s];
-    const size_t col = (size_t)a.rank * g.row_bytes;
-    if (g.row_bytes % 16 == 0 && g.src_ld % 16 == 0 && g.dst_ld % 16 == 0 && g.dst_off % 16 == 0 &&
-        (reinterpret_cast<uintptr_t>(g.src) & 15u) == 0) {
-      const long per_row = (long)(g.row_bytes / 16), n = per_row * a.rows;
-      for (long i = t0; i < n; i += nth) {
-        const long r = i / per_row, c = i - r * per_row;
-        const uint4 v = __ldcg(reinterpret_cast<const uint4*>(g.src + r * g.src_ld) + c);
-        const size_t off = g.dst_off + (size_t)r * g.dst_ld + col + (size_t)c * 16;
-        for (int p = 0; p < a.world; ++p) *reinterpret_cast<uint4*>(a.base[p] + off) = v;
-      }
-    } else {
-      // ragged rows (the E8M0 scales of a slice): byte stores
-      const long per_row = (long)g.row_bytes, n = per_row * a.rows;
-      for (long i = t0; i < n; i += nth) {
-        const long r = i / per_row, c = i - r * per_row;
-        const uint8_t v = __ldcg(g.src + r * g.src_ld + c);
-        const size_t off = g.dst_off + (size_t)r * g.dst_ld + col + (size_t)c;
-        for (int p = 0; p < a.world; ++p) a.base[p][off] = v;
-      }
-    }
+  const long per_row = (long)(a.row_bytes / 16), n = per_row * a.rows;
+  for (long i = (long)blockIdx.x * kTpThreads + threadIdx.x; i < n; i += nth) {
+    const long r = i / per_row, c = i - r * per_row;
+    const uint4 v = __ldcg(reinterpret_cast<const uint4*>(a.src) + i);
+    const size_t off = a.dst_off + ((size_t)r * a.world + a.rank) * a.row_bytes + (size_t)c * 16;
+    for (int p = 0; p < a.world; ++p) *reinterpret_cast<uint4*>(a.base[p] + off) = v;
   }
   __syncthreads();
   if (threadIdx.x == 0) {
@@ -81,18 +65,13 @@ __global__ void __launch_bounds__(kTpThreads) tp_gather_kernel(TpGatherArgs a) {
 }  // namespace
 
 cudaError_t launch_tp_gather(const TpGatherArgs& a, cudaStream_t st) {
-  if (a.world < 1 || a.world > kMaxPeers || a.rank < 0 || a.rank >= a.world || a.rows < 1 || a.nseg < 1 ||
-      a.nseg > 2 || !a.wait_flags || !a.seq || !a.grid_cnt)
+  if (a.world < 1 || a.world > kMaxPeers || a.rank < 0 || a.rank >= a.world || a.rows < 1 || !a.src ||
+      a.row_bytes == 0 || a.row_bytes % 16 || a.dst_off % 16 || (reinterpret_cast<uintptr_t>(a.src) & 15u) ||
+      !a.wait_flags || !a.seq || !a.grid_cnt)
     return cudaErrorInvalidValue;
   for (int r = 0; r < a.world; ++r)
-    if (!a.base[r] || !a.flag_out[r]) return cudaErrorInvalidValue;
-  long units = 0;
-  for (int s = 0; s < a.nseg; ++s) {
-    const TpSegment& g = a.seg[s];
-    if (!g.src || g.row_bytes == 0 || g.src_ld < g.row_bytes || g.dst_ld < g.row_bytes * (size_t)a.world)
-      return cudaErrorInvalidValue;
-    units += (long)((g.row_bytes + 15) / 16) * a.rows;
-  }
+    if (!a.base[r] || !a.flag_out[r] || (reinterpret_cast<uintptr_t>(a.base[r]) & 15u)) return cudaErrorInvalidValue;
+  const long units = (long)(a.row_bytes / 16) * a.rows;
   // about one 16-byte piece per thread for a decode step's few kilobytes,
   // at most four CTAs per SM for a prompt chunk's megabytes
   long ctas = (units + kTpThreads - 1) / kTpThreads;

@@ -466,28 +466,32 @@ MXQ_API int mxq_decoder_create(mxq_ctx ctx, const mxq_decoder_config* cfg,
 /* The same decoder tensor-parallel over `world` GPUs of one node (one process
  * and context per GPU; world 1..8 dividing n_heads, ffn a multiple of
  * 32 * world).  Rank `rank` holds the q, k, v rows, K/V cache and attention
- * of heads [rank * n_heads / world, (rank + 1) * n_heads / world) and rows
- * [rank * n / world, (rank + 1) * n / world) of the O, gate, up and down
- * weights (output-feature sharding of mx_gemv,
- * nn/tests/test_auto_generated.cpp:56: whole rows, full K); the embedding,
- * RMSNorm weights and vocabulary head are replicated, and every weight row
- * is the unsharded decoder's for the same seed.  After the attention, the O
- * linear, the SwiGLU and the down linear of every layer, one kernel stores
- * this rank's columns into every rank's mailbox (peer stores over NVLink
- * into CUDA IPC memory), sets its flag there and waits (bounded) for every
- * rank's flag; no NCCL on the data path.  Usage:
+ * of heads [rank * n_heads / world, (rank + 1) * n_heads / world), the gate
+ * and up rows of FFN units [rank * ffn / world, (rank + 1) * ffn / world),
+ * and the O and down columns (K) of those heads and units, whole 32-blocks
+ * (the MX block dots of mx_gemv, nn/tests/test_auto_generated.cpp:56, are
+ * the unsharded weight's); every weight byte is the unsharded decoder's for
+ * the same seed.  The embedding, RMSNorm weights and vocabulary head are
+ * replicated.  After the O and after the down linear of every layer, one
+ * kernel stores this rank's partial sums into every rank's mailbox (peer
+ * stores over NVLink into CUDA IPC memory), sets its flag there and waits
+ * (bounded) for every rank's flag; the residual kernel adds the partials in
+ * rank order, so every rank holds the same hidden state.  No NCCL on the
+ * data path.  Usage:
  *   mxq_decoder_create_sharded(ctx, cfg, seed, rank, world, &dec, handle)
  *     -- handle: MXQ_PEER_HANDLE_BYTES to exchange;
  *   (the caller gathers every rank's handle, in rank order)
  *   mxq_decoder_connect(dec, handles)   -- world * 64 bytes
  * then prefill / decode / score as on one GPU, with the same tokens in the
- * same order on every rank; every rank returns the full logits.  A wait that
+ * same order on every rank; every rank returns the same full logits.  They
+ * equal the unsharded decoder's within fp32 rounding (the block sums of O
+ * and down are added in another order); with world 1 (the sharded code path
+ * on one GPU, exchanging through its own mailbox) bit for bit.  A wait that
  * runs out (mxq_decoder_set_wait_limit, default 2 s) sets the context's
  * status word (mxq_synchronize returns MXQ_ERR_TIMEOUT) and the group must
- * be created again.  With world 1 the sharded code path runs on one GPU,
- * exchanging through its own mailbox.  Trace points QKV, ROPE and GU hold
- * this rank's columns ([rows][3 d / world], [rows][2 ffn / world]); the
- * others the full rows. */
+ * be created again.  Trace points QKV, ROPE, ATT and GU hold this rank's
+ * columns ([rows][3 d / world], [rows][d / world], [rows][2 ffn / world]);
+ * the others the full rows. */
 MXQ_API int mxq_decoder_create_sharded(mxq_ctx ctx, const mxq_decoder_config* cfg,
                                        uint64_t seed, int rank, int world,
                                        mxq_decoder* out, void* handle_out);

@@ -1,19 +1,19 @@
 """The tensor-parallel decoder (mxq_decoder_create_sharded): each rank holds
-its heads and whole rows of every linear, and four peer all-gathers a layer
-rebuild the full activation in every rank's mailbox.
+its heads (q/k/v rows, K/V cache, attention) and FFN units (gate/up rows),
+and the O and down columns of both; two peer exchanges a layer bring every
+rank's partial sums into every mailbox, added in rank order by the residual.
 
 - one rank (the sharded code path on one GPU, exchanging through its own
-  mailbox): prompt logits, decode steps (batch 2 on the fp32 exchange,
-  batch 1 on the MX-byte exchange, both graph-replayed) and scored
-  log-probs bit-identical to the unsharded decoder of the same seed, at a
-  small shape and at the 7B layer shape;
-- every rank's weights are exactly the unsharded weights' rows for that
-  rank (heads' q/k/v rows, O, gate, up and down rows); the head is whole;
+  mailbox): prompt logits, decode steps (batch 2 and batch 1, both
+  graph-replayed) and scored log-probs bit-identical to the unsharded
+  decoder of the same seed, at a small shape and at the 7B layer shape;
+- every rank's weights are exactly the unsharded weights' bytes for that
+  rank (heads' q/k/v rows, gate and up rows, O and down columns); the head
+  is whole;
 - bad groups are refused, and a pass before connect() is refused;
 - two ranks on two GPUs (skipped with fewer): both ranks return the same
-  logits, within 1e-5 of the unsharded decoder on one GPU (the tensor-core
-  GEMM may split K differently over fewer rows, so prompt rows can differ
-  in the last bits; the one-token path is compared the same way).
+  logits, within 1e-5 of the unsharded decoder on one GPU (the block sums
+  of O and down are added in another fp32 order).
 """
 import os
 import socket
@@ -105,17 +105,21 @@ def test_rank_weights_are_rows_of_the_unsharded_weights(ctx, world, cfg):
         for rank in range(world):
             sh = mx.Decoder(seed=9, ctx=ctx, rank=rank, world=world, **cfg)
             try:
+                per = 2 if cfg["fmt"] == 4 else 1          # elements a data byte
                 for layer in range(cfg["n_layers"]):
                     for which, rows in [
                         (mx.DEC_QKV, [np.arange(rank * dl, (rank + 1) * dl) + j * d for j in range(3)]),
-                        (mx.DEC_O, [np.arange(rank * dl, (rank + 1) * dl)]),
                         (mx.DEC_GATE_UP, [np.arange(rank * fl, (rank + 1) * fl) + j * f for j in range(2)]),
-                        (mx.DEC_DOWN, [np.arange(rank * dl, (rank + 1) * dl)]),
                     ]:
                         full_d, full_s = plain.download(layer, which)
                         got_d, got_s = sh.download(layer, which)
                         idx = np.concatenate(rows)
                         assert np.array_equal(got_d, full_d[idx]) and np.array_equal(got_s, full_s[idx])
+                    for which, c0, n in [(mx.DEC_O, rank * dl, dl), (mx.DEC_DOWN, rank * fl, fl)]:
+                        full_d, full_s = plain.download(layer, which)
+                        got_d, got_s = sh.download(layer, which)
+                        assert np.array_equal(got_d, full_d[:, c0 // per:(c0 + n) // per])
+                        assert np.array_equal(got_s, full_s[:, c0 // 32:(c0 + n) // 32])
                 hd, hs = plain.download(0, mx.DEC_LM_HEAD)
                 gd, gs = sh.download(0, mx.DEC_LM_HEAD)
                 assert np.array_equal(gd, hd) and np.array_equal(gs, hs)
