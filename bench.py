@@ -817,6 +817,40 @@ def time_sharded(ctx, dev, args, world, rank, max_over_ranks, barrier):
     out["moe_expert_parallel"] = {"ms_per_step": ms, "tokens_per_s": MOE["tokens"] / (ms / 1e3),
                                   "experts_per_rank": e_hi - e_lo, "tokens_per_rank": t_local,
                                   "collective": "all_to_all_single (NCCL) dispatch + return"}
+    if MOE["experts"] % world == 0:
+        # the same layer in libmxq (mxq_moe_swiglu_sharded): every rank holds
+        # all 4096 tokens, runs its experts, and the expert outputs cross
+        # NVLink once, into every rank's mailbox; the full y on every rank
+        import torch.distributed as dist
+        G = mx.MoEGroup(rank, world, MOE["tokens"], MOE["top_k"], MOE["d"], ctx)
+        handles = [None] * world
+        dist.all_gather_object(handles, G.handle())
+        G.connect(handles)
+        xf = torch.from_numpy(synth.normal((MOE["tokens"], MOE["d"]), 201)).to(dev)
+        lf = torch.from_numpy(synth.normal((MOE["tokens"], MOE["experts"]), 202)).to(dev)
+        yb = torch.empty_like(xf)
+        gw, uw, dw = ([m[i][0] for m in experts] for i in range(3))
+
+        def layer_peer():
+            G.moe_swiglu(xf, lf, gw, uw, dw, MOE["top_k"], out=yb)
+
+        for _ in range(2):
+            layer_peer()
+        barrier()
+        torch.cuda.synchronize()
+        e0.record()
+        for _ in range(steps):
+            layer_peer()
+        e1.record()
+        torch.cuda.synchronize()
+        ms = max_over_ranks(e0.elapsed_time(e1) / steps)
+        out["moe_expert_parallel_peer"] = {
+            "ms_per_step": ms, "tokens_per_s": MOE["tokens"] / (ms / 1e3), "experts_per_rank": e_hi - e_lo,
+            "tokens_per_rank": MOE["tokens"], "api": "mxq_moe_swiglu_sharded",
+            "exchange": "expert-output rows over NVLink peer stores, one exchange a layer"}
+        torch.cuda.synchronize()
+        barrier()
+        G.close()
     for mats in experts:
         for m in mats:
             m[0].close()

@@ -93,6 +93,11 @@ SIGNATURES = {
     "mxq_hashed_route": [_vp, _vp, _sz, _sz, _sz, _sz, _sz, ctypes.c_uint64, _vp, _vp],
     "mxq_hashed_route_host": [_vp, _vp, _sz, _sz, _sz, _sz, _sz, ctypes.c_uint64, _vp, _vp],
     "mxq_moe_swiglu": [_vp, _vp, _vp, _vp, _sz, _vp, _vp, _sz, _sz, _vp],
+    "mxq_moe_group_create": [_vp, _i, _i, _sz, _sz, _sz, ctypes.POINTER(_vp), _vp],
+    "mxq_moe_group_connect": [_vp, _vp],
+    "mxq_moe_group_set_wait_limit": [_vp, ctypes.c_uint32],
+    "mxq_moe_group_destroy": [_vp],
+    "mxq_moe_swiglu_sharded": [_vp, _vp, _vp, _vp, _vp, _sz, _vp, _vp, _sz, _sz, _vp],
     "mxq_policy_head": [_vp, _vp, _vp, _sz, _sz, _vp, _vp, _vp],
     "mxq_gae": [_vp, _vp, _vp, _vp, _vp, _sz, _sz, _f, _f, _vp, _vp],
     "mxq_gae_ring": [_vp, _vp, _vp, _vp, _vp, _sz, _sz, _sz, _sz, _sz, _f, _f, _vp, _vp],

@@ -1653,6 +1653,26 @@ static int moe_gemm(mxq_context* c, mxq_weight w, int b, int BN, int Bpad, float
   return after_launch(c, launch_gemm(ga, c->stream, true), "moe gemm");
 }
 
+// Expert-parallel MoE group: this rank's mailbox (flags [8] u32, then two
+// halves of expert-output rows [max_routes][D] fp32, alternating by call)
+// and every rank's as mapped here.
+struct mxq_moe_group_s {
+  mxq_context* ctx = nullptr;
+  int rank = 0, world = 1;
+  size_t max_routes = 0, D = 0;
+  uint8_t* mbox = nullptr;
+  size_t off_yr = 256, half_bytes = 0, bytes = 0;
+  uint8_t* base[kMaxPeers] = {};
+  bool opened[kMaxPeers] = {};
+  uint32_t* local = nullptr;       // [0] exchanges completed, [1] grid counter
+  uint64_t calls = 0;              // host: calls made (selects the half)
+  uint64_t wait_ns = kWaitLimitNs;
+};
+
+static int moe_layer(mxq_context* c, const mxq_weight* w_gate, const mxq_weight* w_up, const mxq_weight* w_down,
+                     int E, int e_lo, int n_local, const float* x, const float* logits, int T, int K, int D, int F,
+                     float* y, mxq_moe_group_s* G);
+
 int mxq_moe_swiglu(mxq_ctx c, const mxq_weight* w_gate, const mxq_weight* w_up,
                    const mxq_weight* w_down, size_t n_experts, const float* x,
                    const float* logits, size_t t, size_t k, float* y) {
@@ -1680,7 +1700,20 @@ int mxq_moe_swiglu(mxq_ctx c, const mxq_weight* w_gate, const mxq_weight* w_up,
     if (t == 0) return MXQ_OK;
     if (t > (1u << 24) || t * k > (1u << 26)) return fail(c, MXQ_ERR_INVALID_ARGUMENT, "too many tokens");
     DeviceGuard g(c->device);
-    const int T = (int)t, K = (int)k, R = T * K;
+    return moe_layer(c, w_gate, w_up, w_down, E, 0, E, x, logits, (int)t, (int)k, D, F, y, nullptr);
+  })
+}
+
+// The MoE layer after validation: routes and slots over all E experts, the
+// expert GEMMs of experts [e_lo, e_lo + n_local) (weights w_*[0 .. n_local)),
+// the combine.  With a group G, the expert outputs land in this rank's
+// mailbox and one exchange copies this rank's slot rows to every other
+// rank's mailbox before the combine.
+static int moe_layer(mxq_context* c, const mxq_weight* w_gate, const mxq_weight* w_up, const mxq_weight* w_down,
+                     int E, int e_lo, int n_local, const float* x, const float* logits, int T, int K, int D, int F,
+                     float* y, mxq_moe_group_s* G) {
+  {
+    const int R = T * K;
     int rc;
     // bookkeeping: idx[R] gate[R] counts[E] offsets[E+1] slot_token[R] route_pos[R]
     const size_t moe_ints = (size_t)4 * R + 2 * E + 1;
@@ -1709,13 +1742,18 @@ int mxq_moe_swiglu(mxq_ctx c, const mxq_weight* w_gate, const mxq_weight* w_up,
                                         c->stream))
       return cuda_fail(c, e, "moe counts");
     if (cudaError_t e = cudaStreamSynchronize(c->stream)) return cuda_fail(c, e, "moe counts");
-    int nmax = 0;
-    for (int e = 0; e < E; ++e) nmax = c->moe_counts_host[e] > nmax ? c->moe_counts_host[e] : nmax;
+    int nmax = 0, off_lo = 0, off_hi = 0;
+    for (int e = 0; e < E; ++e) {
+      const int ne = c->moe_counts_host[e];
+      if (e < e_lo) off_lo += ne;
+      if (e < e_lo + n_local) off_hi += ne;
+      if (e >= e_lo && e < e_lo + n_local) nmax = ne > nmax ? ne : nmax;
+    }
     if (nmax > 0) {
       const int BNm = gemm_pick_bn(nmax);
       const size_t Bpm = (size_t)(nmax + BNm - 1) / BNm * BNm;
       int kmax = 0;
-      for (int e = 0; e < E; ++e) {
+      for (int e = 0; e < n_local; ++e) {
         kmax = w_gate[e]->v.Kpad > kmax ? w_gate[e]->v.Kpad : kmax;
         kmax = w_up[e]->v.Kpad > kmax ? w_up[e]->v.Kpad : kmax;
         kmax = w_down[e]->v.Kpad > kmax ? w_down[e]->v.Kpad : kmax;
@@ -1736,7 +1774,13 @@ int mxq_moe_swiglu(mxq_ctx c, const mxq_weight* w_gate, const mxq_weight* w_up,
           if (e != cudaSuccess) return cuda_fail(c, e, "moe lane event");
         }
     }
-    if ((rc = ensure(c, c->ws_yr, c->ws_yr_bytes, (size_t)R * D * 4, "workspace expert outputs"))) return rc;
+    float* yr = nullptr;
+    if (G) {
+      yr = reinterpret_cast<float*>(G->mbox + G->off_yr + (size_t)(G->calls & 1u) * G->half_bytes);
+    } else {
+      if ((rc = ensure(c, c->ws_yr, c->ws_yr_bytes, (size_t)R * D * 4, "workspace expert outputs"))) return rc;
+      yr = c->ws_yr;
+    }
     // fork the expert lanes off the caller's stream
     if (nmax > 0) {
       cudaError_t e = cudaEventRecord(c->moe_ev[mxq_context::kMoeLanes], c->stream);
@@ -1780,16 +1824,23 @@ int mxq_moe_swiglu(mxq_ctx c, const mxq_weight* w_gate, const mxq_weight* w_up,
     int off = 0, lane_j = 0;
     for (int e = 0; e < E; ++e) {
       const int ne = c->moe_counts_host[e];
+      if (e < e_lo || e >= e_lo + n_local) {   // another rank's expert: its slots stay in place
+        off += ne;
+        continue;
+      }
       if (ne == 0) continue;
+      const mxq_weight* wg = w_gate - e_lo;
+      const mxq_weight* wu = w_up - e_lo;
+      const mxq_weight* wdn = w_down - e_lo;
       LaneSwap lane(c);
       lane.use(lane_j++ % mxq_context::kMoeLanes);
       const int BN = gemm_pick_bn(ne), Bpad = (ne + BN - 1) / BN * BN;
-      const WeightView &gv = w_gate[e]->v, &uv = w_up[e]->v;
-      if ((rc = moe_operand(c, w_gate[e], x, slot_token + off, ne, D, BN, Bpad))) return rc;
-      if ((rc = moe_gemm(c, w_gate[e], ne, BN, Bpad, c->ws_f0))) return rc;
+      const WeightView &gv = wg[e]->v, &uv = wu[e]->v;
+      if ((rc = moe_operand(c, wg[e], x, slot_token + off, ne, D, BN, Bpad))) return rc;
+      if ((rc = moe_gemm(c, wg[e], ne, BN, Bpad, c->ws_f0))) return rc;
       if (uv.fmt != gv.fmt || uv.gemm_shift != gv.gemm_shift || uv.Kpad != gv.Kpad)
-        if ((rc = moe_operand(c, w_up[e], x, slot_token + off, ne, D, BN, Bpad))) return rc;
-      if ((rc = moe_gemm(c, w_up[e], ne, BN, Bpad, c->ws_f1))) return rc;
+        if ((rc = moe_operand(c, wu[e], x, slot_token + off, ne, D, BN, Bpad))) return rc;
+      if ((rc = moe_gemm(c, wu[e], ne, BN, Bpad, c->ws_f1))) return rc;
       // silu(gate) * up -> the down projection's operand
       QuantArgs qa{};
       qa.x = c->ws_f0;
@@ -1798,12 +1849,12 @@ int mxq_moe_swiglu(mxq_ctx c, const mxq_weight* w_gate, const mxq_weight* w_up,
       qa.K = F;
       qa.opnd = reinterpret_cast<__nv_bfloat16*>(c->ws_op);
       qa.Bpad = Bpad;
-      qa.Kpad = w_down[e]->v.Kpad;
+      qa.Kpad = wdn[e]->v.Kpad;
       qa.BN = BN;
-      qa.int4_order = w_down[e]->v.fmt == 4;
-      qa.shift = w_down[e]->v.gemm_shift;
+      qa.int4_order = wdn[e]->v.fmt == 4;
+      qa.shift = wdn[e]->v.gemm_shift;
       if ((rc = after_launch(c, launch_quantize(qa, 2, c->stream, true), "moe swiglu"))) return rc;
-      if ((rc = moe_gemm(c, w_down[e], ne, BN, Bpad, c->ws_yr + (size_t)off * D))) return rc;
+      if ((rc = moe_gemm(c, wdn[e], ne, BN, Bpad, yr + (size_t)off * D))) return rc;
       off += ne;
     }
     // join: the combine on the caller's stream waits for every lane
@@ -1816,7 +1867,150 @@ int mxq_moe_swiglu(mxq_ctx c, const mxq_weight* w_gate, const mxq_weight* w_up,
       }
       if (e != cudaSuccess) return cuda_fail(c, e, "moe join");
     }
-    return after_launch(c, launch_moe_combine(c->ws_yr, gate, route_pos, T, D, K, y, c->stream), "moe combine");
+    if (G) {
+      // this rank's slot rows [off_lo, off_hi) to the same rows of every other
+      // rank's mailbox; then wait for every rank's
+      TpGatherArgs a{};
+      a.world = G->world;
+      a.rank = G->rank;
+      a.rows = off_hi - off_lo;
+      a.skip_rank = G->rank;
+      a.src = reinterpret_cast<const uint8_t*>(yr + (size_t)off_lo * D);
+      a.row_bytes = (size_t)D * 4;
+      a.dst_off = G->off_yr + (size_t)(G->calls & 1u) * G->half_bytes + (size_t)off_lo * D * 4;
+      a.row_stride = (size_t)D * 4;
+      a.rank_stride = 0;
+      for (int r = 0; r < G->world; ++r) {
+        a.base[r] = G->base[r];
+        a.flag_out[r] = reinterpret_cast<uint32_t*>(G->base[r]) + G->rank;
+      }
+      a.wait_flags = reinterpret_cast<const uint32_t*>(G->mbox);
+      a.seq = G->local;
+      a.grid_cnt = G->local + 1;
+      a.status = c->status;
+      a.wait_ns = G->wait_ns;
+      if ((rc = after_launch(c, launch_tp_gather(a, c->stream), "moe expert-output exchange"))) return rc;
+      G->calls += 1;
+    }
+    return after_launch(c, launch_moe_combine(yr, gate, route_pos, T, D, K, y, c->stream), "moe combine");
+  }
+}
+
+int mxq_moe_group_create(mxq_ctx c, int rank, int world, size_t max_tokens, size_t top_k, size_t d_model,
+                         mxq_moe_group* out, void* handle_out) {
+  MXQ_TRY({
+    if (int rc = check_ctx(c)) return rc;
+    if (!out || !handle_out) return fail(c, MXQ_ERR_INVALID_ARGUMENT, "null pointer");
+    *out = nullptr;
+    if (world < 1 || world > kMaxPeers || rank < 0 || rank >= world)
+      return fail(c, MXQ_ERR_INVALID_ARGUMENT, "moe group: rank %d of world %d (1..%d ranks)", rank, world, kMaxPeers);
+    if (max_tokens == 0 || top_k == 0 || d_model == 0 || d_model % 4 || max_tokens * top_k > (1u << 26))
+      return fail(c, MXQ_ERR_INVALID_ARGUMENT, "moe group: max_tokens, top_k > 0, d_model a multiple of 4");
+    DeviceGuard g(c->device);
+    auto* G = new mxq_moe_group_s();
+    G->ctx = c;
+    G->rank = rank;
+    G->world = world;
+    G->max_routes = max_tokens * top_k;
+    G->D = d_model;
+    G->half_bytes = (G->max_routes * d_model * 4 + 255) / 256 * 256;
+    G->bytes = G->off_yr + 2 * G->half_bytes;
+    cudaError_t e = cudaMalloc(&G->mbox, G->bytes);
+    if (e == cudaSuccess) e = cudaMemset(G->mbox, 0, G->off_yr);
+    if (e == cudaSuccess) e = cudaMalloc(&G->local, 4 * sizeof(uint32_t));
+    if (e == cudaSuccess) e = cudaMemset(G->local, 0, 4 * sizeof(uint32_t));
+    cudaIpcMemHandle_t h{};
+    if (e == cudaSuccess) e = cudaIpcGetMemHandle(&h, G->mbox);
+    if (e == cudaSuccess) e = cudaDeviceSynchronize();
+    if (e != cudaSuccess) {
+      cudaFree(G->mbox);
+      cudaFree(G->local);
+      delete G;
+      return cuda_fail(c, e, "moe group mailbox");
+    }
+    std::memcpy(handle_out, &h, sizeof(h));
+    G->base[rank] = G->mbox;
+    *out = G;
+    return MXQ_OK;
+  })
+}
+
+int mxq_moe_group_connect(mxq_moe_group G, const void* handles) {
+  MXQ_TRY({
+    if (!G || !handles) return fail(nullptr, MXQ_ERR_INVALID_ARGUMENT, "null pointer");
+    mxq_context* c = G->ctx;
+    DeviceGuard g(c->device);
+    for (int r = 0; r < G->world; ++r) {
+      if (r == G->rank || G->base[r]) continue;
+      cudaIpcMemHandle_t h;
+      std::memcpy(&h, static_cast<const uint8_t*>(handles) + (size_t)r * sizeof(h), sizeof(h));
+      void* p = nullptr;
+      const cudaError_t e = cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess);
+      if (e != cudaSuccess) return cuda_fail(c, e, "open a peer's moe mailbox");
+      G->base[r] = static_cast<uint8_t*>(p);
+      G->opened[r] = true;
+    }
+    return MXQ_OK;
+  })
+}
+
+int mxq_moe_group_set_wait_limit(mxq_moe_group G, uint32_t wait_us) {
+  if (!G) return fail(nullptr, MXQ_ERR_INVALID_ARGUMENT, "null moe group");
+  if (wait_us == 0 || wait_us > 10000000u)
+    return fail(G->ctx, MXQ_ERR_INVALID_ARGUMENT, "moe group wait limit must be in [1, 1e7] microseconds");
+  G->wait_ns = (uint64_t)wait_us * 1000ull;
+  return MXQ_OK;
+}
+
+int mxq_moe_group_destroy(mxq_moe_group G) {
+  if (!G) return fail(nullptr, MXQ_ERR_INVALID_ARGUMENT, "null moe group");
+  DeviceGuard g(G->ctx->device);
+  cudaDeviceSynchronize();
+  for (int r = 0; r < G->world; ++r)
+    if (G->opened[r]) cudaIpcCloseMemHandle(G->base[r]);
+  cudaFree(G->mbox);
+  cudaFree(G->local);
+  delete G;
+  return MXQ_OK;
+}
+
+int mxq_moe_swiglu_sharded(mxq_ctx c, mxq_moe_group G, const mxq_weight* w_gate, const mxq_weight* w_up,
+                           const mxq_weight* w_down, size_t n_experts, const float* x, const float* logits,
+                           size_t t, size_t k, float* y) {
+  MXQ_TRY({
+    if (int rc = check_ctx(c)) return rc;
+    if (!G || !w_gate || !w_up || !w_down || !x || !logits || !y || n_experts == 0)
+      return fail(c, MXQ_ERR_INVALID_ARGUMENT, "null pointer or no experts");
+    if (G->ctx != c) return fail(c, MXQ_ERR_INVALID_ARGUMENT, "moe group belongs to another context");
+    for (int r = 0; r < G->world; ++r)
+      if (!G->base[r]) return fail(c, MXQ_ERR_INVALID_ARGUMENT, "moe group not connected (mxq_moe_group_connect)");
+    if (!aligned16(x)) return fail(c, MXQ_ERR_INVALID_ARGUMENT, "fp32 input must be 16-byte aligned (it is read in 16-byte vectors)");
+    if (n_experts % (size_t)G->world)
+      return fail(c, MXQ_ERR_INVALID_ARGUMENT, "expert-parallel moe: %zu experts do not split over %d ranks", n_experts,
+                  G->world);
+    if (k == 0 || k > n_experts)
+      return fail(c, MXQ_ERR_INVALID_ARGUMENT, "top-k: k=%zu must be in [1, n_experts=%zu]", k, n_experts);
+    if (k > 64 || n_experts > 4096) return fail(c, MXQ_ERR_UNSUPPORTED, "top-k: k <= 64 and n_experts <= 4096");
+    const int E = (int)n_experts, El = E / G->world;
+    for (int e = 0; e < El; ++e) {
+      if (int rc = check_weight(c, w_gate[e])) return rc;
+      if (int rc = check_weight(c, w_up[e])) return rc;
+      if (int rc = check_weight(c, w_down[e])) return rc;
+    }
+    const int D = w_gate[0]->v.K, F = w_gate[0]->v.N;
+    for (int e = 0; e < El; ++e) {
+      const WeightView &g = w_gate[e]->v, &u = w_up[e]->v, &d = w_down[e]->v;
+      if (g.K != D || g.N != F || u.K != D || u.N != F || d.K != F || d.N != D)
+        return fail(c, MXQ_ERR_INVALID_ARGUMENT,
+                    "expert %d shapes: gate/up must be [%d][%d] and down [%d][%d]", e, F, D, D, F);
+    }
+    if ((size_t)D != G->D) return fail(c, MXQ_ERR_INVALID_ARGUMENT, "moe group sized for d_model %zu, experts have %d", G->D, D);
+    if (t == 0) return MXQ_OK;
+    if (t * k > G->max_routes)
+      return fail(c, MXQ_ERR_INVALID_ARGUMENT, "moe group sized for %zu routes, got %zu tokens x top-%zu", G->max_routes,
+                  t, k);
+    DeviceGuard g(c->device);
+    return moe_layer(c, w_gate, w_up, w_down, E, G->rank * El, El, x, logits, (int)t, (int)k, D, F, y, G);
   })
 }
 

@@ -184,9 +184,12 @@ int tp_gather(mxq_decoder_s* D, int slot, int rows, const uint8_t* src, size_t r
   a.world = D->world;
   a.rank = D->rank;
   a.rows = rows;
+  a.skip_rank = -1;
   a.src = src;
   a.row_bytes = row_bytes;
   a.dst_off = tp_slot_off(D, slot);
+  a.row_stride = row_bytes * D->world;       // [row][rank][values]
+  a.rank_stride = row_bytes;
   if (a.dst_off + (size_t)rows * row_bytes * D->world > tp_slot_off(D, slot + 1))
     return dfail(D, MXQ_ERR_INVALID_ARGUMENT, "tensor-parallel exchange larger than its mailbox slot");
   for (int r = 0; r < D->world; ++r) {

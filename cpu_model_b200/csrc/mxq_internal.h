@@ -166,16 +166,17 @@ struct PeerArgs {
 // role 1 / 2: the first / second linear of the pair (see the kernel)
 cudaError_t launch_cogemv_peer(const GemvArgs& a, const PeerArgs& p, int role, cudaStream_t st, bool pdl);
 
-// Peer all-gather of the tensor-parallel decoder (mxq_tp.cu).  Each rank
-// holds `rows` rows of row_bytes (a multiple of 16) at src, contiguous; the
-// launch stores row r at dst_off + (r * world + rank) * row_bytes of every
-// rank's mailbox, sets this rank's flag word in every mailbox to the slot's
-// next sequence number, and its last CTA waits (bounded) until every rank's
-// flag in the local mailbox has reached it.
+// Peer exchange over mailboxes (mxq_tp.cu).  This rank's `rows` rows of
+// row_bytes (a multiple of 16) at src, contiguous, go to every rank's
+// mailbox (but skip_rank's, -1 for none): row r at
+// dst_off + r * row_stride + rank * rank_stride.  The launch then sets this
+// rank's flag word in every mailbox to the slot's next sequence number, and
+// its last CTA waits (bounded) until every rank's flag in the local mailbox
+// has reached it.  rows may be 0 (only the flags).
 struct TpGatherArgs {
-  int world, rank, rows;
+  int world, rank, rows, skip_rank;
   const uint8_t* src;              // 16-byte aligned
-  size_t row_bytes, dst_off;
+  size_t row_bytes, dst_off, row_stride, rank_stride;
   uint8_t* base[kMaxPeers];        // every rank's mailbox as mapped here
   uint32_t* flag_out[kMaxPeers];   // per rank: this rank's flag word of the slot
   const uint32_t* wait_flags;      // local mailbox: the slot's flags, [world]

@@ -1,4 +1,5 @@
-// mxq_tp.cu -- the peer all-gather of the tensor-parallel decoder.
+// mxq_tp.cu -- peer exchanges over mailboxes: the partial sums of the
+// tensor-parallel decoder and the expert outputs of the expert-parallel MoE.
 //
 // Each rank of a sharded decoder computes, for the O and down linears, a
 // partial sum of every output row over its part of K (whole 32-blocks, so
@@ -11,7 +12,9 @@
 // mailbox, then waits, bounded, until every rank's flag in its own mailbox
 // shows the same sequence number.  The kernel after it (the residual) reads
 // the partials from the local mailbox once this grid has completed and adds
-// them in rank order.
+// them in rank order.  The expert-parallel MoE uses the same launch to
+// copy this rank's expert-output rows (a contiguous slot range) to the same
+// rows of every other rank's mailbox.
 //
 // Ordering: the copy starts after griddepcontrol.wait, so the producer's
 // rows are complete; each CTA's stores are ordered before its arrival on the
@@ -39,8 +42,9 @@ __global__ void __launch_bounds__(kTpThreads) tp_gather_kernel(TpGatherArgs a) {
   for (long i = (long)blockIdx.x * kTpThreads + threadIdx.x; i < n; i += nth) {
     const long r = i / per_row, c = i - r * per_row;
     const uint4 v = __ldcg(reinterpret_cast<const uint4*>(a.src) + i);
-    const size_t off = a.dst_off + ((size_t)r * a.world + a.rank) * a.row_bytes + (size_t)c * 16;
-    for (int p = 0; p < a.world; ++p) *reinterpret_cast<uint4*>(a.base[p] + off) = v;
+    const size_t off = a.dst_off + (size_t)r * a.row_stride + (size_t)a.rank * a.rank_stride + (size_t)c * 16;
+    for (int p = 0; p < a.world; ++p)
+      if (p != a.skip_rank) *reinterpret_cast<uint4*>(a.base[p] + off) = v;
   }
   __syncthreads();
   if (threadIdx.x == 0) {
@@ -65,8 +69,9 @@ __global__ void __launch_bounds__(kTpThreads) tp_gather_kernel(TpGatherArgs a) {
 }  // namespace
 
 cudaError_t launch_tp_gather(const TpGatherArgs& a, cudaStream_t st) {
-  if (a.world < 1 || a.world > kMaxPeers || a.rank < 0 || a.rank >= a.world || a.rows < 1 || !a.src ||
-      a.row_bytes == 0 || a.row_bytes % 16 || a.dst_off % 16 || (reinterpret_cast<uintptr_t>(a.src) & 15u) ||
+  if (a.world < 1 || a.world > kMaxPeers || a.rank < 0 || a.rank >= a.world || a.rows < 0 ||
+      (a.rows > 0 && (!a.src || a.row_bytes == 0 || a.row_bytes % 16 || a.dst_off % 16 || a.row_stride % 16 ||
+                      a.rank_stride % 16 || (reinterpret_cast<uintptr_t>(a.src) & 15u))) ||
       !a.wait_flags || !a.seq || !a.grid_cnt)
     return cudaErrorInvalidValue;
   for (int r = 0; r < a.world; ++r)

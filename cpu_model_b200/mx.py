@@ -619,6 +619,62 @@ def moe_swiglu(x, logits, gate_w, up_w, down_w, k, ctx=None):
     return y
 
 
+class MoEGroup:
+    """One rank of the expert-parallel MoE layer over `world` GPUs
+    (mxq_moe_group_*, mxq_moe_swiglu_sharded): rank r owns experts
+    [r E/world, (r+1) E/world); every rank passes all T tokens and gets the
+    full y, bit-identical to moe_swiglu over all experts on one GPU.
+
+    handle() gives this rank's 64-byte mailbox handle; the caller gathers
+    every rank's (e.g. torch.distributed.all_gather_object) and passes the
+    list, in rank order, to connect()."""
+
+    def __init__(self, rank, world, max_tokens, top_k, d_model, ctx=None):
+        self.ctx = ctx or context()
+        self.rank, self.world = rank, world
+        h = ctypes.c_void_p()
+        self._handle = ctypes.create_string_buffer(_lib.PEER_HANDLE_BYTES)
+        self.ctx._bind()
+        check(self.ctx.lib.mxq_moe_group_create(self.ctx.h, rank, world, max_tokens, top_k, d_model, ctypes.byref(h),
+                                                ctypes.cast(self._handle, ctypes.c_void_p)), self.ctx.h)
+        self.h = h
+
+    def handle(self):
+        return bytes(self._handle.raw)
+
+    def connect(self, handles):
+        assert len(handles) == self.world and all(len(b) == _lib.PEER_HANDLE_BYTES for b in handles)
+        buf = ctypes.create_string_buffer(b"".join(handles), _lib.PEER_HANDLE_BYTES * self.world)
+        check(self.ctx.lib.mxq_moe_group_connect(self.h, ctypes.cast(buf, ctypes.c_void_p)), self.ctx.h)
+
+    def set_wait_limit(self, us):
+        check(self.ctx.lib.mxq_moe_group_set_wait_limit(self.h, int(us)), self.ctx.h)
+
+    def moe_swiglu(self, x, logits, gate_w, up_w, down_w, k, out=None):
+        """x [T][D], logits [T][E] (the same on every rank); gate_w/up_w/down_w
+        this rank's E/world experts.  Returns y [T][D]."""
+        _need_cuda(x, torch.float32, "x")
+        _need_cuda(logits, torch.float32, "logits")
+        t, d = x.shape
+        e = logits.shape[1]
+        n = len(gate_w)
+        if n * self.world != e or len(up_w) != n or len(down_w) != n:
+            raise ValueError("moe group: each rank passes E/world gate/up/down weights")
+        arr = lambda ws: (ctypes.c_void_p * n)(*[w.h.value for w in ws])
+        g, u, dn = arr(gate_w), arr(up_w), arr(down_w)
+        y = out if out is not None else torch.empty((t, d), dtype=torch.float32, device=x.device)
+        self.ctx._bind()
+        check(self.ctx.lib.mxq_moe_swiglu_sharded(self.ctx.h, self.h, ctypes.cast(g, ctypes.c_void_p),
+                                                  ctypes.cast(u, ctypes.c_void_p), ctypes.cast(dn, ctypes.c_void_p),
+                                                  e, _ptr(x), _ptr(logits), t, k, _ptr(y)), self.ctx.h)
+        return y
+
+    def close(self):
+        if getattr(self, "h", None):
+            self.ctx.lib.mxq_moe_group_destroy(self.h)
+            self.h = None
+
+
 def policy_head(logits, actions, ctx=None):
     """PPO rollout head (mxq_policy_head): (log_probs [R][C], action_logp [R],
     entropy [R]) from logits and action weights [R][C]."""

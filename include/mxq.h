@@ -357,6 +357,44 @@ MXQ_API int mxq_moe_swiglu(mxq_ctx ctx, const mxq_weight* w_gate,
                            const float* logits, size_t t, size_t k,
                            float* y);
 
+/* The same layer expert-parallel over `world` GPUs of one node (one process
+ * and context per GPU): rank r owns experts [r E/world, (r+1) E/world)
+ * (E a multiple of world) and passes only their weights.  Every rank passes
+ * the same x and logits (all T tokens) and gets the full y.  Each rank routes
+ * every token the same way, runs its own experts' GEMMs on the tokens
+ * routed to them, writing the expert outputs into its mailbox, then one
+ * kernel copies those rows into every other rank's mailbox over NVLink
+ * (peer stores into CUDA IPC memory), sets its flag there and waits
+ * (bounded) for every rank's flag; the combine then runs as on one GPU.
+ * No NCCL on the data path.  y is bit-identical to mxq_moe_swiglu over all
+ * E experts on one GPU.  Usage:
+ *   mxq_moe_group_create(ctx, rank, world, max_tokens, top_k, d_model, &g,
+ *                        handle)  -- handle: MXQ_PEER_HANDLE_BYTES to
+ *     exchange; the mailbox holds 2 x max_tokens x top_k x d_model fp32;
+ *   (the caller gathers every rank's handle, in rank order)
+ *   mxq_moe_group_connect(g, handles)      -- world * 64 bytes
+ *   mxq_moe_swiglu_sharded(ctx, g, w_gate, w_up, w_down, E, x, logits, T,
+ *                          k, y)           -- w_*: this rank's E/world
+ * Every rank must make the same calls in the same order.  A wait that runs
+ * out (mxq_moe_group_set_wait_limit, default 2 s) sets the context's status
+ * word (mxq_synchronize returns MXQ_ERR_TIMEOUT) and the group must be
+ * created again. */
+typedef struct mxq_moe_group_s* mxq_moe_group;
+MXQ_API int mxq_moe_group_create(mxq_ctx ctx, int rank, int world,
+                                 size_t max_tokens, size_t top_k,
+                                 size_t d_model, mxq_moe_group* out,
+                                 void* handle_out);
+MXQ_API int mxq_moe_group_connect(mxq_moe_group g, const void* handles);
+MXQ_API int mxq_moe_group_set_wait_limit(mxq_moe_group g, uint32_t wait_us);
+MXQ_API int mxq_moe_group_destroy(mxq_moe_group g);
+MXQ_API int mxq_moe_swiglu_sharded(mxq_ctx ctx, mxq_moe_group g,
+                                   const mxq_weight* w_gate,
+                                   const mxq_weight* w_up,
+                                   const mxq_weight* w_down,
+                                   size_t n_experts, const float* x,
+                                   const float* logits, size_t t, size_t k,
+                                   float* y);
+
 /* The reference's micro-expert pool (nn/config/model_config.hpp:23-25:
  * 1024 experts, top-16 routed, 2 shared always active; 16-row expert slices
  * of the gate/up matrices, training/fidelity_test.cpp:57-59; executed by

@@ -176,3 +176,54 @@ def decoder_tp_worker(rank, world, port, cfg, seed, steps, outdir):
              ref_outs=ref[0], ref_one=ref[1], ref_logp=ref[2])
     dist.barrier()
     dist.destroy_process_group()
+
+
+def moe_experts_dev(ctx, fmt, e, d, f, density, seed):
+    """E experts (gate [F][D], up [F][D], down [D][F]) of block-sparse MX
+    weights from per-expert seeds, as device handles."""
+    from cpu_model_b200 import mx
+    out = []
+    for j in range(e):
+        mats = []
+        for i, (n, k) in enumerate(((f, d), (f, d), (d, f))):
+            w, ws = synth.weights(fmt, n, k, -8, -3, seed + 10 * j + i)
+            mask = synth.block_mask(n, k, density, seed + 10 * j + i + 500)
+            mats.append(mx.MXWeight(torch.from_numpy(w), torch.from_numpy(ws), fmt, n, k, ctx, block_mask=mask))
+        out.append(mats)
+    return out
+
+
+def moe_ep_worker(rank, world, port, fmt, t, d, f, e, k, calls, outdir):
+    """One GPU rank of mxq_moe_swiglu_sharded: handles over a gloo group; the
+    same tokens and logits on every rank; `calls` calls (the mailbox halves
+    alternate), then mxq_moe_swiglu over all experts on this GPU."""
+    from cpu_model_b200 import mx
+    _init(rank, world, port)
+    torch.cuda.set_device(rank)
+    ctx = mx.MXContext(rank)
+    experts = moe_experts_dev(ctx, fmt, e, d, f, 0.25, 700)
+    el = e // world
+    mine = experts[rank * el:(rank + 1) * el]
+    G = mx.MoEGroup(rank, world, t, k, d, ctx)
+    handles = [None] * world
+    dist.all_gather_object(handles, G.handle())
+    G.connect(handles)
+    dist.barrier()
+    outs = []
+    for i in range(calls):
+        x = torch.from_numpy(synth.normal((t, d), 31 + i)).cuda()
+        logits = torch.from_numpy(synth.normal((t, e), 41 + i)).cuda()
+        outs.append(G.moe_swiglu(x, logits, [m[0] for m in mine], [m[1] for m in mine], [m[2] for m in mine],
+                                 k).cpu().numpy())
+    ctx.synchronize()
+    dist.barrier()
+    G.close()
+    refs = []
+    for i in range(calls):
+        x = torch.from_numpy(synth.normal((t, d), 31 + i)).cuda()
+        logits = torch.from_numpy(synth.normal((t, e), 41 + i)).cuda()
+        refs.append(mx.moe_swiglu(x, logits, [m[0] for m in experts], [m[1] for m in experts],
+                                  [m[2] for m in experts], k, ctx).cpu().numpy())
+    np.savez(os.path.join(outdir, "moe_%d.npz" % rank), outs=np.stack(outs), refs=np.stack(refs))
+    dist.barrier()
+    dist.destroy_process_group()
