@@ -229,6 +229,25 @@ __device__ inline int peer_wait(const uint32_t* flags, int world, uint32_t ep, u
   return 1;
 }
 
+// The same wait over every rank's flag but `skip`'s (a rank's own flag, which
+// only its own kernel would set).
+__device__ inline int peer_wait_others(const uint32_t* flags, int world, int skip, uint32_t ep, uint64_t limit_ns,
+                                       uint32_t* status) {
+  const uint64_t t0 = globaltimer_ns();
+  for (int r = 0; r < world; ++r) {
+    if (r == skip) continue;
+    for (uint32_t it = 0;; ++it) {
+      if ((int)(ld_acquire_sys(flags + r) - ep) >= 0) break;
+      if (it > (1u << 26) || globaltimer_ns() - t0 > limit_ns) {
+        if (status) atomicOr(status, kStatusTimeout);
+        return 0;
+      }
+      __nanosleep(100);
+    }
+  }
+  return 1;
+}
+
 // 1-D bulk copy global -> shared, completing bytes on an mbarrier.
 // Both addresses 16-byte aligned and bytes a multiple of 16.
 __device__ __forceinline__ void bulk_g2s(void* dst_smem, const void* src,

@@ -211,6 +211,42 @@ int tp_gather_f32(mxq_decoder_s* D, int slot, const float* src, int R, int n, co
   return MXQ_OK;
 }
 
+// Every rank's partial sums [R][d] of this exchange (this rank's in
+// D->tmp), added in rank order, then the residual and the RMSNorm with
+// gains g into D->hn.  Up to kExchNormMaxRows rows in one kernel (the
+// exchange fused into the residual); more rows through the mailbox slot.
+int tp_exchange_norm(mxq_decoder_s* D, int slot, int R, const float* g) {
+  const int d = D->d;
+  const float eps = D->cfg.norm_eps;
+  if (R <= kExchNormMaxRows) {
+    ExchNormArgs a{};
+    a.h = D->h;
+    a.y_own = D->tmp;
+    a.g = g;
+    a.out = D->hn;
+    a.R = R;
+    a.d = d;
+    a.world = D->world;
+    a.rank = D->rank;
+    a.eps = eps;
+    a.slot_off = tp_slot_off(D, slot);
+    for (int r = 0; r < D->world; ++r) {
+      a.base[r] = D->peer[r];
+      a.flag_out[r] = tp_flags(D, r, slot) + D->rank;
+    }
+    a.wait_flags = tp_flags(D, D->rank, slot);
+    a.seq = D->tpw + slot;
+    a.grid_cnt = D->tpw + 2 + slot;
+    a.status = ctx_status_word(D->c);
+    a.wait_ns = D->wait_ns;
+    return dcheck(D, dk_exchange_add_rmsnorm(a, ctx_stream(D->c)), "exchange + residual + rmsnorm");
+  }
+  const float* full = nullptr;
+  if (int rc = tp_gather_f32(D, slot, D->tmp, R, d, &full)) return rc;
+  return dcheck(D, dk_add_parts_rmsnorm(D->h, full, D->world, g, R, d, eps, D->hn, ctx_stream(D->c)),
+                "residual + rmsnorm");
+}
+
 // The layers of a tensor-parallel decoder (see the file comment): as layers()
 // below, over this rank's heads and FFN units, with the two exchanges.
 int layers_tp(mxq_decoder_s* D, int B, int T, int pos0, bool decode) {
@@ -219,7 +255,6 @@ int layers_tp(mxq_decoder_s* D, int B, int T, int pos0, bool decode) {
   const int R = B * T, d = D->d, dl = D->dl, Fl = D->Fl;
   const float eps = D->cfg.norm_eps;
   int rc;
-  const float* full = nullptr;
   for (int l = 0; l < D->L; ++l) {
     __nv_bfloat16* kc = D->kc + (size_t)l * kv_layer_elems(D);
     __nv_bfloat16* vc = D->vc + (size_t)l * kv_layer_elems(D);
@@ -248,11 +283,7 @@ int layers_tp(mxq_decoder_s* D, int B, int T, int pos0, bool decode) {
     // output row; every rank's partials, added in rank order, then the
     // residual and the RMSNorm
     if ((rc = mxq_linear(c, D->o[l], D->att, (size_t)R, D->tmp))) return rc;
-    if ((rc = tp_gather_f32(D, 0, D->tmp, R, d, &full))) return rc;
-    if ((rc = dcheck(D, dk_add_parts_rmsnorm(D->h, full, D->world, D->gains + (size_t)(2 * l + 1) * d, R, d, eps,
-                                             D->hn, st),
-                     "residual + rmsnorm")))
-      return rc;
+    if ((rc = tp_exchange_norm(D, 0, R, D->gains + (size_t)(2 * l + 1) * d))) return rc;
     if ((rc = trace_copy(D, l, MXQ_TRACE_H1, D->h, (size_t)R * d))) return rc;
     if ((rc = trace_copy(D, l, MXQ_TRACE_NORM2, D->hn, (size_t)R * d))) return rc;
     // this rank's gate rows, then its up rows: [R][2 Fl]
@@ -274,11 +305,7 @@ int layers_tp(mxq_decoder_s* D, int B, int T, int pos0, bool decode) {
       if ((rc = dcheck(D, dk_swiglu(D->gub, R, Fl, D->act, st), "swiglu"))) return rc;
       if ((rc = mxq_linear(c, D->down[l], D->act, (size_t)R, D->tmp))) return rc;
     }
-    if ((rc = tp_gather_f32(D, 1, D->tmp, R, d, &full))) return rc;
-    if ((rc = dcheck(D, dk_add_parts_rmsnorm(D->h, full, D->world, D->gains + (size_t)(2 * l + 2) * d, R, d, eps,
-                                             D->hn, st),
-                     "residual + rmsnorm")))
-      return rc;
+    if ((rc = tp_exchange_norm(D, 1, R, D->gains + (size_t)(2 * l + 2) * d))) return rc;
     if ((rc = trace_copy(D, l, MXQ_TRACE_OUT, D->h, (size_t)R * d))) return rc;
   }
   return trace_copy(D, D->L, MXQ_TRACE_IN, D->h, (size_t)R * d);

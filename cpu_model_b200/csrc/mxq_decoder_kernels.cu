@@ -109,6 +109,95 @@ __global__ void __launch_bounds__(kNormThreads) norm_kernel(float* __restrict__ 
   }
 }
 
+// The exchange of the tensor-parallel decoder's partial sums fused into the
+// residual + RMSNorm (ExchNormArgs).  Waits only on the other GPUs' flags:
+// a rank's own CTAs never wait on each other, and with at most one CTA a
+// row and kExchNormMaxRows rows every CTA of the grid fits on the GPU at
+// once, so each rank's flag is set whatever the others do.
+__global__ void __launch_bounds__(kNormThreads) exch_norm_kernel(ExchNormArgs a) {
+  DK_PDL_PROLOGUE();
+  __shared__ float ws[kNormThreads / 32];
+  __shared__ uint32_t next_s;
+  __shared__ int ok_s;
+  const int r = blockIdx.x, d4 = a.d / 4;
+  if (threadIdx.x == 0) next_s = *a.seq + 1u;     // read before this CTA arrives on the counter
+  const float4* yo = reinterpret_cast<const float4*>(a.y_own + (size_t)r * a.d);
+  float4 own[kNormVec];
+  const size_t row_off = a.slot_off + ((size_t)r * a.world + a.rank) * a.d * 4;
+#pragma unroll
+  for (int u = 0; u < kNormVec; ++u) {
+    const int i = threadIdx.x + u * kNormThreads;
+    own[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (i < d4) {
+      own[u] = yo[i];
+      for (int q = 0; q < a.world; ++q)
+        if (q != a.rank) *reinterpret_cast<float4*>(a.base[q] + row_off + (size_t)i * 16) = own[u];
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const uint32_t next = next_s;
+    __threadfence();
+    const unsigned old = atomicAdd(a.grid_cnt, 1u);
+    if (old == gridDim.x - 1u) {
+      *a.grid_cnt = 0u;
+      if (a.world > 1) {
+        asm volatile("fence.acq_rel.sys;" ::: "memory");
+        for (int q = 0; q < a.world; ++q)
+          if (q != a.rank) st_release_sys(a.flag_out[q], next);
+      }
+      *a.seq = next;
+    }
+    ok_s = a.world == 1 ||
+           peer_wait_others(a.wait_flags, a.world, a.rank, next, a.wait_ns ? a.wait_ns : kWaitLimitNs, a.status);
+  }
+  __syncthreads();
+  // partial sums in rank order (this rank's from registers), then the residual
+  float4* hr = reinterpret_cast<float4*>(a.h + (size_t)r * a.d);
+  const float4* mb = reinterpret_cast<const float4*>(a.base[a.rank] + a.slot_off + (size_t)r * a.world * a.d * 4);
+  float4 v[kNormVec];
+  float s = 0.0f;
+#pragma unroll
+  for (int u = 0; u < kNormVec; ++u) {
+    const int i = threadIdx.x + u * kNormThreads;
+    v[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (i < d4) {
+      float4 b = a.rank == 0 ? own[u] : __ldcg(mb + i);
+      for (int q = 1; q < a.world; ++q) {
+        const float4 c = q == a.rank ? own[u] : __ldcg(mb + (size_t)q * d4 + i);
+        b.x = __fadd_rn(b.x, c.x);
+        b.y = __fadd_rn(b.y, c.y);
+        b.z = __fadd_rn(b.z, c.z);
+        b.w = __fadd_rn(b.w, c.w);
+      }
+      if (!ok_s) b = make_float4(0.f, 0.f, 0.f, 0.f);   // a timed-out exchange: the status word reports it
+      v[u] = hr[i];
+      v[u].x = __fadd_rn(v[u].x, b.x);
+      v[u].y = __fadd_rn(v[u].y, b.y);
+      v[u].z = __fadd_rn(v[u].z, b.z);
+      v[u].w = __fadd_rn(v[u].w, b.w);
+      hr[i] = v[u];
+    }
+    s = __fmaf_rn(v[u].x, v[u].x, s);
+    s = __fmaf_rn(v[u].y, v[u].y, s);
+    s = __fmaf_rn(v[u].z, v[u].z, s);
+    s = __fmaf_rn(v[u].w, v[u].w, s);
+  }
+  const float tot = norm_block_sum(s, ws);
+  const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(tot, (float)a.d), a.eps)));
+  float4* o = reinterpret_cast<float4*>(a.out + (size_t)r * a.d);
+  const float4* g4 = reinterpret_cast<const float4*>(a.g);
+#pragma unroll
+  for (int u = 0; u < kNormVec; ++u) {
+    const int i = threadIdx.x + u * kNormThreads;
+    if (i < d4) {
+      const float4 gg = g4[i];
+      o[i] = make_float4(__fmul_rn(__fmul_rn(v[u].x, inv), gg.x), __fmul_rn(__fmul_rn(v[u].y, inv), gg.y),
+                         __fmul_rn(__fmul_rn(v[u].z, inv), gg.z), __fmul_rn(__fmul_rn(v[u].w, inv), gg.w));
+    }
+  }
+}
+
 // ----------------------------------------------------------- residual ---
 __global__ void add_kernel(float* __restrict__ h, const float* __restrict__ y, size_t n4) {
   DK_PDL_PROLOGUE();
@@ -555,6 +644,15 @@ cudaError_t dk_add_rmsnorm(float* h, const float* y, const float* g, int R, int 
                            cudaStream_t s) {
   if (d % 4 || d / 4 > kNormThreads * kNormVec) return cudaErrorInvalidValue;
   return pdl_launch(norm_kernel<true>, dim3(R), dim3(kNormThreads), 0, s, h, y, g, d, eps, out, 1, (size_t)d);
+}
+cudaError_t dk_exchange_add_rmsnorm(const ExchNormArgs& a, cudaStream_t s) {
+  if (a.d % 4 || a.d / 4 > kNormThreads * kNormVec || a.R < 1 || a.R > kExchNormMaxRows || a.world < 1 ||
+      a.world > kMaxPeers || a.rank < 0 || a.rank >= a.world || a.slot_off % 16 || !a.seq || !a.grid_cnt ||
+      !a.wait_flags)
+    return cudaErrorInvalidValue;
+  for (int q = 0; q < a.world; ++q)
+    if (!a.base[q] || !a.flag_out[q] || (reinterpret_cast<uintptr_t>(a.base[q]) & 15u)) return cudaErrorInvalidValue;
+  return pdl_launch(exch_norm_kernel, dim3(a.R), dim3(kNormThreads), 0, s, a);
 }
 cudaError_t dk_add_parts_rmsnorm(float* h, const float* y, int nparts, const float* g, int R, int d, float eps,
                                  float* out, cudaStream_t s) {

@@ -187,6 +187,32 @@ struct TpGatherArgs {
 };
 cudaError_t launch_tp_gather(const TpGatherArgs& a, cudaStream_t st);
 
+// The tensor-parallel decoder's exchange fused into its residual + RMSNorm
+// (mxq_decoder_kernels.cu), for at most kExchNormMaxRows rows (one CTA a
+// row, all resident at once): each CTA stores this rank's partial row into
+// every other rank's mailbox at [row][rank][d] of the slot, the last CTA
+// releases this rank's flag there, and every CTA waits (bounded) for every
+// other rank's flag, then adds the partials in rank order (its own from
+// y_own), the residual, and normalises.
+constexpr int kExchNormMaxRows = 148;
+struct ExchNormArgs {
+  float* h;                        // [R][d] residual stream (updated)
+  const float* y_own;              // [R][d] this rank's partial sums
+  const float* g;                  // RMSNorm weights [d]
+  float* out;                      // [R][d]
+  int R, d, world, rank;
+  float eps;
+  uint8_t* base[kMaxPeers];        // every rank's mailbox as mapped here
+  size_t slot_off;                 // the slot's [R][world][d] fp32 in every mailbox
+  uint32_t* flag_out[kMaxPeers];   // per rank: this rank's flag word of the slot
+  const uint32_t* wait_flags;      // local mailbox: the slot's flags, [world]
+  uint32_t* seq;                   // local: the slot's completed exchanges
+  uint32_t* grid_cnt;              // local
+  uint32_t* status;
+  uint64_t wait_ns;
+};
+cudaError_t dk_exchange_add_rmsnorm(const ExchNormArgs& a, cudaStream_t s);
+
 // Batch-1 GEMV with two launches resident per SM (mxq_cogemv.cu): MX or fp32
 // input, fp32 output, optionally also MX bytes of the output (GemvArgs.yq).
 bool cogemv_supported(const WeightView& w, int B, bool inf32, bool qout);
