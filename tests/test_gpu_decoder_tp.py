@@ -132,6 +132,34 @@ def test_rank_weights_are_rows_of_the_unsharded_weights(ctx, world, cfg):
         plain.close()
 
 
+@pytest.mark.parametrize("world", [4, 8])
+def test_7b_rank_shard_shapes_in_every_regime(ctx, world):
+    """The linears a rank of a 4- or 8-GPU 7B decoder runs -- QKV and gate|up
+    rows, O and down columns (K = 4096 / world and 11008 / world, the
+    latter an odd number of 32-blocks at 8 GPUs) -- through the batch-1,
+    small-batch and tensor-core paths, against the oracle."""
+    from oracle import oracle
+    from cpu_model_b200 import synth
+    d, f = 4096, 11008
+    shapes = [(3 * d // world, d), (d, d // world), (2 * f // world, d), (d, f // world)]
+    for i, (n, k) in enumerate(shapes):
+        w, ws = synth.weights(4, n, k, -8, -3, 60 + i)
+        W = mx.MXWeight(torch.from_numpy(w), torch.from_numpy(ws), 4, n, k, ctx)
+        try:
+            for b in (1, 8, 32, 130):
+                x = synth.normal((b, k), 70 + b)
+                xq, xs = oracle.quantize_x(x)
+                ref = oracle.gemv(4, xq, xs, w, ws, n, k)
+                y = mx.mx_linear(torch.from_numpy(x).cuda(), W, ctx).cpu().numpy()
+                assert rel_l2(y, ref) <= REL_TOL, (n, k, b)
+                if b == 1:      # the MX-input GEMV the batch-1 down projection runs
+                    a = mx.mx_quantize_x(torch.from_numpy(x).cuda(), ctx)
+                    y = mx.mx_gemv(a, W, ctx).cpu().numpy()
+                    assert rel_l2(y, ref) <= REL_TOL, (n, k, "mx")
+        finally:
+            W.close()
+
+
 @pytest.mark.parametrize("rank,world,cfg", [
     (0, 3, CFG),                                                # 3 does not divide 2 heads
     (2, 2, CFG),                                                # rank out of range
