@@ -227,3 +227,19 @@ def moe_ep_worker(rank, world, port, fmt, t, d, f, e, k, calls, outdir):
     np.savez(os.path.join(outdir, "moe_%d.npz" % rank), outs=np.stack(outs), refs=np.stack(refs))
     dist.barrier()
     dist.destroy_process_group()
+
+
+def idle_rank_worker(kind, args, q, done):
+    """Rank 1 of a two-rank group on this GPU that never calls: it creates
+    its group (a MoE group or a sharded decoder), hands its mailbox handle
+    to the parent and waits, launching nothing, until the parent is done."""
+    from cpu_model_b200 import mx
+    ctx = mx.MXContext(0)
+    if kind == "moe":
+        g = mx.MoEGroup(1, 2, *args, ctx=ctx)
+    else:
+        g = mx.Decoder(seed=5, ctx=ctx, rank=1, world=2, **args)
+    q.put(g.handle())
+    done.wait(120)
+    g.close()
+    ctx.close()
